@@ -1,0 +1,590 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 KV-cache hot path (rsLLM's FP8 KV cache).
+
+Headline workload (``config.workload``): the decode-step batched append of
+the benchmark's config 2 -- 256 sequences with current lengths uniform in
+[1024, 32768], 61 layers, one new bf16 row (512 latent + 64 rope) per sequence
+per layer per step, quantised to FP8 E4M3FN into a paged pool of 64-token
+pages with a seeded random page table; a new page whenever a sequence crosses
+a page boundary.  One step = one launch over all 256 x 61 rows; the K timed
+steps are one CUDA-graph replay.
+
+metric/unit: algorithmic HBM bytes moved per second (GB/s) -- per row 1152 B
+of bf16 read + 672 B of FP8 row written, plus the 4-byte slot index per
+sequence per step; ``tokens_per_s`` (sequence-steps appended per second) is
+reported beside it.  Extra keys measure the other configurations of the same
+path on the same GPU: ``phases.gather`` (config 3: 64 x 32768 tokens x 61
+layers gathered + dequantised), ``phases.topk`` and ``phases.sparse_gather``
+(config 4: 32 x 64 queries over 131072 keys, k = 2048, 61 layers).
+
+Multi-GPU: one process per GPU (torchrun), each rank owns its own pool and
+runs the whole per-GPU workload (weak scaling); no collective in the timed
+region.  ``--impl reference`` times the CPU restatement of rsLLM's path (the
+oracle; rsLLM itself is Rust and cannot be built here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from ctypes import byref, c_void_p
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+N_SEQ_APPEND = 256
+N_LAYERS = 61
+LEN_RANGE = (1024, 32768)
+ROW_IN = 576 * 2           # bf16 row read
+ROW_OUT = 512 + 8 * 4 + 64 * 2  # stored row written (672 B)
+APPEND_ROW_BYTES = ROW_IN + ROW_OUT
+GATHER_ROW_BYTES = ROW_OUT + ROW_IN  # stored row read + bf16 row written
+L2_BYTES = 126 * 2**20
+GB = 1e9
+
+# DRAM bytes per launch from the ncu capture of each kernel, per unit of work
+# (profiles/*.md gives the command and the raw counters); None = not captured.
+NCU_TRAFFIC_PER_ROW = {"append": None, "gather": None, "sparse_gather": None}
+
+
+# ---------------------------------------------------------------------------
+# plumbing
+# ---------------------------------------------------------------------------
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+        torch.cuda.synchronize()
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.barrier()
+            self.pg.destroy_process_group()
+
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of this GPU's clocks and throttle reasons."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.rows: list[list[str]] = []
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={ident}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons, loaded = [], [], set(), 0
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                cur, top, util = float(r[0]), float(r[1]), float(r[3])
+            except (ValueError, IndexError):
+                continue
+            mx.append(top)
+            if util >= 50:
+                loaded += 1
+                sm.append(cur)
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows), "samples_under_load": loaded}
+
+
+def events_time(fn, stream: torch.cuda.Stream) -> float:
+    """Milliseconds of fn() on `stream`, by CUDA events recorded on it."""
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record(stream)
+    fn()
+    b.record(stream)
+    b.synchronize()
+    return a.elapsed_time(b)
+
+
+def flush_l2(dev):
+    buf = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+    buf.fill_(1)
+    del buf
+
+
+# ---------------------------------------------------------------------------
+# config 2: decode-step batched append
+# ---------------------------------------------------------------------------
+
+class AppendWorkload:
+    """Per-rank state of config 2: lengths, page table of the pages the run
+    touches, per-step slot mappings, per-step input rows."""
+
+    def __init__(self, n_steps: int, seed: int, dev: torch.device | None, make_rows: bool = True):
+        from rsllm_b200 import synth
+
+        self.n_steps = n_steps
+        lens = synth.uniform_ints(N_SEQ_APPEND, *LEN_RANGE, seed=seed).numpy().astype(np.int64)
+        first = lens // 64
+        last = (lens + n_steps - 1) // 64
+        need = last - first + 1
+        off = np.concatenate([[0], np.cumsum(need)])
+        self.n_pages = int(off[-1])
+        phys = synth.permutation(self.n_pages, seed=seed + 1).numpy().astype(np.int64)
+        steps = np.arange(n_steps)[:, None]
+        pos = lens[None, :] + steps                          # [steps, seq]
+        local = pos // 64 - first[None, :]
+        page = phys[off[:-1][None, :] + local]
+        self.slots_np = (page * 64 + pos % 64).astype(np.int32)  # [steps, seq]
+        self.new_pages_per_step = (pos % 64 == 0).sum(axis=1)
+        self.rows = None
+        if dev is not None:
+            self.slots = torch.from_numpy(self.slots_np).to(dev)
+            if make_rows:
+                n = N_LAYERS * N_SEQ_APPEND
+                self.rows = torch.empty((n_steps, N_LAYERS, N_SEQ_APPEND, 576), dtype=torch.bfloat16, device=dev)
+                for j in range(n_steps):
+                    self.rows[j].copy_(synth.kv_rows(n, seed=seed * 1000 + j, device=dev).view(N_LAYERS,
+                                                                                                N_SEQ_APPEND, 576))
+
+    @staticmethod
+    def bytes_per_step() -> int:
+        return N_LAYERS * N_SEQ_APPEND * APPEND_ROW_BYTES + N_SEQ_APPEND * 4
+
+
+def bench_append(args, dist: Dist, dev, peak) -> dict:
+    import rsllm_b200 as rk
+
+    W, K = args.warmup, args.steps
+    wl = AppendWorkload(W + K, seed=3 + 7919 * dist.rank, dev=dev)
+    pool = rk.PagedKvPool(wl.n_pages, N_LAYERS, device=dev)
+    pool.storage.zero_()
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for j in range(W):
+            pool.append_layer(0, wl.rows[j], wl.slots[j])
+        pool.check("append warm-up", stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for j in range(W, W + K):
+                pool.append_layer(0, wl.rows[j], wl.slots[j])
+    flush_l2(dev)
+    dist.barrier()
+
+    def replay():
+        with torch.cuda.stream(stream):
+            graph.replay()
+
+    ms = events_time(replay, stream)
+    dist.barrier()
+    pool.check("append", stream)
+    ms = dist.max(ms)
+    del graph
+    step_bytes = wl.bytes_per_step()
+    res = {
+        "ms_per_step": ms / K,
+        "gbs_per_gpu": step_bytes * K / (ms * 1e-3) / GB,
+        "tokens_per_s_per_gpu": N_SEQ_APPEND * K / (ms * 1e-3),
+        "step_bytes": step_bytes,
+        "pool": pool,
+        "wl": wl,
+    }
+    # end to end through the public API: pinned host rows -> device, append,
+    # status word back, every step
+    res["e2e"] = bench_append_e2e(pool, wl, W, K, dist, dev)
+    return res
+
+
+def bench_append_e2e(pool, wl: AppendWorkload, W: int, K: int, dist: Dist, dev) -> dict:
+    n_host = min(K, 8)
+    host_rows = [wl.rows[W + j].cpu().pin_memory() for j in range(n_host)]
+    host_slots = [torch.from_numpy(wl.slots_np[W + j].copy()).pin_memory() for j in range(K)]
+    dev_rows = [torch.empty_like(wl.rows[0]) for _ in range(2)]
+    dev_slots = [torch.empty(N_SEQ_APPEND, dtype=torch.int32, device=dev) for _ in range(2)]
+    status_host = torch.empty(K, dtype=torch.int32).pin_memory()
+    stream = torch.cuda.Stream(device=dev)
+
+    def run():
+        with torch.cuda.stream(stream):
+            for j in range(K):
+                b = j & 1
+                dev_rows[b].copy_(host_rows[j % n_host], non_blocking=True)
+                dev_slots[b].copy_(host_slots[j], non_blocking=True)
+                pool.append_layer(0, dev_rows[b], dev_slots[b])
+                status_host[j:j + 1].copy_(pool.status, non_blocking=True)
+
+    run()  # warm
+    torch.cuda.synchronize()
+    pool.status.zero_()
+    dist.barrier()
+    ms = dist.max(events_time(run, stream))
+    assert int(status_host.abs().sum()) == 0, "append reported device errors"
+    h2d = wl.rows[0].numel() * 2 + N_SEQ_APPEND * 4
+    return {"value": wl.bytes_per_step() * K / (ms * 1e-3) / GB, "unit": "GB/s",
+            "tokens_per_s_per_gpu": N_SEQ_APPEND * K / (ms * 1e-3),
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "ms_per_step": ms / K}
+
+
+def cpu_append_sample(wl: AppendWorkload, W: int, budget_s: float, threads: int) -> dict:
+    """The oracle (C restatement of rsLLM's CPU path) on the same steps."""
+    import oracle
+
+    pool = oracle.new_pool(wl.n_pages, N_LAYERS)
+    steps, t_total, done_bytes = 0, 0.0, 0
+    while steps < wl.n_steps - W and (t_total < budget_s or steps == 0):
+        rows = wl.rows[W + steps].view(torch.int16).cpu().numpy().view(np.uint16)
+        slots = wl.slots_np[W + steps]
+        t0 = time.perf_counter()
+        st = oracle.append_rows(pool, wl.n_pages, N_LAYERS, 0, rows, slots, n_threads=threads)
+        t_total += time.perf_counter() - t0
+        assert st == 0
+        steps += 1
+        done_bytes += AppendWorkload.bytes_per_step()
+    return {"value": done_bytes / t_total / GB, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{steps} decode steps of config 2 ({steps * N_LAYERS * N_SEQ_APPEND} rows), "
+                      f"{t_total:.1f} s on {threads} threads",
+            "tokens_per_s": steps * N_SEQ_APPEND / t_total}
+
+
+# ---------------------------------------------------------------------------
+# config 3: paged gather + dequant; config 4: top-k + sparse gather
+# ---------------------------------------------------------------------------
+
+def fill_pool(pool, n_layers_phys: int, slots_all: torch.Tensor, seed: int, dev):
+    """Fills every slot of every backed layer through the append kernel, from
+    a seeded block of rows reused across chunks."""
+    from rsllm_b200 import synth
+
+    chunk = 1 << 20
+    src = synth.kv_rows(chunk, seed=seed, device=dev)
+    n = slots_all.numel()
+    for layer in range(n_layers_phys):
+        for c0 in range(0, n, chunk):
+            c1 = min(n, c0 + chunk)
+            rot = (layer * 7919 + c0) % chunk
+            rows = src[: c1 - c0] if rot == 0 else torch.roll(src, rot, 0)[: c1 - c0]
+            pool.append_layer(layer, rows.contiguous(), slots_all[c0:c1])
+    pool.check("fill")
+    del src
+
+
+def bench_gather(args, dist: Dist, dev, peak) -> dict:
+    import rsllm_b200 as rk
+    from rsllm_b200 import synth
+
+    n_seq, ctx = 64, 32768
+    pages_per = ctx // 64
+    n_pages = n_seq * pages_per
+    free, _ = torch.cuda.mem_get_info(dev)
+    out_bytes = n_seq * ctx * 576 * 2
+    per_layer = n_pages * rk.PAGE_BYTES
+    l_phys = int(min(N_LAYERS, (free - out_bytes - 8 * 2**30) // per_layer))
+    if l_phys < 1:
+        return {"skipped": "not enough device memory"}
+    perm = synth.permutation(n_pages, seed=4 + 7919 * dist.rank).to(dev)
+    pt = perm.view(n_seq, pages_per).contiguous()
+    tok = torch.arange(ctx, device=dev, dtype=torch.int32)
+    slots_all = (pt[:, tok // 64] * 64 + (tok % 64)).reshape(-1).contiguous()
+    pool = rk.PagedKvPool(n_pages, l_phys, device=dev)
+    fill_pool(pool, l_phys, slots_all, seed=40 + dist.rank, dev=dev)
+    del slots_all
+    cu = torch.arange(0, (n_seq + 1) * ctx, ctx, dtype=torch.int32, device=dev)
+    out = torch.empty((n_seq * ctx, 576), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        for layer in range(N_LAYERS):
+            pool.rows(layer % l_phys, pt, cu, ctx, out=out, stream=stream)
+
+    for _ in range(args.phase_warmup):
+        step()
+    pool.check("gather", stream)
+    dist.barrier()
+    ms = dist.max(events_time(lambda: [step() for _ in range(args.phase_steps)], stream))
+    pool.check("gather", stream)
+    # per-launch duration of the kernel alone
+    one = events_time(lambda: pool.rows(0, pt, cu, ctx, out=out, stream=stream), stream)
+    rows = n_seq * ctx
+    step_bytes = N_LAYERS * (rows * GATHER_ROW_BYTES + n_pages * 4)
+    res = {"config": "c3: 64 seqs x 32768 ctx x 61 layers, random page order",
+           "layers_backed": l_phys, "ms_per_step": ms / args.phase_steps,
+           "gbs_per_gpu": step_bytes * args.phase_steps / (ms * 1e-3) / GB,
+           "frac_of_hbm_peak": None, "kernel_ms_per_layer": one,
+           "launches_per_step": N_LAYERS}
+    res["frac_of_hbm_peak"] = res["gbs_per_gpu"] / peak
+    del pool, out
+    torch.cuda.empty_cache()
+    return res
+
+
+def bench_sparse(args, dist: Dist, dev, peak) -> dict:
+    import rsllm_b200 as rk
+    from rsllm_b200 import synth
+
+    n_seq, ctx, n_qpos, k = 32, 131072, 64, 2048
+    pages_per = ctx // 64
+    n_pages = n_seq * pages_per
+    n_q = n_seq * n_qpos
+    n_score_mats = 4
+    out_bytes = n_q * k * 576 * 2
+    score_bytes = n_score_mats * n_q * ctx * 4
+    idx_bytes = N_LAYERS * n_q * k * 4
+    free, _ = torch.cuda.mem_get_info(dev)
+    per_layer = n_pages * rk.PAGE_BYTES
+    l_phys = int(min(N_LAYERS, (free - out_bytes - score_bytes - idx_bytes - 10 * 2**30) // per_layer))
+    if l_phys < 1:
+        return {"skipped": "not enough device memory"}
+    perm = synth.permutation(n_pages, seed=6 + 7919 * dist.rank).to(dev)
+    pt = perm.view(n_seq, pages_per).contiguous()
+    tok = torch.arange(ctx, device=dev, dtype=torch.int32)
+    slots_all = (pt[:, tok // 64] * 64 + (tok % 64)).reshape(-1).contiguous()
+    pool = rk.PagedKvPool(n_pages, l_phys, device=dev)
+    fill_pool(pool, l_phys, slots_all, seed=60 + dist.rank, dev=dev)
+    del slots_all
+    torch.cuda.empty_cache()
+    scores = [synth.scores(n_q, ctx, seed=500 + 31 * i + 7919 * dist.rank, device=dev) for i in range(n_score_mats)]
+    # query i of sequence s sits at position ctx - n_qpos + i: causal visibility
+    n_visible = (ctx - n_qpos + 1 + torch.arange(n_qpos, device=dev, dtype=torch.int32)).repeat(n_seq).contiguous()
+    seq_of_query = torch.arange(n_seq, device=dev, dtype=torch.int32).repeat_interleave(n_qpos).contiguous()
+    seq_lens = torch.full((n_seq,), ctx, dtype=torch.int32, device=dev)
+    idx = torch.empty((N_LAYERS, n_q, k), dtype=torch.int32, device=dev)
+    out = torch.empty((n_q, k, 576), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def topk_step():
+        for layer in range(N_LAYERS):
+            rk.select_top_k(scores[layer % n_score_mats], n_visible, k, out=idx[layer], stream=stream)
+
+    def sparse_step():
+        for layer in range(N_LAYERS):
+            pool.sparse_rows(layer % l_phys, pt, seq_of_query, seq_lens, idx[layer], out=out, stream=stream)
+
+    for _ in range(args.phase_warmup):
+        topk_step()
+        sparse_step()
+    pool.check("sparse", stream)
+    dist.barrier()
+    ms_topk = dist.max(events_time(lambda: [topk_step() for _ in range(args.phase_steps)], stream))
+    dist.barrier()
+    ms_sparse = dist.max(events_time(lambda: [sparse_step() for _ in range(args.phase_steps)], stream))
+    pool.check("sparse", stream)
+    one_topk = events_time(lambda: rk.select_top_k(scores[0], n_visible, k, out=idx[0], stream=stream), stream)
+    one_sparse = events_time(lambda: pool.sparse_rows(0, pt, seq_of_query, seq_lens, idx[0], out=out,
+                                                      stream=stream), stream)
+    sel = n_q * k
+    sparse_bytes = N_LAYERS * sel * (GATHER_ROW_BYTES + 4 + 4)
+    vis = int(n_visible.sum().item())
+    topk_bytes = N_LAYERS * (vis * 4 + sel * 4)
+    P = args.phase_steps
+    res = {
+        "topk": {"config": "c4: 2048 queries (32 seqs x last 64 positions, causal) over 131072 keys, k=2048, "
+                           f"61 layers cycling {n_score_mats} seeded N(0,1) score matrices",
+                 "ms_per_step": ms_topk / P, "gbs_per_gpu": topk_bytes * P / (ms_topk * 1e-3) / GB,
+                 "frac_of_hbm_peak": topk_bytes * P / (ms_topk * 1e-3) / GB / peak,
+                 "queries_per_s_per_gpu": N_LAYERS * n_q * P / (ms_topk * 1e-3),
+                 "kernel_ms_per_layer": one_topk},
+        "sparse_gather": {"config": "c4: 2048 queries x 2048 selected rows x 61 layers, random page order",
+                          "layers_backed": l_phys, "ms_per_step": ms_sparse / P,
+                          "gbs_per_gpu": sparse_bytes * P / (ms_sparse * 1e-3) / GB,
+                          "frac_of_hbm_peak": sparse_bytes * P / (ms_sparse * 1e-3) / GB / peak,
+                          "kernel_ms_per_layer": one_sparse},
+    }
+    del pool, out, scores, idx
+    torch.cuda.empty_cache()
+    return res
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the CPU restatement of rsLLM's path on the host cores
+# ---------------------------------------------------------------------------
+
+def run_reference(args, dist: Dist) -> None:
+    if dist.rank != 0:
+        return
+    import oracle
+
+    threads = oracle.threads()
+    W, K = args.warmup, args.steps
+    wl = AppendWorkload(W + K, seed=3, dev=None)
+    rows_cache = {}
+
+    def rows(j):
+        from rsllm_b200 import synth
+
+        if j not in rows_cache:
+            n = N_LAYERS * N_SEQ_APPEND
+            rows_cache.clear()
+            rows_cache[j] = synth.kv_rows(n, seed=3 * 1000 + j).view(torch.int16).numpy().view(np.uint16)
+        return rows_cache[j]
+
+    pool = oracle.new_pool(wl.n_pages, N_LAYERS)
+    for j in range(W):
+        oracle.append_rows(pool, wl.n_pages, N_LAYERS, 0, rows(j), wl.slots_np[j], n_threads=threads)
+    t = 0.0
+    for j in range(W, W + K):
+        r = rows(j)
+        t0 = time.perf_counter()
+        st = oracle.append_rows(pool, wl.n_pages, N_LAYERS, 0, r, wl.slots_np[j], n_threads=threads)
+        t += time.perf_counter() - t0
+        assert st == 0
+    value = AppendWorkload.bytes_per_step() * K / t / GB
+    line = {
+        "metric": "KV append GB/s (config 2 decode append; CPU restatement of rsLLM's codec + append)",
+        "value": value, "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus, "steps": K, "warmup": W,
+        "ms_per_step": t / K * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u8", "data": "synthetic (seeded)",
+        "config": {"workload": "c2-decode-append", "sequences": N_SEQ_APPEND, "layers": N_LAYERS,
+                   "page_tokens": 64, "row": "512 latent fp8 + 64 rope bf16"},
+        "tokens_per_s": N_SEQ_APPEND * K / t,
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{K} full decode steps of config 2 ({K * N_LAYERS * N_SEQ_APPEND} rows)"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "rsLLM is Rust (no cargo/rustc here); this arm times the C restatement of its CPU path "
+                "(oracle/rkv_oracle.c) with the same loop structure, on all host threads",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--phases", default="gather,sparse", help="extra configs to measure (comma list or 'none')")
+    ap.add_argument("--phase-steps", type=int, default=3)
+    ap.add_argument("--phase-warmup", type=int, default=1)
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        ap.error("--warmup must be >= 3")
+
+    dist = Dist()
+    if args.impl == "reference":
+        run_reference(args, dist)
+        dist.close()
+        return
+    import oracle  # noqa: F401  (cpu_baseline leg)
+    import rsllm_b200 as rk
+
+    dev = torch.device("cuda", dist.local if dist.world > 1 else torch.cuda.current_device())
+    torch.cuda.set_device(dev)
+    peak, peak_kind = peaks()
+    clocks = ClockSampler(dev)
+    t_start = time.time()
+
+    app = bench_append(args, dist, dev, peak)
+    phases = {}
+    wanted = [] if args.phases == "none" else args.phases.split(",")
+    if "gather" in wanted:
+        phases["gather"] = bench_gather(args, dist, dev, peak)
+    if "sparse" in wanted:
+        phases.update(bench_sparse(args, dist, dev, peak))
+    clk = clocks.stop()
+
+    K, W = args.steps, args.warmup
+    line = None
+    if dist.rank == 0:
+        cpu = cpu_append_sample(app["wl"], W, args.cpu_budget, threads=__import__("oracle").threads())
+        value = app["gbs_per_gpu"] * dist.world
+        traffic = NCU_TRAFFIC_PER_ROW["append"]
+        rows_per_launch = N_LAYERS * N_SEQ_APPEND
+        line = {
+            "metric": "KV append GB/s (config 2 decode append: FP8 quantize-on-append into paged pool); "
+                      "see phases for gather / top-k / sparse gather",
+            "value": value, "unit": "GB/s", "n_gpus": dist.world, "steps": K, "warmup": W,
+            "ms_per_step": app["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u8", "data": "synthetic (seeded N(0,1) bf16 rows, 1% x20 outliers; seeded page tables)",
+            "config": {"workload": "c2-decode-append", "sequences_per_gpu": N_SEQ_APPEND, "layers": N_LAYERS,
+                       "seq_len": "U[1024,32768]", "page_tokens": 64, "row": "512 latent fp8 + 64 rope bf16",
+                       "parallelism": f"request-sharded x{dist.world}, no collective",
+                       "l2": "inputs larger than L2 (fresh rows every step, 1.9 GB total) + L2 flush before timing",
+                       "launch": "K steps captured in one CUDA graph"},
+            "tokens_per_s": app["tokens_per_s_per_gpu"] * dist.world,
+            "rows_per_s": app["tokens_per_s_per_gpu"] * dist.world * N_LAYERS,
+            "frac_of_hbm_peak_per_gpu": app["gbs_per_gpu"] / peak,
+            "roofline": {"bound": "hbm", "achieved": app["gbs_per_gpu"], "peak": peak, "unit": "GB/s",
+                         "frac": app["gbs_per_gpu"] / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                         if peak_kind == "measured" else "fallback 6650 GB/s",
+                         "kernel": "append_quant_kernel", "algorithmic_bytes_per_launch": app["step_bytes"],
+                         "traffic": None if traffic is None else traffic * rows_per_launch},
+            "cpu_baseline": cpu,
+            "e2e": {k: v for k, v in app["e2e"].items() if k in ("value", "unit", "h2d_bytes_per_step",
+                                                                   "d2h_bytes_per_step")},
+            "e2e_detail": app["e2e"],
+            "gpu_launches": K,
+            "phases": phases,
+            "clocks": clk,
+            "wall_s": time.time() - t_start,
+        }
+        if dist.world > 1:
+            line["e2e"]["value"] = app["e2e"]["value"] * dist.world
+    del app
+    dist.close()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

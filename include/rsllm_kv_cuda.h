@@ -1,0 +1,204 @@
+/*
+ * rsllm_kv_cuda.h -- C ABI of the B200 (sm_100a) KV-cache path for rsLLM.
+ *
+ * This is the boundary a `rsllm-backend-cuda` crate binds with `extern "C"`
+ * declarations: plain pointers, sizes and status codes, no C++ or torch types.
+ * Every entry point states the rsLLM interface it replaces (path within the
+ * rsLLM tree, file:line).
+ *
+ * Conventions (mirroring rsLLM's kernel conventions, crates/rsllm-backend-cpu/
+ * src/lib.rs:43-60 and crates/rsllm-kvcache/src/lib.rs:28-70):
+ *   - The caller owns every buffer.  Device pointers are CUDA device memory of
+ *     the current device; nothing on a hot path allocates.
+ *   - Calls are asynchronous on the given stream.  Errors the host can see
+ *     before launch are returned at once; errors found per row on the device
+ *     (bad page id, non-finite input) are OR-ed into a caller-provided device
+ *     word as (1u << status) and the offending row is skipped -- never a trap.
+ *     rkv_status_from_bits() maps such a word to one status.
+ *   - A status maps 1:1 onto rsLLM's error variants (see rkv_status below).
+ *   - Entry points are thread-safe; a stream must not be shared across threads
+ *     without the caller's own ordering, as with any CUDA stream.
+ */
+#ifndef RSLLM_KV_CUDA_H
+#define RSLLM_KV_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define RKV_API __attribute__((visibility("default")))
+#else
+#define RKV_API
+#endif
+
+/* Same type as cudaStream_t / CUstream; NULL is the legacy default stream. */
+typedef struct CUstream_st* rkv_stream_t;
+
+/* ---- status codes ------------------------------------------------------ */
+typedef int32_t rkv_status;
+#define RKV_OK 0
+/* rsllm-kvcache Error::ShapeMismatch (crates/rsllm-kvcache/src/lib.rs:31-39)
+ * and rsllm-backend-cpu Error::ShapeMismatch (crates/rsllm-backend-cpu/src/error.rs:12). */
+#define RKV_ERR_SHAPE_MISMATCH 1
+/* Error::IndexOutOfRange (crates/rsllm-kvcache/src/lib.rs:41-50). */
+#define RKV_ERR_INDEX_OUT_OF_RANGE 2
+/* Error::InvalidLayer (crates/rsllm-kvcache/src/lib.rs:52-59). */
+#define RKV_ERR_INVALID_LAYER 3
+/* Error::CompressedPoolFull (crates/rsllm-kvcache/src/lib.rs:61-69): the page
+ * pool has no free page left. */
+#define RKV_ERR_POOL_FULL 4
+/* rsllm-backend-cpu Error::NonFiniteInput (crates/rsllm-backend-cpu/src/error.rs:33). */
+#define RKV_ERR_NON_FINITE_INPUT 5
+/* Null pointer, misaligned pointer or bad handle (Rust's types rule these out;
+ * no rsLLM counterpart). */
+#define RKV_ERR_INVALID_ARGUMENT 6
+/* A CUDA runtime call failed; rkv_last_error() has the message. */
+#define RKV_ERR_CUDA 7
+
+/* ---- layout -------------------------------------------------------------
+ * A row is one token of one layer: 512 MLA-latent lanes + 64 RoPE lanes
+ * (rsLLM's fp8_kv_quantize_row_inplace(row, 576, 64), dsv4_quant.rs:316).
+ * Stored form: 512 E4M3FN codes, 8 f32 power-of-two scales (one per 64 lanes),
+ * 64 bf16 RoPE lanes.  A page holds 64 rows of one layer as a structure of
+ * arrays: codes[64][512] u8 | scales[64][8] f32 | rope[64][64] bf16.
+ * A slot is page * 64 + row-in-page. */
+#define RKV_PAGE_TOKENS 64
+#define RKV_LATENT_DIM 512
+#define RKV_ROPE_DIM 64
+#define RKV_ROW_DIM 576
+#define RKV_BLOCK 64
+#define RKV_PAGE_BYTES 43008
+
+/* A pool: n_layers regions of n_pages pages, page p of layer l at
+ * base + (l * n_pages + p) * RKV_PAGE_BYTES.  base must be 256-byte aligned. */
+typedef struct rkv_pool_view {
+  void* base;
+  int64_t n_pages;  /* pages per layer; slots are < n_pages * 64 */
+  int32_t n_layers;
+  int32_t reserved; /* must be 0 */
+} rkv_pool_view;
+
+/* ---- utilities ----------------------------------------------------------- */
+
+/* Library version, "major.minor.patch". */
+RKV_API const char* rkv_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+RKV_API const char* rkv_last_error(void);
+
+/* Highest-priority status in a device status word (0 -> RKV_OK).  Priority:
+ * INVALID_ARGUMENT, INVALID_LAYER, SHAPE_MISMATCH, INDEX_OUT_OF_RANGE,
+ * POOL_FULL, NON_FINITE_INPUT. */
+RKV_API rkv_status rkv_status_from_bits(uint32_t bits);
+
+/* Bytes of one page and of a whole pool (n_layers * n_pages pages). */
+RKV_API int64_t rkv_pool_bytes(int64_t n_pages, int32_t n_layers);
+
+/* ---- quantize-on-append ---------------------------------------------------
+ * Replaces fp8_kv_quantize_row_inplace (crates/rsllm-backend-cpu/src/ops/
+ * dsv4_quant.rs:316-362) applied to each appended row, fused with the row
+ * append of ThreeTierKvCache::append_layer / RawSwaRing::append
+ * (crates/rsllm-kvcache/src/dsv4/three_tier.rs:187-202, swa.rs:73-94), into a
+ * paged pool.
+ *
+ * rows:   bf16 [n_layers_in][n_tokens][576], 16-byte aligned.  Row t of layer
+ *         layer0 + i is written to slot slot_mapping[t] of that layer.
+ * slot_mapping: int32 [n_tokens], shared by the n_layers_in layers (one page
+ *         table serves every layer); a negative slot skips the token.
+ * Per row on the device: a slot >= n_pages * 64 sets INDEX_OUT_OF_RANGE, a
+ * non-finite latent lane sets NON_FINITE_INPUT; such a row writes nothing.
+ * Non-finite RoPE lanes are stored as they are (the reference never reads
+ * them, dsv4_quant.rs:865-874).
+ * Host errors: INVALID_LAYER if layer0 < 0 or layer0 + n_layers_in > n_layers;
+ * INVALID_ARGUMENT for null / misaligned pointers.
+ * d_status may be NULL (no per-row reporting). */
+RKV_API rkv_status rkv_append_quant_bf16(const rkv_pool_view* pool, int32_t layer0, int32_t n_layers_in,
+                                 const uint16_t* rows, int64_t n_tokens, const int32_t* slot_mapping,
+                                 uint32_t* d_status, rkv_stream_t stream);
+
+/* ---- paged gather + dequant -----------------------------------------------
+ * Replaces the chronological row reads RawSwaRing::rows / ::row
+ * (crates/rsllm-kvcache/src/dsv4/swa.rs:131-149) and CompressedKvPool::rows
+ * (compressed.rs:203-205) over a page table, with the E4M3 decode of
+ * dsv4_quant.rs:359 ((sign * e4m3fn_value) * scale), rounded to bf16.
+ *
+ * page_table: int32 [n_seq][pt_stride], physical page of each 64-token page.
+ * cu_seqlens: int32 [n_seq + 1], exclusive prefix sum of sequence lengths;
+ *             row t of sequence s goes to out[cu_seqlens[s] + t].
+ * max_seq_len: an upper bound of every sequence length (sizes the grid).
+ * out:        bf16 [cu_seqlens[n_seq]][576], 16-byte aligned.
+ * A page id outside [0, n_pages) sets INDEX_OUT_OF_RANGE and zero-fills the
+ * rows it covers. */
+RKV_API rkv_status rkv_gather_dequant_bf16(const rkv_pool_view* pool, int32_t layer, const int32_t* page_table,
+                                   int64_t pt_stride, const int32_t* cu_seqlens, int32_t n_seq,
+                                   int32_t max_seq_len, uint16_t* out, uint32_t* d_status,
+                                   rkv_stream_t stream);
+
+/* ---- indexer top-k selection -----------------------------------------------
+ * Replaces the selection half of IndexerPool::select_top_k
+ * (crates/rsllm-kvcache/src/dsv4/indexer.rs:218-236).  For query q the
+ * candidates are keys [0, n_visible[q]) of row q of scores (f32 [n_q][ld]);
+ * causal masking is expressed by n_visible.  effective_k = min(k, n_visible[q])
+ * indices are written to out_idx[q][0..effective_k) in the reference's order:
+ * descending score, ties to the lowest index; NaN and -inf never win, and when
+ * fewer than effective_k candidates beat -inf the rest of the effective_k
+ * entries are 0 (the reference's repeated index-0 pick).  Entries
+ * [effective_k, k) are -1.
+ * Limits: 1 <= k <= 4096, n_visible[q] <= ld, n_keys_max >= every n_visible.
+ * scores need 4-byte alignment (16-byte alignment and ld % 4 == 0 take the
+ * vectorised path). */
+RKV_API rkv_status rkv_topk_select_f32(const float* scores, int64_t ld, int32_t n_q, const int32_t* n_visible,
+                               int32_t n_keys_max, int32_t k, int32_t* out_idx, rkv_stream_t stream);
+
+/* ---- sparse gather + dequant ----------------------------------------------
+ * Replaces the top-k restricted row read of ThreeTierAttention::run_layer
+ * (crates/rsllm-models/src/dsv4/attention.rs:549-560: only rows in the
+ * selected set are read), over a page table, decoded as in the gather above.
+ *
+ * idx:          int32 [n_q][k] token positions (e.g. rkv_topk_select_f32
+ *               output); a negative entry writes a zero row.
+ * seq_of_query: int32 [n_q], the sequence (page-table row) of each query.
+ * seq_lens:     int32 [n_seq], to bound-check positions (INDEX_OUT_OF_RANGE,
+ *               zero row).
+ * out:          bf16 [n_q][k][576], 16-byte aligned. */
+RKV_API rkv_status rkv_sparse_gather_dequant_bf16(const rkv_pool_view* pool, int32_t layer,
+                                          const int32_t* page_table, int64_t pt_stride,
+                                          const int32_t* seq_of_query, const int32_t* seq_lens,
+                                          const int32_t* idx, int32_t n_q, int32_t k, uint16_t* out,
+                                          uint32_t* d_status, rkv_stream_t stream);
+
+/* ---- page moves: copy-on-write and compaction -------------------------------
+ * No rsLLM implementation exists; the planned design is refcounted shared
+ * prefix blocks with a free list (docs/03-HLD.md:363-369) and radix-tree
+ * prefix reuse with LRU eviction (docs/03-HLD.md:371-376).
+ *
+ * rkv_copy_pages: for every layer, page dst[i] <- page src[i], i < n.  The
+ * src and dst sets must be disjoint (copy-on-write targets are fresh pages;
+ * compaction moves live pages into holes).  Ids outside [0, n_pages) set
+ * INDEX_OUT_OF_RANGE and skip that pair. */
+RKV_API rkv_status rkv_copy_pages(const rkv_pool_view* pool, const int32_t* src, const int32_t* dst, int64_t n,
+                          uint32_t* d_status, rkv_stream_t stream);
+
+/* rkv_remap_pages: page_table[i] <- remap[page_table[i]] for every entry
+ * i < n_entries that is >= 0; remap is int32 [n_pages] (identity for pages
+ * that did not move).  An entry >= n_pages sets INDEX_OUT_OF_RANGE and is
+ * left unchanged. */
+RKV_API rkv_status rkv_remap_pages(int32_t* page_table, int64_t n_entries, const int32_t* remap, int64_t n_pages,
+                           uint32_t* d_status, rkv_stream_t stream);
+
+/* ---- codec pin ---------------------------------------------------------------
+ * out[i] = E4M3 code the append kernel stores for the f32 lane value whose
+ * bit pattern is first_bits + i (already divided by its block scale), i < n:
+ * the device side of e4m3fn_dequant (dsv4_quant.rs:128-163) with the code byte
+ * sign(x < 0) | index.  Used to check the device codec exhaustively. */
+RKV_API rkv_status rkv_e4m3fn_code_range(uint32_t first_bits, int64_t n, uint8_t* out, rkv_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RSLLM_KV_CUDA_H */

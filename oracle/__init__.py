@@ -1,0 +1,185 @@
+"""TEST INFRASTRUCTURE ONLY: Python access to the CPU oracle (rkv_oracle.c).
+
+The oracle is a plain-C restatement of rsLLM's KV-cache hot path on the CPU
+(see the header of rkv_oracle.c for the reference file:line of each function
+and how it is pinned).  Only tests/, __graft_entry__.smoke() and bench.py's
+cpu_baseline / reference legs use it, as the checker and as the timed CPU
+baseline; the rsllm_b200 package never imports it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from ctypes import c_float, c_int, c_int32, c_int64, c_uint8, c_uint16, c_uint32, c_void_p
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "librkv_oracle.so"
+
+PAGE_TOKENS, LATENT, ROPE, ROW_DIM, BLOCK = 64, 512, 64, 576, 64
+PAGE_BYTES = 43008
+OK, SHAPE_MISMATCH, INDEX_OUT_OF_RANGE, INVALID_LAYER, POOL_FULL, NON_FINITE_INPUT = 0, 1, 2, 3, 4, 5
+
+_lib = None
+
+
+def build() -> Path:
+    """Compiles the oracle with its Makefile (gcc, no fast-math)."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    src = HERE / "rkv_oracle.c"
+    if not LIB_PATH.exists() or (src.exists() and src.stat().st_mtime > LIB_PATH.stat().st_mtime):
+        build()
+    L = ctypes.CDLL(str(LIB_PATH))
+    P = c_void_p
+    sig = {
+        "rkvo_page_bytes": (c_int, []),
+        "rkvo_f32_to_bf16": (c_uint16, [c_float]),
+        "rkvo_e4m3fn_value": (c_float, [c_uint32]),
+        "rkvo_e4m3fn_dequant": (c_float, [c_float]),
+        "rkvo_e4m3fn_code": (c_uint8, [c_float]),
+        "rkvo_e4m3fn_code_range": (None, [c_uint32, ctypes.c_uint64, P, c_int]),
+        "rkvo_libm_ldexpf": (c_float, [c_float, c_int]),
+        "rkvo_scale_exponent": (c_int, [c_float]),
+        "rkvo_fp8_kv_quantize_row_inplace": (c_int, [P, c_int64, c_int64, c_int64]),
+        "rkvo_quantize_row_bf16": (c_int, [P, c_int64, c_int64, P, P, P]),
+        "rkvo_dequant_row_bf16": (None, [P, P, P, c_int64, c_int64, P]),
+        "rkvo_fp8_e4m3_to_f32": (c_float, [c_uint8]),
+        "rkvo_f32_to_fp8_e4m3": (c_uint8, [c_float]),
+        "rkvo_select_top_k_scan": (c_int64, [P, c_int64, c_int64, P]),
+        "rkvo_select_top_k_sorted": (c_int64, [P, c_int64, c_int64, P]),
+        "rkvo_topk_batch": (None, [P, c_int64, c_int32, P, c_int32, P, c_int, c_int]),
+        "rkvo_append_rows": (c_uint32, [P, c_int64, c_int32, c_int32, c_int32, P, c_int64, P, c_int]),
+        "rkvo_gather_rows": (c_uint32, [P, c_int64, c_int32, c_int32, P, c_int64, P, c_int32, P, c_int]),
+        "rkvo_sparse_gather_rows": (c_uint32, [P, c_int64, c_int32, c_int32, P, c_int64, P, P, P, c_int32, c_int32,
+                                               P, c_int]),
+        "rkvo_copy_pages": (None, [P, c_int64, c_int32, P, P, c_int64]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def _p(a: np.ndarray) -> c_void_p:
+    assert a.flags["C_CONTIGUOUS"], "oracle arrays must be C-contiguous"
+    return c_void_p(a.ctypes.data)
+
+
+def threads() -> int:
+    return max(1, len(os.sched_getaffinity(0)))
+
+
+# ---- codec ----------------------------------------------------------------
+
+def quantize_row_inplace(x: np.ndarray, head_dim: int, n_rot: int) -> int:
+    """dsv4_quant.rs:316-362 on a float32 row, in place; returns the status."""
+    assert x.dtype == np.float32
+    return lib().rkvo_fp8_kv_quantize_row_inplace(_p(x), x.size, head_dim, n_rot)
+
+
+def quantize_rows_bf16(rows: np.ndarray):
+    """bf16 rows (uint16 [n, 576]) -> (codes u8 [n,512], scales f32 [n,8], rope u16 [n,64], status i32 [n])."""
+    rows = np.ascontiguousarray(rows, dtype=np.uint16).reshape(-1, ROW_DIM)
+    n = rows.shape[0]
+    codes = np.zeros((n, LATENT), np.uint8)
+    scales = np.zeros((n, LATENT // BLOCK), np.float32)
+    rope = np.zeros((n, ROPE), np.uint16)
+    st = np.zeros(n, np.int32)
+    L = lib()
+    for i in range(n):
+        st[i] = L.rkvo_quantize_row_bf16(_p(rows[i]), ROW_DIM, ROPE, _p(codes[i]), _p(scales[i]), _p(rope[i]))
+    return codes, scales, rope, st
+
+
+def dequant_rows_bf16(codes: np.ndarray, scales: np.ndarray, rope: np.ndarray) -> np.ndarray:
+    codes = np.ascontiguousarray(codes, np.uint8).reshape(-1, LATENT)
+    scales = np.ascontiguousarray(scales, np.float32).reshape(-1, LATENT // BLOCK)
+    rope = np.ascontiguousarray(rope, np.uint16).reshape(-1, ROPE)
+    out = np.zeros((codes.shape[0], ROW_DIM), np.uint16)
+    L = lib()
+    for i in range(codes.shape[0]):
+        L.rkvo_dequant_row_bf16(_p(codes[i]), _p(scales[i]), _p(rope[i]), LATENT, ROPE, _p(out[i]))
+    return out
+
+
+def e4m3fn_code_range(first_bits: int, n: int, n_threads: int | None = None) -> np.ndarray:
+    out = np.empty(n, np.uint8)
+    lib().rkvo_e4m3fn_code_range(first_bits, n, _p(out), n_threads or threads())
+    return out
+
+
+# ---- top-k ----------------------------------------------------------------
+
+def select_top_k(scores: np.ndarray, top_k: int, scan: bool = True) -> np.ndarray:
+    """indexer.rs:218-236 on one score vector; returns the effective_k indices."""
+    s = np.ascontiguousarray(scores, np.float32)
+    out = np.empty(max(0, min(top_k, s.size)), np.int32)
+    fn = lib().rkvo_select_top_k_scan if scan else lib().rkvo_select_top_k_sorted
+    got = fn(_p(s), s.size, top_k, _p(out))
+    return out[:got]
+
+
+def topk_batch(scores: np.ndarray, n_visible: np.ndarray, k: int, scan: bool = False,
+               n_threads: int | None = None) -> np.ndarray:
+    s = np.ascontiguousarray(scores, np.float32)
+    nv = np.ascontiguousarray(n_visible, np.int32)
+    out = np.empty((s.shape[0], k), np.int32)
+    lib().rkvo_topk_batch(_p(s), s.shape[1], s.shape[0], _p(nv), k, _p(out), int(scan), n_threads or threads())
+    return out
+
+
+# ---- paged pool model -----------------------------------------------------
+
+def new_pool(n_pages: int, n_layers: int) -> np.ndarray:
+    return np.zeros(n_layers * n_pages * PAGE_BYTES, np.uint8)
+
+
+def append_rows(pool: np.ndarray, n_pages: int, n_layers: int, layer0: int, rows: np.ndarray,
+                slots: np.ndarray, n_threads: int = 1) -> int:
+    rows = np.ascontiguousarray(rows, np.uint16)
+    n_layers_in = rows.shape[0] if rows.ndim == 3 else 1
+    n_tokens = rows.shape[-2]
+    slots = np.ascontiguousarray(slots, np.int32)
+    return lib().rkvo_append_rows(_p(pool), n_pages, n_layers, layer0, n_layers_in, _p(rows), n_tokens, _p(slots),
+                                  n_threads)
+
+
+def gather_rows(pool: np.ndarray, n_pages: int, n_layers: int, layer: int, page_table: np.ndarray,
+                cu_seqlens: np.ndarray, n_threads: int = 1):
+    pt = np.ascontiguousarray(page_table, np.int32)
+    cu = np.ascontiguousarray(cu_seqlens, np.int32)
+    out = np.zeros((int(cu[-1]), ROW_DIM), np.uint16)
+    st = lib().rkvo_gather_rows(_p(pool), n_pages, n_layers, layer, _p(pt), pt.shape[1], _p(cu), cu.size - 1,
+                                _p(out), n_threads)
+    return out, st
+
+
+def sparse_gather_rows(pool: np.ndarray, n_pages: int, n_layers: int, layer: int, page_table: np.ndarray,
+                       seq_of_query: np.ndarray, seq_lens: np.ndarray, idx: np.ndarray, n_threads: int = 1):
+    pt = np.ascontiguousarray(page_table, np.int32)
+    sq = np.ascontiguousarray(seq_of_query, np.int32)
+    sl = np.ascontiguousarray(seq_lens, np.int32)
+    ix = np.ascontiguousarray(idx, np.int32)
+    n_q, k = ix.shape
+    out = np.zeros((n_q, k, ROW_DIM), np.uint16)
+    st = lib().rkvo_sparse_gather_rows(_p(pool), n_pages, n_layers, layer, _p(pt), pt.shape[1], _p(sq), _p(sl),
+                                       _p(ix), n_q, k, _p(out), n_threads)
+    return out, st
+
+
+def copy_pages(pool: np.ndarray, n_pages: int, n_layers: int, src: np.ndarray, dst: np.ndarray) -> None:
+    s = np.ascontiguousarray(src, np.int32)
+    d = np.ascontiguousarray(dst, np.int32)
+    lib().rkvo_copy_pages(_p(pool), n_pages, n_layers, _p(s), _p(d), s.size)

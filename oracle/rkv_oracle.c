@@ -1,0 +1,592 @@
+/*
+ * rkv_oracle.c -- TEST INFRASTRUCTURE ONLY.
+ *
+ * A plain-C restatement, on the CPU, of rsLLM's KV-cache hot path.  It is the
+ * checker the parity tests compare the CUDA path against, and the CPU
+ * baseline that bench.py times beside the GPU.  Only tests/,
+ * __graft_entry__.smoke() and bench.py's cpu_baseline / reference legs load
+ * it; the product library (rsllm_b200) never links, loads or calls it.
+ *
+ * What it restates (paths are relative to the rsLLM source tree):
+ *   - FP8 E4M3FN KV codec:  crates/rsllm-backend-cpu/src/ops/dsv4_quant.rs
+ *       e4m3fn_value :103-111 (table :71-78, subnormal step :82),
+ *       e4m3fn_dequant :128-163, fp8_kv_quantize_row_inplace :316-362,
+ *       libm_ldexpf :422-433, constants :43-66.
+ *   - byte-level E4M3 codec: crates/rsllm-gguf/src/dequant/fp8_e4m3.rs:37-136.
+ *   - top-k selection rule:  crates/rsllm-kvcache/src/dsv4/indexer.rs:218-236.
+ *   - row append / chronological read semantics: crates/rsllm-kvcache/src/
+ *       dsv4/swa.rs:73-94,131-149 and compressed.rs:203-205, generalised to a
+ *       page-table-indexed pool (the reference has no paged pool; its plan is
+ *       docs/03-HLD.md:363-369).
+ *   - sparse row read: crates/rsllm-models/src/dsv4/attention.rs:549-560.
+ *
+ * Parity pin: the reference is Rust and cannot be built here (no cargo or
+ * rustc), so this restatement is pinned by the reference's own known-answer
+ * tests, transcribed into tests/golden/kat_reference.json with a file:line per
+ * case, plus exhaustive checks (every f32 in [0, 448] through the snap, every
+ * bf16 block amax through the exponent rule).  The paged layout itself has no
+ * reference implementation and is checked for self-consistency only.
+ *
+ * Build: oracle/Makefile (gcc -O2, no fast-math, no FP contraction).
+ */
+#include <math.h>
+#include <pthread.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* Status bits shared with the product (include/rsllm_kv_cuda.h): an
+ * operation over many rows ORs (1 << code) for every row that failed. */
+enum {
+    RKVO_OK = 0,
+    RKVO_SHAPE_MISMATCH = 1,
+    RKVO_INDEX_OUT_OF_RANGE = 2,
+    RKVO_INVALID_LAYER = 3,
+    RKVO_POOL_FULL = 4,
+    RKVO_NON_FINITE_INPUT = 5,
+};
+
+/* Paged layout: one page = 64 token rows of one layer, structure of arrays:
+ * codes[64][512] u8 | scales[64][8] f32 | rope[64][64] bf16 = 43008 bytes. */
+#define PAGE_TOKENS 64
+#define LATENT 512
+#define ROPE 64
+#define ROW_DIM (LATENT + ROPE)
+#define BLOCK 64
+#define NBLK (LATENT / BLOCK)
+#define CODES_BYTES (PAGE_TOKENS * LATENT)
+#define SCALES_BYTES (PAGE_TOKENS * NBLK * 4)
+#define ROPE_BYTES (PAGE_TOKENS * ROPE * 2)
+#define PAGE_BYTES (CODES_BYTES + SCALES_BYTES + ROPE_BYTES)
+
+int rkvo_page_bytes(void) { return PAGE_BYTES; }
+
+/* ------------------------------------------------------------------------ */
+/* bit helpers                                                              */
+/* ------------------------------------------------------------------------ */
+static inline float f_from_bits(uint32_t b) { float f; memcpy(&f, &b, 4); return f; }
+static inline uint32_t bits_of(float f) { uint32_t b; memcpy(&b, &f, 4); return b; }
+static inline float bf16_to_f32(uint16_t h) { return f_from_bits((uint32_t)h << 16); }
+
+/* f32 -> bf16, round to nearest even (NaN kept quiet). */
+uint16_t rkvo_f32_to_bf16(float f) {
+    uint32_t b = bits_of(f);
+    if ((b & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((b >> 16) | 0x40u);
+    b += 0x7fffu + ((b >> 16) & 1u);
+    return (uint16_t)(b >> 16);
+}
+
+/* ------------------------------------------------------------------------ */
+/* dsv4_quant.rs: the E4M3 simulation the reference runs on KV rows          */
+/* ------------------------------------------------------------------------ */
+
+/* dsv4_quant.rs:43-66 */
+#define FP8_KV_GROUP 64
+#define FP8_E4M3_MAX 448.0f
+#define FP8_KV_AMAX_FLOOR 1.0e-4f
+#define FP8_E4M3_CODE_MAX 126
+
+/* dsv4_quant.rs:71-78: 2^(exp-7) for the normal exponents; slot 0 unused. */
+static const float E4M3FN_EXP_SCALE[16] = {
+    0.0f, 0.015625f, 0.03125f, 0.0625f, 0.125f, 0.25f, 0.5f, 1.0f,
+    2.0f, 4.0f,      8.0f,     16.0f,   32.0f, 64.0f, 128.0f, 256.0f};
+
+/* dsv4_quant.rs:103-111 */
+float rkvo_e4m3fn_value(uint32_t i) {
+    uint32_t e = (i >> 3) & 0xfu;
+    float mant = (float)(i & 7u);
+    if (e == 0) return mant * 0.001953125f; /* :82 subnormal step 1/512 */
+    return (1.0f + mant * 0.125f) * E4M3FN_EXP_SCALE[e];
+}
+
+/* The magnitude-index search of dsv4_quant.rs:128-163 on ax = min(|x|, 448):
+ * binary search for the largest code with value <= ax, then the one-sided
+ * even tie-break against the next code. */
+static int snap_index(float ax) {
+    int lo = 0, hi = FP8_E4M3_CODE_MAX;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (rkvo_e4m3fn_value((uint32_t)mid) <= ax) lo = mid;
+        else hi = mid - 1;
+    }
+    int best = lo;
+    if (best < FP8_E4M3_CODE_MAX) {
+        float best_diff = fabsf(ax - rkvo_e4m3fn_value((uint32_t)best));
+        float next_diff = fabsf(ax - rkvo_e4m3fn_value((uint32_t)(best + 1)));
+        if (next_diff < best_diff ||
+            (next_diff == best_diff && ((best + 1) & 1) == 0 && (best & 1) != 0))
+            best += 1;
+    }
+    return best;
+}
+
+/* dsv4_quant.rs:128-163.  Rust's f32::min returns the non-NaN operand, as
+ * fminf does. */
+float rkvo_e4m3fn_dequant(float x) {
+    float sign = x < 0.0f ? -1.0f : 1.0f;
+    float ax = fminf(fabsf(x), FP8_E4M3_MAX);
+    return sign * rkvo_e4m3fn_value((uint32_t)snap_index(ax));
+}
+
+/* The code byte the snap above stands for: sign from (x < 0) -- so -0.0 maps
+ * to 0x00 -- and the magnitude index in the low 7 bits. */
+uint8_t rkvo_e4m3fn_code(float x) {
+    uint8_t s = x < 0.0f ? 0x80 : 0x00;
+    return (uint8_t)(s | (uint8_t)snap_index(fminf(fabsf(x), FP8_E4M3_MAX)));
+}
+
+/* Codes for a contiguous range of f32 bit patterns (exhaustive checks). */
+typedef struct { uint32_t first; uint64_t n; uint8_t* out; } snap_job;
+static void* snap_range_worker(void* p) {
+    snap_job* j = (snap_job*)p;
+    for (uint64_t i = 0; i < j->n; ++i)
+        j->out[i] = rkvo_e4m3fn_code(f_from_bits(j->first + (uint32_t)i));
+    return NULL;
+}
+void rkvo_e4m3fn_code_range(uint32_t first_bits, uint64_t n, uint8_t* out, int n_threads) {
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > 256) n_threads = 256;
+    pthread_t th[256];
+    snap_job jobs[256];
+    uint64_t per = (n + (uint64_t)n_threads - 1) / (uint64_t)n_threads;
+    int started = 0;
+    for (int t = 0; t < n_threads; ++t) {
+        uint64_t b = per * (uint64_t)t;
+        if (b >= n) break;
+        uint64_t e = b + per < n ? b + per : n;
+        jobs[t].first = first_bits + (uint32_t)b;
+        jobs[t].n = e - b;
+        jobs[t].out = out + b;
+        pthread_create(&th[t], NULL, snap_range_worker, &jobs[t]);
+        ++started;
+    }
+    for (int t = 0; t < started; ++t) pthread_join(th[t], NULL);
+}
+
+/* dsv4_quant.rs:422-433 */
+float rkvo_libm_ldexpf(float x, int n) {
+    if (n < -126) n = -126;
+    if (n > 127) n = 127;
+    return x * f_from_bits((uint32_t)(n + 127) << 23);
+}
+
+/* The scale exponent of dsv4_quant.rs:346-355 for one block amax, exactly as
+ * the reference evaluates it: floor, divide by 448, glibc log2f, ceil. */
+int rkvo_scale_exponent(float amax) {
+    if (amax < FP8_KV_AMAX_FLOOR) amax = FP8_KV_AMAX_FLOOR;
+    float l = ceilf(log2f(amax / FP8_E4M3_MAX));
+    /* Rust `as i32` saturates and maps NaN to 0. */
+    if (l != l) return 0;
+    if (l >= 2147483647.0f) return 2147483647;
+    if (l <= -2147483648.0f) return (-2147483647 - 1);
+    return (int)l;
+}
+
+/* dsv4_quant.rs:316-362, the reference's in-place f32 round trip. */
+int rkvo_fp8_kv_quantize_row_inplace(float* x, int64_t x_len, int64_t head_dim, int64_t n_rot) {
+    if (x_len != head_dim) return RKVO_SHAPE_MISMATCH;
+    if (n_rot > head_dim) return RKVO_SHAPE_MISMATCH;
+    int64_t n_nope = head_dim - n_rot;
+    if (n_nope <= 0 || n_nope % FP8_KV_GROUP != 0) return RKVO_SHAPE_MISMATCH;
+    for (int64_t b = 0; b < n_nope; b += FP8_KV_GROUP) {
+        float amax = 0.0f;
+        for (int i = 0; i < FP8_KV_GROUP; ++i) {
+            float v = x[b + i];
+            if (!isfinite(v)) return RKVO_NON_FINITE_INPUT; /* earlier blocks stay modified, as in Rust */
+            float av = fabsf(v);
+            if (av > amax) amax = av;
+        }
+        int e = rkvo_scale_exponent(amax);
+        float scale = rkvo_libm_ldexpf(1.0f, e);
+        for (int i = 0; i < FP8_KV_GROUP; ++i) {
+            float t = x[b + i] / scale;
+            if (t < -FP8_E4M3_MAX) t = -FP8_E4M3_MAX; /* f32::clamp */
+            if (t > FP8_E4M3_MAX) t = FP8_E4M3_MAX;
+            x[b + i] = rkvo_e4m3fn_dequant(t) * scale;
+        }
+    }
+    return RKVO_OK;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Stored form of one row: the same arithmetic as above, keeping the code    */
+/* bytes and the power-of-two scale instead of the simulated f32 values.     */
+/* ------------------------------------------------------------------------ */
+
+/* One bf16 row [head_dim] -> codes[n_nope], scales[n_nope/64] (f32 2^e),
+ * rope[n_rot] (bf16 passthrough).  A non-finite latent lane rejects the row
+ * before anything is written. */
+int rkvo_quantize_row_bf16(const uint16_t* row, int64_t head_dim, int64_t n_rot,
+                           uint8_t* codes, float* scales, uint16_t* rope) {
+    if (n_rot > head_dim) return RKVO_SHAPE_MISMATCH;
+    int64_t n_nope = head_dim - n_rot;
+    if (n_nope <= 0 || n_nope % FP8_KV_GROUP != 0) return RKVO_SHAPE_MISMATCH;
+    for (int64_t i = 0; i < n_nope; ++i)
+        if (!isfinite(bf16_to_f32(row[i]))) return RKVO_NON_FINITE_INPUT;
+    for (int64_t b = 0; b < n_nope; b += FP8_KV_GROUP) {
+        float amax = 0.0f;
+        for (int i = 0; i < FP8_KV_GROUP; ++i) {
+            float av = fabsf(bf16_to_f32(row[b + i]));
+            if (av > amax) amax = av;
+        }
+        int e = rkvo_scale_exponent(amax);
+        float scale = rkvo_libm_ldexpf(1.0f, e);
+        scales[b / FP8_KV_GROUP] = scale;
+        for (int i = 0; i < FP8_KV_GROUP; ++i) {
+            float t = bf16_to_f32(row[b + i]) / scale;
+            if (t < -FP8_E4M3_MAX) t = -FP8_E4M3_MAX;
+            if (t > FP8_E4M3_MAX) t = FP8_E4M3_MAX;
+            codes[b + i] = rkvo_e4m3fn_code(t);
+        }
+    }
+    memcpy(rope, row + n_nope, (size_t)n_rot * 2);
+    return RKVO_OK;
+}
+
+/* Stored row -> bf16 [n_nope + n_rot]: (sign * e4m3fn_value) * scale, the
+ * product the reference forms at dsv4_quant.rs:359, rounded to bf16. */
+void rkvo_dequant_row_bf16(const uint8_t* codes, const float* scales, const uint16_t* rope,
+                           int64_t n_nope, int64_t n_rot, uint16_t* out) {
+    for (int64_t j = 0; j < n_nope; ++j) {
+        uint8_t c = codes[j];
+        float sign = (c & 0x80) ? -1.0f : 1.0f;
+        float v = (sign * rkvo_e4m3fn_value(c & 0x7fu)) * scales[j / FP8_KV_GROUP];
+        out[j] = rkvo_f32_to_bf16(v);
+    }
+    memcpy(out + n_nope, rope, (size_t)n_rot * 2);
+}
+
+/* ------------------------------------------------------------------------ */
+/* fp8_e4m3.rs:37-136, the byte-level codec (differs on -0.0: 0x80 here).   */
+/* ------------------------------------------------------------------------ */
+float rkvo_fp8_e4m3_to_f32(uint8_t byte) {
+    uint8_t sign_bit = byte & 0x80;
+    uint8_t e = (byte >> 3) & 0x0f;
+    uint8_t m = byte & 0x07;
+    float a;
+    if (e == 0) {
+        a = (float)m / 512.0f;
+    } else if (e == 0x0f && m == 0x07) {
+        return NAN;
+    } else {
+        float mant_f = 1.0f + (float)m / 8.0f;
+        int ei = (int)e - 7;
+        float sc = ei >= 0 ? (float)(1ull << ei) : 1.0f / (float)(1ull << -ei);
+        a = mant_f * sc;
+    }
+    return sign_bit ? -a : a;
+}
+
+uint8_t rkvo_f32_to_fp8_e4m3(float value) {
+    if (isnan(value)) return 0x7f;
+    uint8_t sign_bit = signbit(value) ? 0x80 : 0x00;
+    float a = fabsf(value);
+    if (a >= 448.0f) return sign_bit | 0x7e;
+    if (a == 0.0f) return sign_bit;
+    int unbiased = (int)floorf(log2f(a));
+    if (unbiased < -6) {
+        float scaled = a * 512.0f;
+        uint32_t m = (uint32_t)rintf(scaled); /* round_ties_even */
+        if (m >= 8) return sign_bit | 0x08;
+        return (uint8_t)(sign_bit | (m & 0x07));
+    }
+    int e = unbiased + 7;
+    if (e < 1) e = 1;
+    if (e > 15) e = 15;
+    float exp_scale = unbiased >= 0 ? (float)(1ull << unbiased) : 1.0f / (float)(1ull << -unbiased);
+    float mant_f = (a / exp_scale - 1.0f) * 8.0f;
+    int m = (int)rintf(mant_f);
+    if (m == 8) {
+        m = 0;
+        e = e + 1;
+        if (e >= 0x0f) return sign_bit | 0x7e;
+    }
+    if (m < 0) m = 0;
+    if (m > 7) m = 7;
+    return (uint8_t)(sign_bit | (e << 3) | (m & 0x07));
+}
+
+/* ------------------------------------------------------------------------ */
+/* indexer.rs:218-236, top-k selection                                       */
+/* ------------------------------------------------------------------------ */
+
+/* The reference's repeated best-scan: effective_k = min(k, n) picks, each the
+ * not-yet-selected row with the largest score by strict `>` from -inf (ties go
+ * to the lowest index; NaN and -inf never win).  When no candidate beats -inf
+ * the pick is index 0, emitted again.  Returns the number of indices written. */
+int64_t rkvo_select_top_k_scan(const float* scores, int64_t n, int64_t top_k, int32_t* out) {
+    if (n <= 0 || top_k <= 0) return 0;
+    int64_t k = top_k < n ? top_k : n;
+    uint8_t* allowed = (uint8_t*)calloc((size_t)n, 1);
+    for (int64_t it = 0; it < k; ++it) {
+        int64_t best_idx = 0;
+        float best_score = -INFINITY;
+        for (int64_t c = 0; c < n; ++c) {
+            if (!allowed[c] && scores[c] > best_score) {
+                best_score = scores[c];
+                best_idx = c;
+            }
+        }
+        allowed[best_idx] = 1;
+        out[it] = (int32_t)best_idx;
+    }
+    free(allowed);
+    return k;
+}
+
+/* The same output computed by a sort: the candidates that can win (score >
+ * -inf, not NaN) in descending score with ascending index on ties, then index
+ * 0 repeated up to effective_k.  -0.0 and +0.0 compare equal under `>`, so
+ * they are ordered as one value. */
+static inline uint64_t topk_key(float s, int64_t idx) {
+    if (s == 0.0f) s = 0.0f; /* fold -0.0 into +0.0 */
+    uint32_t b = bits_of(s);
+    uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((uint64_t)ord << 32) | (uint64_t)(0xffffffffu - (uint32_t)idx);
+}
+static int cmp_desc_u64(const void* a, const void* b) {
+    uint64_t x = *(const uint64_t*)a, y = *(const uint64_t*)b;
+    return x < y ? 1 : (x > y ? -1 : 0);
+}
+int64_t rkvo_select_top_k_sorted(const float* scores, int64_t n, int64_t top_k, int32_t* out) {
+    if (n <= 0 || top_k <= 0) return 0;
+    int64_t k = top_k < n ? top_k : n;
+    uint64_t* keys = (uint64_t*)malloc((size_t)n * 8);
+    int64_t m = 0;
+    for (int64_t c = 0; c < n; ++c)
+        if (scores[c] > -INFINITY) keys[m++] = topk_key(scores[c], c);
+    qsort(keys, (size_t)m, 8, cmp_desc_u64);
+    int64_t i = 0;
+    for (; i < k && i < m; ++i) out[i] = (int32_t)(0xffffffffu - (uint32_t)(keys[i] & 0xffffffffu));
+    for (; i < k; ++i) out[i] = 0;
+    free(keys);
+    return k;
+}
+
+/* Batched top-k over rows of a [n_q][ld] score matrix; query q sees keys
+ * [0, n_visible[q]) (causal masking = the pool holding only visible rows).
+ * Indices past a query's effective_k are -1. */
+typedef struct {
+    const float* scores; int64_t ld; int32_t q0, q1; const int32_t* n_visible;
+    int32_t k; int32_t* out; int scan;
+} topk_job;
+static void* topk_worker(void* p) {
+    topk_job* j = (topk_job*)p;
+    for (int32_t q = j->q0; q < j->q1; ++q) {
+        int32_t* o = j->out + (int64_t)q * j->k;
+        int64_t got = j->scan ? rkvo_select_top_k_scan(j->scores + (int64_t)q * j->ld, j->n_visible[q], j->k, o)
+                              : rkvo_select_top_k_sorted(j->scores + (int64_t)q * j->ld, j->n_visible[q], j->k, o);
+        for (int64_t i = got; i < j->k; ++i) o[i] = -1;
+    }
+    return NULL;
+}
+void rkvo_topk_batch(const float* scores, int64_t ld, int32_t n_q, const int32_t* n_visible,
+                     int32_t k, int32_t* out, int scan, int n_threads) {
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > 256) n_threads = 256;
+    pthread_t th[256];
+    topk_job jobs[256];
+    int32_t per = (n_q + n_threads - 1) / n_threads;
+    int started = 0;
+    for (int t = 0; t < n_threads; ++t) {
+        int32_t b = per * t;
+        if (b >= n_q) break;
+        jobs[t] = (topk_job){scores, ld, b, b + per < n_q ? b + per : n_q, n_visible, k, out, scan};
+        pthread_create(&th[t], NULL, topk_worker, &jobs[t]);
+        ++started;
+    }
+    for (int t = 0; t < started; ++t) pthread_join(th[t], NULL);
+}
+
+/* ------------------------------------------------------------------------ */
+/* Paged pool model                                                          */
+/* ------------------------------------------------------------------------ */
+/* Pool: n_layers regions of n_pages pages each; page p of layer l starts at
+ * pool + (l * n_pages + p) * PAGE_BYTES.  A slot is page * 64 + offset. */
+static inline uint8_t* page_ptr(uint8_t* pool, int64_t n_pages, int32_t layer, int64_t page) {
+    return pool + ((int64_t)layer * n_pages + page) * (int64_t)PAGE_BYTES;
+}
+
+typedef struct {
+    uint8_t* pool; int64_t n_pages; int32_t n_layers; int32_t layer0; int32_t n_layers_in;
+    const uint16_t* rows; int64_t n_tokens; const int32_t* slots;
+    int64_t r0, r1; uint32_t status;
+} append_job;
+
+static void* append_worker(void* p) {
+    append_job* j = (append_job*)p;
+    uint8_t codes[LATENT];
+    float scales[NBLK];
+    uint16_t rope[ROPE];
+    for (int64_t r = j->r0; r < j->r1; ++r) {
+        int64_t li = r / j->n_tokens, t = r % j->n_tokens;
+        int32_t layer = j->layer0 + (int32_t)li;
+        int32_t slot = j->slots[t];
+        if (slot < 0) continue; /* padding row */
+        if (layer < 0 || layer >= j->n_layers) { j->status |= 1u << RKVO_INVALID_LAYER; continue; }
+        int64_t page = slot / PAGE_TOKENS, off = slot % PAGE_TOKENS;
+        if (page >= j->n_pages) { j->status |= 1u << RKVO_INDEX_OUT_OF_RANGE; continue; }
+        int rc = rkvo_quantize_row_bf16(j->rows + r * ROW_DIM, ROW_DIM, ROPE, codes, scales, rope);
+        if (rc != RKVO_OK) { j->status |= 1u << rc; continue; }
+        uint8_t* pg = page_ptr(j->pool, j->n_pages, layer, page);
+        memcpy(pg + off * LATENT, codes, LATENT);
+        memcpy(pg + CODES_BYTES + off * NBLK * 4, scales, NBLK * 4);
+        memcpy(pg + CODES_BYTES + SCALES_BYTES + off * ROPE * 2, rope, ROPE * 2);
+    }
+    return NULL;
+}
+
+/* rows: [n_layers_in][n_tokens][576] bf16; slots: [n_tokens] (shared by the
+ * layers, < 0 = skip).  Returns the OR of (1 << status) over failed rows. */
+uint32_t rkvo_append_rows(uint8_t* pool, int64_t n_pages, int32_t n_layers, int32_t layer0,
+                          int32_t n_layers_in, const uint16_t* rows, int64_t n_tokens,
+                          const int32_t* slots, int n_threads) {
+    int64_t n_rows = (int64_t)n_layers_in * n_tokens;
+    if (n_rows <= 0) return 0;
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > 256) n_threads = 256;
+    pthread_t th[256];
+    append_job jobs[256];
+    int64_t per = (n_rows + n_threads - 1) / n_threads;
+    int started = 0;
+    for (int t = 0; t < n_threads; ++t) {
+        int64_t b = per * t;
+        if (b >= n_rows) break;
+        jobs[t] = (append_job){pool, n_pages, n_layers, layer0, n_layers_in, rows, n_tokens, slots,
+                               b, b + per < n_rows ? b + per : n_rows, 0};
+        if (n_threads == 1) append_worker(&jobs[t]);
+        else pthread_create(&th[t], NULL, append_worker, &jobs[t]);
+        ++started;
+    }
+    uint32_t st = 0;
+    for (int t = 0; t < started; ++t) {
+        if (n_threads > 1) pthread_join(th[t], NULL);
+        st |= jobs[t].status;
+    }
+    return st;
+}
+
+/* Read one stored row (layer, page, off) back as bf16 [576]. */
+static void read_row(const uint8_t* pool, int64_t n_pages, int32_t layer, int64_t page, int64_t off,
+                     uint16_t* out) {
+    const uint8_t* pg = page_ptr((uint8_t*)pool, n_pages, layer, page);
+    rkvo_dequant_row_bf16(pg + off * LATENT, (const float*)(pg + CODES_BYTES + off * NBLK * 4),
+                          (const uint16_t*)(pg + CODES_BYTES + SCALES_BYTES + off * ROPE * 2),
+                          LATENT, ROPE, out);
+}
+
+typedef struct {
+    const uint8_t* pool; int64_t n_pages; int32_t layer;
+    const int32_t* page_table; int64_t pt_stride; const int32_t* cu_seqlens; int32_t n_seq;
+    uint16_t* out; int64_t r0, r1; uint32_t status;
+} gather_job;
+
+static void* gather_worker(void* p) {
+    gather_job* j = (gather_job*)p;
+    int32_t s = 0;
+    for (int64_t r = j->r0; r < j->r1; ++r) {
+        while (s + 1 <= j->n_seq && j->cu_seqlens[s + 1] <= r) ++s;
+        int64_t t = r - j->cu_seqlens[s];
+        int32_t page = j->page_table[(int64_t)s * j->pt_stride + t / PAGE_TOKENS];
+        if (page < 0 || page >= j->n_pages) {
+            j->status |= 1u << RKVO_INDEX_OUT_OF_RANGE;
+            memset(j->out + r * ROW_DIM, 0, ROW_DIM * 2);
+            continue;
+        }
+        read_row(j->pool, j->n_pages, j->layer, page, t % PAGE_TOKENS, j->out + r * ROW_DIM);
+    }
+    return NULL;
+}
+
+/* Chronological read of n_seq sequences (swa.rs:131 rows() generalised to a
+ * page table): row t of sequence s lands at out[cu_seqlens[s] + t]. */
+uint32_t rkvo_gather_rows(const uint8_t* pool, int64_t n_pages, int32_t n_layers, int32_t layer,
+                          const int32_t* page_table, int64_t pt_stride, const int32_t* cu_seqlens,
+                          int32_t n_seq, uint16_t* out, int n_threads) {
+    if (layer < 0 || layer >= n_layers) return 1u << RKVO_INVALID_LAYER;
+    int64_t n_rows = cu_seqlens[n_seq];
+    if (n_rows <= 0) return 0;
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > 256) n_threads = 256;
+    pthread_t th[256];
+    gather_job jobs[256];
+    int64_t per = (n_rows + n_threads - 1) / n_threads;
+    int started = 0;
+    for (int t = 0; t < n_threads; ++t) {
+        int64_t b = per * t;
+        if (b >= n_rows) break;
+        jobs[t] = (gather_job){pool, n_pages, layer, page_table, pt_stride, cu_seqlens, n_seq, out,
+                               b, b + per < n_rows ? b + per : n_rows, 0};
+        if (n_threads == 1) gather_worker(&jobs[t]);
+        else pthread_create(&th[t], NULL, gather_worker, &jobs[t]);
+        ++started;
+    }
+    uint32_t st = 0;
+    for (int t = 0; t < started; ++t) {
+        if (n_threads > 1) pthread_join(th[t], NULL);
+        st |= jobs[t].status;
+    }
+    return st;
+}
+
+typedef struct {
+    const uint8_t* pool; int64_t n_pages; int32_t layer;
+    const int32_t* page_table; int64_t pt_stride; const int32_t* seq_of_query; const int32_t* seq_lens;
+    const int32_t* idx; int32_t k; uint16_t* out; int64_t r0, r1; uint32_t status;
+} sparse_job;
+
+static void* sparse_worker(void* p) {
+    sparse_job* j = (sparse_job*)p;
+    for (int64_t r = j->r0; r < j->r1; ++r) {
+        int64_t q = r / j->k;
+        int32_t s = j->seq_of_query[q];
+        int32_t t = j->idx[r];
+        uint16_t* o = j->out + r * ROW_DIM;
+        if (t < 0) { memset(o, 0, ROW_DIM * 2); continue; } /* unused selection slot */
+        if (t >= j->seq_lens[s]) { j->status |= 1u << RKVO_INDEX_OUT_OF_RANGE; memset(o, 0, ROW_DIM * 2); continue; }
+        int32_t page = j->page_table[(int64_t)s * j->pt_stride + t / PAGE_TOKENS];
+        if (page < 0 || page >= j->n_pages) { j->status |= 1u << RKVO_INDEX_OUT_OF_RANGE; memset(o, 0, ROW_DIM * 2); continue; }
+        read_row(j->pool, j->n_pages, j->layer, page, t % PAGE_TOKENS, o);
+    }
+    return NULL;
+}
+
+/* Selected-row read (attention.rs:549-560 reads only rows in the top-k set):
+ * out[q][i] = row idx[q][i] of sequence seq_of_query[q]. */
+uint32_t rkvo_sparse_gather_rows(const uint8_t* pool, int64_t n_pages, int32_t n_layers, int32_t layer,
+                                 const int32_t* page_table, int64_t pt_stride, const int32_t* seq_of_query,
+                                 const int32_t* seq_lens, const int32_t* idx, int32_t n_q, int32_t k,
+                                 uint16_t* out, int n_threads) {
+    if (layer < 0 || layer >= n_layers) return 1u << RKVO_INVALID_LAYER;
+    int64_t n_rows = (int64_t)n_q * k;
+    if (n_rows <= 0) return 0;
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > 256) n_threads = 256;
+    pthread_t th[256];
+    sparse_job jobs[256];
+    int64_t per = (n_rows + n_threads - 1) / n_threads;
+    int started = 0;
+    for (int t = 0; t < n_threads; ++t) {
+        int64_t b = per * t;
+        if (b >= n_rows) break;
+        jobs[t] = (sparse_job){pool, n_pages, layer, page_table, pt_stride, seq_of_query, seq_lens, idx, k, out,
+                               b, b + per < n_rows ? b + per : n_rows, 0};
+        if (n_threads == 1) sparse_worker(&jobs[t]);
+        else pthread_create(&th[t], NULL, sparse_worker, &jobs[t]);
+        ++started;
+    }
+    uint32_t st = 0;
+    for (int t = 0; t < started; ++t) {
+        if (n_threads > 1) pthread_join(th[t], NULL);
+        st |= jobs[t].status;
+    }
+    return st;
+}
+
+/* Whole-page copies for copy-on-write and compaction, every layer. */
+void rkvo_copy_pages(uint8_t* pool, int64_t n_pages, int32_t n_layers, const int32_t* src,
+                     const int32_t* dst, int64_t n) {
+    for (int32_t l = 0; l < n_layers; ++l)
+        for (int64_t i = 0; i < n; ++i)
+            memcpy(page_ptr(pool, n_pages, l, dst[i]), page_ptr(pool, n_pages, l, src[i]), PAGE_BYTES);
+}

@@ -1,0 +1,90 @@
+"""ctypes bindings of ``include/rsllm_kv_cuda.h`` (the C ABI of the library).
+
+Loading fails loudly: there is no CPU fallback for any entry point.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, Structure, c_char_p, c_int32, c_int64, c_uint8, c_uint16, c_uint32, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "librsllm_kv_cuda.so"
+HEADER = Path(__file__).resolve().parent.parent / "include" / "rsllm_kv_cuda.h"
+
+RKV_OK = 0
+RKV_ERR_SHAPE_MISMATCH = 1
+RKV_ERR_INDEX_OUT_OF_RANGE = 2
+RKV_ERR_INVALID_LAYER = 3
+RKV_ERR_POOL_FULL = 4
+RKV_ERR_NON_FINITE_INPUT = 5
+RKV_ERR_INVALID_ARGUMENT = 6
+RKV_ERR_CUDA = 7
+
+PAGE_TOKENS = 64
+LATENT_DIM = 512
+ROPE_DIM = 64
+ROW_DIM = 576
+BLOCK = 64
+PAGE_BYTES = 43008
+
+
+class PoolView(Structure):
+    """``rkv_pool_view``: device base pointer, pages per layer, layers."""
+
+    _fields_ = [("base", c_void_p), ("n_pages", c_int64), ("n_layers", c_int32), ("reserved", c_int32)]
+
+
+_P = POINTER
+_u8p, _u16p, _u32p, _i32p, _f32p = c_void_p, c_void_p, c_void_p, c_void_p, c_void_p
+
+# name -> (restype, argtypes); every function the header declares.
+SIGNATURES = {
+    "rkv_version": (c_char_p, []),
+    "rkv_last_error": (c_char_p, []),
+    "rkv_status_from_bits": (c_int32, [c_uint32]),
+    "rkv_pool_bytes": (c_int64, [c_int64, c_int32]),
+    "rkv_append_quant_bf16": (c_int32, [_P(PoolView), c_int32, c_int32, _u16p, c_int64, _i32p, _u32p, c_void_p]),
+    "rkv_gather_dequant_bf16": (c_int32, [_P(PoolView), c_int32, _i32p, c_int64, _i32p, c_int32, c_int32, _u16p,
+                                          _u32p, c_void_p]),
+    "rkv_topk_select_f32": (c_int32, [_f32p, c_int64, c_int32, _i32p, c_int32, c_int32, _i32p, c_void_p]),
+    "rkv_sparse_gather_dequant_bf16": (c_int32, [_P(PoolView), c_int32, _i32p, c_int64, _i32p, _i32p, _i32p,
+                                                 c_int32, c_int32, _u16p, _u32p, c_void_p]),
+    "rkv_copy_pages": (c_int32, [_P(PoolView), _i32p, _i32p, c_int64, _u32p, c_void_p]),
+    "rkv_remap_pages": (c_int32, [_i32p, c_int64, _i32p, c_int64, _u32p, c_void_p]),
+    "rkv_e4m3fn_code_range": (c_int32, [c_uint32, c_int64, _u8p, c_void_p]),
+}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads the CUDA library (building it first if sources are newer)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        from . import build
+
+        build.build()
+    if not LIB_PATH.exists():
+        raise ImportError(f"rsllm_b200: CUDA library missing at {LIB_PATH}")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def last_error() -> str:
+    return load().rkv_last_error().decode("utf-8", "replace")
+
+
+def header_functions() -> list[str]:
+    """Names of the functions the public header declares (parsed from it)."""
+    import re
+
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*RKV_API\s+[^;()]*?\b(rkv_[a-z0-9_]+)\s*\(", text, flags=re.M)))

@@ -1,0 +1,25 @@
+// rkv_host.h -- host-side helpers shared by the C-ABI entry points:
+// argument validation, the per-thread last-error message, launch checks.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/rsllm_kv_cuda.h"
+
+namespace rkv {
+
+// Records a printf-style message as this thread's last error; returns `st`.
+rkv_status fail(rkv_status st, const char* fmt, ...);
+
+// Clears this thread's last error (a call that succeeds leaves "" behind).
+void clear_error();
+
+// Maps a pending launch error (cudaGetLastError) to RKV_ERR_CUDA.
+rkv_status check_launch(const char* what);
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// Validates a pool view: non-null 256-byte aligned base, positive sizes.
+rkv_status check_pool(const rkv_pool_view* p, const char* what);
+
+}  // namespace rkv
