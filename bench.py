@@ -331,13 +331,14 @@ def bench_gather(args, dist: Dist, dev, peak) -> dict:
     import rsllm_b200 as rk
     from rsllm_b200 import synth
 
-    n_seq, ctx = 64, 32768
+    n_seq, ctx = (8, 32768) if args.small else (64, 32768)
     pages_per = ctx // 64
     n_pages = n_seq * pages_per
     free, _ = torch.cuda.mem_get_info(dev)
     out_bytes = n_seq * ctx * 576 * 2
     per_layer = n_pages * rk.PAGE_BYTES
-    l_phys = int(min(N_LAYERS, (free - out_bytes - 8 * 2**30) // per_layer))
+    n_layers = 1 if args.small else N_LAYERS
+    l_phys = int(min(n_layers, (free - out_bytes - 8 * 2**30) // per_layer))
     if l_phys < 1:
         return {"skipped": "not enough device memory"}
     perm = synth.permutation(n_pages, seed=4 + 7919 * dist.rank).to(dev)
@@ -352,7 +353,7 @@ def bench_gather(args, dist: Dist, dev, peak) -> dict:
     stream = torch.cuda.Stream(device=dev)
 
     def step():
-        for layer in range(N_LAYERS):
+        for layer in range(n_layers):
             pool.rows(layer % l_phys, pt, cu, ctx, out=out, stream=stream)
 
     for _ in range(args.phase_warmup):
@@ -364,12 +365,12 @@ def bench_gather(args, dist: Dist, dev, peak) -> dict:
     # per-launch duration of the kernel alone
     one = events_time(lambda: pool.rows(0, pt, cu, ctx, out=out, stream=stream), stream)
     rows = n_seq * ctx
-    step_bytes = N_LAYERS * (rows * GATHER_ROW_BYTES + n_pages * 4)
-    res = {"config": "c3: 64 seqs x 32768 ctx x 61 layers, random page order",
+    step_bytes = n_layers * (rows * GATHER_ROW_BYTES + n_pages * 4)
+    res = {"config": f"c3: {n_seq} seqs x {ctx} ctx x {n_layers} layers, random page order",
            "layers_backed": l_phys, "ms_per_step": ms / args.phase_steps,
            "gbs_per_gpu": step_bytes * args.phase_steps / (ms * 1e-3) / GB,
            "frac_of_hbm_peak": None, "kernel_ms_per_layer": one,
-           "launches_per_step": N_LAYERS}
+           "launches_per_step": n_layers}
     res["frac_of_hbm_peak"] = res["gbs_per_gpu"] / peak
     del pool, out
     torch.cuda.empty_cache()
@@ -380,17 +381,18 @@ def bench_sparse(args, dist: Dist, dev, peak) -> dict:
     import rsllm_b200 as rk
     from rsllm_b200 import synth
 
-    n_seq, ctx, n_qpos, k = 32, 131072, 64, 2048
+    n_seq, ctx, n_qpos, k = (4 if args.small else 32), 131072, 64, 2048
     pages_per = ctx // 64
     n_pages = n_seq * pages_per
     n_q = n_seq * n_qpos
-    n_score_mats = 4
+    n_score_mats = 1 if args.small else 4
+    n_layers = 1 if args.small else N_LAYERS
     out_bytes = n_q * k * 576 * 2
     score_bytes = n_score_mats * n_q * ctx * 4
-    idx_bytes = N_LAYERS * n_q * k * 4
+    idx_bytes = n_layers * n_q * k * 4
     free, _ = torch.cuda.mem_get_info(dev)
     per_layer = n_pages * rk.PAGE_BYTES
-    l_phys = int(min(N_LAYERS, (free - out_bytes - score_bytes - idx_bytes - 10 * 2**30) // per_layer))
+    l_phys = int(min(n_layers, (free - out_bytes - score_bytes - idx_bytes - 10 * 2**30) // per_layer))
     if l_phys < 1:
         return {"skipped": "not enough device memory"}
     perm = synth.permutation(n_pages, seed=6 + 7919 * dist.rank).to(dev)
@@ -406,16 +408,16 @@ def bench_sparse(args, dist: Dist, dev, peak) -> dict:
     n_visible = (ctx - n_qpos + 1 + torch.arange(n_qpos, device=dev, dtype=torch.int32)).repeat(n_seq).contiguous()
     seq_of_query = torch.arange(n_seq, device=dev, dtype=torch.int32).repeat_interleave(n_qpos).contiguous()
     seq_lens = torch.full((n_seq,), ctx, dtype=torch.int32, device=dev)
-    idx = torch.empty((N_LAYERS, n_q, k), dtype=torch.int32, device=dev)
+    idx = torch.empty((n_layers, n_q, k), dtype=torch.int32, device=dev)
     out = torch.empty((n_q, k, 576), dtype=torch.bfloat16, device=dev)
     stream = torch.cuda.Stream(device=dev)
 
     def topk_step():
-        for layer in range(N_LAYERS):
+        for layer in range(n_layers):
             rk.select_top_k(scores[layer % n_score_mats], n_visible, k, out=idx[layer], stream=stream)
 
     def sparse_step():
-        for layer in range(N_LAYERS):
+        for layer in range(n_layers):
             pool.sparse_rows(layer % l_phys, pt, seq_of_query, seq_lens, idx[layer], out=out, stream=stream)
 
     for _ in range(args.phase_warmup):
@@ -431,18 +433,18 @@ def bench_sparse(args, dist: Dist, dev, peak) -> dict:
     one_sparse = events_time(lambda: pool.sparse_rows(0, pt, seq_of_query, seq_lens, idx[0], out=out,
                                                       stream=stream), stream)
     sel = n_q * k
-    sparse_bytes = N_LAYERS * sel * (GATHER_ROW_BYTES + 4 + 4)
+    sparse_bytes = n_layers * sel * (GATHER_ROW_BYTES + 4 + 4)
     vis = int(n_visible.sum().item())
-    topk_bytes = N_LAYERS * (vis * 4 + sel * 4)
+    topk_bytes = n_layers * (vis * 4 + sel * 4)
     P = args.phase_steps
     res = {
-        "topk": {"config": "c4: 2048 queries (32 seqs x last 64 positions, causal) over 131072 keys, k=2048, "
-                           f"61 layers cycling {n_score_mats} seeded N(0,1) score matrices",
+        "topk": {"config": f"c4: {n_q} queries ({n_seq} seqs x last 64 positions, causal) over 131072 keys, "
+                           f"k=2048, {n_layers} layers cycling {n_score_mats} seeded N(0,1) score matrices",
                  "ms_per_step": ms_topk / P, "gbs_per_gpu": topk_bytes * P / (ms_topk * 1e-3) / GB,
                  "frac_of_hbm_peak": topk_bytes * P / (ms_topk * 1e-3) / GB / peak,
-                 "queries_per_s_per_gpu": N_LAYERS * n_q * P / (ms_topk * 1e-3),
+                 "queries_per_s_per_gpu": n_layers * n_q * P / (ms_topk * 1e-3),
                  "kernel_ms_per_layer": one_topk},
-        "sparse_gather": {"config": "c4: 2048 queries x 2048 selected rows x 61 layers, random page order",
+        "sparse_gather": {"config": f"c4: {n_q} queries x 2048 selected rows x {n_layers} layers, random page order",
                           "layers_backed": l_phys, "ms_per_step": ms_sparse / P,
                           "gbs_per_gpu": sparse_bytes * P / (ms_sparse * 1e-3) / GB,
                           "frac_of_hbm_peak": sparse_bytes * P / (ms_sparse * 1e-3) / GB / peak,
@@ -516,6 +518,10 @@ def main():
     ap.add_argument("--phase-steps", type=int, default=3)
     ap.add_argument("--phase-warmup", type=int, default=1)
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
+    ap.add_argument("--only", choices=["all", "append", "gather", "sparse"], default="all",
+                    help="run one workload alone (profiling)")
+    ap.add_argument("--small", action="store_true",
+                    help="profiling sizes for the phases: 8 seqs / 1 layer (gather), 4 seqs / 1 layer (sparse)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         ap.error("--warmup must be >= 3")
@@ -533,6 +539,20 @@ def main():
     peak, peak_kind = peaks()
     clocks = ClockSampler(dev)
     t_start = time.time()
+
+    if args.only != "all":
+        if args.only == "append":
+            res = bench_append(args, dist, dev, peak)
+            res = {k: v for k, v in res.items() if k not in ("pool", "wl")}
+        elif args.only == "gather":
+            res = bench_gather(args, dist, dev, peak)
+        else:
+            res = bench_sparse(args, dist, dev, peak)
+        clocks.stop()
+        dist.close()
+        if dist.rank == 0:
+            print(json.dumps({"only": args.only, "small": args.small, **res}), flush=True)
+        return
 
     app = bench_append(args, dist, dev, peak)
     phases = {}

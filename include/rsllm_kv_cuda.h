@@ -105,7 +105,7 @@ RKV_API int64_t rkv_pool_bytes(int64_t n_pages, int32_t n_layers);
  * (crates/rsllm-kvcache/src/dsv4/three_tier.rs:187-202, swa.rs:73-94), into a
  * paged pool.
  *
- * rows:   bf16 [n_layers_in][n_tokens][576], 16-byte aligned.  Row t of layer
+ * rows:   bf16 [n_layers_in][n_tokens][576], 32-byte aligned.  Row t of layer
  *         layer0 + i is written to slot slot_mapping[t] of that layer.
  * slot_mapping: int32 [n_tokens], shared by the n_layers_in layers (one page
  *         table serves every layer); a negative slot skips the token.
@@ -130,7 +130,7 @@ RKV_API rkv_status rkv_append_quant_bf16(const rkv_pool_view* pool, int32_t laye
  * cu_seqlens: int32 [n_seq + 1], exclusive prefix sum of sequence lengths;
  *             row t of sequence s goes to out[cu_seqlens[s] + t].
  * max_seq_len: an upper bound of every sequence length (sizes the grid).
- * out:        bf16 [cu_seqlens[n_seq]][576], 16-byte aligned.
+ * out:        bf16 [cu_seqlens[n_seq]][576], 32-byte aligned.
  * A page id outside [0, n_pages) sets INDEX_OUT_OF_RANGE and zero-fills the
  * rows it covers. */
 RKV_API rkv_status rkv_gather_dequant_bf16(const rkv_pool_view* pool, int32_t layer, const int32_t* page_table,
@@ -164,7 +164,7 @@ RKV_API rkv_status rkv_topk_select_f32(const float* scores, int64_t ld, int32_t 
  * seq_of_query: int32 [n_q], the sequence (page-table row) of each query.
  * seq_lens:     int32 [n_seq], to bound-check positions (INDEX_OUT_OF_RANGE,
  *               zero row).
- * out:          bf16 [n_q][k][576], 16-byte aligned. */
+ * out:          bf16 [n_q][k][576], 32-byte aligned. */
 RKV_API rkv_status rkv_sparse_gather_dequant_bf16(const rkv_pool_view* pool, int32_t layer,
                                           const int32_t* page_table, int64_t pt_stride,
                                           const int32_t* seq_of_query, const int32_t* seq_lens,

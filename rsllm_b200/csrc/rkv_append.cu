@@ -1,12 +1,15 @@
 // rkv_append.cu -- quantize-on-append of bf16 KV rows into the paged pool.
 //
-// One warp per row (576 bf16 = 1152 B in, 672 B out).  Lane l loads 16 B of
-// each latent half (lanes 8j..8j+7 cover 64-lane block j of that half) and,
-// for l < 8, 16 B of the RoPE part; all loads are issued before any math.
-// The block amax is a 3-step xor-shuffle inside each 8-lane group on the bf16
-// magnitude bits (integer max, so NaN/inf are caught by the same value).
-// Codes go out as one 256 B coalesced run per half, the 8 block scales as one
-// 32 B sector, the RoPE part as 128 B.
+// A persistent grid (one wave of 256-thread CTAs) where each warp moves one
+// row (576 bf16 = 1152 B in, 672 B out) at a time and prefetches its next row
+// before quantising the current one.  Lane l loads 32 B of latent (lanes
+// 16l..16l+15, inside 64-lane block l/4) with one 256-bit load, lanes 0..3
+// also 32 B of RoPE.  The block amax is an integer max over the bf16
+// magnitude bits (NaN and inf show up as >= 0x7f80) reduced over the 4 lanes
+// of the block; the power-of-two scale exponent comes from the amax bits; the
+// lanes are scaled with packed f32x2 multiplies and converted two at a time
+// to E4M3 with saturating RNE.  Codes go out as one 512 B run per warp, the 8
+// block scales as one 32 B sector, the RoPE part as 128 B.
 //
 // Semantics: crates/rsllm-backend-cpu/src/ops/dsv4_quant.rs:316-362 applied
 // per row (see rkv_common.cuh), row placement of crates/rsllm-kvcache/src/
@@ -16,68 +19,81 @@
 
 namespace rkv {
 
-constexpr int kAppendWarps = 8;  // rows per 256-thread CTA
+constexpr int kAppendWarps = 8;  // 256-thread CTAs
 
-__global__ void __launch_bounds__(kAppendWarps * 32)
+// One input row as a warp holds it: lane l has latent lanes 16l..16l+15 (32 B,
+// inside 64-lane block l/4); lanes 0..3 also hold 32 B of the RoPE part.
+struct AppendRow {
+  uint32_t lat[8];
+  uint32_t rope[8];
+  int32_t slot;
+};
+
+__device__ __forceinline__ void load_append_row(const uint8_t* __restrict__ rows, const int32_t* __restrict__ slots,
+                                                uint32_t r, uint32_t n_tokens, int lane, AppendRow& a) {
+  const uint8_t* src = rows + (size_t)r * (kRowDim * 2);
+  ld_stream32(src + lane * 32, a.lat);
+  if (lane < 4) ld_stream32(src + 1024 + lane * 32, a.rope);
+  a.slot = __ldg(slots + (r % n_tokens));
+}
+
+// Persistent grid: warp w handles rows w, w + W, ... (W = all warps), with the
+// loads of its next row issued before the current row is quantised, so every
+// warp keeps two rows (2.3 KB) in flight.
+__global__ void __launch_bounds__(kAppendWarps * 32, 5)
 append_quant_kernel(rkv_pool_view pool, int layer0, uint32_t n_tokens, uint32_t n_rows,
                     const uint16_t* __restrict__ rows, const int32_t* __restrict__ slots,
                     uint32_t* __restrict__ status) {
   const unsigned FULL = 0xffffffffu;
   const int lane = threadIdx.x & 31;
-  const uint32_t r = blockIdx.x * kAppendWarps + (threadIdx.x >> 5);
+  const uint32_t stride = gridDim.x * kAppendWarps;
+  uint32_t r = blockIdx.x * kAppendWarps + (threadIdx.x >> 5);
   if (r >= n_rows) return;
-  const uint32_t li = r / n_tokens;
-  const uint32_t t = r - li * n_tokens;
-  const int32_t slot = __ldg(slots + t);
-  if (slot < 0) return;  // padding token
-  const int64_t page = slot >> 6;
-  const int off = slot & 63;
-  if (page >= pool.n_pages) {
-    if (lane == 0) set_status(status, RKV_ERR_INDEX_OUT_OF_RANGE);
-    return;
-  }
+  const uint8_t* rows8 = reinterpret_cast<const uint8_t*>(rows);
+  AppendRow cur, nxt;
+  load_append_row(rows8, slots, r, n_tokens, lane, cur);
+  for (; r < n_rows; r += stride) {
+    const uint32_t rn = r + stride;
+    if (rn < n_rows) load_append_row(rows8, slots, rn, n_tokens, lane, nxt);
 
-  const uint8_t* src = reinterpret_cast<const uint8_t*>(rows) + (size_t)r * (kRowDim * 2);
-  const uint4 a = ld_stream16(src + lane * 16);
-  const uint4 b = ld_stream16(src + 512 + lane * 16);
-  uint4 rp = make_uint4(0, 0, 0, 0);
-  if (lane < 8) rp = ld_stream16(src + 1024 + lane * 16);
-
-  uint32_t ma = absmax_bits8(a), mb = absmax_bits8(b);
-#pragma unroll
-  for (int o = 1; o < 8; o <<= 1) {
-    ma = max(ma, __shfl_xor_sync(FULL, ma, o));
-    mb = max(mb, __shfl_xor_sync(FULL, mb, o));
-  }
-  // A non-finite latent lane rejects the whole row before anything is written.
-  if (__any_sync(FULL, (ma >= 0x7f80u) | (mb >= 0x7f80u))) {
-    if (lane == 0) set_status(status, RKV_ERR_NON_FINITE_INPUT);
-    return;
-  }
-  const int ea = scale_exponent_bf16amax(__uint_as_float(ma << 16));
-  const int eb = scale_exponent_bf16amax(__uint_as_float(mb << 16));
-  const uint2 ca = quant8(a, __uint_as_float((uint32_t)(127 - ea) << 23));
-  const uint2 cb = quant8(b, __uint_as_float((uint32_t)(127 - eb) << 23));
-
-  uint8_t* pg = page_base(pool, layer0 + (int)li, page);
-  st_stream8(pg + codes_off(off) + lane * 8, ca);
-  st_stream8(pg + codes_off(off) + 256 + lane * 8, cb);
-  // Lane j < 8 stores the scale of block j: blocks 0..3 live on lanes
-  // 0,8,16,24 of the first half, blocks 4..7 on the same lanes of the second.
-  const float sa = __shfl_sync(FULL, __uint_as_float((uint32_t)(ea + 127) << 23), (lane & 3) * 8);
-  const float sb = __shfl_sync(FULL, __uint_as_float((uint32_t)(eb + 127) << 23), (lane & 3) * 8);
-  if (lane < 8) {
-    reinterpret_cast<float*>(pg + scales_off(off))[lane] = lane < 4 ? sa : sb;
-    st_stream16(pg + rope_off(off) + lane * 16, rp);
+    const int32_t slot = cur.slot;
+    if (slot >= 0) {
+      const int64_t page = slot >> 6;
+      const int off = slot & 63;
+      uint32_t m = absmax_bits16(cur.lat);
+      m = max(m, __shfl_xor_sync(FULL, m, 1));
+      m = max(m, __shfl_xor_sync(FULL, m, 2));
+      if (page >= pool.n_pages) {
+        if (lane == 0) set_status(status, RKV_ERR_INDEX_OUT_OF_RANGE);
+      } else if (__any_sync(FULL, m >= 0x7f80u)) {
+        // a non-finite latent lane rejects the whole row before any write
+        if (lane == 0) set_status(status, RKV_ERR_NON_FINITE_INPUT);
+      } else {
+        const int e = scale_exponent_bf16bits(m);
+        const uint4 codes = quant16(cur.lat, __uint_as_float((uint32_t)(127 - e) << 23));
+        uint8_t* pg = page_base(pool, layer0 + (int)(r / n_tokens), page);
+        st_stream16(pg + codes_off(off) + lane * 16, codes);
+        // lane j < 8 stores the scale of block j, held by lane 4j
+        const float sc = __shfl_sync(FULL, __uint_as_float((uint32_t)(e + 127) << 23), (lane & 7) * 4);
+        if (lane < 8) reinterpret_cast<float*>(pg + scales_off(off))[lane] = sc;
+        if (lane < 4)
+          st_stream32(pg + rope_off(off) + lane * 32, make_uint4(cur.rope[0], cur.rope[1], cur.rope[2], cur.rope[3]),
+                      make_uint4(cur.rope[4], cur.rope[5], cur.rope[6], cur.rope[7]));
+      }
+    }
+    cur = nxt;
   }
 }
 
-// Exhaustive-check helper: the same per-lane conversion on raw f32 values.
+// Exhaustive-check helper: the append kernel's lane conversion (packed
+// multiply by the inverse scale, here 1.0, + 0.0, saturating RNE) applied to
+// raw f32 values that are already divided by their block scale.
 __global__ void e4m3_code_range_kernel(uint32_t first, int64_t n, uint8_t* __restrict__ out) {
+  const unsigned long long one2 = 0x3f8000003f800000ull;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    float x = __uint_as_float(first + (uint32_t)i);
-    float t = __fadd_rn(fminf(fmaxf(x, -448.0f), 448.0f), 0.0f);
-    out[i] = (uint8_t)(cvt_e4m3x2(t, 0.0f) & 0xffu);
+    const unsigned long long x = first + (uint32_t)i;  // lane 0 = x, lane 1 = +0.0
+    const unsigned long long t = add_f32x2(mul_f32x2(x, one2), 0ull);
+    out[i] = (uint8_t)(cvt_e4m3x2(__uint_as_float((uint32_t)t), 0.0f) & 0xffu);
   }
 }
 
@@ -99,9 +115,18 @@ extern "C" rkv_status rkv_append_quant_bf16(const rkv_pool_view* pool, int32_t l
     return RKV_OK;
   }
   if (n_rows > (int64_t)INT32_MAX) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_append_quant_bf16: too many rows in one call");
-  if (!rows || !aligned(rows, 16) || !slot_mapping || !aligned(slot_mapping, 4))
-    return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_append_quant_bf16: rows (16-byte aligned) and slot_mapping are required");
-  const unsigned grid = (unsigned)((n_rows + kAppendWarps - 1) / kAppendWarps);
+  if (!rows || !aligned(rows, 32) || !slot_mapping || !aligned(slot_mapping, 4))
+    return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_append_quant_bf16: rows (32-byte aligned) and slot_mapping are required");
+  static int resident = 0;  // CTAs of this kernel one wave holds on the device
+  if (resident == 0) {
+    int dev = 0, sms = 0, per_sm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, append_quant_kernel, kAppendWarps * 32, 0);
+    resident = (sms > 0 && per_sm > 0) ? sms * per_sm : 148 * 4;
+  }
+  const int64_t need = (n_rows + kAppendWarps - 1) / kAppendWarps;
+  const unsigned grid = (unsigned)(need < resident ? need : resident);
   append_quant_kernel<<<grid, kAppendWarps * 32, 0, (cudaStream_t)stream>>>(
       *pool, layer0, (uint32_t)n_tokens, (uint32_t)n_rows, rows, slot_mapping, d_status);
   return check_launch("rkv_append_quant_bf16");

@@ -51,18 +51,18 @@ __device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
   return r;
 }
 
-// Block scale exponent e = ceil(log2(y)), y = RN(max(amax,1e-4) / 448), for a
-// block amax that is a bf16 value.  y is a positive normal f32, so ceil(log2)
-// is its unbiased exponent plus one unless y is an exact power of two.  For
-// bf16 amax this equals the reference's ceil(log2f(y)): y = (m/7) * 2^j with
-// an 8-bit m, which is either an exact power of two or at least 1/224 away
-// from one (verified over every bf16 value by the GPU parity tests).
-__device__ __forceinline__ int scale_exponent_bf16amax(float amax) {
-  amax = fmaxf(amax, 1.0e-4f);
-  float y = __fdiv_rn(amax, 448.0f);
-  uint32_t b = __float_as_uint(y);
-  int e = (int)((b >> 23) & 0xffu) - 127;
-  return e + ((b & 0x7fffffu) != 0u ? 1 : 0);
+// Block scale exponent e = ceil(log2f(max(amax, 1e-4) / 448)) for a block
+// amax that is a bf16 value, from its bits.  With amax = (m/128) * 2^E
+// (m the 8-bit significand, 128..255): amax/448 = (m/7) * 2^(E-13) and
+// m/7 lies in (16, 36.5), so e = E - 8 + (m > 224): the quotient is a power
+// of two only at m = 224 and otherwise at least 1/224 away from one, so the
+// reference's f32 division and glibc log2f land on the same integer
+// (checked on the GPU for every finite bf16 amax against the CPU oracle).
+// Every amax below 1e-4 (the reference's floor) gives e = -22.
+__device__ __forceinline__ int scale_exponent_bf16bits(uint32_t amax_bits) {
+  if (amax_bits < 0x38D2u) return -22;  // bf16 0x38D2 = 1.0014e-4 is the first value >= 1e-4f
+  const int E = (int)(amax_bits >> 7) - 127;
+  return E - 8 + ((amax_bits & 0x7fu) > 96u ? 1 : 0);
 }
 
 // One quantised lane pair: t = v * 2^-e (equal to v / 2^e, both correctly
@@ -77,6 +77,28 @@ __device__ __forceinline__ float quant_lane(float v, float inv_scale) {
 // bf16 pair (packed u32, lo lane in bits 0..15) -> f32 lanes.
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Packed f32x2 arithmetic (sm_100): lo lane in bits 0..31.
+__device__ __forceinline__ unsigned long long mul_f32x2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long add_f32x2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// One bf16 pair -> two E4M3 codes (bits 0..15): t = v * 2^-e exactly as the
+// reference's v / 2^e (both correctly rounded), + 0.0 folds -0.0 into +0.0
+// (the reference's sign is `x < 0`), then RNE with saturation.  For bf16
+// inputs |t| <= 448 always holds, so the reference's clamp is the identity.
+__device__ __forceinline__ uint32_t quant_pair(uint32_t w, unsigned long long inv2) {
+  const unsigned long long v = ((unsigned long long)(w & 0xffff0000u) << 32) | (unsigned long long)(w << 16);
+  const unsigned long long t = add_f32x2(mul_f32x2(v, inv2), 0ull);
+  return cvt_e4m3x2(__uint_as_float((uint32_t)t), __uint_as_float((uint32_t)(t >> 32)));
+}
 
 // 8 bf16 lanes (one uint4) -> 8 codes (uint2), with the block's inverse scale.
 __device__ __forceinline__ uint2 quant8(const uint4& v, float inv) {
@@ -156,7 +178,36 @@ __device__ __forceinline__ void dequant16(const uint4& c, const DecodeScale& d, 
   o1.w = dequant2(c.w >> 16, d);
 }
 
+// 16 bf16 lanes (8 words) -> 16 codes (uint4).
+__device__ __forceinline__ uint4 quant16(const uint32_t (&w)[8], float inv) {
+  const unsigned long long inv2 = ((unsigned long long)__float_as_uint(inv) << 32) | __float_as_uint(inv);
+  uint32_t c[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) c[i] = quant_pair(w[i], inv2);
+  return make_uint4(c[0] | (c[1] << 16), c[2] | (c[3] << 16), c[4] | (c[5] << 16), c[6] | (c[7] << 16));
+}
+
+// Largest |bf16| magnitude bits over 16 lanes (>= 0x7f80: inf or NaN present).
+__device__ __forceinline__ uint32_t absmax_bits16(const uint32_t (&w)[8]) {
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = __vmaxu2(m, w[i] & 0x7fff7fffu);
+  return max(m & 0xffffu, m >> 16);
+}
+
 // ---- cache-policy loads and stores ----------------------------------------
+// 256-bit accesses (sm_100): one instruction moves 32 B per lane, a whole
+// 1 KB latent row per warp.
+__device__ __forceinline__ void ld_stream32(const void* p, uint32_t (&v)[8]) {
+  asm volatile("ld.global.nc.L1::no_allocate.L2::evict_first.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "l"(p));
+}
+__device__ __forceinline__ void st_stream32(void* p, const uint4& a, const uint4& b) {
+  asm volatile("st.global.L1::no_allocate.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+               :: "l"(p), "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+               : "memory");
+}
 // Streaming data is touched once: keep it out of L1 so the page tables and
 // indices stay cached there.
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {

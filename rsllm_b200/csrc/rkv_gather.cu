@@ -1,11 +1,12 @@
 // rkv_gather.cu -- paged gather + dequant (dense, per sequence) and sparse
 // gather + dequant (top-k selected rows) to bf16 [*, 576].
 //
-// Both read a stored row as 512 B of codes (16 B per lane), the lane's block
-// scale (4 B, lanes 4j..4j+3 share block j) and, on lanes 0..7, 16 B of the
-// bf16 RoPE part; they write 1152 B per row (32 B of decoded latent per lane
-// plus the RoPE part).  Loads for several rows are issued before any decode
-// so each warp keeps several KB in flight.
+// A stored row is read as 512 B of codes (16 B per lane), the lane's block
+// scale (4 B; lanes 4j..4j+3 share block j) and 128 B of bf16 RoPE (16 B on
+// each lane of one 8-lane group); it is written as 1 KB of decoded latent
+// (one 256-bit store per lane, 1 KB contiguous per warp) plus the RoPE part.
+// A warp moves kRows rows at a time with every load issued before any
+// decode.  Output rows must be 32-byte aligned (1152 B rows keep that).
 //
 // Decode: (sign * e4m3fn_value(code)) * 2^e rounded to bf16, the value the
 // reference forms at crates/rsllm-backend-cpu/src/ops/dsv4_quant.rs:359;
@@ -15,42 +16,33 @@
 
 namespace rkv {
 
-struct RowLoad {
-  uint4 codes;
-  float scale;
+// A batch of kRows rows as one warp holds it: for every row, lane l has codes
+// 16l..16l+15 (16 B) and the scale of their block (l/4); for RoPE, lane l has
+// 16 B of row l/8 of the batch (8 lanes per 128 B RoPE part).
+constexpr int kRows = 4;
+
+struct RowBatch {
+  uint4 codes[kRows];
+  float scale[kRows];
   uint4 rope;
 };
 
-__device__ __forceinline__ RowLoad load_row(const uint8_t* pg, int off, int lane) {
-  RowLoad r;
-  r.codes = ld_stream16(pg + codes_off(off) + lane * 16);
-  r.scale = __ldg(reinterpret_cast<const float*>(pg + scales_off(off)) + (lane >> 2));
-  r.rope = make_uint4(0, 0, 0, 0);
-  if (lane < 8) r.rope = ld_stream16(pg + rope_off(off) + lane * 16);
-  return r;
+__device__ __forceinline__ void load_latent(const uint8_t* pg, int off, int lane, uint4& codes, float& scale) {
+  codes = ld_stream16(pg + codes_off(off) + lane * 16);
+  scale = __ldg(reinterpret_cast<const float*>(pg + scales_off(off)) + (lane >> 2));
 }
 
-__device__ __forceinline__ void store_row(uint8_t* out_row, const RowLoad& r, int lane) {
+__device__ __forceinline__ void store_latent(uint8_t* out_row, const uint4& codes, float scale, int lane) {
   uint4 o0, o1;
-  dequant16(r.codes, decode_scale(r.scale), o0, o1);
-  st_stream16(out_row + lane * 32, o0);
-  st_stream16(out_row + lane * 32 + 16, o1);
-  if (lane < 8) st_stream16(out_row + 1024 + lane * 16, r.rope);
-}
-
-__device__ __forceinline__ void zero_row(uint8_t* out_row, int lane) {
-  const uint4 z = make_uint4(0, 0, 0, 0);
-  st_stream16(out_row + lane * 32, z);
-  st_stream16(out_row + lane * 32 + 16, z);
-  if (lane < 8) st_stream16(out_row + 1024 + lane * 16, z);
+  dequant16(codes, decode_scale(scale), o0, o1);
+  st_stream32(out_row + lane * 32, o0, o1);  // 1 KB per warp, one instruction
 }
 
 constexpr int kGatherWarps = 8;  // one 256-thread CTA per (sequence, page)
-constexpr int kRowsInFlight = 4;  // rows each warp loads before decoding
 
-// grid = (pages per longest sequence, n_seq).  Warp w handles rows
-// w, w+8, ..., w+56 of the page, kRowsInFlight at a time.
-__global__ void __launch_bounds__(kGatherWarps * 32)
+// grid = (pages of the longest sequence, n_seq).  Warp w handles rows
+// w + 8i of the page, kRows at a time (two batches cover 64 rows).
+__global__ void __launch_bounds__(kGatherWarps * 32, 6)
 gather_dequant_kernel(rkv_pool_view pool, int layer, const int32_t* __restrict__ page_table, int64_t pt_stride,
                       const int32_t* __restrict__ cu_seqlens, uint16_t* __restrict__ out,
                       uint32_t* __restrict__ status) {
@@ -64,75 +56,106 @@ gather_dequant_kernel(rkv_pool_view pool, int layer, const int32_t* __restrict__
   const int32_t page = __ldg(page_table + (int64_t)s * pt_stride + p);
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   uint8_t* out_page = reinterpret_cast<uint8_t*>(out + ((int64_t)start + t0) * kRowDim);
+  const uint4 z = make_uint4(0, 0, 0, 0);
   if (page < 0 || page >= pool.n_pages) {
     if (threadIdx.x == 0) set_status(status, RKV_ERR_INDEX_OUT_OF_RANGE);
-    for (int row = w; row < nrows; row += kGatherWarps) zero_row(out_page + (int64_t)row * (kRowDim * 2), lane);
+    for (int row = w; row < nrows; row += kGatherWarps) {
+      uint8_t* o = out_page + (int64_t)row * (kRowDim * 2);
+      st_stream32(o + lane * 32, z, z);
+      if (lane < 8) st_stream16(o + 1024 + lane * 16, z);
+    }
     return;
   }
   const uint8_t* pg = page_base(pool, layer, page);
+  const int rl = lane >> 3;  // the batch row whose RoPE part this lane moves
 #pragma unroll
-  for (int base = 0; base < kPageTokens; base += kGatherWarps * kRowsInFlight) {
-    RowLoad ld[kRowsInFlight];
+  for (int base = 0; base < kPageTokens; base += kGatherWarps * kRows) {
+    RowBatch b;
 #pragma unroll
-    for (int i = 0; i < kRowsInFlight; ++i) {
+    for (int i = 0; i < kRows; ++i) {
       const int row = base + w + i * kGatherWarps;
-      if (row < nrows) ld[i] = load_row(pg, row, lane);
+      if (row < nrows) load_latent(pg, row, lane, b.codes[i], b.scale[i]);
     }
+    const int rrow = base + w + rl * kGatherWarps;
+    if (rrow < nrows) b.rope = ld_stream16(pg + rope_off(rrow) + (lane & 7) * 16);
 #pragma unroll
-    for (int i = 0; i < kRowsInFlight; ++i) {
+    for (int i = 0; i < kRows; ++i) {
       const int row = base + w + i * kGatherWarps;
-      if (row < nrows) store_row(out_page + (int64_t)row * (kRowDim * 2), ld[i], lane);
+      if (row < nrows) store_latent(out_page + (int64_t)row * (kRowDim * 2), b.codes[i], b.scale[i], lane);
     }
+    if (rrow < nrows) st_stream16(out_page + (int64_t)rrow * (kRowDim * 2) + 1024 + (lane & 7) * 16, b.rope);
   }
 }
 
 constexpr int kSparseWarps = 8;
-constexpr int kSparseRowsPerWarp = 4;
+constexpr int kSparseRows = 8;  // selections per warp, resolved by lanes 0..7
 
-// One warp per kSparseRowsPerWarp consecutive selections of out[n_q][k].
-__global__ void __launch_bounds__(kSparseWarps * 32)
+// One warp per kSparseRows consecutive selections of out[n_q][k].  Lanes
+// 0..7 resolve index -> sequence -> page in parallel and broadcast; the rows
+// are then moved kRows at a time.
+__global__ void __launch_bounds__(kSparseWarps * 32, 5)
 sparse_gather_dequant_kernel(rkv_pool_view pool, int layer, const int32_t* __restrict__ page_table,
                              int64_t pt_stride, const int32_t* __restrict__ seq_of_query,
                              const int32_t* __restrict__ seq_lens, const int32_t* __restrict__ idx, int64_t n_sel,
                              int k, uint16_t* __restrict__ out, uint32_t* __restrict__ status) {
+  const unsigned FULL = 0xffffffffu;
   const int lane = threadIdx.x & 31;
-  const int64_t g0 = ((int64_t)blockIdx.x * kSparseWarps + (threadIdx.x >> 5)) * kSparseRowsPerWarp;
+  const int64_t g0 = ((int64_t)blockIdx.x * kSparseWarps + (threadIdx.x >> 5)) * kSparseRows;
   if (g0 >= n_sel) return;
-  int64_t page[kSparseRowsPerWarp];
-  int off[kSparseRowsPerWarp];
-#pragma unroll
-  for (int i = 0; i < kSparseRowsPerWarp; ++i) {
-    const int64_t g = g0 + i;
-    page[i] = -2;  // -2: past the end, -1: write zeros
-    off[i] = 0;
-    if (g < n_sel) {
-      const int32_t t = __ldg(idx + g);
-      const int32_t s = __ldg(seq_of_query + g / k);
-      page[i] = -1;
-      if (t >= 0) {
-        if (t < __ldg(seq_lens + s)) {
-          const int32_t pgid = __ldg(page_table + (int64_t)s * pt_stride + (t >> 6));
-          if (pgid >= 0 && pgid < pool.n_pages) {
-            page[i] = pgid;
-            off[i] = t & 63;
-          } else if (lane == 0) {
-            set_status(status, RKV_ERR_INDEX_OUT_OF_RANGE);
-          }
-        } else if (lane == 0) {
+  // lane i < kSparseRows: where selection g0 + i lives (page = -2: past the
+  // end of the output, -1: write zeros)
+  int32_t my_page = -2, my_off = 0;
+  if (lane < kSparseRows && g0 + lane < n_sel) {
+    const int64_t g = g0 + lane;
+    const int32_t t = __ldg(idx + g);
+    const int32_t s = __ldg(seq_of_query + g / k);
+    my_page = -1;
+    if (t >= 0) {
+      if (t < __ldg(seq_lens + s)) {
+        const int32_t pgid = __ldg(page_table + (int64_t)s * pt_stride + (t >> 6));
+        if (pgid >= 0 && pgid < pool.n_pages) {
+          my_page = pgid;
+          my_off = t & 63;
+        } else {
           set_status(status, RKV_ERR_INDEX_OUT_OF_RANGE);
         }
+      } else {
+        set_status(status, RKV_ERR_INDEX_OUT_OF_RANGE);
       }
     }
   }
-  RowLoad ld[kSparseRowsPerWarp];
+  const int rl = lane >> 3;
+  const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
-  for (int i = 0; i < kSparseRowsPerWarp; ++i)
-    if (page[i] >= 0) ld[i] = load_row(page_base(pool, layer, page[i]), off[i], lane);
+  for (int base = 0; base < kSparseRows; base += kRows) {
+    int32_t page[kRows], off[kRows];
 #pragma unroll
-  for (int i = 0; i < kSparseRowsPerWarp; ++i) {
-    uint8_t* orow = reinterpret_cast<uint8_t*>(out + (g0 + i) * kRowDim);
-    if (page[i] >= 0) store_row(orow, ld[i], lane);
-    else if (page[i] == -1) zero_row(orow, lane);
+    for (int i = 0; i < kRows; ++i) {
+      page[i] = __shfl_sync(FULL, my_page, base + i);
+      off[i] = __shfl_sync(FULL, my_off, base + i);
+    }
+    RowBatch b;
+#pragma unroll
+    for (int i = 0; i < kRows; ++i)
+      if (page[i] >= 0) load_latent(page_base(pool, layer, page[i]), off[i], lane, b.codes[i], b.scale[i]);
+    // RoPE of batch row rl (register-indexed selects, no local memory)
+    int32_t rpage = page[0], roff = off[0];
+#pragma unroll
+    for (int i = 1; i < kRows; ++i)
+      if (rl == i) {
+        rpage = page[i];
+        roff = off[i];
+      }
+    if (rpage >= 0) b.rope = ld_stream16(page_base(pool, layer, rpage) + rope_off(roff) + (lane & 7) * 16);
+#pragma unroll
+    for (int i = 0; i < kRows; ++i) {
+      uint8_t* orow = reinterpret_cast<uint8_t*>(out + (g0 + base + i) * kRowDim);
+      if (page[i] >= 0) store_latent(orow, b.codes[i], b.scale[i], lane);
+      else if (page[i] == -1) st_stream32(orow + lane * 32, z, z);
+    }
+    uint8_t* rrow = reinterpret_cast<uint8_t*>(out + (g0 + base + rl) * kRowDim) + 1024 + (lane & 7) * 16;
+    if (rpage >= 0) st_stream16(rrow, b.rope);
+    else if (rpage == -1) st_stream16(rrow, z);
   }
 }
 
@@ -158,8 +181,8 @@ extern "C" rkv_status rkv_gather_dequant_bf16(const rkv_pool_view* pool, int32_t
     return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_gather_dequant_bf16: pt_stride %lld < %lld pages", (long long)pt_stride,
                 (long long)pages);
   if (n_seq > 65535) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_gather_dequant_bf16: at most 65535 sequences per call");
-  if (!page_table || !cu_seqlens || !out || !aligned(out, 16))
-    return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_gather_dequant_bf16: page_table, cu_seqlens and a 16-byte aligned out are required");
+  if (!page_table || !cu_seqlens || !out || !aligned(out, 32))
+    return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_gather_dequant_bf16: page_table, cu_seqlens and a 32-byte aligned out are required");
   dim3 grid((unsigned)pages, (unsigned)n_seq);
   gather_dequant_kernel<<<grid, kGatherWarps * 32, 0, (cudaStream_t)stream>>>(*pool, layer, page_table, pt_stride,
                                                                             cu_seqlens, out, d_status);
@@ -183,10 +206,10 @@ extern "C" rkv_status rkv_sparse_gather_dequant_bf16(const rkv_pool_view* pool, 
     clear_error();
     return RKV_OK;
   }
-  if (!page_table || !seq_of_query || !seq_lens || !idx || !out || !aligned(out, 16))
+  if (!page_table || !seq_of_query || !seq_lens || !idx || !out || !aligned(out, 32))
     return fail(RKV_ERR_INVALID_ARGUMENT,
-                "rkv_sparse_gather_dequant_bf16: page_table, seq_of_query, seq_lens, idx and a 16-byte aligned out are required");
-  const int64_t per_cta = (int64_t)kSparseWarps * kSparseRowsPerWarp;
+                "rkv_sparse_gather_dequant_bf16: page_table, seq_of_query, seq_lens, idx and a 32-byte aligned out are required");
+  const int64_t per_cta = (int64_t)kSparseWarps * kSparseRows;
   const int64_t grid = (n_sel + per_cta - 1) / per_cta;
   if (grid > INT32_MAX) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_sparse_gather_dequant_bf16: too many rows");
   sparse_gather_dequant_kernel<<<(unsigned)grid, kSparseWarps * 32, 0, (cudaStream_t)stream>>>(

@@ -26,9 +26,10 @@ def test_device_encoder_every_f32_up_to_512(cuda, orc):
             want = orc.e4m3fn_code_range(sign + first, n)
             bad = np.nonzero(got != want)[0]
             assert bad.size == 0, f"code mismatch at f32 bits 0x{sign + first + int(bad[0]):08x}"
-    # infinities and a stride through the saturating range
-    tail = [0x7F800000, 0xFF800000, 0x7F7FFFFF, 0xFF7FFFFF]
-    for b in tail + list(range(hi, 0x7F800000, 0x10001)):
+    # the largest finite values and a stride through the saturating range (the
+    # append path never converts a value above 448; this pins saturation)
+    tail = [0x7F7FFFFF, 0xFF7FFFFF]
+    for b in tail + list(range(hi, 0x7F800000, 0x100001)) + list(range(0x80000000 + hi, 0xFF800000, 0x100001)):
         got = int(rk.e4m3fn_code_range(b, 1, device=cuda).item())
         assert got == int(orc.e4m3fn_code_range(b, 1)[0]), hex(b)
 
