@@ -227,13 +227,16 @@ def bench_append(args, dist: Dist, dev, peak) -> dict:
         with torch.cuda.graph(graph, stream=stream):
             for j in range(W, W + K):
                 pool.append_layer(0, wl.rows[j], wl.slots[j])
-    flush_l2(dev)
-    dist.barrier()
-
     def replay():
         with torch.cuda.stream(stream):
             graph.replay()
 
+    # one untimed replay uploads the graph (it rewrites the same rows into the
+    # same slots); the timed replay then measures only the K steps
+    replay()
+    stream.synchronize()
+    flush_l2(dev)
+    dist.barrier()
     ms = events_time(replay, stream)
     dist.barrier()
     pool.check("append", stream)
@@ -580,7 +583,7 @@ def main():
                        "seq_len": "U[1024,32768]", "page_tokens": 64, "row": "512 latent fp8 + 64 rope bf16",
                        "parallelism": f"request-sharded x{dist.world}, no collective",
                        "l2": "inputs larger than L2 (fresh rows every step, 1.9 GB total) + L2 flush before timing",
-                       "launch": "K steps captured in one CUDA graph"},
+                       "launch": "K steps captured in one CUDA graph (uploaded by an untimed replay)"},
             "tokens_per_s": app["tokens_per_s_per_gpu"] * dist.world,
             "rows_per_s": app["tokens_per_s_per_gpu"] * dist.world * N_LAYERS,
             "frac_of_hbm_peak_per_gpu": app["gbs_per_gpu"] / peak,

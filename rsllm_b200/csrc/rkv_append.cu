@@ -1,15 +1,15 @@
 // rkv_append.cu -- quantize-on-append of bf16 KV rows into the paged pool.
 //
-// A persistent grid (one wave of 256-thread CTAs) where each warp moves one
-// row (576 bf16 = 1152 B in, 672 B out) at a time and prefetches its next row
-// before quantising the current one.  Lane l loads 32 B of latent (lanes
-// 16l..16l+15, inside 64-lane block l/4) with one 256-bit load, lanes 0..3
-// also 32 B of RoPE.  The block amax is an integer max over the bf16
-// magnitude bits (NaN and inf show up as >= 0x7f80) reduced over the 4 lanes
-// of the block; the power-of-two scale exponent comes from the amax bits; the
-// lanes are scaled with packed f32x2 multiplies and converted two at a time
-// to E4M3 with saturating RNE.  Codes go out as one 512 B run per warp, the 8
-// block scales as one 32 B sector, the RoPE part as 128 B.
+// A persistent grid (at most one wave of 256-thread CTAs) in which each warp
+// moves one row (576 bf16 = 1152 B in, 672 B out) at a time and prefetches
+// its next row before quantising the current one.  Lane l loads 32 B of
+// latent (lanes 16l..16l+15, inside 64-lane block l/4) with one 256-bit load;
+// lanes 0..7 also 16 B of RoPE.  The block amax is an integer max over the
+// bf16 magnitude bits (NaN and inf show up as >= 0x7f80) reduced over the 4
+// lanes of the block; the power-of-two scale exponent comes from the amax
+// bits; the lanes are scaled with packed f32x2 multiplies and converted two at
+// a time to E4M3 with saturating RNE.  Codes go out as one 512 B run per row,
+// the 8 block scales as one 32 B sector, the RoPE part as 128 B.
 //
 // Semantics: crates/rsllm-backend-cpu/src/ops/dsv4_quant.rs:316-362 applied
 // per row (see rkv_common.cuh), row placement of crates/rsllm-kvcache/src/
@@ -19,69 +19,79 @@
 
 namespace rkv {
 
+static inline rkv_pool_view pool_copy(const rkv_pool_view& p) { return p; }
+
 constexpr int kAppendWarps = 8;  // 256-thread CTAs
 
-// One input row as a warp holds it: lane l has latent lanes 16l..16l+15 (32 B,
-// inside 64-lane block l/4); lanes 0..3 also hold 32 B of the RoPE part.
-struct AppendRow {
-  uint32_t lat[8];
-  uint32_t rope[8];
-  int32_t slot;
-};
-
-__device__ __forceinline__ void load_append_row(const uint8_t* __restrict__ rows, const int32_t* __restrict__ slots,
-                                                uint32_t r, uint32_t n_tokens, int lane, AppendRow& a) {
-  const uint8_t* src = rows + (size_t)r * (kRowDim * 2);
-  ld_stream32(src + lane * 32, a.lat);
-  if (lane < 4) ld_stream32(src + 1024 + lane * 32, a.rope);
-  a.slot = __ldg(slots + (r % n_tokens));
+// Quantise and store one row a warp holds: lane l has latent lanes
+// 16l..16l+15 in lat (inside 64-lane block l/4), lanes 0..7 hold 16 B each of
+// the RoPE part.  Every lane sees the same slot, so the branches are uniform.
+__device__ __forceinline__ void append_row(const rkv_pool_view& pool, int layer, int32_t slot,
+                                           const uint32_t (&lat)[8], const uint4& rope, uint32_t* status,
+                                           int lane) {
+  const unsigned FULL = 0xffffffffu;
+  if (slot < 0) return;  // padding token
+  const int64_t page = slot >> 6;
+  const int off = slot & 63;
+  uint32_t m = absmax_bits16(lat);
+  m = max(m, __shfl_xor_sync(FULL, m, 1));
+  m = max(m, __shfl_xor_sync(FULL, m, 2));
+  if (page >= pool.n_pages) {
+    if (lane == 0) set_status(status, RKV_ERR_INDEX_OUT_OF_RANGE);
+    return;
+  }
+  if (__any_sync(FULL, m >= 0x7f80u)) {  // a non-finite latent lane rejects the row before any write
+    if (lane == 0) set_status(status, RKV_ERR_NON_FINITE_INPUT);
+    return;
+  }
+  const int e = scale_exponent_bf16bits(m);
+  const uint4 codes = quant16(lat, __uint_as_float((uint32_t)(127 - e) << 23));
+  uint8_t* pg = page_base(pool, layer, page);
+  st_stream16(pg + codes_off(off) + lane * 16, codes);
+  // lane j < 8 stores the scale of block j, held by lane 4j, and 16 B of RoPE
+  const float sc = __shfl_sync(FULL, __uint_as_float((uint32_t)(e + 127) << 23), (lane & 7) * 4);
+  if (lane < 8) {
+    reinterpret_cast<float*>(pg + scales_off(off))[lane] = sc;
+    st_stream16(pg + rope_off(off) + lane * 16, rope);
+  }
 }
 
-// Persistent grid: warp w handles rows w, w + W, ... (W = all warps), with the
-// loads of its next row issued before the current row is quantised, so every
-// warp keeps two rows (2.3 KB) in flight.
-__global__ void __launch_bounds__(kAppendWarps * 32, 5)
+// Persistent grid (at most one wave): warp w handles rows w, w + W, ...
+// (W = warps in the grid) and issues the loads of its next row -- 32 B of
+// latent per lane (one 256-bit load), 16 B of RoPE on lanes 0..7 and the
+// slot index -- before it quantises the current one, so two rows per warp
+// are in flight.  Launched with Programmatic Dependent Launch: the CTAs of
+// the next launch become resident while this one drains and wait
+// (griddepcontrol.wait) for it before touching memory.
+__global__ void __launch_bounds__(kAppendWarps * 32)
 append_quant_kernel(rkv_pool_view pool, int layer0, uint32_t n_tokens, uint32_t n_rows,
                     const uint16_t* __restrict__ rows, const int32_t* __restrict__ slots,
                     uint32_t* __restrict__ status) {
-  const unsigned FULL = 0xffffffffu;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = threadIdx.x & 31;
   const uint32_t stride = gridDim.x * kAppendWarps;
   uint32_t r = blockIdx.x * kAppendWarps + (threadIdx.x >> 5);
   if (r >= n_rows) return;
   const uint8_t* rows8 = reinterpret_cast<const uint8_t*>(rows);
-  AppendRow cur, nxt;
-  load_append_row(rows8, slots, r, n_tokens, lane, cur);
+  uint32_t lat[8], nlat[8];
+  uint4 rope = make_uint4(0, 0, 0, 0), nrope = rope;
+  int32_t slot, nslot = -1;
+  ld_stream32(rows8 + (size_t)r * (kRowDim * 2) + lane * 32, lat);
+  if (lane < 8) rope = ld_stream16(rows8 + (size_t)r * (kRowDim * 2) + 1024 + lane * 16);
+  slot = __ldg(slots + r % n_tokens);
   for (; r < n_rows; r += stride) {
     const uint32_t rn = r + stride;
-    if (rn < n_rows) load_append_row(rows8, slots, rn, n_tokens, lane, nxt);
-
-    const int32_t slot = cur.slot;
-    if (slot >= 0) {
-      const int64_t page = slot >> 6;
-      const int off = slot & 63;
-      uint32_t m = absmax_bits16(cur.lat);
-      m = max(m, __shfl_xor_sync(FULL, m, 1));
-      m = max(m, __shfl_xor_sync(FULL, m, 2));
-      if (page >= pool.n_pages) {
-        if (lane == 0) set_status(status, RKV_ERR_INDEX_OUT_OF_RANGE);
-      } else if (__any_sync(FULL, m >= 0x7f80u)) {
-        // a non-finite latent lane rejects the whole row before any write
-        if (lane == 0) set_status(status, RKV_ERR_NON_FINITE_INPUT);
-      } else {
-        const int e = scale_exponent_bf16bits(m);
-        const uint4 codes = quant16(cur.lat, __uint_as_float((uint32_t)(127 - e) << 23));
-        uint8_t* pg = page_base(pool, layer0 + (int)(r / n_tokens), page);
-        st_stream16(pg + codes_off(off) + lane * 16, codes);
-        // lane j < 8 stores the scale of block j, held by lane 4j
-        const float sc = __shfl_sync(FULL, __uint_as_float((uint32_t)(e + 127) << 23), (lane & 7) * 4);
-        if (lane < 8) reinterpret_cast<float*>(pg + scales_off(off))[lane] = sc;
-        if (lane < 4)
-          st_stream32(pg + rope_off(off) + lane * 32, make_uint4(cur.rope[0], cur.rope[1], cur.rope[2], cur.rope[3]),
-                      make_uint4(cur.rope[4], cur.rope[5], cur.rope[6], cur.rope[7]));
-      }
+    if (rn < n_rows) {
+      ld_stream32(rows8 + (size_t)rn * (kRowDim * 2) + lane * 32, nlat);
+      if (lane < 8) nrope = ld_stream16(rows8 + (size_t)rn * (kRowDim * 2) + 1024 + lane * 16);
+      nslot = __ldg(slots + rn % n_tokens);
     }
-    cur = nxt;
+    append_row(pool, layer0 + (int)(r / n_tokens), slot, lat, rope, status, lane);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) lat[j] = nlat[j];
+    rope = nrope;
+    slot = nslot;
   }
 }
 
@@ -127,8 +137,19 @@ extern "C" rkv_status rkv_append_quant_bf16(const rkv_pool_view* pool, int32_t l
   }
   const int64_t need = (n_rows + kAppendWarps - 1) / kAppendWarps;
   const unsigned grid = (unsigned)(need < resident ? need : resident);
-  append_quant_kernel<<<grid, kAppendWarps * 32, 0, (cudaStream_t)stream>>>(
-      *pool, layer0, (uint32_t)n_tokens, (uint32_t)n_rows, rows, slot_mapping, d_status);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kAppendWarps * 32);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, append_quant_kernel, pool_copy(*pool), (int)layer0, (uint32_t)n_tokens,
+                                     (uint32_t)n_rows, rows, slot_mapping, d_status);
+  if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_append_quant_bf16: launch failed: %s", cudaGetErrorString(e));
   return check_launch("rkv_append_quant_bf16");
 }
 

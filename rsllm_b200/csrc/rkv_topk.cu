@@ -6,13 +6,14 @@
 // -inf.  The scan is O(k*n); this kernel produces the same list in one pass
 // over the scores in the common case.
 //
-// One 1024-thread CTA per query.  Scores map to order-preserving u32 keys
+// One 512-thread CTA per query, two per SM.  Scores map to order-preserving u32 keys
 // (0 = cannot win; -0.0 folded into +0.0 because `>` ties them), so "key >= t"
 // is "score >= float(t)".
 //  * n <= 8192: every key goes to the shared-memory candidate buffer.
-//  * Otherwise a 4096-key sample (32 contiguous chunks of 128) gives a
-//    threshold t, the sample's r-th largest key with r chosen so that about
-//    1.5 * effective_k scores are expected at or above it.  One pass over the
+//  * Otherwise a 4096-key sample (32 contiguous chunks of 128, held in
+//    registers) gives a threshold t, the sample's r-th largest key, with r
+//    set from the sampling error so that effective_k to ~1.5 effective_k
+//    scores are expected at or above it.  One pass over the
 //    scores appends every score >= t to the candidate buffer (8192 entries,
 //    warp-aggregated).  If that set holds at least effective_k and fits, it
 //    contains the exact top-k (the k-th largest score is >= t), ties included.
@@ -20,23 +21,30 @@
 //    an exact radix selection runs: 11 + 11 + 10-bit histogram passes until
 //    the keys at or above the selected bin fit, then a collection pass; keys
 //    equal to a fully resolved threshold are taken lowest index first.
-// The candidates (key << 32 | ~index) are bitonic-sorted in shared memory and
-// the first effective_k indices written.
+// The candidates (key << 32 | ~index) are cut to the keys >= the
+// effective_k-th largest by one more radix selection in shared memory,
+// bitonic-sorted (register stages for strides below 64) and the first
+// effective_k indices written.
 #include "rkv_common.cuh"
 #include "rkv_host.h"
 
 namespace rkv {
 
-constexpr int kTopkThreads = 1024;
+constexpr int kTopkThreads = 512;  // two CTAs per SM, 64 registers per thread
+constexpr int kTopkWarps = kTopkThreads / 32;
 constexpr int kTopkMaxK = 4096;
 constexpr int kCandCap = 8192;
-constexpr int kSampleChunk = 128;                            // keys per chunk: one float4 per lane
-constexpr int kSample = (kTopkThreads / 32) * kSampleChunk;  // 4096, one chunk per warp
+constexpr int kCutCap = 2048;
+constexpr int kSampleChunk = 128;                         // keys per chunk: one float4 per lane
+constexpr int kSampleChunks = 32;
+constexpr int kSample = kSampleChunks * kSampleChunk;     // 4096
+constexpr int kSamplePerThread = kSample / kTopkThreads;  // 8, held in registers
+constexpr int kBinsPerThread = 2048 / kTopkThreads;       // 4
 
 struct TopkSmem {
   uint32_t hist[2048];
   unsigned long long cand[kCandCap];
-  uint32_t sample[kSample];
+  unsigned long long cut[kCutCap];
   uint32_t warp_sums[32];
   uint32_t sel_bin, sel_above, n_cand;
 };
@@ -70,14 +78,20 @@ __device__ __forceinline__ void for_each_key(const float* __restrict__ row, int 
   }
 }
 
-// Finds the bin b (of nbins) with above(b) < rank <= above(b) + hist[b],
-// above(b) = sum of hist over bins > b.  Thread t owns bins nbins-1-2t and
-// nbins-2-2t.  Result in sm.sel_bin / sm.sel_above (valid after a barrier).
+// Finds the bin b (of nbins <= 2048) with above(b) < rank <= above(b) +
+// hist[b], above(b) = sum of hist over bins > b.  Thread t owns the
+// kBinsPerThread bins counted down from nbins-1-t*kBinsPerThread.  Result in
+// sm.sel_bin / sm.sel_above (valid after a barrier).
 __device__ void select_bin(TopkSmem& sm, int nbins, uint32_t rank) {
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const int b0 = nbins - 1 - 2 * tid, b1 = b0 - 1;
-  const uint32_t h0 = b0 >= 0 ? sm.hist[b0] : 0u, h1 = b1 >= 0 ? sm.hist[b1] : 0u;
-  uint32_t v = h0 + h1, incl = v;
+  const int top = nbins - 1 - tid * kBinsPerThread;
+  uint32_t h[kBinsPerThread], v = 0;
+#pragma unroll
+  for (int j = 0; j < kBinsPerThread; ++j) {
+    h[j] = top - j >= 0 ? sm.hist[top - j] : 0u;
+    v += h[j];
+  }
+  uint32_t incl = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
@@ -86,24 +100,23 @@ __device__ void select_bin(TopkSmem& sm, int nbins, uint32_t rank) {
   if (lane == 31) sm.warp_sums[w] = incl;
   __syncthreads();
   if (w == 0) {
-    uint32_t s = sm.warp_sums[lane], si = s;
+    uint32_t x = lane < kTopkWarps ? sm.warp_sums[lane] : 0u, xi = x;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xffffffffu, si, o);
-      if (lane >= o) si += y;
+      const uint32_t y = __shfl_up_sync(0xffffffffu, xi, o);
+      if (lane >= o) xi += y;
     }
-    sm.warp_sums[lane] = si - s;  // exclusive
+    if (lane < kTopkWarps) sm.warp_sums[lane] = xi - x;  // exclusive
   }
   __syncthreads();
-  const uint32_t above0 = sm.warp_sums[w] + incl - v;
-  if (b0 >= 0 && above0 < rank && rank <= above0 + h0) {
-    sm.sel_bin = (uint32_t)b0;
-    sm.sel_above = above0;
-  }
-  const uint32_t above1 = above0 + h0;
-  if (b1 >= 0 && above1 < rank && rank <= above1 + h1) {
-    sm.sel_bin = (uint32_t)b1;
-    sm.sel_above = above1;
+  uint32_t above = sm.warp_sums[w] + incl - v;
+#pragma unroll
+  for (int j = 0; j < kBinsPerThread; ++j) {
+    if (top - j >= 0 && above < rank && rank <= above + h[j]) {
+      sm.sel_bin = (uint32_t)(top - j);
+      sm.sel_above = above;
+    }
+    above += h[j];
   }
 }
 
@@ -116,7 +129,7 @@ __device__ __forceinline__ uint32_t block_scan_flag(TopkSmem& sm, bool flag, uin
   if (lane == 0) sm.warp_sums[w] = __popc(bal);
   __syncthreads();
   uint32_t before = 0, all = 0;
-  for (int i = 0; i < kTopkThreads / 32; ++i) {
+  for (int i = 0; i < kTopkWarps; ++i) {
     const uint32_t c = sm.warp_sums[i];
     before += i < w ? c : 0u;
     all += c;
@@ -129,13 +142,16 @@ __device__ __forceinline__ float key_to_float(uint32_t key) {
   return __uint_as_float((key & 0x80000000u) ? (key & 0x7fffffffu) : ~key);
 }
 
-// The rank-th largest of `count` keys held in shared memory (rank >= 1), or 0
-// when fewer than `rank` of them can win.  Three histogram passes (11, 11, 10
-// bits); key(i) reads the i-th key.
+// Radix selection over `count` keys in shared memory (key(i) reads the
+// i-th): the lower bound of the narrowest bin (11, then 11, then 10 bits)
+// holding the rank-th largest key (rank >= 1), stopping once the keys at or
+// above the bin number at most `fit`; after three passes the bound is the
+// rank-th largest key itself.  *n_at_least = keys >= the returned bound.
 template <class KeyAt>
-__device__ uint32_t smem_select(TopkSmem& sm, int count, uint32_t rank, KeyAt key) {
+__device__ uint32_t smem_select(TopkSmem& sm, int count, uint32_t rank, uint32_t fit, uint32_t* n_at_least,
+                                KeyAt key) {
   const int tid = threadIdx.x;
-  uint32_t prefix = 0u, pmask = 0u;
+  uint32_t prefix = 0u, pmask = 0u, above_total = 0u, in_bin = (uint32_t)count;
   for (int pass = 0; pass < 3; ++pass) {
     const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
     const uint32_t dmask = pass == 2 ? 0x3ffu : 0x7ffu;
@@ -146,25 +162,60 @@ __device__ uint32_t smem_select(TopkSmem& sm, int count, uint32_t rank, KeyAt ke
       if ((x & pmask) == prefix) atomicAdd(&sm.hist[(x >> shift) & dmask], 1u);
     }
     __syncthreads();
-    if (pass == 0 && (uint32_t)count - sm.hist[0] < rank) return 0u;  // bin 0 holds only keys that cannot win
     select_bin(sm, (int)dmask + 1, rank);
     __syncthreads();
     const uint32_t b = sm.sel_bin, above = sm.sel_above;
+    in_bin = sm.hist[b];
     __syncthreads();
     rank -= above;
+    above_total += above;
     prefix |= b << shift;
     pmask |= dmask << shift;
+    if (above_total + in_bin <= fit) break;
+  }
+  *n_at_least = above_total + in_bin;
+  return prefix;
+}
+
+// Radix selection over the kSample sample keys, kSamplePerThread of them in
+// each thread's registers: the lower bound of the narrowest bin (11, then 11,
+// then 10 bits) holding the rank-th largest sample key (rank >= 1), stopping
+// once the sample keys at or above the bin number at most `fit`.  Returns 0
+// when fewer than `rank` sample keys can win.
+__device__ uint32_t sample_select(TopkSmem& sm, const uint32_t (&keys)[kSamplePerThread], uint32_t rank,
+                                  uint32_t fit) {
+  const int tid = threadIdx.x;
+  uint32_t prefix = 0u, pmask = 0u, above_total = 0u;
+  for (int pass = 0; pass < 3; ++pass) {
+    const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
+    const uint32_t dmask = pass == 2 ? 0x3ffu : 0x7ffu;
+    for (int b = tid; b < 2048; b += kTopkThreads) sm.hist[b] = 0u;
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kSamplePerThread; ++j)
+      if ((keys[j] & pmask) == prefix) atomicAdd(&sm.hist[(keys[j] >> shift) & dmask], 1u);
+    __syncthreads();
+    if (pass == 0 && (uint32_t)kSample - sm.hist[0] < rank) return 0u;  // bin 0 holds only keys that cannot win
+    select_bin(sm, (int)dmask + 1, rank);
+    __syncthreads();
+    const uint32_t b = sm.sel_bin, above = sm.sel_above, in_bin = sm.hist[b];
+    __syncthreads();
+    rank -= above;
+    above_total += above;
+    prefix |= b << shift;
+    pmask |= dmask << shift;
+    if (above_total + in_bin <= fit) break;
   }
   return prefix;
 }
 
 // One compare-exchange stage of a descending bitonic sort on the 64-element
 // segment a warp holds in registers (e0 = element base + lane, e1 = element
-// base + lane + 32), for merge size `size` and stride < 64.
-__device__ __forceinline__ void reg_stage(unsigned long long& e0, unsigned long long& e1, uint32_t base,
-                                          uint32_t size, uint32_t stride, int lane) {
-  if (stride == 32) {
-    const bool desc = ((base + lane) & size) == 0;
+// base + lane + 32), for merge size kSize and stride kStride < 64.
+template <uint32_t kSize, uint32_t kStride>
+__device__ __forceinline__ void reg_stage(unsigned long long& e0, unsigned long long& e1, uint32_t base, int lane) {
+  if (kStride == 32) {
+    const bool desc = ((base + lane) & kSize) == 0;
     if ((e0 < e1) == desc) {
       const unsigned long long t = e0;
       e0 = e1;
@@ -172,107 +223,139 @@ __device__ __forceinline__ void reg_stage(unsigned long long& e0, unsigned long 
     }
     return;
   }
-  const bool lower = (lane & stride) == 0;
+  const bool lower = (lane & kStride) == 0;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     unsigned long long& e = h ? e1 : e0;
-    const unsigned long long p = __shfl_xor_sync(0xffffffffu, e, stride);
-    const uint32_t i_lo = (base + lane + 32 * h) & ~stride;
-    const bool desc = (i_lo & size) == 0;
+    const unsigned long long p = __shfl_xor_sync(0xffffffffu, e, kStride);
+    const bool desc = (((base + lane + 32 * h) & ~kStride) & kSize) == 0;
     const bool take_max = lower == desc;
     e = take_max ? (e > p ? e : p) : (e < p ? e : p);
   }
 }
 
-// Descending bitonic sort of a[0..P), P a power of two in [64, 8192], by the
-// whole block: strides >= 64 go through shared memory with a barrier, the
-// six strides below 64 run on 64-element segments in registers (warp
-// shuffles), so a sort of 2048 needs 15 block barriers instead of 66.
-__device__ void bitonic_sort_desc(unsigned long long* a, uint32_t P) {
+template <uint32_t kSize, uint32_t kStride>
+__device__ __forceinline__ void reg_stages_down(unsigned long long& e0, unsigned long long& e1, uint32_t base,
+                                                int lane) {
+  reg_stage<kSize, kStride>(e0, e1, base, lane);
+  if constexpr (kStride > 1) reg_stages_down<kSize, kStride / 2>(e0, e1, base, lane);
+}
+
+template <uint32_t kSize>
+__device__ __forceinline__ void reg_sort64(unsigned long long& e0, unsigned long long& e1, uint32_t base, int lane) {
+  if constexpr (kSize > 2) reg_sort64<kSize / 2>(e0, e1, base, lane);
+  reg_stages_down<kSize, kSize / 2>(e0, e1, base, lane);
+}
+
+template <uint32_t P, uint32_t kSize>
+__device__ __forceinline__ void merge_level(unsigned long long* a) {
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const uint32_t nseg = P >> 6;
-  for (uint32_t seg = w; seg < nseg; seg += kTopkThreads / 32) {
+#pragma unroll
+  for (uint32_t stride = kSize >> 1; stride >= 64; stride >>= 1) {
+    for (uint32_t t = tid; t < (P >> 1); t += kTopkThreads) {
+      const uint32_t lo = 2 * t - (t & (stride - 1)), hi = lo + stride;
+      const bool desc = (lo & kSize) == 0;
+      const unsigned long long x = a[lo], y = a[hi];
+      if ((x < y) == desc) {
+        a[lo] = y;
+        a[hi] = x;
+      }
+    }
+    __syncthreads();
+  }
+  for (uint32_t seg = w; seg < (P >> 6); seg += kTopkWarps) {
     unsigned long long e0 = a[seg * 64 + lane], e1 = a[seg * 64 + lane + 32];
-    for (uint32_t size = 2; size <= 64; size <<= 1)
-      for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) reg_stage(e0, e1, seg * 64, size, stride, lane);
+    reg_stages_down<kSize, 32>(e0, e1, seg * 64, lane);
     a[seg * 64 + lane] = e0;
     a[seg * 64 + lane + 32] = e1;
   }
   __syncthreads();
-  for (uint32_t size = 128; size <= P; size <<= 1) {
-    for (uint32_t stride = size >> 1; stride >= 64; stride >>= 1) {
-      for (uint32_t t = tid; t < (P >> 1); t += kTopkThreads) {
-        const uint32_t lo = 2 * t - (t & (stride - 1)), hi = lo + stride;
-        const bool desc = (lo & size) == 0;
-        const unsigned long long x = a[lo], y = a[hi];
-        if ((x < y) == desc) {
-          a[lo] = y;
-          a[hi] = x;
-        }
-      }
-      __syncthreads();
-    }
-    for (uint32_t seg = w; seg < nseg; seg += kTopkThreads / 32) {
-      unsigned long long e0 = a[seg * 64 + lane], e1 = a[seg * 64 + lane + 32];
-      for (uint32_t stride = 32; stride > 0; stride >>= 1) reg_stage(e0, e1, seg * 64, size, stride, lane);
-      a[seg * 64 + lane] = e0;
-      a[seg * 64 + lane + 32] = e1;
-    }
-    __syncthreads();
+  if constexpr (kSize < P) merge_level<P, kSize * 2>(a);
+}
+
+// Descending bitonic sort of a[0..P) by the whole block, P a power of two in
+// [64, 8192], fully unrolled: strides >= 64 go through shared memory with a
+// barrier, the six strides below 64 run on 64-element segments in registers
+// (warp shuffles); a sort of 2048 needs 20 block barriers instead of 66.
+template <uint32_t P>
+__device__ void bitonic_sort_desc_t(unsigned long long* a) {
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  for (uint32_t seg = w; seg < (P >> 6); seg += kTopkWarps) {
+    unsigned long long e0 = a[seg * 64 + lane], e1 = a[seg * 64 + lane + 32];
+    reg_sort64<64>(e0, e1, seg * 64, lane);
+    a[seg * 64 + lane] = e0;
+    a[seg * 64 + lane + 32] = e1;
+  }
+  __syncthreads();
+  if constexpr (P > 64) merge_level<P, 128>(a);
+}
+
+__device__ void bitonic_sort_desc(unsigned long long* a, uint32_t P) {
+  switch (P) {
+    case 64: bitonic_sort_desc_t<64>(a); break;
+    case 128: bitonic_sort_desc_t<128>(a); break;
+    case 256: bitonic_sort_desc_t<256>(a); break;
+    case 512: bitonic_sort_desc_t<512>(a); break;
+    case 1024: bitonic_sort_desc_t<1024>(a); break;
+    case 2048: bitonic_sort_desc_t<2048>(a); break;
+    case 4096: bitonic_sort_desc_t<4096>(a); break;
+    default: bitonic_sort_desc_t<8192>(a); break;
   }
 }
 
 // Appends (key, index) of every score >= thr to the candidate buffer, warp
-// by warp; sm.n_cand counts all matches (even past the cap).  kVec: 2 = the
-// row is 32-byte aligned (256-bit loads), 1 = 16-byte aligned, 0 = scalar.
+// by warp; sm.n_cand counts all matches (even past the cap).  Each lane tests
+// 16 consecutive scores per round into a bit mask; a warp scan of the mask
+// counts places the matches, and only the (rare) matching scores are read
+// again to form their keys.  kVec: 2 = the row is 32-byte aligned (256-bit
+// loads), 1 = 16-byte aligned, 0 = scalar.
 template <int kVec>
 __device__ __forceinline__ void collect_at_least(TopkSmem& sm, const float* __restrict__ row, int n, float thr) {
   const unsigned FULL = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
-  // 8 consecutive scores per lane per round
-  const int n8 = kVec ? (n >> 3) : 0;
-  for (int base = 0; base < n8; base += kTopkThreads) {  // uniform trip count for the warp-wide scan
-    const int c8 = base + tid;
-    float v[8];
-    if (c8 < n8) {
+  const int n16 = kVec ? (n >> 4) : 0;
+  for (int base = 0; base < n16; base += kTopkThreads) {  // uniform trip count for the warp-wide scan
+    const int c16 = base + tid;
+    uint32_t m = 0;
+    if (c16 < n16) {
+      float v[16];
       if (kVec == 2) {
-        uint32_t w[8];
-        ld_stream32(row + (size_t)c8 * 8, w);
+        uint32_t w0[8], w1[8];
+        ld_stream32(row + (size_t)c16 * 16, w0);
+        ld_stream32(row + (size_t)c16 * 16 + 8, w1);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(w[j]);
+        for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(w0[j]), v[8 + j] = __uint_as_float(w1[j]);
       } else {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(row) + 2 * c8);
-        const float4 b = __ldg(reinterpret_cast<const float4*>(row) + 2 * c8 + 1);
-        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 a = __ldg(reinterpret_cast<const float4*>(row) + 4 * c16 + q);
+          v[4 * q] = a.x, v[4 * q + 1] = a.y, v[4 * q + 2] = a.z, v[4 * q + 3] = a.w;
+        }
       }
-    } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = -INFINITY;
+      for (int j = 0; j < 16; ++j) m |= (v[j] >= thr ? 1u : 0u) << j;
     }
-    uint32_t c = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) c += v[j] >= thr ? 1u : 0u;
+    const uint32_t c = __popc(m);
+    if (!__any_sync(FULL, c != 0u)) continue;
     uint32_t incl = c;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const uint32_t y = __shfl_up_sync(FULL, incl, o);
       if (lane >= o) incl += y;
     }
-    const uint32_t tot = __shfl_sync(FULL, incl, 31);
-    if (tot) {
-      uint32_t pos = 0;
-      if (lane == 31) pos = atomicAdd(&sm.n_cand, tot);
-      pos = __shfl_sync(FULL, pos, 31) + incl - c;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (v[j] >= thr) {
-          if (pos < (uint32_t)kCandCap) sm.cand[pos] = composite(topk_key(v[j]), (uint32_t)(c8 * 8 + j));
-          ++pos;
-        }
+    uint32_t pos = 0;
+    if (lane == 31) pos = atomicAdd(&sm.n_cand, incl);
+    pos = __shfl_sync(FULL, pos, 31) + incl - c;
+    while (m) {
+      const int j = __ffs(m) - 1;
+      m &= m - 1;
+      const int i = c16 * 16 + j;
+      if (pos < (uint32_t)kCandCap) sm.cand[pos] = composite(topk_key(__ldg(row + i)), (uint32_t)i);
+      ++pos;
     }
   }
-  for (int i = n8 * 8 + tid; i < n; i += kTopkThreads) {
+  for (int i = n16 * 16 + tid; i < n; i += kTopkThreads) {
     const float v = __ldg(row + i);
     if (v >= thr) {
       const uint32_t pos = atomicAdd(&sm.n_cand, 1u);
@@ -281,7 +364,7 @@ __device__ __forceinline__ void collect_at_least(TopkSmem& sm, const float* __re
   }
 }
 
-__global__ void __launch_bounds__(kTopkThreads)
+__global__ void __launch_bounds__(kTopkThreads, 2)
 topk_select_kernel(const float* __restrict__ scores, int64_t ld, const int32_t* __restrict__ n_visible, int k,
                    int32_t* __restrict__ out, int vec) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -309,25 +392,33 @@ topk_select_kernel(const float* __restrict__ scores, int64_t ld, const int32_t* 
     nsel = min(sm.n_cand, (uint32_t)kk);
     done = true;
   } else {
-    // sample of kSample keys: chunk w of 128 consecutive scores
+    // 4096 sample keys in registers: warp w reads chunks 2w, 2w+1 of 128
+    // consecutive scores spread evenly over the row
     const int w = tid >> 5, lane = tid & 31;
-    int64_t c0 = (int64_t)w * (n - kSampleChunk) / (kTopkThreads / 32 - 1);
-    if (vec) c0 &= ~(int64_t)3;
-    if (vec) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(row + c0) + lane);
-      sm.sample[w * kSampleChunk + lane * 4 + 0] = topk_key(v.x);
-      sm.sample[w * kSampleChunk + lane * 4 + 1] = topk_key(v.y);
-      sm.sample[w * kSampleChunk + lane * 4 + 2] = topk_key(v.z);
-      sm.sample[w * kSampleChunk + lane * 4 + 3] = topk_key(v.w);
-    } else {
-      for (int j = 0; j < 4; ++j) sm.sample[w * kSampleChunk + lane * 4 + j] = topk_key(__ldg(row + c0 + lane * 4 + j));
+    uint32_t skeys[kSamplePerThread];
+#pragma unroll
+    for (int c = 0; c < kSampleChunks / kTopkWarps; ++c) {
+      const int chunk = w * (kSampleChunks / kTopkWarps) + c;
+      int64_t c0 = (int64_t)chunk * (n - kSampleChunk) / (kSampleChunks - 1);
+      if (vec) {
+        c0 &= ~(int64_t)3;
+        const float4 v = __ldg(reinterpret_cast<const float4*>(row + c0) + lane);
+        skeys[4 * c] = topk_key(v.x), skeys[4 * c + 1] = topk_key(v.y);
+        skeys[4 * c + 2] = topk_key(v.z), skeys[4 * c + 3] = topk_key(v.w);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) skeys[4 * c + j] = topk_key(__ldg(row + c0 + lane * 4 + j));
+      }
     }
-    __syncthreads();
-    // about 1.5 * kk scores expected at or above the threshold
-    const double want = 1.5 * (double)kk;
-    uint32_t rank = (uint32_t)(want * kSample / (double)n + 0.5);
+    // Expected scores at or above the sample's rank-th largest key: rank * n /
+    // kSample, with a relative spread of about 1/sqrt(rank).  rank = q +
+    // 3.5 sqrt(q) + 2 (q = kk * kSample / n) keeps the count >= kk in all but
+    // ~0.1% of rows and far under the 8192-entry buffer for k <= 2048.
+    const float q = (float)kk * (float)kSample / (float)n;
+    uint32_t rank = (uint32_t)ceilf(q + 3.5f * sqrtf(q) + 2.0f);
     rank = max(1u, min(rank, (uint32_t)kSample));
-    const uint32_t t = smem_select(sm, kSample, rank, [&](int i) { return sm.sample[i]; });
+    const uint32_t fit = (uint32_t)(0.75f * (float)kCandCap * (float)kSample / (float)n);
+    const uint32_t t = sample_select(sm, skeys, rank, max(fit, rank));
     if (t != 0u) {
       if (tid == 0) sm.n_cand = 0u;
       __syncthreads();
@@ -410,26 +501,23 @@ topk_select_kernel(const float* __restrict__ scores, int64_t ld, const int32_t* 
   __syncthreads();
   unsigned long long* cand = sm.cand;
   uint32_t m = min(sm.n_cand, (uint32_t)kCandCap);
-  if (m > 2048u && nsel <= 2048u) {
-    // Cut the candidates to the keys >= the nsel-th largest key (all of its
-    // ties kept, the sort orders them by index): normally exactly nsel.
-    const uint32_t kth = smem_select(sm, (int)m, nsel, [&](int i) { return (uint32_t)(cand[i] >> 32); });
-    unsigned long long* dst = reinterpret_cast<unsigned long long*>(sm.sample);  // 2048 entries
-    if (tid == 0) sm.n_cand = 0u;
-    __syncthreads();
-    for (uint32_t i = tid; i < m; i += kTopkThreads) {
-      const unsigned long long c = cand[i];
-      if ((uint32_t)(c >> 32) >= kth) {
-        const uint32_t pos = atomicAdd(&sm.n_cand, 1u);
-        if (pos < 2048u) dst[pos] = c;
+  if (m > (uint32_t)kCutCap && nsel <= (uint32_t)kCutCap) {
+    // Cut the candidates to the keys >= the nsel-th largest key (its ties
+    // kept, the sort orders them by index): normally exactly nsel entries.
+    uint32_t n_ge;
+    const uint32_t kth =
+        smem_select(sm, (int)m, nsel, (uint32_t)kCutCap, &n_ge, [&](int i) { return (uint32_t)(cand[i] >> 32); });
+    if (n_ge <= (uint32_t)kCutCap) {
+      if (tid == 0) sm.n_cand = 0u;
+      __syncthreads();
+      for (uint32_t i = tid; i < m; i += kTopkThreads) {
+        const unsigned long long c = cand[i];
+        if ((uint32_t)(c >> 32) >= kth) sm.cut[atomicAdd(&sm.n_cand, 1u)] = c;
       }
+      __syncthreads();
+      cand = sm.cut;
+      m = n_ge;
     }
-    __syncthreads();
-    if (sm.n_cand <= 2048u) {
-      cand = dst;
-      m = sm.n_cand;
-    }
-    __syncthreads();
   }
   uint32_t P = 64u;
   while (P < m) P <<= 1;
