@@ -459,6 +459,150 @@ def bench_sparse(args, dist: Dist, dev, peak) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# config 5: prefix cache -- copy-on-write branches, LRU eviction, compaction
+# ---------------------------------------------------------------------------
+
+def bench_prefix(args, dist: Dist, dev, peak, tail: int = 37) -> dict:
+    """Per GPU: a pool of 2^20 pages (1 layer) filled to 90% by released
+    resident sequences (lengths U[1024, 32768], seeded), a shared prefix of
+    8192 + tail tokens in the radix store, 512 branches that match it,
+    copy-on-write its partial last page and append 2048 tokens each; then LRU
+    eviction of 30% of the used pages and compaction (page moves + device
+    page-table remap).  Host planning is timed with a wall clock; the device
+    work of each phase with CUDA events on the pool's stream -- for the
+    copy-on-write copies and the compaction moves by replaying the same page
+    moves (their sources are unchanged free or shared pages, and the remap is
+    idempotent), so no host planning time lands between the events."""
+    import rsllm_b200 as rk
+    from rsllm_b200 import synth
+    from rsllm_b200.prefix_pool import PrefixKvPool
+
+    n_pages = 1 << 14 if args.small else 1 << 20
+    n_branch, new_tok = (64, 2048) if args.small else (512, 2048)
+    prefix_len = 8192 + tail
+    stream = torch.cuda.Stream(device=dev)
+    t0 = time.perf_counter()
+    pool = PrefixKvPool(n_pages, 1, device=dev.index)
+    pool.kv.storage.random_(0, 256)  # resident pages hold arbitrary bytes
+    rng = np.random.default_rng(6 + 7919 * dist.rank)
+    residents = []
+    target = int(0.9 * n_pages)
+    live = 0
+    while live < target:
+        s = pool.create_sequence()
+        n = min(int(rng.integers(1024, 32769)), (target - live) * 64)
+        pool.reserve([s], [n], stream=stream)
+        live += (n + 63) // 64
+        residents.append(s)
+    for s in residents:
+        pool.release(s)
+    owner = pool.create_sequence()
+    slots = pool.reserve([owner], [prefix_len], stream=stream)
+    with torch.cuda.stream(stream):
+        rows = synth.kv_rows(prefix_len, seed=70 + dist.rank, device=dev)
+        pool.kv.append_layer(0, rows, torch.from_numpy(slots).to(dev))
+    prefix_tokens = np.arange(prefix_len, dtype=np.int32)
+    pool.insert_prefix(prefix_tokens, owner)
+    pool.free(owner)
+    branch_rows = synth.kv_rows(n_branch * new_tok, seed=80 + dist.rank, device=dev)
+    stream.synchronize()
+    setup_s = time.perf_counter() - t0
+
+    def ev_pair():
+        return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    # (A) branches: radix match and batched reserve with copy-on-write (host
+    # plan; the copies are enqueued), then 2048 rows appended per branch
+    dist.barrier()
+    h0 = time.perf_counter()
+    branches = []
+    for _ in range(n_branch):
+        m, b = pool.match_prefix(prefix_tokens)
+        assert m == prefix_len
+        branches.append(b)
+    shared_page = int(pool.page_table(branches[0])[-1])
+    slots = pool.reserve(branches, [new_tok] * n_branch, stream=stream)
+    h1 = time.perf_counter()
+    d_slots = torch.from_numpy(slots).to(dev)
+    stream.synchronize()
+    a, b = ev_pair()
+    a.record(stream)
+    with torch.cuda.stream(stream):
+        pool.kv.append_layer(0, branch_rows, d_slots)
+    b.record(stream)
+    stream.synchronize()
+    append_ms = a.elapsed_time(b)
+    cow_ms = None
+    if tail:
+        src = torch.full((n_branch,), shared_page, dtype=torch.int32, device=dev)
+        dst = torch.tensor([int(pool.page_table(x)[prefix_len // 64]) for x in branches], dtype=torch.int32,
+                           device=dev)
+        a, b = ev_pair()
+        a.record(stream)
+        pool.kv.copy_pages(src, dst, stream=stream)
+        b.record(stream)
+        stream.synchronize()
+        cow_ms = a.elapsed_time(b)
+
+    # (B) LRU eviction of 30% of the used pages, then compaction with the
+    # branches' device page table remapped in place
+    tabs = [pool.page_table(x) for x in branches]
+    stride = max(len(t) for t in tabs)
+    pt = np.full((n_branch, stride), -1, np.int32)
+    for i, t in enumerate(tabs):
+        pt[i, :len(t)] = t
+    d_pt = torch.from_numpy(pt).to(dev)
+    used = pool.stats()["live_pages"]
+    stream.synchronize()
+    dist.barrier()
+    h2 = time.perf_counter()
+    freed = pool.evict(int(0.3 * used))
+    h3 = time.perf_counter()
+    moved = pool.compact(device_tables=d_pt, stream=stream)
+    h4 = time.perf_counter()
+    stream.synchronize()
+    assert pool.device_status() == 0
+    remap = pool.last_remap()
+    movers = np.nonzero(remap != np.arange(n_pages, dtype=np.int32))[0].astype(np.int32)
+    d_src = torch.from_numpy(movers).to(dev)
+    d_dst = torch.from_numpy(remap[movers]).to(dev)
+    d_remap = torch.from_numpy(remap).to(dev)
+    stream.synchronize()
+    a, b = ev_pair()
+    c = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    pool.kv.copy_pages(d_src, d_dst, stream=stream)
+    c.record(stream)
+    rk.remap_pages(d_pt, d_remap, stream=stream)
+    b.record(stream)
+    stream.synchronize()
+    compact_copy_ms, compact_ms = a.elapsed_time(c), a.elapsed_time(b)
+    st = pool.stats()
+    ok_tables = all(np.array_equal(pool.page_table(x), d_pt[i, :len(tabs[i])].cpu().numpy())
+                    for i, x in enumerate(branches))
+    moved_bytes = 2 * moved * rk.PAGE_BYTES
+    res = {
+        "config": f"c5: pool 2^{int(np.log2(n_pages))} pages x 1 layer at 90% (released residents), prefix "
+                  f"{prefix_len} tokens, {n_branch} branches x {new_tok} tokens, evict 30% of used, compact",
+        "setup_s": setup_s,
+        "host_match_reserve_ms": (h1 - h0) * 1e3, "cow_copies": n_branch if tail else 0,
+        "device_cow_ms": cow_ms, "device_append_ms": append_ms,
+        "append_gbs": n_branch * new_tok * APPEND_ROW_BYTES / (append_ms * 1e-3) / GB,
+        "pages_used_before_evict": used, "pages_freed": freed, "host_evict_ms": (h3 - h2) * 1e3,
+        "pages_moved": moved, "host_compact_ms": (h4 - h3) * 1e3, "device_compact_ms": compact_ms,
+        "device_compact_copy_ms": compact_copy_ms,
+        "compact_gbs": moved_bytes / (compact_copy_ms * 1e-3) / GB if moved else None,
+        "compact_frac_of_hbm_peak": moved_bytes / (compact_copy_ms * 1e-3) / GB / peak if moved else None,
+        "high_water_after": st["high_water"], "live_after": st["live_pages"],
+        "device_tables_match_host": ok_tables,
+    }
+    pool.close()
+    del pool, branch_rows, d_pt
+    torch.cuda.empty_cache()
+    return res
+
+
+# ---------------------------------------------------------------------------
 # reference arm: the CPU restatement of rsLLM's path on the host cores
 # ---------------------------------------------------------------------------
 
@@ -517,11 +661,12 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--phases", default="gather,sparse", help="extra configs to measure (comma list or 'none')")
+    ap.add_argument("--phases", default="gather,sparse,prefix",
+                    help="extra configs to measure (comma list of gather,sparse,prefix or 'none')")
     ap.add_argument("--phase-steps", type=int, default=3)
     ap.add_argument("--phase-warmup", type=int, default=1)
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
-    ap.add_argument("--only", choices=["all", "append", "gather", "sparse"], default="all",
+    ap.add_argument("--only", choices=["all", "append", "gather", "sparse", "prefix"], default="all",
                     help="run one workload alone (profiling)")
     ap.add_argument("--small", action="store_true",
                     help="profiling sizes for the phases: 8 seqs / 1 layer (gather), 4 seqs / 1 layer (sparse)")
@@ -549,6 +694,8 @@ def main():
             res = {k: v for k, v in res.items() if k not in ("pool", "wl")}
         elif args.only == "gather":
             res = bench_gather(args, dist, dev, peak)
+        elif args.only == "prefix":
+            res = bench_prefix(args, dist, dev, peak)
         else:
             res = bench_sparse(args, dist, dev, peak)
         clocks.stop()
@@ -564,6 +711,8 @@ def main():
         phases["gather"] = bench_gather(args, dist, dev, peak)
     if "sparse" in wanted:
         phases.update(bench_sparse(args, dist, dev, peak))
+    if "prefix" in wanted:
+        phases["prefix_cow_evict_compact"] = bench_prefix(args, dist, dev, peak)
     clk = clocks.stop()
 
     K, W = args.steps, args.warmup

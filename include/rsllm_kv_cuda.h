@@ -190,6 +190,96 @@ RKV_API rkv_status rkv_copy_pages(const rkv_pool_view* pool, const int32_t* src,
 RKV_API rkv_status rkv_remap_pages(int32_t* page_table, int64_t n_entries, const int32_t* remap, int64_t n_pages,
                            uint32_t* d_status, rkv_stream_t stream);
 
+/* ---- paged pool: allocator, page tables, radix prefix store ------------------
+ * The host side of rsLLM's planned paged KV cache and radix-tree prefix cache
+ * (docs/03-HLD.md:363-376; crates/rsllm-kvcache/src/lib.rs:9-13 lists them as
+ * future layouts).  Rules, all deterministic:
+ *   - a new page is the lowest-numbered free page;
+ *   - sequences share prefix pages by refcount (fork, prefix match); writing
+ *     into a partially filled last page that is shared first copies it to a
+ *     fresh page (copy-on-write, enqueued on the caller's stream);
+ *   - eviction drops released sequences and radix leaves in increasing
+ *     (last use, sequences before nodes, id) order until enough pages are
+ *     free;
+ *   - compaction moves the highest live page into the lowest hole until all
+ *     live pages sit below the live-page count, on the device, and rewrites
+ *     every host page table (and, optionally, a device table).
+ * A pool is single-owner: calls on one pool must not overlap, and its device
+ * work must go to one stream (or be ordered by the caller).  Pool calls are
+ * not capturable in CUDA graphs (they upload page lists from host memory).
+ * Errors: an unknown sequence or a length past a sequence's end is
+ * INDEX_OUT_OF_RANGE; not enough free pages is POOL_FULL and changes nothing. */
+typedef struct rkv_pool rkv_pool;
+
+/* rkv_pool_desc.device for a plan-only pool: no device memory; the page moves
+ * it decides (copy-on-write copies, compaction moves) are handed to the
+ * caller by rkv_pool_take_moves instead of being enqueued. */
+#define RKV_PLAN_ONLY (-1)
+
+typedef struct rkv_pool_desc {
+  int64_t n_pages;   /* pages per layer */
+  int32_t n_layers;
+  int32_t device;    /* CUDA device ordinal, or RKV_PLAN_ONLY */
+  void* storage;     /* optional caller-owned device memory of rkv_pool_bytes() bytes, 256-byte
+                        aligned; NULL: the pool allocates it at creation */
+} rkv_pool_desc;
+
+typedef struct rkv_pool_stats {
+  int64_t free_pages, live_pages, sequences, prefix_nodes, tick, high_water;
+} rkv_pool_stats;
+
+/* Create / destroy (allocation happens here only, never on a hot path). */
+RKV_API rkv_status rkv_pool_create(const rkv_pool_desc* desc, rkv_pool** out);
+RKV_API void rkv_pool_destroy(rkv_pool* pool);
+RKV_API rkv_status rkv_pool_get_view(const rkv_pool* pool, rkv_pool_view* out);
+RKV_API rkv_status rkv_pool_get_stats(const rkv_pool* pool, rkv_pool_stats* out);
+/* Refcount of every page (int32 [n_pages]); 0 = free. */
+RKV_API rkv_status rkv_page_refcount(const rkv_pool* pool, int32_t* out, int64_t cap);
+
+/* Sequences (rsLLM's per-session block table, HLD 8.1). */
+RKV_API rkv_status rkv_seq_create(rkv_pool* pool, int64_t* seq);
+/* New sequence sharing the first n_tokens of parent (its pages refcounted). */
+RKV_API rkv_status rkv_seq_fork(rkv_pool* pool, int64_t parent, int64_t n_tokens, int64_t* child);
+/* Reserves n_tokens[i] more positions at the end of each seqs[i] (distinct
+ * sequences): copy-on-write of a shared partial last page, new pages for the
+ * rest; writes the slots of the new positions, sequence after sequence, to
+ * slots (may be NULL).  All-or-nothing: POOL_FULL changes nothing.  The
+ * copy-on-write copies are enqueued on stream before the call returns; write
+ * the new rows on the same stream after it (rkv_append_quant_bf16). */
+RKV_API rkv_status rkv_seq_reserve(rkv_pool* pool, int64_t n_seqs, const int64_t* seqs, const int64_t* n_tokens,
+                                   int32_t* slots, rkv_stream_t stream);
+/* Marks a finished sequence evictable (it keeps its pages until evicted). */
+RKV_API rkv_status rkv_seq_release(rkv_pool* pool, int64_t seq);
+/* Records a use for LRU. */
+RKV_API rkv_status rkv_seq_touch(rkv_pool* pool, int64_t seq);
+/* Drops a sequence now (ThreeTierKvCache::clear analogue, three_tier.rs:229). */
+RKV_API rkv_status rkv_seq_free(rkv_pool* pool, int64_t seq);
+RKV_API rkv_status rkv_seq_info(const rkv_pool* pool, int64_t seq, int64_t* len, int64_t* n_pages);
+/* The sequence's page table (int32, one entry per 64 tokens). */
+RKV_API rkv_status rkv_seq_page_table(const rkv_pool* pool, int64_t seq, int32_t* out, int64_t cap);
+
+/* Radix prefix store (HLD 8.2).  Insert the first n tokens of seq (their
+ * pages are refcounted by the tree); match returns the longest stored prefix
+ * of tokens as a new sequence of that length sharing its pages. */
+RKV_API rkv_status rkv_prefix_insert(rkv_pool* pool, const int32_t* tokens, int64_t n, int64_t seq);
+RKV_API rkv_status rkv_prefix_match(rkv_pool* pool, const int32_t* tokens, int64_t n, int64_t* matched,
+                                    int64_t* seq_out);
+
+/* LRU eviction until target_pages pages were freed (or nothing is evictable). */
+RKV_API rkv_status rkv_pool_evict(rkv_pool* pool, int64_t target_pages, int64_t* freed);
+/* Compaction: page moves enqueued on stream (rkv_copy_pages); if d_tables is
+ * given, its n_entries page ids are remapped on the device after the moves. */
+RKV_API rkv_status rkv_pool_compact(rkv_pool* pool, int32_t* d_tables, int64_t n_entries, int64_t* moved,
+                                    rkv_stream_t stream);
+/* old page -> new page of the last compaction (identity before any). */
+RKV_API rkv_status rkv_pool_last_remap(const rkv_pool* pool, int32_t* out, int64_t cap);
+/* Plan-only pools: returns and clears the page moves decided so far, in order
+ * (dst[i] <- src[i]; apply them in order).  *n = count; 0 for device pools.
+ * With src == dst == NULL it only reports the count. */
+RKV_API rkv_status rkv_pool_take_moves(rkv_pool* pool, int32_t* src, int32_t* dst, int64_t cap, int64_t* n);
+/* Reads and clears the status bits of the pool's own device work (syncs). */
+RKV_API rkv_status rkv_pool_device_status(rkv_pool* pool, uint32_t* bits);
+
 /* ---- codec pin ---------------------------------------------------------------
  * out[i] = E4M3 code the append kernel stores for the f32 lane value whose
  * bit pattern is first_bits + i (already divided by its block scale), i < n:

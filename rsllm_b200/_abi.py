@@ -34,6 +34,21 @@ class PoolView(Structure):
     _fields_ = [("base", c_void_p), ("n_pages", c_int64), ("n_layers", c_int32), ("reserved", c_int32)]
 
 
+class PoolDesc(Structure):
+    """``rkv_pool_desc``."""
+
+    _fields_ = [("n_pages", c_int64), ("n_layers", c_int32), ("device", c_int32), ("storage", c_void_p)]
+
+
+class PoolStats(Structure):
+    """``rkv_pool_stats``."""
+
+    _fields_ = [("free_pages", c_int64), ("live_pages", c_int64), ("sequences", c_int64), ("prefix_nodes", c_int64),
+                ("tick", c_int64), ("high_water", c_int64)]
+
+
+PLAN_ONLY = -1
+
 _P = POINTER
 _u8p, _u16p, _u32p, _i32p, _f32p = c_void_p, c_void_p, c_void_p, c_void_p, c_void_p
 
@@ -52,6 +67,26 @@ SIGNATURES = {
     "rkv_copy_pages": (c_int32, [_P(PoolView), _i32p, _i32p, c_int64, _u32p, c_void_p]),
     "rkv_remap_pages": (c_int32, [_i32p, c_int64, _i32p, c_int64, _u32p, c_void_p]),
     "rkv_e4m3fn_code_range": (c_int32, [c_uint32, c_int64, _u8p, c_void_p]),
+    "rkv_pool_create": (c_int32, [_P(PoolDesc), _P(c_void_p)]),
+    "rkv_pool_destroy": (None, [c_void_p]),
+    "rkv_pool_get_view": (c_int32, [c_void_p, _P(PoolView)]),
+    "rkv_pool_get_stats": (c_int32, [c_void_p, _P(PoolStats)]),
+    "rkv_page_refcount": (c_int32, [c_void_p, _i32p, c_int64]),
+    "rkv_seq_create": (c_int32, [c_void_p, _P(c_int64)]),
+    "rkv_seq_fork": (c_int32, [c_void_p, c_int64, c_int64, _P(c_int64)]),
+    "rkv_seq_reserve": (c_int32, [c_void_p, c_int64, c_void_p, c_void_p, _i32p, c_void_p]),
+    "rkv_seq_release": (c_int32, [c_void_p, c_int64]),
+    "rkv_seq_touch": (c_int32, [c_void_p, c_int64]),
+    "rkv_seq_free": (c_int32, [c_void_p, c_int64]),
+    "rkv_seq_info": (c_int32, [c_void_p, c_int64, _P(c_int64), _P(c_int64)]),
+    "rkv_seq_page_table": (c_int32, [c_void_p, c_int64, _i32p, c_int64]),
+    "rkv_prefix_insert": (c_int32, [c_void_p, _i32p, c_int64, c_int64]),
+    "rkv_prefix_match": (c_int32, [c_void_p, _i32p, c_int64, _P(c_int64), _P(c_int64)]),
+    "rkv_pool_evict": (c_int32, [c_void_p, c_int64, _P(c_int64)]),
+    "rkv_pool_compact": (c_int32, [c_void_p, _i32p, c_int64, _P(c_int64), c_void_p]),
+    "rkv_pool_last_remap": (c_int32, [c_void_p, _i32p, c_int64]),
+    "rkv_pool_take_moves": (c_int32, [c_void_p, _i32p, _i32p, c_int64, _P(c_int64)]),
+    "rkv_pool_device_status": (c_int32, [c_void_p, _P(c_uint32)]),
 }
 
 _lib = None
