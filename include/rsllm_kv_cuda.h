@@ -280,6 +280,32 @@ RKV_API rkv_status rkv_pool_take_moves(rkv_pool* pool, int32_t* src, int32_t* ds
 /* Reads and clears the status bits of the pool's own device work (syncs). */
 RKV_API rkv_status rkv_pool_device_status(rkv_pool* pool, uint32_t* bits);
 
+/* ---- page moves without allocation -----------------------------------------
+ * No counterpart in rsLLM: an addition of this library for callers that cannot
+ * allocate device memory -- an engine that reserves all of its device memory
+ * at start-up and hands it out through its own allocator, or the owner of a
+ * plan-only pool (RKV_PLAN_ONLY) moving its pages with memory it already has.
+ * rkv_pool_compact stages its move lists in memory the pool allocated; this
+ * entry point allocates nothing (no cudaMalloc, cudaFree or allocating library
+ * call).  It stages the moves in a fixed array inside the library -- a 2 MB
+ * __device__ array that every GPU which loads the library holds until the
+ * process exits -- then copies page src[i] to dst[i] in every layer and, if
+ * d_tables is given, rewrites its n_entries page ids (an id equal to src[i]
+ * becomes dst[i]).
+ * src: host int32 [n_moves], strictly ascending; dst: host int32 [n_moves],
+ * no destination also a source (the moves of one compaction, e.g. from
+ * rkv_pool_last_remap or rkv_pool_take_moves, sorted by source).  At most
+ * RKV_STATIC_MAX_MOVES moves per call: more is SHAPE_MISMATCH.
+ * The first call on a device looks up the array's device address with that
+ * device current (once per device); make that first call before any stream
+ * capture.  Every call shares the array and leaves its contents behind; calls
+ * whose device work overlaps (other streams, other threads) race on it, so
+ * order them on one stream. */
+#define RKV_STATIC_MAX_MOVES 262144
+RKV_API rkv_status rkv_apply_page_moves_static(const rkv_pool_view* pool, const int32_t* src, const int32_t* dst,
+                                               int64_t n_moves, int32_t* d_tables, int64_t n_entries,
+                                               uint32_t* d_status, rkv_stream_t stream);
+
 /* ---- codec pin ---------------------------------------------------------------
  * out[i] = E4M3 code the append kernel stores for the f32 lane value whose
  * bit pattern is first_bits + i (already divided by its block scale), i < n:

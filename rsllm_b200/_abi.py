@@ -87,7 +87,10 @@ SIGNATURES = {
     "rkv_pool_last_remap": (c_int32, [c_void_p, _i32p, c_int64]),
     "rkv_pool_take_moves": (c_int32, [c_void_p, _i32p, _i32p, c_int64, _P(c_int64)]),
     "rkv_pool_device_status": (c_int32, [c_void_p, _P(c_uint32)]),
+    "rkv_apply_page_moves_static": (c_int32, [_P(PoolView), _i32p, _i32p, c_int64, _i32p, c_int64, _u32p,
+                                              c_void_p]),
 }
+STATIC_MAX_MOVES = 262144
 
 _lib = None
 
