@@ -50,9 +50,12 @@ GATHER_ROW_BYTES = ROW_OUT + ROW_IN  # stored row read + bf16 row written
 L2_BYTES = 126 * 2**20
 GB = 1e9
 
-# DRAM bytes per launch from the ncu capture of each kernel, per unit of work
-# (profiles/*.md gives the command and the raw counters); None = not captured.
-NCU_TRAFFIC_PER_ROW = {"append": None, "gather": None, "sparse_gather": None}
+# DRAM bytes (read + write) per row from one ncu capture of each kernel
+# (profiles/append_quant_c2.md, gather_dequant_c3_small.md,
+# topk_sparse_c4_small.md).  The append's page writes drain from L2 after the
+# launch, so its figure is the bf16 input read: 17,997,824 B / 15,616 rows.
+NCU_TRAFFIC_PER_ROW = {"append": 17997824 / 15616, "gather": (176206080 + 248001536) / 262144,
+                       "sparse_gather": (335133696 + 548617728) / 524288}
 
 
 # ---------------------------------------------------------------------------
@@ -68,30 +71,41 @@ def peaks() -> tuple[float, str]:
 
 
 class Dist:
-    def __init__(self):
+    """One process per GPU (torchrun env vars); NCCL between GPUs, gloo when
+    no GPU is present (the CPU tests of the multi-rank path).  Only used
+    outside timed regions: barriers and the max over ranks of a time."""
+
+    def __init__(self, backend: str | None = None):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         self.pg = None
+        self.dev = torch.device("cpu")
         if self.world > 1:
             import datetime
 
             import torch.distributed as dist
 
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                    device_id=torch.device("cuda", self.local))
+            backend = backend or ("nccl" if torch.cuda.is_available() else "gloo")
+            timeout = datetime.timedelta(seconds=300)
+            if backend == "nccl":
+                torch.cuda.set_device(self.local)
+                self.dev = torch.device("cuda", self.local)
+                dist.init_process_group("nccl", timeout=timeout, device_id=self.dev)
+            else:
+                dist.init_process_group(backend, timeout=timeout)
             self.pg = dist
 
     def barrier(self):
         if self.pg:
             self.pg.barrier()
-        torch.cuda.synchronize()
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
 
     def max(self, x: float) -> float:
         if not self.pg:
             return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        t = torch.tensor([x], dtype=torch.float64, device=self.dev)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
@@ -478,7 +492,7 @@ def bench_prefix(args, dist: Dist, dev, peak, tail: int = 37) -> dict:
     from rsllm_b200.prefix_pool import PrefixKvPool
 
     n_pages = 1 << 14 if args.small else 1 << 20
-    n_branch, new_tok = (64, 2048) if args.small else (512, 2048)
+    n_branch, new_tok = (16, 2048) if args.small else (512, 2048)
     prefix_len = 8192 + tail
     stream = torch.cuda.Stream(device=dev)
     t0 = time.perf_counter()
@@ -622,7 +636,8 @@ def run_reference(args, dist: Dist) -> None:
         if j not in rows_cache:
             n = N_LAYERS * N_SEQ_APPEND
             rows_cache.clear()
-            rows_cache[j] = synth.kv_rows(n, seed=3 * 1000 + j).view(torch.int16).numpy().view(np.uint16)
+            rows_cache[j] = synth.kv_rows(n, seed=3 * 1000 + j).view(torch.int16).numpy().view(np.uint16).reshape(
+                N_LAYERS, N_SEQ_APPEND, 576)
         return rows_cache[j]
 
     pool = oracle.new_pool(wl.n_pages, N_LAYERS)

@@ -152,6 +152,9 @@ def append_rows(pool: np.ndarray, n_pages: int, n_layers: int, layer0: int, rows
     n_layers_in = rows.shape[0] if rows.ndim == 3 else 1
     n_tokens = rows.shape[-2]
     slots = np.ascontiguousarray(slots, np.int32)
+    if rows.shape[-1] != ROW_DIM or slots.shape != (n_tokens,):
+        raise ValueError(f"append_rows: rows [layers, n_tokens, 576] with slots [n_tokens], got {rows.shape} "
+                         f"and {slots.shape}")
     return lib().rkvo_append_rows(_p(pool), n_pages, n_layers, layer0, n_layers_in, _p(rows), n_tokens, _p(slots),
                                   n_threads)
 

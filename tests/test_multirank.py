@@ -1,0 +1,76 @@
+"""The multi-GPU path on the CPU: two gloo ranks (one process each, as
+torchrun launches them) run the per-rank setup of the benchmark -- each rank
+owns its own pool and its own seeded sequences, no collective touches the
+data -- and the max-over-ranks timing reduction; the reference arm prints
+from rank 0 only."""
+import json
+import os
+import socket
+import subprocess
+import sys
+import textwrap
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent.parent
+
+CHILD = textwrap.dedent("""
+    import json, sys
+    sys.path.insert(0, {root!r})
+    import numpy as np
+    import bench
+    d = bench.Dist(backend="gloo")
+    wl = bench.AppendWorkload(12, seed=3 + 7919 * d.rank, dev=None)
+    slots = wl.slots_np
+    # every slot inside this rank's pool, no slot written twice, a new page
+    # whenever a sequence crosses a 64-token boundary
+    ok = bool((slots >= 0).all() and (slots < wl.n_pages * 64).all() and
+              len(np.unique(slots)) == slots.size)
+    t = d.max(1.0 + d.rank)  # per-rank time -> job time is the slowest rank
+    print(json.dumps({{"rank": d.rank, "ok": ok, "max": t, "first": slots[0, :4].tolist(),
+                       "pages": wl.n_pages}}), flush=True)
+    d.close()
+""")
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def launch(code: str, world: int = 2, extra_args=()) -> list[str]:
+    port = free_port()
+    procs = []
+    for r in range(world):
+        env = dict(os.environ, RANK=str(r), LOCAL_RANK=str(r), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1",
+                   MASTER_PORT=str(port), CUDA_VISIBLE_DEVICES="")
+        procs.append(subprocess.Popen([sys.executable, "-c", code, *extra_args], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.PIPE, text=True, cwd=str(ROOT)))
+    outs = []
+    for p in procs:
+        out, err = p.communicate(timeout=300)
+        assert p.returncode == 0, err[-2000:]
+        outs.append(out)
+    return outs
+
+
+def test_two_gloo_ranks_own_their_work():
+    outs = launch(CHILD.format(root=str(ROOT)))
+    res = [json.loads(o.strip().splitlines()[-1]) for o in outs]
+    assert [r["rank"] for r in res] == [0, 1]
+    assert all(r["ok"] for r in res)
+    assert all(r["max"] == 2.0 for r in res)  # max over ranks reaches every rank
+    assert res[0]["first"] != res[1]["first"]  # each rank its own seeded sequences
+
+
+def test_reference_arm_prints_from_rank_zero_only():
+    code = "import sys, runpy; sys.argv=['bench.py','--impl','reference','--gpus','2','--steps','1','--warmup','0']; " \
+           "runpy.run_path('bench.py', run_name='__main__')"
+    outs = launch(code)
+    lines = [[ln for ln in o.splitlines() if ln.startswith("{")] for o in outs]
+    assert len(lines[0]) == 1 and len(lines[1]) == 0
+    line = json.loads(lines[0][0])
+    assert line["impl"] == "reference" and line["value"] > 0 and line["e2e"]["h2d_bytes_per_step"] == 0
+    assert line["cpu_baseline"]["kind"] == "port"
