@@ -34,7 +34,10 @@ constexpr int kTopkThreads = 512;  // two CTAs per SM, 64 registers per thread
 constexpr int kTopkWarps = kTopkThreads / 32;
 constexpr int kTopkMaxK = 4096;
 constexpr int kCandCap = 8192;
-constexpr int kCutCap = 2048;
+constexpr int kCutCap = 2048;           // cut + bitonic path (sorts at most 2048)
+constexpr int kBucketBins = 2048;
+constexpr uint32_t kBucketMax = 32;     // bucket sort: largest bucket sorted by one thread
+constexpr int kSortedCap = kTopkMaxK + kBucketMax;
 constexpr int kSampleChunk = 128;                         // keys per chunk: one float4 per lane
 constexpr int kSampleChunks = 32;
 constexpr int kSample = kSampleChunks * kSampleChunk;     // 4096
@@ -44,9 +47,10 @@ constexpr int kBinsPerThread = 2048 / kTopkThreads;       // 4
 struct TopkSmem {
   uint32_t hist[2048];
   unsigned long long cand[kCandCap];
-  unsigned long long cut[kCutCap];
+  unsigned long long cut[kSortedCap];  // cut output (<= 2048) or bucket-sorted output (<= k + 32)
+  uint32_t keep[kBucketBins / 32];
   uint32_t warp_sums[32];
-  uint32_t sel_bin, sel_above, n_cand;
+  uint32_t sel_bin, sel_above, n_cand, flag, kept_end;
 };
 
 __device__ __forceinline__ uint32_t topk_key(float s) {
@@ -303,38 +307,53 @@ __device__ void bitonic_sort_desc(unsigned long long* a, uint32_t P) {
   }
 }
 
-// Appends (key, index) of every score >= thr to the candidate buffer, warp
-// by warp; sm.n_cand counts all matches (even past the cap).  Each lane tests
-// 16 consecutive scores per round into a bit mask; a warp scan of the mask
-// counts places the matches, and only the (rare) matching scores are read
-// again to form their keys.  kVec: 2 = the row is 32-byte aligned (256-bit
-// loads), 1 = 16-byte aligned, 0 = scalar.
+// Appends the index of every score >= thr to the candidate buffer, warp by
+// warp; sm.n_cand counts all matches (even past the cap).  Per round a warp
+// tests 1024 consecutive scores: each lane issues all of its loads (four
+// 256-bit loads when the row is 32-byte aligned, eight 128-bit loads when
+// 16-byte aligned; every load instruction covers 1 KB contiguous across the
+// warp) before testing them into a 32-bit mask, so 128 B per thread are in
+// flight.  A warp scan of the mask counts places the matches.  Only indices
+// are stored here; fill_keys() forms the keys afterwards with all of its
+// loads in flight at once, which keeps dependent loads out of this loop.
+// The loads keep the default L2 policy so that those re-reads mostly hit L2.
+// kVec: 2 = 32-byte aligned row, 1 = 16-byte aligned, 0 = scalar.
 template <int kVec>
 __device__ __forceinline__ void collect_at_least(TopkSmem& sm, const float* __restrict__ row, int n, float thr) {
   const unsigned FULL = 0xffffffffu;
-  const int lane = threadIdx.x & 31;
-  const int tid = threadIdx.x;
-  const int n16 = kVec ? (n >> 4) : 0;
-  for (int base = 0; base < n16; base += kTopkThreads) {  // uniform trip count for the warp-wide scan
-    const int c16 = base + tid;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  constexpr int kWarpChunk = 1024;
+  const int n_chunks = kVec ? (n / kWarpChunk) : 0;
+  // uniform trip count for the warp-wide scan: every warp runs the same rounds
+  for (int c0 = 0; c0 < n_chunks; c0 += kTopkWarps) {
+    const int chunk = c0 + w;
+    const float* base = row + (size_t)chunk * kWarpChunk;
     uint32_t m = 0;
-    if (c16 < n16) {
-      float v[16];
+    if (chunk < n_chunks) {
       if (kVec == 2) {
-        uint32_t w0[8], w1[8];
-        ld_stream32(row + (size_t)c16 * 16, w0);
-        ld_stream32(row + (size_t)c16 * 16 + 8, w1);
+        uint32_t u[4][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(w0[j]), v[8 + j] = __uint_as_float(w1[j]);
+        for (int q = 0; q < 4; ++q)
+          asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                       : "=r"(u[q][0]), "=r"(u[q][1]), "=r"(u[q][2]), "=r"(u[q][3]), "=r"(u[q][4]), "=r"(u[q][5]),
+                         "=r"(u[q][6]), "=r"(u[q][7])
+                       : "l"(base + q * 256 + lane * 8));
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) m |= (__uint_as_float(u[q][j]) >= thr ? 1u : 0u) << (q * 8 + j);
       } else {
+        float4 v[8];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 a = __ldg(reinterpret_cast<const float4*>(row) + 4 * c16 + q);
-          v[4 * q] = a.x, v[4 * q + 1] = a.y, v[4 * q + 2] = a.z, v[4 * q + 3] = a.w;
+        for (int q = 0; q < 8; ++q) v[q] = __ldg(reinterpret_cast<const float4*>(base + q * 128) + lane);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          m |= (v[q].x >= thr ? 1u : 0u) << (q * 4);
+          m |= (v[q].y >= thr ? 1u : 0u) << (q * 4 + 1);
+          m |= (v[q].z >= thr ? 1u : 0u) << (q * 4 + 2);
+          m |= (v[q].w >= thr ? 1u : 0u) << (q * 4 + 3);
         }
       }
-#pragma unroll
-      for (int j = 0; j < 16; ++j) m |= (v[j] >= thr ? 1u : 0u) << j;
     }
     const uint32_t c = __popc(m);
     if (!__any_sync(FULL, c != 0u)) continue;
@@ -348,21 +367,146 @@ __device__ __forceinline__ void collect_at_least(TopkSmem& sm, const float* __re
     if (lane == 31) pos = atomicAdd(&sm.n_cand, incl);
     pos = __shfl_sync(FULL, pos, 31) + incl - c;
     while (m) {
-      const int j = __ffs(m) - 1;
+      const int b = __ffs(m) - 1;
       m &= m - 1;
-      const int i = c16 * 16 + j;
-      if (pos < (uint32_t)kCandCap) sm.cand[pos] = composite(topk_key(__ldg(row + i)), (uint32_t)i);
+      // bit b of lane `lane`: piece b/8 (b/4) of the lane, element b%8 (b%4)
+      const int off = kVec == 2 ? (b >> 3) * 256 + lane * 8 + (b & 7) : (b >> 2) * 128 + lane * 4 + (b & 3);
+      if (pos < (uint32_t)kCandCap) sm.cand[pos] = (unsigned long long)(uint32_t)(chunk * kWarpChunk + off);
       ++pos;
     }
   }
-  for (int i = n16 * 16 + tid; i < n; i += kTopkThreads) {
-    const float v = __ldg(row + i);
-    if (v >= thr) {
+  for (int i = n_chunks * kWarpChunk + threadIdx.x; i < n; i += kTopkThreads) {
+    if (__ldg(row + i) >= thr) {
       const uint32_t pos = atomicAdd(&sm.n_cand, 1u);
-      if (pos < (uint32_t)kCandCap) sm.cand[pos] = composite(topk_key(v), (uint32_t)i);
+      if (pos < (uint32_t)kCandCap) sm.cand[pos] = (unsigned long long)(uint32_t)i;
     }
   }
 }
+
+// The collection pass stores indices only; this forms every candidate's key
+// with all of a thread's score loads issued together (mostly L2 hits).
+__device__ __forceinline__ void fill_keys(TopkSmem& sm, const float* __restrict__ row, uint32_t m) {
+  constexpr int U = 8;
+  for (uint32_t base = 0; base < m; base += U * kTopkThreads) {
+    uint32_t idx[U];
+    float v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t i = base + u * kTopkThreads + threadIdx.x;
+      idx[u] = i < m ? (uint32_t)sm.cand[i] : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) v[u] = __ldg(row + idx[u]);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t i = base + u * kTopkThreads + threadIdx.x;
+      if (i < m) sm.cand[i] = composite(topk_key(v[u]), idx[u]);
+    }
+  }
+}
+
+// Exact ordering of the top `need` candidates a[0..m) by bucket sort: 2048
+// buckets split the candidates' key range evenly (descending), a histogram
+// and a block scan place each bucket, the buckets that start before `need`
+// are scattered to out (need + kBucketMax entries), and every kept element
+// goes to sorted[its bucket start + the number of its bucket mates above it]
+// on the full (key, ~index) composite, so sorted[0..need) is exactly ordered.
+// sorted may alias a.  Returns false (nothing written to sorted) when such a
+// bucket holds more than kBucketMax entries (heavy ties); the caller then
+// sorts another way.
+__device__ bool bucket_sort_top(TopkSmem& sm, const unsigned long long* __restrict__ a, uint32_t m, uint32_t need,
+                                unsigned long long* __restrict__ out, unsigned long long* __restrict__ sorted) {
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  uint32_t mn = 0xffffffffu, mx = 0u;
+  for (uint32_t i = tid; i < m; i += kTopkThreads) {
+    const uint32_t k = (uint32_t)(a[i] >> 32);
+    mn = min(mn, k);
+    mx = max(mx, k);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  __syncthreads();  // warp_sums may still be read by an earlier phase
+  if (lane == 0) {
+    sm.warp_sums[w] = mn;
+    sm.warp_sums[16 + w] = mx;
+  }
+  for (int b = tid; b < kBucketBins; b += kTopkThreads) sm.hist[b] = 0u;
+  if (tid < kBucketBins / 32) sm.keep[tid] = 0u;
+  if (tid == 0) {
+    sm.flag = 0u;
+    sm.kept_end = 0u;
+  }
+  __syncthreads();
+  mn = 0xffffffffu;
+  mx = 0u;
+  for (int i = 0; i < kTopkWarps; ++i) {
+    mn = min(mn, sm.warp_sums[i]);
+    mx = max(mx, sm.warp_sums[16 + i]);
+  }
+  const uint32_t range = mx - mn;
+  int shift = 0;
+  while ((range >> shift) >= (uint32_t)kBucketBins) ++shift;
+  for (uint32_t i = tid; i < m; i += kTopkThreads)
+    atomicAdd(&sm.hist[kBucketBins - 1 - (((uint32_t)(a[i] >> 32) - mn) >> shift)], 1u);
+  __syncthreads();
+  // exclusive scan of the bucket counts; thread t owns buckets B*t .. B*t+B-1
+  constexpr int B = kBucketBins / kTopkThreads;
+  uint32_t c[B], tot = 0;
+#pragma unroll
+  for (int j = 0; j < B; ++j) {
+    c[j] = sm.hist[tid * B + j];
+    tot += c[j];
+  }
+  uint32_t incl = tot;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  __syncthreads();
+  if (lane == 31) sm.warp_sums[w] = incl;
+  __syncthreads();
+  uint32_t start = incl - tot;
+  for (int i = 0; i < w; ++i) start += sm.warp_sums[i];
+#pragma unroll
+  for (int j = 0; j < B; ++j) {
+    const int b = tid * B + j;
+    if (start < need) {
+      atomicOr(&sm.keep[b >> 5], 1u << (b & 31));
+      if (c[j] > kBucketMax) sm.flag = 1u;
+      if (start + c[j] >= need) sm.kept_end = start + c[j];  // the bucket holding position need - 1
+    }
+    sm.hist[b] = start;
+    start += c[j];
+  }
+  __syncthreads();
+  if (sm.flag) return false;
+  for (uint32_t i = tid; i < m; i += kTopkThreads) {
+    const unsigned long long v = a[i];
+    const int b = kBucketBins - 1 - (int)((((uint32_t)(v >> 32)) - mn) >> shift);
+    const uint32_t p = atomicAdd(&sm.hist[b], 1u);
+    if (sm.keep[b >> 5] >> (b & 31) & 1u) out[p] = v;
+  }
+  __syncthreads();
+  // hist[b] now holds the end of bucket b (the start of bucket b + 1).  Each
+  // kept element's final place is its bucket's start plus the number of
+  // bucket mates above it (composites are distinct); written to `sorted`.
+  const uint32_t kept_end = sm.kept_end;
+  for (uint32_t p = tid; p < kept_end; p += kTopkThreads) {
+    const unsigned long long x = out[p];
+    const int b = kBucketBins - 1 - (int)((((uint32_t)(x >> 32)) - mn) >> shift);
+    const uint32_t s0 = b ? sm.hist[b - 1] : 0u, e = sm.hist[b];
+    uint32_t r = 0;
+    for (uint32_t q = s0; q < e; ++q) r += out[q] > x ? 1u : 0u;
+    sorted[s0 + r] = x;
+  }
+  __syncthreads();
+  return true;
+}
+
 
 __global__ void __launch_bounds__(kTopkThreads, 2)
 topk_select_kernel(const float* __restrict__ scores, int64_t ld, const int32_t* __restrict__ n_visible, int k,
@@ -430,6 +574,10 @@ topk_select_kernel(const float* __restrict__ scores, int64_t ld, const int32_t* 
       const uint32_t got = sm.n_cand;
       done = got >= (uint32_t)kk && got <= (uint32_t)kCandCap;
       __syncthreads();
+      if (done) {
+        fill_keys(sm, row, got);
+        __syncthreads();
+      }
     }
   }
 
@@ -501,6 +649,11 @@ topk_select_kernel(const float* __restrict__ scores, int64_t ld, const int32_t* 
   __syncthreads();
   unsigned long long* cand = sm.cand;
   uint32_t m = min(sm.n_cand, (uint32_t)kCandCap);
+  if (nsel > 0u && bucket_sort_top(sm, cand, m, nsel, sm.cut, cand)) {
+    for (uint32_t i = tid; i < (uint32_t)kk; i += kTopkThreads)
+      o[i] = i < nsel ? (int32_t)(0xffffffffu - (uint32_t)(cand[i] & 0xffffffffull)) : 0;
+    return;
+  }
   if (m > (uint32_t)kCutCap && nsel <= (uint32_t)kCutCap) {
     // Cut the candidates to the keys >= the nsel-th largest key (its ties
     // kept, the sort orders them by index): normally exactly nsel entries.
