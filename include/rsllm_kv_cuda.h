@@ -120,6 +120,24 @@ RKV_API rkv_status rkv_append_quant_bf16(const rkv_pool_view* pool, int32_t laye
                                  const uint16_t* rows, int64_t n_tokens, const int32_t* slot_mapping,
                                  uint32_t* d_status, rkv_stream_t stream);
 
+/* The same append for f32 rows, rsLLM's own row type: the arguments, status
+ * rules and stored form of rkv_append_quant_bf16, with rows f32
+ * [n_layers_in][n_tokens][576] (32-byte aligned).  The block exponent is
+ * ceil(log2f(max(amax, 1e-4) / 448)) with the host's log2f, as the reference
+ * evaluates it (dsv4_quant.rs:346-355), through the threshold table below; the
+ * RoPE lanes are stored rounded to bf16 (nearest even).  Gathered rows equal
+ * the reference's f32 round trip rounded to bf16. */
+RKV_API rkv_status rkv_append_quant_f32(const rkv_pool_view* pool, int32_t layer0, int32_t n_layers_in,
+                                        const float* rows, int64_t n_tokens, const int32_t* slot_mapping,
+                                        uint32_t* d_status, rkv_stream_t stream);
+
+/* The table rkv_append_quant_f32 decides the exponent with (no reference
+ * counterpart; exposed for testing): for y = RN(max(amax, 1e-4) / 448) with
+ * biased exponent b and mantissa m, the exponent is (b - 127) + (m >= out[b]).
+ * out[b] is the smallest mantissa at which the host's log2f(y) exceeds b - 127
+ * (0x800000 where none does).  Built once per process from log2f. */
+RKV_API void rkv_scale_threshold_table(uint32_t out[256]);
+
 /* ---- paged gather + dequant -----------------------------------------------
  * Replaces the chronological row reads RawSwaRing::rows / ::row
  * (crates/rsllm-kvcache/src/dsv4/swa.rs:131-149) and CompressedKvPool::rows

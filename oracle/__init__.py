@@ -58,7 +58,9 @@ def lib() -> ctypes.CDLL:
         "rkvo_select_top_k_scan": (c_int64, [P, c_int64, c_int64, P]),
         "rkvo_select_top_k_sorted": (c_int64, [P, c_int64, c_int64, P]),
         "rkvo_topk_batch": (None, [P, c_int64, c_int32, P, c_int32, P, c_int, c_int]),
-        "rkvo_append_rows": (c_uint32, [P, c_int64, c_int32, c_int32, c_int32, P, c_int64, P, c_int]),
+        "rkvo_quantize_row_f32": (c_int, [P, c_int64, c_int64, P, P, P]),
+        "rkvo_threshold_mismatches": (ctypes.c_uint64, [P, c_int, c_int, c_int, P]),
+        "rkvo_append_rows": (c_uint32, [P, c_int64, c_int32, c_int32, c_int32, P, c_int, c_int64, P, c_int]),
         "rkvo_gather_rows": (c_uint32, [P, c_int64, c_int32, c_int32, P, c_int64, P, c_int32, P, c_int]),
         "rkvo_sparse_gather_rows": (c_uint32, [P, c_int64, c_int32, c_int32, P, c_int64, P, P, P, c_int32, c_int32,
                                                P, c_int]),
@@ -101,6 +103,31 @@ def quantize_rows_bf16(rows: np.ndarray):
     for i in range(n):
         st[i] = L.rkvo_quantize_row_bf16(_p(rows[i]), ROW_DIM, ROPE, _p(codes[i]), _p(scales[i]), _p(rope[i]))
     return codes, scales, rope, st
+
+
+def quantize_rows_f32(rows: np.ndarray):
+    """f32 rows [n, 576] -> (codes, scales, rope bf16 bits, status), the stored
+    form of the reference's f32 round trip."""
+    rows = np.ascontiguousarray(rows, dtype=np.float32).reshape(-1, ROW_DIM)
+    n = rows.shape[0]
+    codes = np.zeros((n, LATENT), np.uint8)
+    scales = np.zeros((n, LATENT // BLOCK), np.float32)
+    rope = np.zeros((n, ROPE), np.uint16)
+    st = np.zeros(n, np.int32)
+    L = lib()
+    for i in range(n):
+        st[i] = L.rkvo_quantize_row_f32(_p(rows[i]), ROW_DIM, ROPE, _p(codes[i]), _p(scales[i]), _p(rope[i]))
+    return codes, scales, rope, st
+
+
+def threshold_mismatches(table: np.ndarray, eb_lo: int, eb_hi: int, n_threads: int | None = None):
+    """(count, first bad y bits) of a scale-exponent threshold table against
+    ceilf(log2f(y)) over every y with biased exponent in [eb_lo, eb_hi]."""
+    t = np.ascontiguousarray(table, np.uint32)
+    assert t.shape == (256,)
+    first = np.zeros(1, np.uint32)
+    n = lib().rkvo_threshold_mismatches(_p(t), eb_lo, eb_hi, n_threads or threads(), _p(first))
+    return int(n), int(first[0])
 
 
 def dequant_rows_bf16(codes: np.ndarray, scales: np.ndarray, rope: np.ndarray) -> np.ndarray:
@@ -148,15 +175,17 @@ def new_pool(n_pages: int, n_layers: int) -> np.ndarray:
 
 def append_rows(pool: np.ndarray, n_pages: int, n_layers: int, layer0: int, rows: np.ndarray,
                 slots: np.ndarray, n_threads: int = 1) -> int:
-    rows = np.ascontiguousarray(rows, np.uint16)
+    """rows: bf16 bits (uint16) or float32 ``[n_layers_in, n_tokens, 576]``."""
+    is_f32 = rows.dtype == np.float32
+    rows = np.ascontiguousarray(rows, np.float32 if is_f32 else np.uint16)
     n_layers_in = rows.shape[0] if rows.ndim == 3 else 1
     n_tokens = rows.shape[-2]
     slots = np.ascontiguousarray(slots, np.int32)
     if rows.shape[-1] != ROW_DIM or slots.shape != (n_tokens,):
         raise ValueError(f"append_rows: rows [layers, n_tokens, 576] with slots [n_tokens], got {rows.shape} "
                          f"and {slots.shape}")
-    return lib().rkvo_append_rows(_p(pool), n_pages, n_layers, layer0, n_layers_in, _p(rows), n_tokens, _p(slots),
-                                  n_threads)
+    return lib().rkvo_append_rows(_p(pool), n_pages, n_layers, layer0, n_layers_in, _p(rows), int(is_f32), n_tokens,
+                                  _p(slots), n_threads)
 
 
 def gather_rows(pool: np.ndarray, n_pages: int, n_layers: int, layer: int, page_table: np.ndarray,

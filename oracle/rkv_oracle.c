@@ -243,6 +243,82 @@ int rkvo_quantize_row_bf16(const uint16_t* row, int64_t head_dim, int64_t n_rot,
     return RKVO_OK;
 }
 
+/* The same stored form for an f32 row (the reference's own row type): the
+ * codes and scale of dsv4_quant.rs:346-361 for each latent block, and the
+ * RoPE lanes rounded to bf16 (the stored row holds bf16 RoPE). */
+int rkvo_quantize_row_f32(const float* row, int64_t head_dim, int64_t n_rot,
+                          uint8_t* codes, float* scales, uint16_t* rope) {
+    if (n_rot > head_dim) return RKVO_SHAPE_MISMATCH;
+    int64_t n_nope = head_dim - n_rot;
+    if (n_nope <= 0 || n_nope % FP8_KV_GROUP != 0) return RKVO_SHAPE_MISMATCH;
+    for (int64_t i = 0; i < n_nope; ++i)
+        if (!isfinite(row[i])) return RKVO_NON_FINITE_INPUT;
+    for (int64_t b = 0; b < n_nope; b += FP8_KV_GROUP) {
+        float amax = 0.0f;
+        for (int i = 0; i < FP8_KV_GROUP; ++i) {
+            float av = fabsf(row[b + i]);
+            if (av > amax) amax = av;
+        }
+        int e = rkvo_scale_exponent(amax);
+        float scale = rkvo_libm_ldexpf(1.0f, e);
+        scales[b / FP8_KV_GROUP] = scale;
+        for (int i = 0; i < FP8_KV_GROUP; ++i) {
+            float t = row[b + i] / scale;
+            if (t < -FP8_E4M3_MAX) t = -FP8_E4M3_MAX;
+            if (t > FP8_E4M3_MAX) t = FP8_E4M3_MAX;
+            codes[b + i] = rkvo_e4m3fn_code(t);
+        }
+    }
+    for (int64_t i = 0; i < n_rot; ++i) rope[i] = rkvo_f32_to_bf16(row[n_nope + i]);
+    return RKVO_OK;
+}
+
+/* Checks a threshold table (exponent of y = (b - 127) + (mantissa >= t[b]))
+ * against ceilf(log2f(y)) for every normal y with biased exponent in
+ * [eb_lo, eb_hi].  Returns the number of disagreeing y; the first one's bits
+ * go to *first_bad. */
+typedef struct { const uint32_t* t; int eb_lo, eb_hi; uint64_t bad; uint32_t first; } table_job;
+
+static void* table_worker(void* p) {
+    table_job* j = (table_job*)p;
+    j->bad = 0;
+    j->first = 0;
+    for (int eb = j->eb_lo; eb <= j->eb_hi; ++eb) {
+        for (uint32_t m = 0; m < 0x800000u; ++m) {
+            uint32_t yb = ((uint32_t)eb << 23) | m;
+            int want = (int)ceilf(log2f(f_from_bits(yb)));
+            int got = eb - 127 + (m >= j->t[eb] ? 1 : 0);
+            if (got != want) {
+                if (j->bad++ == 0) j->first = yb;
+            }
+        }
+    }
+    return NULL;
+}
+
+uint64_t rkvo_threshold_mismatches(const uint32_t* table, int eb_lo, int eb_hi, int n_threads, uint32_t* first_bad) {
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > 256) n_threads = 256;
+    int n = eb_hi - eb_lo + 1;
+    if (n <= 0) return 0;
+    if (n_threads > n) n_threads = n;
+    pthread_t th[256];
+    table_job jobs[256];
+    for (int t = 0; t < n_threads; ++t) {
+        jobs[t] = (table_job){table, eb_lo + (int)((int64_t)n * t / n_threads),
+                              eb_lo + (int)((int64_t)n * (t + 1) / n_threads) - 1, 0, 0};
+        pthread_create(&th[t], NULL, table_worker, &jobs[t]);
+    }
+    uint64_t bad = 0;
+    *first_bad = 0;
+    for (int t = 0; t < n_threads; ++t) {
+        pthread_join(th[t], NULL);
+        if (jobs[t].bad && bad == 0) *first_bad = jobs[t].first;
+        bad += jobs[t].bad;
+    }
+    return bad;
+}
+
 /* Stored row -> bf16 [n_nope + n_rot]: (sign * e4m3fn_value) * scale, the
  * product the reference forms at dsv4_quant.rs:359, rounded to bf16. */
 void rkvo_dequant_row_bf16(const uint8_t* codes, const float* scales, const uint16_t* rope,
@@ -409,7 +485,7 @@ static inline uint8_t* page_ptr(uint8_t* pool, int64_t n_pages, int32_t layer, i
 
 typedef struct {
     uint8_t* pool; int64_t n_pages; int32_t n_layers; int32_t layer0; int32_t n_layers_in;
-    const uint16_t* rows; int64_t n_tokens; const int32_t* slots;
+    const void* rows; int is_f32; int64_t n_tokens; const int32_t* slots;
     int64_t r0, r1; uint32_t status;
 } append_job;
 
@@ -426,7 +502,10 @@ static void* append_worker(void* p) {
         if (layer < 0 || layer >= j->n_layers) { j->status |= 1u << RKVO_INVALID_LAYER; continue; }
         int64_t page = slot / PAGE_TOKENS, off = slot % PAGE_TOKENS;
         if (page >= j->n_pages) { j->status |= 1u << RKVO_INDEX_OUT_OF_RANGE; continue; }
-        int rc = rkvo_quantize_row_bf16(j->rows + r * ROW_DIM, ROW_DIM, ROPE, codes, scales, rope);
+        int rc = j->is_f32
+                     ? rkvo_quantize_row_f32((const float*)j->rows + r * ROW_DIM, ROW_DIM, ROPE, codes, scales, rope)
+                     : rkvo_quantize_row_bf16((const uint16_t*)j->rows + r * ROW_DIM, ROW_DIM, ROPE, codes, scales,
+                                              rope);
         if (rc != RKVO_OK) { j->status |= 1u << rc; continue; }
         uint8_t* pg = page_ptr(j->pool, j->n_pages, layer, page);
         memcpy(pg + off * LATENT, codes, LATENT);
@@ -436,10 +515,11 @@ static void* append_worker(void* p) {
     return NULL;
 }
 
-/* rows: [n_layers_in][n_tokens][576] bf16; slots: [n_tokens] (shared by the
- * layers, < 0 = skip).  Returns the OR of (1 << status) over failed rows. */
+/* rows: [n_layers_in][n_tokens][576] bf16 (is_f32 = 0) or f32 (is_f32 = 1);
+ * slots: [n_tokens] (shared by the layers, < 0 = skip).  Returns the OR of
+ * (1 << status) over failed rows. */
 uint32_t rkvo_append_rows(uint8_t* pool, int64_t n_pages, int32_t n_layers, int32_t layer0,
-                          int32_t n_layers_in, const uint16_t* rows, int64_t n_tokens,
+                          int32_t n_layers_in, const void* rows, int is_f32, int64_t n_tokens,
                           const int32_t* slots, int n_threads) {
     int64_t n_rows = (int64_t)n_layers_in * n_tokens;
     if (n_rows <= 0) return 0;
@@ -452,7 +532,7 @@ uint32_t rkvo_append_rows(uint8_t* pool, int64_t n_pages, int32_t n_layers, int3
     for (int t = 0; t < n_threads; ++t) {
         int64_t b = per * t;
         if (b >= n_rows) break;
-        jobs[t] = (append_job){pool, n_pages, n_layers, layer0, n_layers_in, rows, n_tokens, slots,
+        jobs[t] = (append_job){pool, n_pages, n_layers, layer0, n_layers_in, rows, is_f32, n_tokens, slots,
                                b, b + per < n_rows ? b + per : n_rows, 0};
         if (n_threads == 1) append_worker(&jobs[t]);
         else pthread_create(&th[t], NULL, append_worker, &jobs[t]);

@@ -1,0 +1,89 @@
+"""GPU parity of the f32-row append (rkv_append_quant_f32) against the oracle:
+the pool bytes equal the oracle's stored form of the same f32 rows, and the
+gathered bf16 rows equal rsLLM's own f32 round trip
+(fp8_kv_quantize_row_inplace, dsv4_quant.rs:316-362) rounded to bf16 -- on
+rows whose block maxima sit at the log2f threshold of every binade, on N(0,1)
+rows over several layers, and with padding, out-of-range and non-finite rows."""
+import numpy as np
+import pytest
+import torch
+
+import rsllm_b200 as rk
+from test_oracle_f32 import f32_rows_at_thresholds, product_table, reference_roundtrip_f32
+
+pytestmark = pytest.mark.gpu
+
+
+def u16(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def i32(a, dev) -> torch.Tensor:
+    return torch.as_tensor(np.ascontiguousarray(a, np.int32)).to(dev)
+
+
+def gather_all(pool, n_tok: int, pages: np.ndarray, dev) -> np.ndarray:
+    pt = pages.reshape(1, -1).astype(np.int32)
+    cu = np.array([0, n_tok], np.int32)
+    out = u16(pool.rows(0, i32(pt, dev), i32(cu, dev), n_tok))
+    pool.check("gather")
+    return out
+
+
+def test_thresholds_every_binade(cuda, orc):
+    rows = f32_rows_at_thresholds(product_table(), seed=1)
+    n_tok = rows.shape[0]
+    n_pages = (n_tok + 63) // 64
+    perm = np.random.default_rng(2).permutation(n_pages).astype(np.int32)
+    slots = (perm[np.arange(n_tok) // 64] * 64 + np.arange(n_tok) % 64).astype(np.int32)
+    pool = rk.PagedKvPool(n_pages, 1, device=cuda)
+    pool.storage.zero_()
+    pool.append_layer(0, torch.from_numpy(rows).to(cuda), i32(slots, cuda))
+    pool.check("append")
+    ref = orc.new_pool(n_pages, 1)
+    assert orc.append_rows(ref, n_pages, 1, 0, rows, slots) == 0
+    got = pool.storage.cpu().numpy()
+    bad = np.nonzero(got != ref)[0]
+    assert bad.size == 0, f"{bad.size} pool bytes differ, first at byte {int(bad[0])}"
+    assert np.array_equal(gather_all(pool, n_tok, perm, cuda), reference_roundtrip_f32(orc, rows))
+
+
+def test_multilayer_normal_rows_with_padding(cuda, orc):
+    n_pages, n_layers, n_tok = 12, 4, 700
+    rng = np.random.default_rng(5)
+    rows = rng.standard_normal((3, n_tok, 576)).astype(np.float32)
+    rows[:, :, :512] *= np.exp(rng.uniform(-12, 12, (3, n_tok, 8))).repeat(64, axis=2).astype(np.float32)
+    slots = rng.permutation(n_pages * 64)[:n_tok].astype(np.int32)
+    slots[rng.random(n_tok) < 0.1] = -1
+    pool = rk.PagedKvPool(n_pages, n_layers, device=cuda)
+    pool.storage.zero_()
+    pool.append_layer(1, torch.from_numpy(rows).to(cuda), i32(slots, cuda))
+    pool.check("append")
+    ref = orc.new_pool(n_pages, n_layers)
+    assert orc.append_rows(ref, n_pages, n_layers, 1, rows, slots) == 0
+    assert np.array_equal(pool.storage.cpu().numpy(), ref)
+
+
+def test_bad_rows_write_nothing(cuda, orc):
+    n_pages, n_tok = 2, 70
+    rng = np.random.default_rng(9)
+    rows = rng.standard_normal((n_tok, 576)).astype(np.float32)
+    rows[3, 17] = np.nan
+    rows[4, 500] = -np.inf
+    rows[5, 540] = np.inf      # RoPE lane: stored
+    rows[6, 520] = np.nan      # RoPE lane: stored as a quiet NaN
+    slots = np.arange(n_tok, dtype=np.int32)
+    slots[10] = n_pages * 64   # out of range
+    pool = rk.PagedKvPool(n_pages, 1, device=cuda)
+    pool.storage.zero_()
+    pool.append_layer(0, torch.from_numpy(rows).to(cuda), i32(slots, cuda))
+    bits = pool.take_status()
+    ref = orc.new_pool(n_pages, 1)
+    want = orc.append_rows(ref, n_pages, 1, 0, rows, slots)
+    assert bits == want == (1 << rk._abi.RKV_ERR_NON_FINITE_INPUT) | (1 << rk._abi.RKV_ERR_INDEX_OUT_OF_RANGE)
+    assert np.array_equal(pool.storage.cpu().numpy(), ref)
+    pool.append_layer(0, torch.from_numpy(rows[:3]).to(cuda), i32(slots[:3], cuda))
+    pool.check("clean append")
+    with pytest.raises(rk.NonFiniteInput):
+        pool.append_layer(0, torch.from_numpy(rows[3:4]).to(cuda), i32(slots[3:4], cuda))
+        pool.check("append")
