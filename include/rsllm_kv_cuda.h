@@ -324,6 +324,42 @@ RKV_API rkv_status rkv_apply_page_moves_static(const rkv_pool_view* pool, const 
                                                int64_t n_moves, int32_t* d_tables, int64_t n_entries,
                                                uint32_t* d_status, rkv_stream_t stream);
 
+/* ---- MLA decode attention over the FP8 pages -------------------------------
+ * Replaces the per-token attention read of rsLLM's mixed sweep
+ * (crates/rsllm-models/src/dsv4/attention.rs:493-663) -- logits over the
+ * cached rows, softmax with the per-head sink as a value-less virtual key,
+ * weighted sum of the rows -- for one query position per entry of q, reading
+ * the FP8 pages directly (no bf16 copy of the rows is written).
+ *
+ * q:            bf16 [n_q][64 heads][576], 16-byte aligned; query qi belongs to
+ *               sequence seq_of_query[qi] (int32 [n_q]).
+ * keys:         idx == NULL: every row [0, seq_lens[seq]) of the sequence
+ *               (page_table [n_seq][pt_stride], one entry per 64 rows);
+ *               idx != NULL: the rows whose positions appear in idx [n_q][k]
+ *               (the sparse mask of attention.rs:548-556): entries outside
+ *               [0, seq_len) are ignored and a repeated 0 counts once (the
+ *               top-k selection's fill value, indexer.rs:222-235).
+ * logit:        (q_h . row) * softmax_scale over the 576 stored lanes (latent
+ *               dequantised exactly, RoPE lanes as stored).
+ * sinks:        f32 [64] or NULL (no sink).
+ * out:          f32 [n_q][64][512] = softmax-weighted sum of the 512 latent
+ *               lanes, 16-byte aligned; a head with no key and no sink, or a
+ *               zero denominator, gives zeros (attention.rs:618-641).
+ * n_splits:     dense only: the rows of a sequence are cut into n_splits page
+ *               ranges processed in parallel and merged through workspace
+ *               (rkv_mla_decode_workspace_bytes(n_q, n_splits) bytes, 16-byte
+ *               aligned; may be NULL when n_splits == 1).
+ * Device status: a page id outside the pool sets INDEX_OUT_OF_RANGE (that
+ * row is skipped); RKV_ERR_CUDA means a device-side wait timed out.
+ * Numerics: P = exp2(...) is rounded to bf16 before the tensor-core product
+ * (relative 2^-9 per weight), logits and sums are f32. */
+RKV_API int64_t rkv_mla_decode_workspace_bytes(int32_t n_q, int32_t n_splits);
+RKV_API rkv_status rkv_mla_decode_fp8(const rkv_pool_view* pool, int32_t layer, const int32_t* page_table,
+                                      int64_t pt_stride, const int32_t* seq_lens, const int32_t* seq_of_query,
+                                      const uint16_t* q, int32_t n_q, const int32_t* idx, int32_t k,
+                                      const float* sinks, float softmax_scale, int32_t n_splits, void* workspace,
+                                      float* out, uint32_t* d_status, rkv_stream_t stream);
+
 /* ---- codec pin ---------------------------------------------------------------
  * out[i] = E4M3 code the append kernel stores for the f32 lane value whose
  * bit pattern is first_bits + i (already divided by its block scale), i < n:

@@ -65,6 +65,8 @@ def lib() -> ctypes.CDLL:
         "rkvo_sparse_gather_rows": (c_uint32, [P, c_int64, c_int32, c_int32, P, c_int64, P, P, P, c_int32, c_int32,
                                                P, c_int]),
         "rkvo_copy_pages": (None, [P, c_int64, c_int32, P, P, c_int64]),
+        "rkvo_mla_decode": (c_uint32, [P, c_int64, c_int32, c_int32, P, c_int64, P, P, P, c_int32, P, c_int32, P,
+                                       c_float, P, c_int]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -215,3 +217,31 @@ def copy_pages(pool: np.ndarray, n_pages: int, n_layers: int, src: np.ndarray, d
     s = np.ascontiguousarray(src, np.int32)
     d = np.ascontiguousarray(dst, np.int32)
     lib().rkvo_copy_pages(_p(pool), n_pages, n_layers, _p(s), _p(d), s.size)
+
+
+# ---- MLA decode attention ------------------------------------------------------
+
+def mla_decode(pool: np.ndarray, n_pages: int, n_layers: int, layer: int, page_table: np.ndarray,
+               seq_lens: np.ndarray, seq_of_query: np.ndarray, q: np.ndarray, idx: np.ndarray | None,
+               sinks: np.ndarray | None, scale: float, n_threads: int | None = None):
+    """attention.rs:493-663 over pooled rows: q bf16 bits [n_q, 64, 576];
+    idx int32 [n_q, k] (sparse) or None (every row); returns (out f32
+    [n_q, 64, 512], status bits)."""
+    pt = np.ascontiguousarray(page_table, np.int32)
+    sl = np.ascontiguousarray(seq_lens, np.int32)
+    sq = np.ascontiguousarray(seq_of_query, np.int32)
+    q = np.ascontiguousarray(q, np.uint16)
+    n_q = q.shape[0]
+    assert q.shape == (n_q, 64, 576) and sq.shape == (n_q,)
+    out = np.zeros((n_q, 64, 512), np.float32)
+    if idx is not None:
+        idx = np.ascontiguousarray(idx, np.int32)
+        assert idx.shape[0] == n_q
+        k, ip = idx.shape[1], _p(idx)
+    else:
+        k, ip = 0, None
+    sk = None if sinks is None else np.ascontiguousarray(sinks, np.float32)
+    st = lib().rkvo_mla_decode(_p(pool), n_pages, n_layers, layer, _p(pt), pt.shape[1], _p(sl), _p(sq), _p(q), n_q,
+                               ip, k, None if sk is None else _p(sk), float(scale), _p(out),
+                               n_threads or threads())
+    return out, st

@@ -670,3 +670,138 @@ void rkvo_copy_pages(uint8_t* pool, int64_t n_pages, int32_t n_layers, const int
         for (int64_t i = 0; i < n; ++i)
             memcpy(page_ptr(pool, n_pages, l, dst[i]), page_ptr(pool, n_pages, l, src[i]), PAGE_BYTES);
 }
+
+/* ------------------------------------------------------------------------ */
+/* MLA decode attention over the paged pool                                  */
+/* ------------------------------------------------------------------------ */
+/* The mixed sweep of crates/rsllm-models/src/dsv4/attention.rs:493-663 for
+ * one query position, restated over a sequence's pooled rows:
+ *   keys    = every row [0, len) of the query's sequence (dense), or the rows
+ *             whose positions appear in idx[q][0..k) and are < len (sparse:
+ *             the `allowed` set of :548-556, duplicates count once);
+ *   logit   = (sum_d q_h[d] * k[d]) * scale over the 576 stored lanes
+ *             (dequantised latent + bf16 RoPE), rows in ascending order (:582-606);
+ *   softmax = max over the sink and the logits, exp(l - max), the sink's
+ *             exp(sink - max) in the denominator only (:627-643);
+ *   output  = sum (e * inv_denom) * v over the 512 latent lanes (:646-663);
+ *   a non-finite max or a zero / non-finite denominator gives zeros (:618-641).
+ * q: bf16 [n_q][64][576]; out: f32 [n_q][64][512]; sinks: f32 [64] or NULL. */
+#define MLA_HEADS 64
+#define MLA_QK 576
+#define MLA_V 512
+
+typedef struct {
+    const uint8_t* pool; int64_t n_pages; int32_t layer;
+    const int32_t* pt; int64_t pt_stride; const int32_t* seq_lens; const int32_t* seq_of_query;
+    const uint16_t* q; const int32_t* idx; int32_t k; const float* sinks; float scale; float* out;
+    int32_t q0, q1; uint32_t status;
+} mla_job;
+
+static int mla_row(const mla_job* j, int32_t seq, int64_t pos, float* row) {
+    int32_t page = j->pt[(int64_t)seq * j->pt_stride + pos / PAGE_TOKENS];
+    if (page < 0 || page >= j->n_pages) return 0;
+    const uint8_t* pg = page_ptr((uint8_t*)j->pool, j->n_pages, j->layer, page);
+    int64_t off = pos % PAGE_TOKENS;
+    const uint8_t* codes = pg + off * LATENT;
+    const float* sc = (const float*)(pg + CODES_BYTES + off * NBLK * 4);
+    const uint16_t* rope = (const uint16_t*)(pg + CODES_BYTES + SCALES_BYTES + off * ROPE * 2);
+    for (int d = 0; d < LATENT; ++d) {
+        uint8_t c = codes[d];
+        float sign = (c & 0x80) ? -1.0f : 1.0f;
+        row[d] = (sign * rkvo_e4m3fn_value(c & 0x7fu)) * sc[d / BLOCK];
+    }
+    for (int d = 0; d < ROPE; ++d) row[LATENT + d] = bf16_to_f32(rope[d]);
+    return 1;
+}
+
+static void* mla_worker(void* p) {
+    mla_job* j = (mla_job*)p;
+    for (int32_t qi = j->q0; qi < j->q1; ++qi) {
+        int32_t seq = j->seq_of_query[qi];
+        int64_t len = j->seq_lens[seq];
+        /* the key set in ascending row order */
+        uint8_t* allowed = (uint8_t*)calloc((size_t)(len > 0 ? len : 1), 1);
+        if (j->idx) {
+            for (int32_t t = 0; t < j->k; ++t) {
+                int32_t c = j->idx[(int64_t)qi * j->k + t];
+                if (c >= 0 && c < len) allowed[c] = 1;
+            }
+        } else {
+            memset(allowed, 1, (size_t)len);
+        }
+        int64_t n_keys = 0;
+        for (int64_t c = 0; c < len; ++c) n_keys += allowed[c];
+        float* rows = (float*)malloc((size_t)(n_keys > 0 ? n_keys : 1) * MLA_QK * sizeof(float));
+        int64_t r = 0;
+        for (int64_t c = 0; c < len; ++c) {
+            if (!allowed[c]) continue;
+            if (!mla_row(j, seq, c, rows + r * MLA_QK)) {
+                j->status |= 1u << RKVO_INDEX_OUT_OF_RANGE; /* a row on a bad page is not a key */
+                continue;
+            }
+            ++r;
+        }
+        n_keys = r;
+        float* logits = (float*)malloc((size_t)(n_keys > 0 ? n_keys : 1) * sizeof(float));
+        for (int h = 0; h < MLA_HEADS; ++h) {
+            const uint16_t* qh = j->q + ((int64_t)qi * MLA_HEADS + h) * MLA_QK;
+            float qf[MLA_QK];
+            for (int d = 0; d < MLA_QK; ++d) qf[d] = bf16_to_f32(qh[d]);
+            float sink = j->sinks ? j->sinks[h] : -INFINITY;
+            float max_logit = sink;
+            for (int64_t t = 0; t < n_keys; ++t) {
+                const float* kr = rows + t * MLA_QK;
+                float dot = 0.0f;
+                for (int d = 0; d < MLA_QK; ++d) dot += qf[d] * kr[d];
+                float l = dot * j->scale;
+                if (l > max_logit) max_logit = l;
+                logits[t] = l;
+            }
+            float* oh = j->out + ((int64_t)qi * MLA_HEADS + h) * MLA_V;
+            for (int d = 0; d < MLA_V; ++d) oh[d] = 0.0f;
+            if (!isfinite(max_logit)) continue;
+            float denom = isfinite(sink) ? expf(sink - max_logit) : 0.0f;
+            for (int64_t t = 0; t < n_keys; ++t) {
+                logits[t] = expf(logits[t] - max_logit);
+                denom += logits[t];
+            }
+            if (!isfinite(denom) || denom == 0.0f) continue;
+            float inv = 1.0f / denom;
+            for (int64_t t = 0; t < n_keys; ++t) {
+                float w = logits[t] * inv;
+                const float* vr = rows + t * MLA_QK;
+                for (int d = 0; d < MLA_V; ++d) oh[d] += w * vr[d];
+            }
+        }
+        free(logits);
+        free(rows);
+        free(allowed);
+    }
+    return NULL;
+}
+
+uint32_t rkvo_mla_decode(const uint8_t* pool, int64_t n_pages, int32_t n_layers, int32_t layer,
+                         const int32_t* page_table, int64_t pt_stride, const int32_t* seq_lens,
+                         const int32_t* seq_of_query, const uint16_t* q, int32_t n_q, const int32_t* idx,
+                         int32_t k, const float* sinks, float scale, float* out, int n_threads) {
+    if (n_q <= 0) return 0;
+    if (layer < 0 || layer >= n_layers) return 1u << RKVO_INVALID_LAYER;
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > 256) n_threads = 256;
+    if (n_threads > n_q) n_threads = n_q;
+    pthread_t th[256];
+    mla_job jobs[256];
+    for (int t = 0; t < n_threads; ++t) {
+        jobs[t] = (mla_job){pool, n_pages, layer, page_table, pt_stride, seq_lens, seq_of_query, q, idx, k, sinks,
+                            scale, out, (int32_t)((int64_t)n_q * t / n_threads),
+                            (int32_t)((int64_t)n_q * (t + 1) / n_threads), 0};
+        if (n_threads == 1) mla_worker(&jobs[t]);
+        else pthread_create(&th[t], NULL, mla_worker, &jobs[t]);
+    }
+    uint32_t st = 0;
+    for (int t = 0; t < n_threads; ++t) {
+        if (n_threads > 1) pthread_join(th[t], NULL);
+        st |= jobs[t].status;
+    }
+    return st;
+}

@@ -5,7 +5,7 @@ Loading fails loudly: there is no CPU fallback for any entry point.
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, Structure, c_char_p, c_int32, c_int64, c_uint8, c_uint16, c_uint32, c_void_p
+from ctypes import c_float, POINTER, Structure, c_char_p, c_int32, c_int64, c_uint8, c_uint16, c_uint32, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "librsllm_kv_cuda.so"
@@ -69,6 +69,9 @@ SIGNATURES = {
     "rkv_copy_pages": (c_int32, [_P(PoolView), _i32p, _i32p, c_int64, _u32p, c_void_p]),
     "rkv_remap_pages": (c_int32, [_i32p, c_int64, _i32p, c_int64, _u32p, c_void_p]),
     "rkv_e4m3fn_code_range": (c_int32, [c_uint32, c_int64, _u8p, c_void_p]),
+    "rkv_mla_decode_workspace_bytes": (c_int64, [c_int32, c_int32]),
+    "rkv_mla_decode_fp8": (c_int32, [_P(PoolView), c_int32, _i32p, c_int64, _i32p, _i32p, _u16p, c_int32, _i32p,
+                                     c_int32, _f32p, c_float, c_int32, c_void_p, _f32p, _u32p, c_void_p]),
     "rkv_pool_create": (c_int32, [_P(PoolDesc), _P(c_void_p)]),
     "rkv_pool_destroy": (None, [c_void_p]),
     "rkv_pool_get_view": (c_int32, [c_void_p, _P(PoolView)]),

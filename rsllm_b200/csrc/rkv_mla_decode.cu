@@ -1,0 +1,641 @@
+// rkv_mla_decode.cu -- MLA decode attention that reads the FP8 pages directly.
+//
+// The consumer of the paged rows: rsLLM's mixed attention sweep
+// (crates/rsllm-models/src/dsv4/attention.rs:493-663) for one query position
+// per CTA, 64 heads sharing one latent KV row per token (MQA form of MLA):
+//   S = Q K^T * scale over the 576 stored lanes, softmax with the per-head sink
+//   as a value-less virtual key, O = P V over the 512 latent lanes; the keys
+//   are every row of the query's sequence (dense) or only the rows an index
+//   list selects (the sparse mask of attention.rs:548-556).
+//
+// The FP8 rows are never written back as bf16: loader warps read a page's
+// codes, scales and RoPE lanes, dequantise them (exactly, see rkv_common.cuh)
+// straight into a 128-byte-swizzled shared-memory tile, and the 5th-generation
+// tensor cores consume that tile twice -- as K (K-major) for S and as V
+// (MN-major) for O -- with both accumulators in tensor memory:
+//
+//   warps 0-3  softmax: S from TMEM, online max / exp2 / row sums per head,
+//              P (bf16) to shared memory, lazy rescale of O in TMEM, epilogue
+//   warps 4-7  loaders: pages -> registers -> dequant -> swizzled K/V tile
+//   warp 8     TMEM allocation and the single MMA-issuing thread
+//
+// Shapes per tile (64 key rows, one page in dense mode), M = 64 heads:
+//   S[64 x 64]   = Q[64 x 576] . K^T    36 MMAs of K = 16 (N = 64)
+//   O[64 x 512] += P[64 x 64]  . V      2 x 4 MMAs of N = 256
+// TMEM (512 columns): O lanes 0-15 (+32k) cols 0-255 = latent 0-255,
+// O lanes 16-31 (+32k) cols 0-255 = latent 256-511 (the M = 64 accumulator
+// occupies half of each 32-lane sub-partition), S double-buffered at columns
+// 256 and 320.  Head h lives in TMEM lane (h % 16) + 32 (h / 16).
+//
+// The online softmax keeps a per-head reference maximum m and rescales O only
+// when a tile's maximum exceeds it by more than 2^8 (P values stay <= 256 in
+// bf16); the final normalisation uses the same m, so the result is the same
+// softmax.  The denominator is the sum of the bf16-rounded P that the tensor
+// core multiplies, plus the sink's exp.
+//
+// Every wait on a barrier is bounded (1 s of %globaltimer); on a timeout the
+// CTA records RKV_ERR_CUDA in the status word, drains its own MMAs, frees its
+// tensor memory and returns.
+#include <cmath>
+
+#include "rkv_common.cuh"
+#include "rkv_host.h"
+
+namespace rkv {
+namespace mla {
+
+constexpr int kHeads = 64;
+constexpr int kQk = 576;                      // key lanes: 512 latent + 64 RoPE
+constexpr int kV = 512;                       // value lanes: the latent
+constexpr int kTile = 64;                     // key rows per tile
+constexpr int kAtom = 1024;                   // 8 rows x 128 B swizzle atom
+constexpr int kColBytes = 8 * kAtom;          // one 64-lane column of a 64-row operand
+constexpr int kOperandBytes = (kQk / 64) * kColBytes;  // 73728: 64 rows x 576 bf16
+constexpr int kSmemQ = 0;
+constexpr int kSmemK0 = kSmemQ + kOperandBytes;
+constexpr int kSmemP = kSmemK0 + 2 * kOperandBytes;
+constexpr int kSmemBar = kSmemP + kColBytes;
+constexpr int kSmemRows = kSmemBar + 128;     // sparse row table: 2 stages x 64 x (page, off)
+constexpr int kSmemTotal = kSmemRows + 2 * 64 * 8;
+constexpr int kSmemAlloc = kSmemTotal + 1024; // slack for the 1024-byte alignment
+constexpr int kThreads = 288;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 256;               // S buffers at 256 and 320
+constexpr float kRescaleLog2 = 8.0f;
+constexpr uint64_t kTimeoutNs = 1000000000ull;
+
+// Barrier / state offsets inside the kSmemBar block.
+constexpr int kBarKFull = 0, kBarKEmpty = 16, kBarSFull = 32, kBarPFull = 48, kBarPvDone = 56, kBarDrain = 64;
+constexpr int kTmemSlot = 72, kAbort = 76, kMask = 80, kFirstZero = 96;
+
+constexpr uint32_t kIdescQK = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((64u >> 4) << 24);
+constexpr uint32_t kIdescPV = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((256u >> 3) << 17) | ((64u >> 4) << 24);
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of the given parity; false on timeout or abort.
+__device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_test(bar, parity)) return true;
+  const uint64_t t0 = now_ns();
+  while (!mbar_test(bar, parity)) {
+    if (*abort_flag) return false;
+    if (now_ns() - t0 > kTimeoutNs) return false;
+  }
+  return true;
+}
+
+// Named barrier over the 128 loader threads that also ANDs a predicate, so
+// that every loader takes the same branch after a bounded wait.
+__device__ __forceinline__ bool loaders_all(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 2, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)ok)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 128-byte-swizzle shared-memory matrix descriptor (sm_100 version field).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)((lbo >> 4) & 0x3fffu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3fffu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Byte offset of 16-byte chunk `c` (8 bf16 lanes) of row `r` in a 64-row
+// operand stored as 64-lane columns of 8-row swizzle atoms.
+__device__ __forceinline__ uint32_t sw_off(int r, int c) {
+  return (uint32_t)((c >> 3) * kColBytes + (r >> 3) * kAtom + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+struct Params {
+  rkv_pool_view pool;
+  int layer;
+  const int32_t* page_table;
+  int64_t pt_stride;
+  const int32_t* seq_lens;
+  const int32_t* seq_of_query;
+  const uint16_t* q;   // bf16 [n_q][64][576]
+  const int32_t* idx;  // [n_q][k] or null (dense)
+  int k;
+  const float* sinks;  // [64] or null
+  float scale_log2;    // softmax scale * log2(e)
+  int n_splits;
+  float* ws_o;         // [n_q][n_splits][64][512] when n_splits > 1
+  float* ws_ml;        // [n_q][n_splits][64][2]
+  float* out;          // [n_q][64][512]
+  uint32_t* status;
+};
+
+__device__ __forceinline__ void set_abort(volatile int* abort_flag, uint32_t* status) {
+  *abort_flag = 1;
+  set_status(status, RKV_ERR_CUDA);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // 1024-byte aligned atoms
+  const uint32_t sbase = smem_u32(smem);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qi = blockIdx.y, split = blockIdx.x;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemBar + kAbort);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + kTmemSlot);
+  uint64_t* masks = reinterpret_cast<uint64_t*>(smem + kSmemBar + kMask);
+  int* first_zero = reinterpret_cast<int*>(smem + kSmemBar + kFirstZero);
+  int2* rows_tab = reinterpret_cast<int2*>(smem + kSmemRows);
+  const uint32_t bar = sbase + kSmemBar;
+
+  const int seq = p.seq_of_query[qi];
+  const int len = max(p.seq_lens[seq], 0);
+  const int n_pages_seq = (len + kTile - 1) / kTile;
+  int page0 = 0, n_tiles;
+  if (p.idx) {
+    n_tiles = (p.k + kTile - 1) / kTile;
+  } else {
+    const int pps = (n_pages_seq + p.n_splits - 1) / p.n_splits;
+    page0 = split * pps;
+    n_tiles = max(0, min(pps, n_pages_seq - page0));
+  }
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar + kBarKFull + 8 * i, 128);
+      mbar_init(bar + kBarKEmpty + 8 * i, 1);
+      mbar_init(bar + kBarSFull + 8 * i, 1);
+    }
+    mbar_init(bar + kBarPFull, 128);
+    mbar_init(bar + kBarPvDone, 1);
+    mbar_init(bar + kBarDrain, 1);
+    *abort_flag = 0;
+    *first_zero = 0x7fffffff;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 8) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // Q of this query into the swizzled A operand (64 heads x 576 lanes).
+  {
+    const uint4* qg = reinterpret_cast<const uint4*>(p.q + (int64_t)qi * kHeads * kQk);
+    for (int c = tid; c < kHeads * kQk / 8; c += kThreads) {
+      const int h = c / (kQk / 8), cc = c % (kQk / 8);
+      *reinterpret_cast<uint4*>(smem + kSmemQ + sw_off(h, cc)) = __ldg(qg + c);
+    }
+  }
+  __syncthreads();
+  if (p.idx && warp >= 4 && warp < 8) {  // the first position holding index 0 (later zeros repeat it)
+    const int32_t* il = p.idx + (int64_t)qi * p.k;
+    int fz = 0x7fffffff;
+    for (int i = tid - 128; i < p.k; i += 128)
+      if (__ldg(il + i) == 0) {
+        fz = i;
+        break;
+      }
+    if (fz != 0x7fffffff) atomicMin(first_zero, fz);
+  }
+  fence_proxy_async();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0 && n_tiles > 0) {
+      bool ok = true;
+      auto issue_qk = [&](int j) {
+        const int b = j & 1;
+        const uint32_t kbase = sbase + kSmemK0 + b * kOperandBytes;
+        const uint32_t d = tmem + kColS + 64 * b;
+#pragma unroll 4
+        for (int s = 0; s < kQk / 16; ++s) {
+          const uint32_t off = (s >> 2) * kColBytes + (s & 3) * 32;
+          mma_bf16(d, sw128_desc(sbase + kSmemQ + off, 16, kAtom), sw128_desc(kbase + off, 16, kAtom), kIdescQK,
+                   s > 0);
+        }
+        mma_commit(bar + kBarSFull + 8 * b);
+      };
+      ok = mbar_wait(bar + kBarKFull, 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0);
+      }
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (j + 1 < n_tiles) {
+          ok = mbar_wait(bar + kBarKFull + 8 * ((j + 1) & 1), ((j + 1) >> 1) & 1, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          issue_qk(j + 1);
+        }
+        ok = mbar_wait(bar + kBarPFull, j & 1, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t vbase = sbase + kSmemK0 + (j & 1) * kOperandBytes;
+#pragma unroll
+        for (int qq = 0; qq < kTile / 16; ++qq) {
+          const uint64_t a = sw128_desc(sbase + kSmemP + qq * 32, 16, kAtom);
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf)
+            mma_bf16(tmem + (hf ? (16u << 16) : 0u), a,
+                     sw128_desc(vbase + hf * 4 * kColBytes + qq * 2 * kAtom, kColBytes, kAtom), kIdescPV,
+                     (j > 0 || qq > 0) ? 1u : 0u);
+        }
+        mma_commit(bar + kBarKEmpty + 8 * (j & 1));
+        mma_commit(bar + kBarPvDone);
+      }
+      if (!ok) set_abort(abort_flag, p.status);
+      mma_commit(bar + kBarDrain);  // every MMA issued here completes before the memory is freed
+      const uint64_t t0 = now_ns();
+      while (!mbar_test(bar + kBarDrain, 0)) {
+        if (now_ns() - t0 > kTimeoutNs) {
+          set_abort(abort_flag, p.status);
+          break;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------- loaders
+    const int lt = tid - 128;
+    const int32_t* pt_row = p.page_table + (int64_t)seq * p.pt_stride;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int b = j & 1;
+      int2* rt = rows_tab + b * 64;
+      // Resolve the 64 rows of this tile to (page, row-in-page); page -1 = no key.
+      if (lt < 64) {
+        int page = -1, off = 0;
+        if (p.idx) {
+          const int pos = j * kTile + lt;
+          if (pos < p.k) {
+            const int tok = __ldg(p.idx + (int64_t)qi * p.k + pos);
+            if (tok >= 0 && tok < len && (tok != 0 || pos == *first_zero)) {
+              const int pg = __ldg(pt_row + tok / kTile);
+              if (pg >= 0 && pg < p.pool.n_pages) {
+                page = pg;
+                off = tok % kTile;
+              } else {
+                set_status(p.status, RKV_ERR_INDEX_OUT_OF_RANGE);
+              }
+            }
+          }
+        } else {
+          const int pi = page0 + j;
+          const int pg = __ldg(pt_row + pi);
+          if (pi * kTile + lt < len) {
+            if (pg >= 0 && pg < p.pool.n_pages) {
+              page = pg;
+              off = lt;
+            } else if (lt == 0) {
+              set_status(p.status, RKV_ERR_INDEX_OUT_OF_RANGE);
+            }
+          }
+        }
+        rt[lt] = make_int2(page, off);
+        const unsigned vb = __ballot_sync(0xffffffffu, page >= 0);
+        if (lane == 0) reinterpret_cast<uint32_t*>(masks + b)[lt >> 5] = vb;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      // Issue every global load of the tile before touching shared memory.
+      const int cr = lt & 31;           // 16-code chunk of the latent row (lanes 16cr..16cr+15)
+      uint4 codes[16];
+      float scl[16];
+      uint4 rope[4];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int2 ro = rt[4 * i + (lt >> 5)];
+        if (ro.x >= 0) {
+          const uint8_t* pg = page_base(p.pool, p.layer, ro.x);
+          codes[i] = ld_stream16(pg + codes_off(ro.y) + cr * 16);
+          scl[i] = __ldg(reinterpret_cast<const float*>(pg + scales_off(ro.y)) + (cr >> 2));
+        } else {
+          codes[i] = make_uint4(0, 0, 0, 0);
+          scl[i] = 1.0f;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int2 ro = rt[16 * i + (lt >> 3)];
+        rope[i] = ro.x >= 0 ? ld_stream16(page_base(p.pool, p.layer, ro.x) + rope_off(ro.y) + (lt & 7) * 16)
+                            : make_uint4(0, 0, 0, 0);
+      }
+      const bool ok = j < 2 || mbar_wait(bar + kBarKEmpty + 8 * b, ((j >> 1) - 1) & 1, abort_flag);
+      if (!loaders_all(ok)) {
+        set_abort(abort_flag, p.status);
+        break;
+      }
+      uint8_t* stage = smem + kSmemK0 + b * kOperandBytes;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int r = 4 * i + (lt >> 5);
+        uint4 o0, o1;
+        dequant16(codes[i], decode_scale(scl[i]), o0, o1);
+        *reinterpret_cast<uint4*>(stage + sw_off(r, 2 * cr)) = o0;
+        *reinterpret_cast<uint4*>(stage + sw_off(r, 2 * cr + 1)) = o1;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = 16 * i + (lt >> 3);
+        *reinterpret_cast<uint4*>(stage + sw_off(r, 64 + (lt & 7))) = rope[i];
+      }
+      fence_proxy_async();
+      mbar_arrive(bar + kBarKFull + 8 * b);
+      // The row table of this stage is rewritten two tiles later, after the
+      // MMA has released the stage (kempty) -- every reader is done by then.
+    }
+  } else {
+    // ------------------------------------------------------------- softmax
+    const int h = warp * 16 + (lane & 15);
+    const bool owner = lane < 16;
+    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+    float m_ref = -INFINITY, l_sum = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int b = j & 1;
+      const bool got = mbar_wait(bar + kBarKFull + 8 * b, (j >> 1) & 1, abort_flag) &&
+                       mbar_wait(bar + kBarSFull + 8 * b, (j >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) {  // warp-uniform: the TMEM accesses below are warp-collective
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t s0[32], s1[32];
+      tmem_ld32(tl + kColS + 64 * b, s0);
+      tmem_ld32(tl + kColS + 64 * b + 32, s1);
+      tmem_wait_ld();
+      const uint64_t mask = masks[b];
+      float x[64];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        x[i] = ((mask >> i) & 1) ? __uint_as_float(s0[i]) * p.scale_log2 : -INFINITY;
+        x[32 + i] = ((mask >> (32 + i)) & 1) ? __uint_as_float(s1[i]) * p.scale_log2 : -INFINITY;
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) mx = fmaxf(mx, x[i]);
+      if (!owner) mx = -INFINITY;
+      float alpha = 1.0f;
+      bool rescale = false;
+      if (mx > -INFINITY && (m_ref == -INFINITY || mx > m_ref + kRescaleLog2)) {
+        alpha = m_ref == -INFINITY ? 0.0f : ex2(m_ref - mx);
+        rescale = m_ref != -INFINITY;
+        m_ref = mx;
+        l_sum *= alpha;
+      }
+      uint32_t pk[32];
+      float lt_sum = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float a = x[2 * i] > -INFINITY ? ex2(x[2 * i] - m_ref) : 0.0f;
+        const float c = x[2 * i + 1] > -INFINITY ? ex2(x[2 * i + 1] - m_ref) : 0.0f;
+        pk[i] = pack_bf16x2(a, c);
+        lt_sum += __uint_as_float(pk[i] << 16) + __uint_as_float(pk[i] & 0xffff0000u);
+      }
+      l_sum += lt_sum;
+      if (!__all_sync(0xffffffffu, j == 0 || mbar_wait(bar + kBarPvDone, (j - 1) & 1, abort_flag))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (__any_sync(0xffffffffu, rescale)) {
+        const float a_lane = __shfl_sync(0xffffffffu, rescale ? alpha : 1.0f, lane & 15);
+#pragma unroll 1
+        for (int c = 0; c < kV / 2; c += 32) {
+          uint32_t o[32];
+          tmem_ld32(tl + c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * a_lane);
+          tmem_st32(tl + c, o);
+        }
+        tmem_wait_st();
+      }
+      if (owner) {
+        uint8_t* prow = smem + kSmemP;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(prow + sw_off(h, c)) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(bar + kBarPFull);
+    }
+    if (ok && n_tiles > 0 &&
+        !__all_sync(0xffffffffu, mbar_wait(bar + kBarPvDone, (n_tiles - 1) & 1, abort_flag)))
+      ok = false;
+    if (!ok) set_abort(abort_flag, p.status);
+    tc_fence_after();
+    // Epilogue: lanes 0-15 hold latent 0-255 of head h, lanes 16-31 latent 256-511.
+    const float m_h = __shfl_sync(0xffffffffu, m_ref, lane & 15);
+    const float l_h = __shfl_sync(0xffffffffu, l_sum, lane & 15);
+    const int half = lane >> 4;
+    float oscale = 0.0f;
+    float* dst;
+    if (p.n_splits > 1) {
+      const int64_t slot = ((int64_t)qi * p.n_splits + split) * kHeads + h;
+      dst = p.ws_o + slot * kV + half * (kV / 2);
+      if (owner) {
+        p.ws_ml[2 * slot] = m_h;
+        p.ws_ml[2 * slot + 1] = l_h;
+      }
+      oscale = 1.0f;
+    } else {
+      dst = p.out + ((int64_t)qi * kHeads + h) * kV + half * (kV / 2);
+      const float sink = p.sinks ? p.sinks[h] * 1.4426950408889634f : -INFINITY;
+      const float M = fmaxf(m_h, sink);
+      if (M > -INFINITY && M < INFINITY) {
+        const float wo = m_h > -INFINITY ? ex2(m_h - M) : 0.0f;
+        const float den = l_h * wo + (sink > -INFINITY ? ex2(sink - M) : 0.0f);
+        if (den > 0.0f && den < INFINITY) oscale = wo / den;
+      }
+    }
+    const bool have_o = ok && n_tiles > 0;
+#pragma unroll 1
+    for (int c = 0; c < kV / 2; c += 32) {
+      uint32_t o[32];
+      if (have_o) {
+        tmem_ld32(tl + c, o);
+        tmem_wait_ld();
+      }
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (have_o)
+          v = make_float4(__uint_as_float(o[i]) * oscale, __uint_as_float(o[i + 1]) * oscale,
+                          __uint_as_float(o[i + 2]) * oscale, __uint_as_float(o[i + 3]) * oscale);
+        *reinterpret_cast<float4*>(dst + c + i) = v;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 8)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+}
+
+// Merges the split partials: per (query, head) the splits' (m, l, O) with the
+// sink, as one softmax (the same guards as the single-split epilogue).
+__global__ void __launch_bounds__(128) mla_combine_kernel(const float* __restrict__ ws_o,
+                                                          const float* __restrict__ ws_ml, int n_splits,
+                                                          const float* __restrict__ sinks, float* __restrict__ out) {
+  const int qi = blockIdx.y, h = blockIdx.x;
+  const float sink = sinks ? sinks[h] * 1.4426950408889634f : -INFINITY;
+  float M = sink;
+  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, ws_ml[2 * (((int64_t)qi * n_splits + s) * kHeads + h)]);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float den = 0.0f;
+  if (M > -INFINITY && M < INFINITY) {
+    den = sink > -INFINITY ? ex2(sink - M) : 0.0f;
+    for (int s = 0; s < n_splits; ++s) {
+      const int64_t slot = ((int64_t)qi * n_splits + s) * kHeads + h;
+      const float m = ws_ml[2 * slot];
+      if (!(m > -INFINITY)) continue;
+      const float w = ex2(m - M);
+      den += w * ws_ml[2 * slot + 1];
+      const float4 v = reinterpret_cast<const float4*>(ws_o + slot * kV)[threadIdx.x];
+      acc.x += w * v.x;
+      acc.y += w * v.y;
+      acc.z += w * v.z;
+      acc.w += w * v.w;
+    }
+  }
+  const float inv = (den > 0.0f && den < INFINITY) ? 1.0f / den : 0.0f;
+  reinterpret_cast<float4*>(out + ((int64_t)qi * kHeads + h) * kV)[threadIdx.x] =
+      make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+}
+
+}  // namespace mla
+}  // namespace rkv
+
+extern "C" int64_t rkv_mla_decode_workspace_bytes(int32_t n_q, int32_t n_splits) {
+  if (n_q < 0 || n_splits < 1) return -1;
+  if (n_splits == 1) return 0;
+  return (int64_t)n_q * n_splits * rkv::mla::kHeads * (rkv::mla::kV + 2) * 4;
+}
+
+extern "C" rkv_status rkv_mla_decode_fp8(const rkv_pool_view* pool, int32_t layer, const int32_t* page_table,
+                                         int64_t pt_stride, const int32_t* seq_lens, const int32_t* seq_of_query,
+                                         const uint16_t* q, int32_t n_q, const int32_t* idx, int32_t k,
+                                         const float* sinks, float softmax_scale, int32_t n_splits, void* workspace,
+                                         float* out, uint32_t* d_status, rkv_stream_t stream) {
+  using namespace rkv;
+  using namespace rkv::mla;
+  rkv_status st = check_pool(pool, "rkv_mla_decode_fp8");
+  if (st != RKV_OK) return st;
+  if (layer < 0 || layer >= pool->n_layers)
+    return fail(RKV_ERR_INVALID_LAYER, "rkv_mla_decode_fp8: layer %d outside pool of %d layers", layer,
+                pool->n_layers);
+  if (n_q < 0 || n_splits < 1 || n_splits > 65535 || pt_stride < 1 || (idx && (k < 0 || n_splits != 1)))
+    return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_mla_decode_fp8: n_q >= 0, pt_stride >= 1, 1 <= n_splits <= 65535 "
+                "(1 with an index list) and k >= 0 are required");
+  if (n_q == 0) {
+    clear_error();
+    return RKV_OK;
+  }
+  if (n_q > 65535) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_mla_decode_fp8: at most 65535 queries per call");
+  if (!page_table || !seq_lens || !seq_of_query || !q || !aligned(q, 16) || !out || !aligned(out, 16) ||
+      (n_splits > 1 && (!workspace || !aligned(workspace, 16))) || (idx && k > 0 && !aligned(idx, 4)))
+    return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_mla_decode_fp8: page_table, seq_lens, seq_of_query, q (16-byte "
+                "aligned), out (16-byte aligned) and, with n_splits > 1, workspace are required");
+  if (!std::isfinite(softmax_scale))
+    return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_mla_decode_fp8: softmax_scale must be finite");
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
+    if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_mla_decode_fp8: %s", cudaGetErrorString(e));
+    attr_set = true;
+  }
+  Params prm;
+  prm.pool = *pool;
+  prm.layer = layer;
+  prm.page_table = page_table;
+  prm.pt_stride = pt_stride;
+  prm.seq_lens = seq_lens;
+  prm.seq_of_query = seq_of_query;
+  prm.q = q;
+  prm.idx = idx;
+  prm.k = idx ? k : 0;
+  prm.sinks = sinks;
+  prm.scale_log2 = (float)((double)softmax_scale * 1.4426950408889634);
+  prm.n_splits = n_splits;
+  float* ws = static_cast<float*>(workspace);
+  prm.ws_o = ws;
+  prm.ws_ml = ws ? ws + (int64_t)n_q * n_splits * kHeads * kV : nullptr;
+  prm.out = out;
+  prm.status = d_status;
+  cudaStream_t s = (cudaStream_t)stream;
+  mla_decode_kernel<<<dim3(n_splits, n_q), kThreads, kSmemAlloc, s>>>(prm);
+  if (n_splits > 1) mla_combine_kernel<<<dim3(kHeads, n_q), 128, 0, s>>>(prm.ws_o, prm.ws_ml, n_splits, sinks, out);
+  return check_launch("rkv_mla_decode_fp8");
+}

@@ -218,6 +218,46 @@ class PagedKvPool:
                                                       idx.shape[1], _ptr(out), _ptr(self.status), _stream(stream)))
         return out
 
+    # -- attention read -------------------------------------------------------
+    def mla_decode(self, layer: int, q: torch.Tensor, page_table: torch.Tensor, seq_lens: torch.Tensor,
+                   seq_of_query: torch.Tensor, idx: torch.Tensor | None = None, sinks: torch.Tensor | None = None,
+                   softmax_scale: float | None = None, n_splits: int = 1, out: torch.Tensor | None = None,
+                   stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """MLA decode attention over the FP8 pages (see ``rkv_mla_decode_fp8``):
+        q bf16 [n_q, 64, 576] -> f32 [n_q, 64, 512]; every row of the query's
+        sequence (idx None) or the rows ``idx`` [n_q, k] selects.  The scale
+        defaults to 1/sqrt(576), as attention.rs:337 takes 1/sqrt(head_dim)."""
+        _need(q, torch.bfloat16, "q", self.device)
+        for t, n in ((page_table, "page_table"), (seq_lens, "seq_lens"), (seq_of_query, "seq_of_query")):
+            _need(t, torch.int32, n, self.device)
+        if q.dim() != 3 or q.shape[1:] != (64, ROW_DIM) or seq_of_query.shape != (q.shape[0],) or \
+                page_table.dim() != 2:
+            raise ShapeMismatch("mla_decode: q [n_q, 64, 576], seq_of_query [n_q], page_table [n_seq, stride]")
+        n_q = q.shape[0]
+        k = 0
+        if idx is not None:
+            _need(idx, torch.int32, "idx", self.device)
+            if idx.dim() != 2 or idx.shape[0] != n_q:
+                raise ShapeMismatch("mla_decode: idx must be [n_q, k]")
+            k = idx.shape[1]
+        if sinks is not None:
+            _need(sinks, torch.float32, "sinks", self.device)
+            if sinks.shape != (64,):
+                raise ShapeMismatch("mla_decode: sinks must be [64]")
+        if out is None:
+            out = torch.empty((n_q, 64, 512), dtype=torch.float32, device=self.device)
+        _need(out, torch.float32, "out", self.device)
+        ws = None
+        nbytes = self.lib.rkv_mla_decode_workspace_bytes(n_q, n_splits)
+        if nbytes > 0:
+            ws = torch.empty(nbytes // 4, dtype=torch.float32, device=self.device)
+        scale = softmax_scale if softmax_scale is not None else 1.0 / ROW_DIM ** 0.5
+        check(self.lib.rkv_mla_decode_fp8(byref(self.view), layer, _ptr(page_table), page_table.shape[1],
+                                          _ptr(seq_lens), _ptr(seq_of_query), _ptr(q), n_q, _ptr(idx), k,
+                                          _ptr(sinks), float(scale), n_splits, _ptr(ws), _ptr(out),
+                                          _ptr(self.status), _stream(stream)))
+        return out
+
     # -- page moves -----------------------------------------------------------
     def copy_pages(self, src: torch.Tensor, dst: torch.Tensor, stream: torch.cuda.Stream | None = None) -> None:
         """Every layer: page dst[i] <- page src[i] (disjoint sets)."""
