@@ -389,9 +389,78 @@ def bench_gather(args, dist: Dist, dev, peak) -> dict:
            "frac_of_hbm_peak": None, "kernel_ms_per_layer": one,
            "launches_per_step": n_layers}
     res["frac_of_hbm_peak"] = res["gbs_per_gpu"] / peak
-    del pool, out
+    del out
     torch.cuda.empty_cache()
-    return res
+    seq_lens = torch.full((n_seq,), ctx, dtype=torch.int32, device=dev)
+    res_mla = bench_mla(args, dist, pool, pt, seq_lens, torch.arange(n_seq, dtype=torch.int32, device=dev), None,
+                        n_layers, l_phys, stream, peak,
+                        f"c3 shape: {n_seq} decode queries (one per sequence) x {ctx} rows x {n_layers} layers",
+                        n_splits=args.mla_splits)
+    del pool
+    torch.cuda.empty_cache()
+    return res, res_mla
+
+
+def mla_flops_bytes(n_q: int, n_keys: int, with_index: bool) -> tuple[float, float]:
+    """Algorithmic FLOPs and HBM bytes of one MLA decode launch over n_keys
+    (query, key) pairs in total: 64 heads x
+    (576 + 512) MACs per (query, key); each key row read once in its stored
+    form (672 B, plus its 4 B page-table entry, plus its 4 B index when an
+    index list selects it), q in bf16, the f32 output."""
+    flops = 2.0 * n_keys * 64 * (576 + 512)
+    per_key = 672 + (8 if with_index else 4.0 / 64)
+    return flops, n_keys * per_key + n_q * (64 * 576 * 2 + 64 * 512 * 4)
+
+
+def bench_mla(args, dist: Dist, pool, pt, seq_lens, seq_of_query, idx, n_layers: int, l_phys: int, stream, peak,
+              config: str, n_splits: int = 1) -> dict:
+    """MLA decode attention over the FP8 pages (rkv_mla_decode_fp8), one launch
+    per layer; idx None = every row of each query's sequence."""
+    dev = pt.device
+    n_q = seq_of_query.numel()
+    g = torch.Generator(device=dev)
+    g.manual_seed(900 + 7919 * dist.rank)
+    q = torch.randn((n_q, 64, 576), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    out = torch.empty((n_q, 64, 512), dtype=torch.float32, device=dev)
+    import rsllm_b200 as rk
+
+    nbytes = rk._abi.load().rkv_mla_decode_workspace_bytes(n_q, n_splits)
+    ws = torch.empty(max(1, nbytes // 4), dtype=torch.float32, device=dev)
+    sinks = torch.zeros(64, dtype=torch.float32, device=dev)
+
+    def one(layer):
+        pool.mla_decode(layer % l_phys, q, pt, seq_lens, seq_of_query, None if idx is None else idx[layer], sinks,
+                        None, n_splits, out=out, workspace=ws, stream=stream)
+
+    def step():
+        for layer in range(n_layers):
+            one(layer)
+
+    for _ in range(args.phase_warmup):
+        step()
+    pool.check("mla", stream)
+    dist.barrier()
+    ms = dist.max(events_time(lambda: [step() for _ in range(args.phase_steps)], stream))
+    pool.check("mla", stream)
+    kernel_ms = events_time(lambda: one(0), stream)
+    if idx is None:
+        n_keys = int(seq_lens[seq_of_query.long()].sum().item())
+    else:
+        n_keys = int(idx.shape[1] * idx.shape[2])
+    flops, nbytes_alg = mla_flops_bytes(n_q, n_keys, idx is not None)
+    peaks_all = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() \
+        else {"bf16_tflops_sustained": 1400.0}
+    tc_peak = float(peaks_all.get("bf16_tflops_sustained", 1400.0))
+    t_layer = ms / args.phase_steps / n_layers * 1e-3
+    t_ideal = max(nbytes_alg / (peak * GB), flops / (tc_peak * 1e12))
+    return {"config": config, "layers_backed": l_phys, "n_splits": n_splits,
+            "ms_per_step": ms / args.phase_steps, "kernel_ms_per_layer": kernel_ms,
+            "gbs_per_gpu": nbytes_alg / t_layer / GB, "tflops_per_gpu": flops / t_layer / 1e12,
+            "frac_of_hbm_peak": nbytes_alg / t_layer / GB / peak,
+            "frac_of_tensor_peak_sustained": flops / t_layer / 1e12 / tc_peak,
+            "roofline_frac": t_ideal / t_layer,
+            "roofline_bound": "hbm" if nbytes_alg / (peak * GB) >= flops / (tc_peak * 1e12) else "tensor",
+            "algorithmic_bytes_per_launch": nbytes_alg, "flops_per_launch": flops}
 
 
 def bench_sparse(args, dist: Dist, dev, peak) -> dict:
@@ -467,7 +536,12 @@ def bench_sparse(args, dist: Dist, dev, peak) -> dict:
                           "frac_of_hbm_peak": sparse_bytes * P / (ms_sparse * 1e-3) / GB / peak,
                           "kernel_ms_per_layer": one_sparse},
     }
-    del pool, out, scores, idx
+    del out, scores
+    torch.cuda.empty_cache()
+    res["mla_decode_sparse"] = bench_mla(
+        args, dist, pool, pt, seq_lens, seq_of_query, idx, n_layers, l_phys, stream, peak,
+        f"c4 shape: {n_q} queries x 2048 top-k rows (the indices above) x {n_layers} layers")
+    del pool, idx
     torch.cuda.empty_cache()
     return res
 
@@ -683,6 +757,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--only", choices=["all", "append", "gather", "sparse", "prefix"], default="all",
                     help="run one workload alone (profiling)")
+    ap.add_argument("--mla-splits", type=int, default=32,
+                    help="page-range splits per query for the dense MLA decode phase")
     ap.add_argument("--small", action="store_true",
                     help="profiling sizes for the phases: 8 seqs / 1 layer (gather), 4 seqs / 1 layer (sparse)")
     args = ap.parse_args()
@@ -708,7 +784,8 @@ def main():
             res = bench_append(args, dist, dev, peak)
             res = {k: v for k, v in res.items() if k not in ("pool", "wl")}
         elif args.only == "gather":
-            res = bench_gather(args, dist, dev, peak)
+            g, m = bench_gather(args, dist, dev, peak)
+            res = {"gather": g, "mla_decode_dense": m}
         elif args.only == "prefix":
             res = bench_prefix(args, dist, dev, peak)
         else:
@@ -723,7 +800,7 @@ def main():
     phases = {}
     wanted = [] if args.phases == "none" else args.phases.split(",")
     if "gather" in wanted:
-        phases["gather"] = bench_gather(args, dist, dev, peak)
+        phases["gather"], phases["mla_decode_dense"] = bench_gather(args, dist, dev, peak)
     if "sparse" in wanted:
         phases.update(bench_sparse(args, dist, dev, peak))
     if "prefix" in wanted:

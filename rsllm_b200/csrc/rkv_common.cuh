@@ -208,6 +208,13 @@ __device__ __forceinline__ void st_stream32(void* p, const uint4& a, const uint4
                :: "l"(p), "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
                : "memory");
 }
+// 256-bit load through L1 (data several lanes of a warp share, e.g. a row's
+// scales).
+__device__ __forceinline__ void ld_cached32(const void* p, uint32_t (&v)[8]) {
+  asm volatile("ld.global.nc.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "l"(p));
+}
 // Streaming data is touched once: keep it out of L1 so the page tables and
 // indices stay cached there.
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {

@@ -9,29 +9,38 @@
 //   list selects (the sparse mask of attention.rs:548-556).
 //
 // The FP8 rows are never written back as bf16: loader warps read a page's
-// codes, scales and RoPE lanes, dequantise them (exactly, see rkv_common.cuh)
-// straight into a 128-byte-swizzled shared-memory tile, and the 5th-generation
-// tensor cores consume that tile twice -- as K (K-major) for S and as V
-// (MN-major) for O -- with both accumulators in tensor memory:
+// codes, scales and RoPE lanes with 256-bit loads, dequantise them (exactly,
+// see rkv_common.cuh) straight into a 128-byte-swizzled shared-memory tile,
+// and the 5th-generation tensor cores consume that tile twice -- as K
+// (K-major) for S and as V (MN-major) for O:
 //
 //   warps 0-3  softmax: S from TMEM, online max / exp2 / row sums per head,
-//              P (bf16) to shared memory, lazy rescale of O in TMEM, epilogue
-//   warps 4-7  loaders: pages -> registers -> dequant -> swizzled K/V tile
-//   warp 8     TMEM allocation and the single MMA-issuing thread
+//              P (bf16) into shared memory, the rare lazy rescale of O,
+//              epilogue
+//   warps 4-11 loaders, software-pipelined over two register buffers: the
+//              loads of tile j + 1 are in flight while tile j is
+//              dequantised into its swizzled K/V stage
+//   warp 12    TMEM allocation and the MMA-issuing thread: issues S = Q K^T
+//              for every loaded tile and O += P V for every softmaxed tile
+//              as each becomes ready
 //
 // Shapes per tile (64 key rows, one page in dense mode), M = 64 heads:
-//   S[64 x 64]   = Q[64 x 576] . K^T    36 MMAs of K = 16 (N = 64)
-//   O[64 x 512] += P[64 x 64]  . V      2 x 4 MMAs of N = 256
-// TMEM (512 columns): O lanes 0-15 (+32k) cols 0-255 = latent 0-255,
-// O lanes 16-31 (+32k) cols 0-255 = latent 256-511 (the M = 64 accumulator
-// occupies half of each 32-lane sub-partition), S double-buffered at columns
-// 256 and 320.  Head h lives in TMEM lane (h % 16) + 32 (h / 16).
+//   S[64 x 64]   = Q[64 x 576] . K^T    36 MMAs of K = 16 (N = 64), Q and K
+//                                       from shared memory
+//   O[64 x 512] += P[64 x 64]  . V      2 x 4 MMAs of N = 256, P from smem
+// TMEM (512 columns): O lanes 0-15 (+32k) cols 0-255 = latent 0-255, O lanes
+// 16-31 (+32k) cols 0-255 = latent 256-511 (an M = 64 accumulator occupies
+// half of each 32-lane sub-partition; the second one interleaves in the other
+// half, which needs both operands in shared memory), S double-buffered at
+// columns 256 and 320.  Head h lives in TMEM lane (h % 16) + 32 (h / 16).
 //
-// The online softmax keeps a per-head reference maximum m and rescales O only
-// when a tile's maximum exceeds it by more than 2^8 (P values stay <= 256 in
-// bf16); the final normalisation uses the same m, so the result is the same
-// softmax.  The denominator is the sum of the bf16-rounded P that the tensor
-// core multiplies, plus the sink's exp.
+// Two K/V stages and two S buffers let the exp of tile j overlap the O update
+// of tile j-1 and the S of tile j+1 (shared memory holds Q, two stages and
+// one P).  The online softmax keeps a per-head reference maximum m and
+// rescales O only when a tile's maximum exceeds it by more than 2^8 (P values
+// stay <= 256 in bf16).  The final normalisation uses the same m, so the
+// result is the same softmax; the denominator is the sum of the bf16-rounded
+// P the tensor core multiplies, plus the sink's exp.
 //
 // Every wait on a barrier is bounded (1 s of %globaltimer); on a timeout the
 // CTA records RKV_ERR_CUDA in the status word, drains its own MMAs, frees its
@@ -53,20 +62,23 @@ constexpr int kColBytes = 8 * kAtom;          // one 64-lane column of a 64-row 
 constexpr int kOperandBytes = (kQk / 64) * kColBytes;  // 73728: 64 rows x 576 bf16
 constexpr int kSmemQ = 0;
 constexpr int kSmemK0 = kSmemQ + kOperandBytes;
-constexpr int kSmemP = kSmemK0 + 2 * kOperandBytes;
+constexpr int kSmemP = kSmemK0 + 2 * kOperandBytes;  // P: 64 heads x 64 keys bf16
 constexpr int kSmemBar = kSmemP + kColBytes;
-constexpr int kSmemRows = kSmemBar + 128;     // sparse row table: 2 stages x 64 x (page, off)
+constexpr int kSmemRows = kSmemBar + 128;     // row tables: 2 x 64 x (page, row in page)
 constexpr int kSmemTotal = kSmemRows + 2 * 64 * 8;
 constexpr int kSmemAlloc = kSmemTotal + 1024; // slack for the 1024-byte alignment
-constexpr int kThreads = 288;
+constexpr int kThreads = 416;                 // warps 0-3 softmax, 4-11 loaders, 12 MMA
+constexpr int kLoaders = 256;
+constexpr int kMmaWarp = 12;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 256;               // S buffers at 256 and 320
 constexpr float kRescaleLog2 = 8.0f;
 constexpr uint64_t kTimeoutNs = 1000000000ull;
 
-// Barrier / state offsets inside the kSmemBar block.
+// Barrier / state offsets inside the kSmemBar block (the stage and S barrier
+// pairs are indexed by j & 1; key masks by j & 3).
 constexpr int kBarKFull = 0, kBarKEmpty = 16, kBarSFull = 32, kBarPFull = 48, kBarPvDone = 56, kBarDrain = 64;
-constexpr int kTmemSlot = 72, kAbort = 76, kMask = 80, kFirstZero = 96;
+constexpr int kTmemSlot = 72, kAbort = 76, kFirstZero = 80, kMask = 96;
 
 constexpr uint32_t kIdescQK = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((64u >> 4) << 24);
 constexpr uint32_t kIdescPV = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((256u >> 3) << 17) | ((64u >> 4) << 24);
@@ -102,18 +114,6 @@ __device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_fla
     if (now_ns() - t0 > kTimeoutNs) return false;
   }
   return true;
-}
-
-// Named barrier over the 128 loader threads that also ANDs a predicate, so
-// that every loader takes the same branch after a bounded wait.
-__device__ __forceinline__ bool loaders_all(bool ok) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 2, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)ok)
-      : "memory");
-  return r != 0;
 }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -201,6 +201,27 @@ __device__ __forceinline__ void set_abort(volatile int* abort_flag, uint32_t* st
   set_status(status, RKV_ERR_CUDA);
 }
 
+__device__ __forceinline__ bool mbar_ready(uint32_t bar, uint32_t parity) {  // non-blocking test
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Named-barrier reductions that keep a role's branches uniform after bounded
+// waits: id 1 over the 128 softmax threads, id 2 over the 256 loaders.
+__device__ __forceinline__ bool bar_all(int id, int n, bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)ok), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
 __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // 1024-byte aligned atoms
@@ -228,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
 
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
-      mbar_init(bar + kBarKFull + 8 * i, 128);
+      mbar_init(bar + kBarKFull + 8 * i, kLoaders);
       mbar_init(bar + kBarKEmpty + 8 * i, 1);
       mbar_init(bar + kBarSFull + 8 * i, 1);
     }
@@ -239,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
     *first_zero = 0x7fffffff;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 8) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kTmemCols)
                  : "memory");
@@ -254,10 +275,10 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
     }
   }
   __syncthreads();
-  if (p.idx && warp >= 4 && warp < 8) {  // the first position holding index 0 (later zeros repeat it)
+  if (p.idx && warp >= 4 && warp < kMmaWarp) {  // the first position holding index 0 (later zeros repeat it)
     const int32_t* il = p.idx + (int64_t)qi * p.k;
     int fz = 0x7fffffff;
-    for (int i = tid - 128; i < p.k; i += 128)
+    for (int i = tid - 128; i < p.k; i += kLoaders)
       if (__ldg(il + i) == 0) {
         fz = i;
         break;
@@ -270,49 +291,65 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
+  if (warp == kMmaWarp) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0 && n_tiles > 0) {
       bool ok = true;
-      auto issue_qk = [&](int j) {
-        const int b = j & 1;
-        const uint32_t kbase = sbase + kSmemK0 + b * kOperandBytes;
-        const uint32_t d = tmem + kColS + 64 * b;
-#pragma unroll 4
-        for (int s = 0; s < kQk / 16; ++s) {
-          const uint32_t off = (s >> 2) * kColBytes + (s & 3) * 32;
-          mma_bf16(d, sw128_desc(sbase + kSmemQ + off, 16, kAtom), sw128_desc(kbase + off, 16, kAtom), kIdescQK,
-                   s > 0);
-        }
-        mma_commit(bar + kBarSFull + 8 * b);
-      };
-      ok = mbar_wait(bar + kBarKFull, 0, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        issue_qk(0);
-      }
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        if (j + 1 < n_tiles) {
-          ok = mbar_wait(bar + kBarKFull + 8 * ((j + 1) & 1), ((j + 1) >> 1) & 1, abort_flag);
-          if (!ok) break;
+      int nq = 0, np = 0;  // next tile to issue S for / O update for
+      uint64_t t_last = now_ns();
+      uint32_t idle = 0;
+      while (np < n_tiles) {
+        bool progressed = false;
+        // S of tile nq once its stage is loaded and its S buffer was read
+        // (the softmax of tile nq - 2 handed over its P: np >= nq - 1).
+        if (nq < n_tiles && nq <= np + 1 && mbar_ready(bar + kBarKFull + 8 * (nq & 1), (nq >> 1) & 1)) {
           tc_fence_after();
-          issue_qk(j + 1);
+          const int b = nq & 1;
+          const uint32_t kbase = sbase + kSmemK0 + b * kOperandBytes;
+          const uint32_t d = tmem + kColS + 64 * b;
+#pragma unroll 4
+          for (int s = 0; s < kQk / 16; ++s) {
+            const uint32_t off = (s >> 2) * kColBytes + (s & 3) * 32;
+            mma_bf16(d, sw128_desc(sbase + kSmemQ + off, 16, kAtom), sw128_desc(kbase + off, 16, kAtom), kIdescQK,
+                     s > 0);
+          }
+          mma_commit(bar + kBarSFull + 8 * b);
+          ++nq;
+          progressed = true;
         }
-        ok = mbar_wait(bar + kBarPFull, j & 1, abort_flag);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t vbase = sbase + kSmemK0 + (j & 1) * kOperandBytes;
+        // O += P V of tile np once its P is in shared memory.
+        if (np < nq && mbar_ready(bar + kBarPFull, np & 1)) {
+          tc_fence_after();
+          const int b = np & 1;
+          const uint32_t vbase = sbase + kSmemK0 + b * kOperandBytes;
 #pragma unroll
-        for (int qq = 0; qq < kTile / 16; ++qq) {
-          const uint64_t a = sw128_desc(sbase + kSmemP + qq * 32, 16, kAtom);
+          for (int qq = 0; qq < kTile / 16; ++qq) {
+            const uint64_t a = sw128_desc(sbase + kSmemP + qq * 32, 16, kAtom);
 #pragma unroll
-          for (int hf = 0; hf < 2; ++hf)
-            mma_bf16(tmem + (hf ? (16u << 16) : 0u), a,
-                     sw128_desc(vbase + hf * 4 * kColBytes + qq * 2 * kAtom, kColBytes, kAtom), kIdescPV,
-                     (j > 0 || qq > 0) ? 1u : 0u);
+            for (int hf = 0; hf < 2; ++hf)
+              mma_bf16(tmem + (hf ? (16u << 16) : 0u), a,
+                       sw128_desc(vbase + hf * 4 * kColBytes + qq * 2 * kAtom, kColBytes, kAtom), kIdescPV,
+                       (np > 0 || qq > 0) ? 1u : 0u);
+          }
+          mma_commit(bar + kBarKEmpty + 8 * b);
+          mma_commit(bar + kBarPvDone);
+          ++np;
+          progressed = true;
         }
-        mma_commit(bar + kBarKEmpty + 8 * (j & 1));
-        mma_commit(bar + kBarPvDone);
+        if (progressed) {
+          idle = 0;
+        } else if ((++idle & 255u) == 0) {
+          if (*abort_flag) {
+            ok = false;
+            break;
+          }
+          const uint64_t t = now_ns();
+          if (idle == 256) t_last = t;
+          else if (t - t_last > kTimeoutNs) {
+            ok = false;
+            break;
+          }
+        }
       }
       if (!ok) set_abort(abort_flag, p.status);
       mma_commit(bar + kBarDrain);  // every MMA issued here completes before the memory is freed
@@ -327,91 +364,119 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------- loaders
-    const int lt = tid - 128;
+    // 256 threads per tile: lane (r8 = lane / 4, q = lane % 4) of loader warp
+    // lw takes row 8 lw + r8: codes [128 s + 32 q, +32) for s = 0..3, the
+    // row's 8 scales and RoPE bytes [32 q, +32), all as 256-bit loads.  The
+    // rows of tile j are resolved two tiles ahead into table j & 1 and key
+    // mask j & 3; the loads of tile j + 1 are issued before tile j is stored.
+    const int lt = tid - 128, lw = lt >> 5;
+    const int r = 8 * lw + (lane >> 2);
     const int32_t* pt_row = p.page_table + (int64_t)seq * p.pt_stride;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int b = j & 1;
-      int2* rt = rows_tab + b * 64;
-      // Resolve the 64 rows of this tile to (page, row-in-page); page -1 = no key.
-      if (lt < 64) {
-        int page = -1, off = 0;
-        if (p.idx) {
-          const int pos = j * kTile + lt;
-          if (pos < p.k) {
-            const int tok = __ldg(p.idx + (int64_t)qi * p.k + pos);
-            if (tok >= 0 && tok < len && (tok != 0 || pos == *first_zero)) {
-              const int pg = __ldg(pt_row + tok / kTile);
-              if (pg >= 0 && pg < p.pool.n_pages) {
-                page = pg;
-                off = tok % kTile;
-              } else {
-                set_status(p.status, RKV_ERR_INDEX_OUT_OF_RANGE);
-              }
-            }
-          }
-        } else {
-          const int pi = page0 + j;
-          const int pg = __ldg(pt_row + pi);
-          if (pi * kTile + lt < len) {
+    auto resolve = [&](int j) {
+      if (lt >= 64) return;
+      int page = -1, off = 0;
+      if (p.idx) {
+        const int pos = j * kTile + lt;
+        if (pos < p.k) {
+          const int tok = __ldg(p.idx + (int64_t)qi * p.k + pos);
+          if (tok >= 0 && tok < len && (tok != 0 || pos == *first_zero)) {
+            const int pg = __ldg(pt_row + tok / kTile);
             if (pg >= 0 && pg < p.pool.n_pages) {
               page = pg;
-              off = lt;
-            } else if (lt == 0) {
+              off = tok % kTile;
+            } else {
               set_status(p.status, RKV_ERR_INDEX_OUT_OF_RANGE);
             }
           }
         }
-        rt[lt] = make_int2(page, off);
-        const unsigned vb = __ballot_sync(0xffffffffu, page >= 0);
-        if (lane == 0) reinterpret_cast<uint32_t*>(masks + b)[lt >> 5] = vb;
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      // Issue every global load of the tile before touching shared memory.
-      const int cr = lt & 31;           // 16-code chunk of the latent row (lanes 16cr..16cr+15)
-      uint4 codes[16];
-      float scl[16];
-      uint4 rope[4];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int2 ro = rt[4 * i + (lt >> 5)];
-        if (ro.x >= 0) {
-          const uint8_t* pg = page_base(p.pool, p.layer, ro.x);
-          codes[i] = ld_stream16(pg + codes_off(ro.y) + cr * 16);
-          scl[i] = __ldg(reinterpret_cast<const float*>(pg + scales_off(ro.y)) + (cr >> 2));
-        } else {
-          codes[i] = make_uint4(0, 0, 0, 0);
-          scl[i] = 1.0f;
+      } else {
+        const int pi = page0 + j;
+        if (pi * kTile + lt < len) {
+          const int pg = __ldg(pt_row + pi);
+          if (pg >= 0 && pg < p.pool.n_pages) {
+            page = pg;
+            off = lt;
+          } else if (lt == 0) {
+            set_status(p.status, RKV_ERR_INDEX_OUT_OF_RANGE);
+          }
         }
       }
+      rows_tab[(j & 1) * 64 + lt] = make_int2(page, off);
+      const unsigned vb = __ballot_sync(0xffffffffu, page >= 0);
+      if (lane == 0) reinterpret_cast<uint32_t*>(masks + (j & 3))[lw] = vb;
+    };
+    struct TileRegs {
+      uint32_t codes[4][8], scl[8], rope[8];
+    };
+    auto load = [&](int j, TileRegs& t) {
+      const int2 ro = rows_tab[(j & 1) * 64 + r];
+      if (ro.x >= 0) {
+        const uint8_t* pg = page_base(p.pool, p.layer, ro.x);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int2 ro = rt[16 * i + (lt >> 3)];
-        rope[i] = ro.x >= 0 ? ld_stream16(page_base(p.pool, p.layer, ro.x) + rope_off(ro.y) + (lt & 7) * 16)
-                            : make_uint4(0, 0, 0, 0);
+        for (int sg = 0; sg < 4; ++sg) ld_stream32(pg + codes_off(ro.y) + sg * 128 + (lane & 3) * 32, t.codes[sg]);
+        ld_cached32(pg + scales_off(ro.y), t.scl);
+        ld_stream32(pg + rope_off(ro.y) + (lane & 3) * 32, t.rope);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+#pragma unroll
+          for (int sg = 0; sg < 4; ++sg) t.codes[sg][i] = 0u;
+          t.scl[i] = 0x3f800000u;
+          t.rope[i] = 0u;
+        }
       }
+    };
+    // Waits for the stage (the O update two tiles back), then dequantises.
+    // Per store instruction the warp writes 8 rows x 4 lanes of 16 B whose
+    // swizzled positions cover the 8 bank groups evenly (4 wavefronts for
+    // 512 B, the minimum).  Returns false on a timeout or abort.
+    auto store = [&](int j, const TileRegs& t) -> bool {
+      const int b = j & 1;
       const bool ok = j < 2 || mbar_wait(bar + kBarKEmpty + 8 * b, ((j >> 1) - 1) & 1, abort_flag);
-      if (!loaders_all(ok)) {
+      if (!bar_all(2, kLoaders, ok)) return false;  // also orders the table and mask accesses
+      uint8_t* stage = smem + kSmemK0 + b * kOperandBytes;
+#pragma unroll
+      for (int sg = 0; sg < 4; ++sg) {
+        const DecodeScale ds = decode_scale(__uint_as_float((lane & 2) ? t.scl[2 * sg + 1] : t.scl[2 * sg]));
+        const int c0 = 8 * (2 * sg + ((lane & 3) >> 1)) + 4 * (lane & 1);
+        uint4 o0, o1, o2, o3;
+        dequant16(make_uint4(t.codes[sg][0], t.codes[sg][1], t.codes[sg][2], t.codes[sg][3]), ds, o0, o1);
+        dequant16(make_uint4(t.codes[sg][4], t.codes[sg][5], t.codes[sg][6], t.codes[sg][7]), ds, o2, o3);
+        *reinterpret_cast<uint4*>(stage + sw_off(r, c0)) = o0;
+        *reinterpret_cast<uint4*>(stage + sw_off(r, c0 + 1)) = o1;
+        *reinterpret_cast<uint4*>(stage + sw_off(r, c0 + 2)) = o2;
+        *reinterpret_cast<uint4*>(stage + sw_off(r, c0 + 3)) = o3;
+      }
+      *reinterpret_cast<uint4*>(stage + sw_off(r, 64 + 2 * (lane & 3))) =
+          make_uint4(t.rope[0], t.rope[1], t.rope[2], t.rope[3]);
+      *reinterpret_cast<uint4*>(stage + sw_off(r, 64 + 2 * (lane & 3) + 1)) =
+          make_uint4(t.rope[4], t.rope[5], t.rope[6], t.rope[7]);
+      fence_proxy_async();
+      mbar_arrive(bar + kBarKFull + 8 * b);
+      return true;
+    };
+    TileRegs ta, tb;
+    if (n_tiles > 0) resolve(0);
+    if (n_tiles > 1) resolve(1);
+    asm volatile("bar.sync 2, 256;" ::: "memory");
+    if (n_tiles > 0) load(0, ta);
+    for (int j = 0; j < n_tiles; j += 2) {
+      // tile j is in ta
+      if (j + 1 < n_tiles) load(j + 1, tb);
+      bool ok = store(j, ta);  // its barrier orders every read of table j & 1 before the next write
+      if (ok && j + 2 < n_tiles) resolve(j + 2);
+      if (ok && j + 1 < n_tiles) {
+        // tile j + 1 is in tb; table j & 1 now holds tile j + 2
+        asm volatile("bar.sync 2, 256;" ::: "memory");
+        if (j + 2 < n_tiles) load(j + 2, ta);
+        ok = store(j + 1, tb);
+        if (ok && j + 3 < n_tiles) resolve(j + 3);
+        if (ok) asm volatile("bar.sync 2, 256;" ::: "memory");
+      }
+      if (!ok) {
         set_abort(abort_flag, p.status);
         break;
       }
-      uint8_t* stage = smem + kSmemK0 + b * kOperandBytes;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int r = 4 * i + (lt >> 5);
-        uint4 o0, o1;
-        dequant16(codes[i], decode_scale(scl[i]), o0, o1);
-        *reinterpret_cast<uint4*>(stage + sw_off(r, 2 * cr)) = o0;
-        *reinterpret_cast<uint4*>(stage + sw_off(r, 2 * cr + 1)) = o1;
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = 16 * i + (lt >> 3);
-        *reinterpret_cast<uint4*>(stage + sw_off(r, 64 + (lt & 7))) = rope[i];
-      }
-      fence_proxy_async();
-      mbar_arrive(bar + kBarKFull + 8 * b);
-      // The row table of this stage is rewritten two tiles later, after the
-      // MMA has released the stage (kempty) -- every reader is done by then.
     }
   } else {
     // ------------------------------------------------------------- softmax
@@ -424,25 +489,27 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
       const int b = j & 1;
       const bool got = mbar_wait(bar + kBarKFull + 8 * b, (j >> 1) & 1, abort_flag) &&
                        mbar_wait(bar + kBarSFull + 8 * b, (j >> 1) & 1, abort_flag);
-      if (!__all_sync(0xffffffffu, got)) {  // warp-uniform: the TMEM accesses below are warp-collective
+      if (!bar_all(1, 128, got)) {  // uniform over the four warps: TMEM accesses and barriers follow
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t s0[32], s1[32];
-      tmem_ld32(tl + kColS + 64 * b, s0);
-      tmem_ld32(tl + kColS + 64 * b + 32, s1);
-      tmem_wait_ld();
-      const uint64_t mask = masks[b];
-      float x[64];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        x[i] = ((mask >> i) & 1) ? __uint_as_float(s0[i]) * p.scale_log2 : -INFINITY;
-        x[32 + i] = ((mask >> (32 + i)) & 1) ? __uint_as_float(s1[i]) * p.scale_log2 : -INFINITY;
+      uint32_t sv[64];
+      {
+        uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[0]);
+        uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[32]);
+        tmem_ld32(tl + kColS + 64 * b, s0);
+        tmem_ld32(tl + kColS + 64 * b + 32, s1);
       }
+      tmem_wait_ld();
+      const uint64_t mask = masks[j & 3];
       float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) mx = fmaxf(mx, x[i]);
+      for (int i = 0; i < 64; ++i) {
+        const float x = ((mask >> i) & 1) ? __uint_as_float(sv[i]) * p.scale_log2 : -INFINITY;
+        sv[i] = __float_as_uint(x);
+        mx = fmaxf(mx, x);
+      }
       if (!owner) mx = -INFINITY;
       float alpha = 1.0f;
       bool rescale = false;
@@ -456,13 +523,15 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
       float lt_sum = 0.0f;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float a = x[2 * i] > -INFINITY ? ex2(x[2 * i] - m_ref) : 0.0f;
-        const float c = x[2 * i + 1] > -INFINITY ? ex2(x[2 * i + 1] - m_ref) : 0.0f;
+        const float x0 = __uint_as_float(sv[2 * i]), x1 = __uint_as_float(sv[2 * i + 1]);
+        const float a = x0 > -INFINITY ? ex2(x0 - m_ref) : 0.0f;
+        const float c = x1 > -INFINITY ? ex2(x1 - m_ref) : 0.0f;
         pk[i] = pack_bf16x2(a, c);
         lt_sum += __uint_as_float(pk[i] << 16) + __uint_as_float(pk[i] & 0xffff0000u);
       }
       l_sum += lt_sum;
-      if (!__all_sync(0xffffffffu, j == 0 || mbar_wait(bar + kBarPvDone, (j - 1) & 1, abort_flag))) {
+      // P and O are free once the O update of tile j - 1 is done.
+      if (!bar_all(1, 128, j == 0 || mbar_wait(bar + kBarPvDone, (j - 1) & 1, abort_flag))) {
         ok = false;
         break;
       }
@@ -490,9 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
       tc_fence_before();
       mbar_arrive(bar + kBarPFull);
     }
-    if (ok && n_tiles > 0 &&
-        !__all_sync(0xffffffffu, mbar_wait(bar + kBarPvDone, (n_tiles - 1) & 1, abort_flag)))
-      ok = false;
+    if (ok && n_tiles > 0 && !bar_all(1, 128, mbar_wait(bar + kBarPvDone, (n_tiles - 1) & 1, abort_flag))) ok = false;
     if (!ok) set_abort(abort_flag, p.status);
     tc_fence_after();
     // Epilogue: lanes 0-15 hold latent 0-255 of head h, lanes 16-31 latent 256-511.
@@ -540,7 +607,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 8)
+  if (warp == kMmaWarp)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
 }
 

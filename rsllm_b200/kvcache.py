@@ -222,7 +222,7 @@ class PagedKvPool:
     def mla_decode(self, layer: int, q: torch.Tensor, page_table: torch.Tensor, seq_lens: torch.Tensor,
                    seq_of_query: torch.Tensor, idx: torch.Tensor | None = None, sinks: torch.Tensor | None = None,
                    softmax_scale: float | None = None, n_splits: int = 1, out: torch.Tensor | None = None,
-                   stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+                   workspace: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """MLA decode attention over the FP8 pages (see ``rkv_mla_decode_fp8``):
         q bf16 [n_q, 64, 576] -> f32 [n_q, 64, 512]; every row of the query's
         sequence (idx None) or the rows ``idx`` [n_q, k] selects.  The scale
@@ -250,7 +250,10 @@ class PagedKvPool:
         ws = None
         nbytes = self.lib.rkv_mla_decode_workspace_bytes(n_q, n_splits)
         if nbytes > 0:
-            ws = torch.empty(nbytes // 4, dtype=torch.float32, device=self.device)
+            if workspace is not None and workspace.is_cuda and workspace.numel() * workspace.element_size() >= nbytes:
+                ws = workspace
+            else:
+                ws = torch.empty(nbytes // 4, dtype=torch.float32, device=self.device)
         scale = softmax_scale if softmax_scale is not None else 1.0 / ROW_DIM ** 0.5
         check(self.lib.rkv_mla_decode_fp8(byref(self.view), layer, _ptr(page_table), page_table.shape[1],
                                           _ptr(seq_lens), _ptr(seq_of_query), _ptr(q), n_q, _ptr(idx), k,
