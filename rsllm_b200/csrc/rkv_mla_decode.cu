@@ -14,29 +14,30 @@
 // and the 5th-generation tensor cores consume that tile twice -- as K
 // (K-major) for S and as V (MN-major) for O:
 //
-//   warps 0-3  softmax: S from TMEM, online max / exp2 / row sums per head,
-//              P (bf16) into shared memory, the rare lazy rescale of O,
-//              epilogue
+//   warps 0-3  softmax: Q into TMEM once; S from TMEM, online max / exp2 /
+//              row sums per head, P (bf16) into shared memory, the rare lazy
+//              rescale of O, epilogue
 //   warps 4-11 loaders, software-pipelined over two register buffers: the
 //              loads of tile j + 1 are in flight while tile j is
-//              dequantised into its swizzled K/V stage
+//              dequantised into its stage
 //   warp 12    TMEM allocation and the MMA-issuing thread: issues S = Q K^T
 //              for every loaded tile and O += P V for every softmaxed tile
 //              as each becomes ready
 //
 // Shapes per tile (64 key rows, one page in dense mode), M = 64 heads:
-//   S[64 x 64]   = Q[64 x 576] . K^T    36 MMAs of K = 16 (N = 64), Q and K
+//   S[64 x 64]   = Q[64 x 576] . K^T    36 MMAs of K = 16, N = 64; Q from
+//                                       TMEM, K from shared memory
+//   O[64 x 512] += P[64 x 64]  . V      2 x 4 MMAs of N = 256, both operands
 //                                       from shared memory
-//   O[64 x 512] += P[64 x 64]  . V      2 x 4 MMAs of N = 256, P from smem
-// TMEM (512 columns): O lanes 0-15 (+32k) cols 0-255 = latent 0-255, O lanes
-// 16-31 (+32k) cols 0-255 = latent 256-511 (an M = 64 accumulator occupies
-// half of each 32-lane sub-partition; the second one interleaves in the other
-// half, which needs both operands in shared memory), S double-buffered at
-// columns 256 and 320.  Head h lives in TMEM lane (h % 16) + 32 (h / 16).
+// An M = 64 operand occupies 16 lanes of each 32-lane TMEM sub-partition
+// (head h in lane (h % 16) + 32 (h / 16) + base).  Lanes 0-15: Q at columns
+// 0-287 (bf16 pairs) and S double-buffered at 288 and 352 -- an MMA with A in
+// TMEM keeps its accumulator in those same lanes.  Lanes 16-31: O, latent
+// 0-255 at columns 0-255 and 256-511 at 256-511.  Keeping Q out of shared
+// memory leaves room for three K/V stages (72 KB each) and P (8 KB).
 //
-// Two K/V stages and two S buffers let the exp of tile j overlap the O update
-// of tile j-1 and the S of tile j+1 (shared memory holds Q, two stages and
-// one P).  The online softmax keeps a per-head reference maximum m and
+// Three stages keep the loads and the dequantisation ahead of the tensor
+// cores.  The online softmax keeps a per-head reference maximum m and
 // rescales O only when a tile's maximum exceeds it by more than 2^8 (P values
 // stay <= 256 in bf16).  The final normalisation uses the same m, so the
 // result is the same softmax; the denominator is the sum of the bf16-rounded
@@ -60,25 +61,28 @@ constexpr int kTile = 64;                     // key rows per tile
 constexpr int kAtom = 1024;                   // 8 rows x 128 B swizzle atom
 constexpr int kColBytes = 8 * kAtom;          // one 64-lane column of a 64-row operand
 constexpr int kOperandBytes = (kQk / 64) * kColBytes;  // 73728: 64 rows x 576 bf16
-constexpr int kSmemQ = 0;
-constexpr int kSmemK0 = kSmemQ + kOperandBytes;
-constexpr int kSmemP = kSmemK0 + 2 * kOperandBytes;  // P: 64 heads x 64 keys bf16
+constexpr int kStages = 3;
+constexpr int kSmemK0 = 0;                    // three K/V stages of 64 rows x 576 bf16
+constexpr int kSmemP = kSmemK0 + kStages * kOperandBytes;  // P: 64 heads x 64 keys bf16
 constexpr int kSmemBar = kSmemP + kColBytes;
-constexpr int kSmemRows = kSmemBar + 128;     // row tables: 2 x 64 x (page, row in page)
-constexpr int kSmemTotal = kSmemRows + 2 * 64 * 8;
+constexpr int kSmemRows = kSmemBar + 336;     // slot tables: 4 x 64 x int32 (page * 64 + row, -1 = none)
+constexpr int kSmemTotal = kSmemRows + 4 * 64 * 4;
 constexpr int kSmemAlloc = kSmemTotal + 1024; // slack for the 1024-byte alignment
-constexpr int kThreads = 416;                 // warps 0-3 softmax, 4-11 loaders, 12 MMA
+constexpr int kThreads = 480;  // warps 0-3 softmax, 4-11 loaders, 12 S issuer, 13 O issuer, 14 resolver
 constexpr int kLoaders = 256;
-constexpr int kMmaWarp = 12;
+constexpr int kQkWarp = 12, kResolverWarp = 14;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 256;               // S buffers at 256 and 320
+constexpr uint32_t kColS = 288;               // S buffers at 288 and 352 (lanes 0-15); Q at 0-287
+constexpr uint32_t kLaneO = 16u << 16;        // O in lanes 16-31 of every sub-partition, columns 0-511
 constexpr float kRescaleLog2 = 8.0f;
 constexpr uint64_t kTimeoutNs = 1000000000ull;
 
-// Barrier / state offsets inside the kSmemBar block (the stage and S barrier
-// pairs are indexed by j & 1; key masks by j & 3).
-constexpr int kBarKFull = 0, kBarKEmpty = 16, kBarSFull = 32, kBarPFull = 48, kBarPvDone = 56, kBarDrain = 64;
-constexpr int kTmemSlot = 72, kAbort = 76, kFirstZero = 80, kMask = 96;
+// Barrier / state offsets inside the kSmemBar block: stage barriers indexed
+// by j % 3, S barriers (full, free) by j & 1, slot tables by j & 3, key
+// masks by j & 15.
+constexpr int kBarKFull = 0, kBarKEmpty = 24, kBarSFull = 48, kBarSFree = 64, kBarPFull = 80, kBarPvDone = 88,
+              kBarDrain = 96, kBarQReady = 112, kBarTabFull = 120, kBarTabFree = 152;  // drain: S and O issuers
+constexpr int kTmemSlot = 184, kAbort = 188, kMask = 200;
 
 constexpr uint32_t kIdescQK = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((64u >> 4) << 24);
 constexpr uint32_t kIdescPV = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((256u >> 3) << 17) | ((64u >> 4) << 24);
@@ -133,6 +137,14 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b
       "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
+// Same with the A operand in tensor memory (K-major bf16 pairs per column).
+__device__ __forceinline__ void mma_bf16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
@@ -155,6 +167,33 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
       "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
       "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+// 16 lanes x 256 bits, 4 repetitions (32 columns): thread t holds lanes
+// t / 4 (registers 4r, 4r + 1) and t / 4 + 8 (4r + 2, 4r + 3) at columns
+// 8r + 2 (t % 4) and 8r + 2 (t % 4) + 1.
+__device__ __forceinline__ void tmem_ld16x256(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld16x256x8(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16x256(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x256b.x4.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -231,8 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemBar + kAbort);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + kTmemSlot);
   uint64_t* masks = reinterpret_cast<uint64_t*>(smem + kSmemBar + kMask);
-  int* first_zero = reinterpret_cast<int*>(smem + kSmemBar + kFirstZero);
-  int2* rows_tab = reinterpret_cast<int2*>(smem + kSmemRows);
+  int32_t* slots = reinterpret_cast<int32_t*>(smem + kSmemRows);
   const uint32_t bar = sbase + kSmemBar;
 
   const int seq = p.seq_of_query[qi];
@@ -248,113 +286,124 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
   }
 
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kStages; ++i) {
       mbar_init(bar + kBarKFull + 8 * i, kLoaders);
       mbar_init(bar + kBarKEmpty + 8 * i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(bar + kBarSFull + 8 * i, 1);
+      mbar_init(bar + kBarSFree + 8 * i, 128);
+      mbar_init(bar + kBarDrain + 8 * i, 1);
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(bar + kBarTabFull + 8 * i, 32);
+      mbar_init(bar + kBarTabFree + 8 * i, kLoaders);
     }
     mbar_init(bar + kBarPFull, 128);
     mbar_init(bar + kBarPvDone, 1);
-    mbar_init(bar + kBarDrain, 1);
+    mbar_init(bar + kBarQReady, 128);
     *abort_flag = 0;
-    *first_zero = 0x7fffffff;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == kMmaWarp) {
+  if (warp == kQkWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // Q of this query into the swizzled A operand (64 heads x 576 lanes).
+  // Q of this query, staged through stage 2 (free until the third tile is
+  // loaded): every thread copies a share (chunk c of head h at 16-byte
+  // position (c & ~7) | ((c ^ h) & 7) of row h, so that 16 heads read in
+  // parallel below fall on different banks).
   {
     const uint4* qg = reinterpret_cast<const uint4*>(p.q + (int64_t)qi * kHeads * kQk);
+    uint8_t* qs = smem + kSmemK0 + 2 * kOperandBytes;
     for (int c = tid; c < kHeads * kQk / 8; c += kThreads) {
       const int h = c / (kQk / 8), cc = c % (kQk / 8);
-      *reinterpret_cast<uint4*>(smem + kSmemQ + sw_off(h, cc)) = __ldg(qg + c);
+      *reinterpret_cast<uint4*>(qs + h * (kQk * 2) + (((cc & ~7) | ((cc ^ h) & 7)) << 4)) = __ldg(qg + c);
     }
   }
-  __syncthreads();
-  if (p.idx && warp >= 4 && warp < kMmaWarp) {  // the first position holding index 0 (later zeros repeat it)
-    const int32_t* il = p.idx + (int64_t)qi * p.k;
-    int fz = 0x7fffffff;
-    for (int i = tid - 128; i < p.k; i += kLoaders)
-      if (__ldg(il + i) == 0) {
-        fz = i;
-        break;
-      }
-    if (fz != 0x7fffffff) atomicMin(first_zero, fz);
-  }
-  fence_proxy_async();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (warp < 4) {
+    // Q into TMEM as the A operand of S = Q K^T: head h in lane
+    // (h % 16) + 32 (h / 16), bf16 pairs along columns 0-287.  Lanes 16-31
+    // receive the same values; they hold O, which the first O update
+    // overwrites.
+    const int h = warp * 16 + (lane & 15);
+    const uint8_t* qrow = smem + kSmemK0 + 2 * kOperandBytes + h * (kQk * 2);
+    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+    for (int c = 0; c < kQk / 64; ++c) {
+      uint32_t v[32];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int cc = 8 * c + i;
+        const uint4 w = *reinterpret_cast<const uint4*>(qrow + (((cc & ~7) | ((cc ^ h) & 7)) << 4));
+        v[4 * i] = w.x;
+        v[4 * i + 1] = w.y;
+        v[4 * i + 2] = w.z;
+        v[4 * i + 3] = w.w;
+      }
+      tmem_st32(tl + 32 * c, v);
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    mbar_arrive(bar + kBarQReady);  // also hands stage 2 back to the loaders
+  }
 
-  if (warp == kMmaWarp) {
-    // ---------------------------------------------------------------- MMA
+  if (warp == kQkWarp || warp == kQkWarp + 1) {
+    // ------------------------------------------------------ MMA issuers
+    // Warp 12's elected thread issues S = Q K^T of every tile once its stage
+    // is loaded and its S buffer was read; warp 13's issues O += P V once P
+    // is written.  Each blocks only on its own inputs, and the tensor pipe
+    // interleaves the two streams.
+    const bool qk = warp == kQkWarp;
     if (lane == 0 && n_tiles > 0) {
       bool ok = true;
-      int nq = 0, np = 0;  // next tile to issue S for / O update for
-      uint64_t t_last = now_ns();
-      uint32_t idle = 0;
-      while (np < n_tiles) {
-        bool progressed = false;
-        // S of tile nq once its stage is loaded and its S buffer was read
-        // (the softmax of tile nq - 2 handed over its P: np >= nq - 1).
-        if (nq < n_tiles && nq <= np + 1 && mbar_ready(bar + kBarKFull + 8 * (nq & 1), (nq >> 1) & 1)) {
+      if (qk) {
+        ok = mbar_wait(bar + kBarQReady, 0, abort_flag);
+        for (int j = 0; ok && j < n_tiles; ++j) {
+          const int b = j & 1;
+          ok = mbar_wait(bar + kBarKFull + 8 * (j % kStages), (j / kStages) & 1, abort_flag) &&
+               (j < 2 || mbar_wait(bar + kBarSFree + 8 * b, ((j >> 1) - 1) & 1, abort_flag));
+          if (!ok) break;
           tc_fence_after();
-          const int b = nq & 1;
-          const uint32_t kbase = sbase + kSmemK0 + b * kOperandBytes;
+          const uint32_t kbase = sbase + kSmemK0 + (j % kStages) * kOperandBytes;
           const uint32_t d = tmem + kColS + 64 * b;
 #pragma unroll 4
-          for (int s = 0; s < kQk / 16; ++s) {
-            const uint32_t off = (s >> 2) * kColBytes + (s & 3) * 32;
-            mma_bf16(d, sw128_desc(sbase + kSmemQ + off, 16, kAtom), sw128_desc(kbase + off, 16, kAtom), kIdescQK,
-                     s > 0);
-          }
+          for (int s = 0; s < kQk / 16; ++s)
+            mma_bf16_ta(d, tmem + 8 * s, sw128_desc(kbase + (s >> 2) * kColBytes + (s & 3) * 32, 16, kAtom),
+                        kIdescQK, s > 0);
           mma_commit(bar + kBarSFull + 8 * b);
-          ++nq;
-          progressed = true;
         }
-        // O += P V of tile np once its P is in shared memory.
-        if (np < nq && mbar_ready(bar + kBarPFull, np & 1)) {
+      } else {
+        for (int j = 0; ok && j < n_tiles; ++j) {
+          ok = mbar_wait(bar + kBarPFull, j & 1, abort_flag);
+          if (!ok) break;
           tc_fence_after();
-          const int b = np & 1;
+          const int b = j % kStages;
           const uint32_t vbase = sbase + kSmemK0 + b * kOperandBytes;
 #pragma unroll
           for (int qq = 0; qq < kTile / 16; ++qq) {
             const uint64_t a = sw128_desc(sbase + kSmemP + qq * 32, 16, kAtom);
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf)
-              mma_bf16(tmem + (hf ? (16u << 16) : 0u), a,
+              mma_bf16(tmem + kLaneO + hf * 256, a,
                        sw128_desc(vbase + hf * 4 * kColBytes + qq * 2 * kAtom, kColBytes, kAtom), kIdescPV,
-                       (np > 0 || qq > 0) ? 1u : 0u);
+                       (j > 0 || qq > 0) ? 1u : 0u);
           }
           mma_commit(bar + kBarKEmpty + 8 * b);
           mma_commit(bar + kBarPvDone);
-          ++np;
-          progressed = true;
-        }
-        if (progressed) {
-          idle = 0;
-        } else if ((++idle & 255u) == 0) {
-          if (*abort_flag) {
-            ok = false;
-            break;
-          }
-          const uint64_t t = now_ns();
-          if (idle == 256) t_last = t;
-          else if (t - t_last > kTimeoutNs) {
-            ok = false;
-            break;
-          }
         }
       }
       if (!ok) set_abort(abort_flag, p.status);
-      mma_commit(bar + kBarDrain);  // every MMA issued here completes before the memory is freed
+      const uint32_t drain = bar + kBarDrain + (qk ? 0 : 8);
+      mma_commit(drain);  // every MMA issued here completes before the memory is freed
       const uint64_t t0 = now_ns();
-      while (!mbar_test(bar + kBarDrain, 0)) {
+      while (!mbar_test(drain, 0)) {
         if (now_ns() - t0 > kTimeoutNs) {
           set_abort(abort_flag, p.status);
           break;
@@ -362,60 +411,85 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
       }
     }
     __syncwarp();
+  } else if (warp == kResolverWarp) {
+    // ------------------------------------------------------------ resolver
+    // Runs up to four tiles ahead of the loaders: lane l resolves rows l and
+    // l + 32 of tile j to slots (page * 64 + row in page, -1 = no key) in
+    // table j & 3 and the key mask j & 15.  Index loads for tile j + 1 are
+    // issued before tile j's page-table loads are consumed.
+    const int32_t* pt_row = p.page_table + (int64_t)seq * p.pt_stride;
+    int first_zero = 0x7fffffff;  // later zeros repeat the top-k fill value
+    if (p.idx) {
+      const int32_t* il = p.idx + (int64_t)qi * p.k;
+      for (int i = lane; i < p.k; i += 32)
+        if (__ldg(il + i) == 0) {
+          first_zero = i;
+          break;
+        }
+      first_zero = __reduce_min_sync(0xffffffffu, first_zero);
+    }
+    // The key position of row (j, l) or -1; for an index list, the entry.
+    auto position = [&](int j, int row) -> int {
+      const int pos = j * kTile + row;
+      if (p.idx) {
+        if (pos >= p.k) return -1;
+        const int tok = __ldg(p.idx + (int64_t)qi * p.k + pos);
+        return (tok >= 0 && tok < len && (tok != 0 || pos == first_zero)) ? tok : -1;
+      }
+      return page0 * kTile + pos < len ? page0 * kTile + pos : -1;
+    };
+    int tok0 = n_tiles > 0 ? position(0, lane) : -1, tok1 = n_tiles > 0 ? position(0, lane + 32) : -1;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int tb = j & 3;
+      const int pg0 = tok0 >= 0 ? __ldg(pt_row + tok0 / 64) : -1;
+      const int pg1 = tok1 >= 0 ? __ldg(pt_row + tok1 / 64) : -1;
+      const int ntok0 = j + 1 < n_tiles ? position(j + 1, lane) : -1;
+      const int ntok1 = j + 1 < n_tiles ? position(j + 1, lane + 32) : -1;
+      if (!__all_sync(0xffffffffu, j < 4 || mbar_wait(bar + kBarTabFree + 8 * tb, ((j >> 2) - 1) & 1, abort_flag))) {
+        set_abort(abort_flag, p.status);
+        break;
+      }
+      int s0 = -1, s1 = -1;
+      if (tok0 >= 0) {
+        if (pg0 >= 0 && pg0 < p.pool.n_pages) s0 = pg0 * 64 + (tok0 & 63);
+        else set_status(p.status, RKV_ERR_INDEX_OUT_OF_RANGE);
+      }
+      if (tok1 >= 0) {
+        if (pg1 >= 0 && pg1 < p.pool.n_pages) s1 = pg1 * 64 + (tok1 & 63);
+        else set_status(p.status, RKV_ERR_INDEX_OUT_OF_RANGE);
+      }
+      slots[tb * 64 + lane] = s0;
+      slots[tb * 64 + lane + 32] = s1;
+      const unsigned b0 = __ballot_sync(0xffffffffu, s0 >= 0), b1 = __ballot_sync(0xffffffffu, s1 >= 0);
+      if (lane == 0) masks[j & 15] = ((uint64_t)b1 << 32) | b0;
+      mbar_arrive(bar + kBarTabFull + 8 * tb);
+      tok0 = ntok0;
+      tok1 = ntok1;
+    }
   } else if (warp >= 4) {
     // ------------------------------------------------------------- loaders
     // 256 threads per tile: lane (r8 = lane / 4, q = lane % 4) of loader warp
     // lw takes row 8 lw + r8: codes [128 s + 32 q, +32) for s = 0..3, the
     // row's 8 scales and RoPE bytes [32 q, +32), all as 256-bit loads.  The
-    // rows of tile j are resolved two tiles ahead into table j & 1 and key
-    // mask j & 3; the loads of tile j + 1 are issued before tile j is stored.
+    // loads of tile j + 1 are issued before tile j is stored.  Every wait is
+    // per thread: a loader never waits for another loader.
     const int lt = tid - 128, lw = lt >> 5;
     const int r = 8 * lw + (lane >> 2);
-    const int32_t* pt_row = p.page_table + (int64_t)seq * p.pt_stride;
-    auto resolve = [&](int j) {
-      if (lt >= 64) return;
-      int page = -1, off = 0;
-      if (p.idx) {
-        const int pos = j * kTile + lt;
-        if (pos < p.k) {
-          const int tok = __ldg(p.idx + (int64_t)qi * p.k + pos);
-          if (tok >= 0 && tok < len && (tok != 0 || pos == *first_zero)) {
-            const int pg = __ldg(pt_row + tok / kTile);
-            if (pg >= 0 && pg < p.pool.n_pages) {
-              page = pg;
-              off = tok % kTile;
-            } else {
-              set_status(p.status, RKV_ERR_INDEX_OUT_OF_RANGE);
-            }
-          }
-        }
-      } else {
-        const int pi = page0 + j;
-        if (pi * kTile + lt < len) {
-          const int pg = __ldg(pt_row + pi);
-          if (pg >= 0 && pg < p.pool.n_pages) {
-            page = pg;
-            off = lt;
-          } else if (lt == 0) {
-            set_status(p.status, RKV_ERR_INDEX_OUT_OF_RANGE);
-          }
-        }
-      }
-      rows_tab[(j & 1) * 64 + lt] = make_int2(page, off);
-      const unsigned vb = __ballot_sync(0xffffffffu, page >= 0);
-      if (lane == 0) reinterpret_cast<uint32_t*>(masks + (j & 3))[lw] = vb;
-    };
     struct TileRegs {
       uint32_t codes[4][8], scl[8], rope[8];
     };
-    auto load = [&](int j, TileRegs& t) {
-      const int2 ro = rows_tab[(j & 1) * 64 + r];
-      if (ro.x >= 0) {
-        const uint8_t* pg = page_base(p.pool, p.layer, ro.x);
+    auto load = [&](int j, TileRegs& t) -> bool {
+      const int tb = j & 3;
+      if (!mbar_wait(bar + kBarTabFull + 8 * tb, (j >> 2) & 1, abort_flag)) return false;
+      const int slot = slots[tb * 64 + r];
+      mbar_arrive(bar + kBarTabFree + 8 * tb);
+      if (slot >= 0) {
+        const uint8_t* pg = page_base(p.pool, p.layer, slot >> 6);
+        const int off = slot & 63;
 #pragma unroll
-        for (int sg = 0; sg < 4; ++sg) ld_stream32(pg + codes_off(ro.y) + sg * 128 + (lane & 3) * 32, t.codes[sg]);
-        ld_cached32(pg + scales_off(ro.y), t.scl);
-        ld_stream32(pg + rope_off(ro.y) + (lane & 3) * 32, t.rope);
+        for (int sg = 0; sg < 4; ++sg) ld_stream32(pg + codes_off(off) + sg * 128 + (lane & 3) * 32, t.codes[sg]);
+        ld_cached32(pg + scales_off(off), t.scl);
+        ld_stream32(pg + rope_off(off) + (lane & 3) * 32, t.rope);
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -425,15 +499,17 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
           t.rope[i] = 0u;
         }
       }
+      return true;
     };
-    // Waits for the stage (the O update two tiles back), then dequantises.
-    // Per store instruction the warp writes 8 rows x 4 lanes of 16 B whose
-    // swizzled positions cover the 8 bank groups evenly (4 wavefronts for
-    // 512 B, the minimum).  Returns false on a timeout or abort.
+    // Waits for the stage (the O update three tiles back; stage 2 also for
+    // Q to leave it), then dequantises.  Per store instruction the warp writes
+    // 8 rows x 4 lanes of 16 B whose swizzled positions cover the 8 bank
+    // groups evenly (4 wavefronts for 512 B, the minimum).
     auto store = [&](int j, const TileRegs& t) -> bool {
-      const int b = j & 1;
-      const bool ok = j < 2 || mbar_wait(bar + kBarKEmpty + 8 * b, ((j >> 1) - 1) & 1, abort_flag);
-      if (!bar_all(2, kLoaders, ok)) return false;  // also orders the table and mask accesses
+      const int b = j % kStages;
+      if (j < kStages ? (j == 2 && !mbar_wait(bar + kBarQReady, 0, abort_flag))
+                      : !mbar_wait(bar + kBarKEmpty + 8 * b, (j / kStages - 1) & 1, abort_flag))
+        return false;
       uint8_t* stage = smem + kSmemK0 + b * kOperandBytes;
 #pragma unroll
       for (int sg = 0; sg < 4; ++sg) {
@@ -456,80 +532,80 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
       return true;
     };
     TileRegs ta, tb;
-    if (n_tiles > 0) resolve(0);
-    if (n_tiles > 1) resolve(1);
-    asm volatile("bar.sync 2, 256;" ::: "memory");
-    if (n_tiles > 0) load(0, ta);
-    for (int j = 0; j < n_tiles; j += 2) {
-      // tile j is in ta
-      if (j + 1 < n_tiles) load(j + 1, tb);
-      bool ok = store(j, ta);  // its barrier orders every read of table j & 1 before the next write
-      if (ok && j + 2 < n_tiles) resolve(j + 2);
+    bool ok = n_tiles == 0 || load(0, ta);
+    for (int j = 0; ok && j < n_tiles; j += 2) {
+      if (j + 1 < n_tiles) ok = load(j + 1, tb);  // tile j is in ta
+      ok = ok && store(j, ta);
       if (ok && j + 1 < n_tiles) {
-        // tile j + 1 is in tb; table j & 1 now holds tile j + 2
-        asm volatile("bar.sync 2, 256;" ::: "memory");
-        if (j + 2 < n_tiles) load(j + 2, ta);
-        ok = store(j + 1, tb);
-        if (ok && j + 3 < n_tiles) resolve(j + 3);
-        if (ok) asm volatile("bar.sync 2, 256;" ::: "memory");
-      }
-      if (!ok) {
-        set_abort(abort_flag, p.status);
-        break;
+        if (j + 2 < n_tiles) ok = load(j + 2, ta);  // tile j + 1 is in tb
+        ok = ok && store(j + 1, tb);
       }
     }
+    if (!ok) set_abort(abort_flag, p.status);
   } else {
     // ------------------------------------------------------------- softmax
-    const int h = warp * 16 + (lane & 15);
-    const bool owner = lane < 16;
-    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-    float m_ref = -INFINITY, l_sum = 0.0f;
+    // Thread t of warp w handles heads hA = 16 w + t / 4 and hB = hA + 8 and,
+    // of each 64-key tile, keys 8 r + 2 (t % 4) + {0, 1} for r = 0..7 (16-lane
+    // TMEM accesses spread the 16 S rows over all 32 threads); the four threads
+    // of a head pair combine maxima with shuffles.  The same accesses at lane
+    // 16 reach O of the same two heads.
+    const int g4 = lane >> 2, t4 = lane & 3;
+    const int hA = warp * 16 + g4, hB = hA + 8;
+    const uint32_t tS = tmem + ((uint32_t)(warp * 32) << 16), tO = tS + kLaneO;
+    float mA = -INFINITY, mB = -INFINITY, lA = 0.0f, lB = 0.0f;  // m: per head; l: this thread's keys
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int b = j & 1;
-      const bool got = mbar_wait(bar + kBarKFull + 8 * b, (j >> 1) & 1, abort_flag) &&
+      const bool got = mbar_wait(bar + kBarKFull + 8 * (j % kStages), (j / kStages) & 1, abort_flag) &&
                        mbar_wait(bar + kBarSFull + 8 * b, (j >> 1) & 1, abort_flag);
       if (!bar_all(1, 128, got)) {  // uniform over the four warps: TMEM accesses and barriers follow
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t sv[64];
-      {
-        uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[0]);
-        uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[32]);
-        tmem_ld32(tl + kColS + 64 * b, s0);
-        tmem_ld32(tl + kColS + 64 * b + 32, s1);
-      }
+      uint32_t sv[32];  // register 4 r + k: head k < 2 ? hA : hB, key 8 r + 2 t4 + (k & 1)
+      tmem_ld16x256x8(tS + kColS + 64 * b, sv);
       tmem_wait_ld();
-      const uint64_t mask = masks[j & 3];
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float x = ((mask >> i) & 1) ? __uint_as_float(sv[i]) * p.scale_log2 : -INFINITY;
-        sv[i] = __float_as_uint(x);
-        mx = fmaxf(mx, x);
-      }
-      if (!owner) mx = -INFINITY;
-      float alpha = 1.0f;
-      bool rescale = false;
-      if (mx > -INFINITY && (m_ref == -INFINITY || mx > m_ref + kRescaleLog2)) {
-        alpha = m_ref == -INFINITY ? 0.0f : ex2(m_ref - mx);
-        rescale = m_ref != -INFINITY;
-        m_ref = mx;
-        l_sum *= alpha;
-      }
-      uint32_t pk[32];
-      float lt_sum = 0.0f;
+      tc_fence_before();
+      mbar_arrive(bar + kBarSFree + 8 * b);  // S buffer b may be overwritten
+      const uint64_t mask = masks[j & 15];
+      float mxA = -INFINITY, mxB = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float x0 = __uint_as_float(sv[2 * i]), x1 = __uint_as_float(sv[2 * i + 1]);
-        const float a = x0 > -INFINITY ? ex2(x0 - m_ref) : 0.0f;
-        const float c = x1 > -INFINITY ? ex2(x1 - m_ref) : 0.0f;
-        pk[i] = pack_bf16x2(a, c);
-        lt_sum += __uint_as_float(pk[i] << 16) + __uint_as_float(pk[i] & 0xffff0000u);
+        const int key = 8 * (i >> 2) + 2 * t4 + (i & 1);
+        const float x = ((mask >> key) & 1) ? __uint_as_float(sv[i]) * p.scale_log2 : -INFINITY;
+        sv[i] = __float_as_uint(x);
+        if (i & 2) mxB = fmaxf(mxB, x);
+        else mxA = fmaxf(mxA, x);
       }
-      l_sum += lt_sum;
+      mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 1));
+      mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 2));
+      mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 1));
+      mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 2));
+      float alA = 1.0f, alB = 1.0f;
+      bool rescale = false;
+      if (mxA > -INFINITY && (mA == -INFINITY || mxA > mA + kRescaleLog2)) {
+        alA = mA == -INFINITY ? 0.0f : ex2(mA - mxA);
+        rescale |= mA != -INFINITY;
+        mA = mxA;
+        lA *= alA;
+      }
+      if (mxB > -INFINITY && (mB == -INFINITY || mxB > mB + kRescaleLog2)) {
+        alB = mB == -INFINITY ? 0.0f : ex2(mB - mxB);
+        rescale |= mB != -INFINITY;
+        mB = mxB;
+        lB *= alB;
+      }
+      uint32_t pa[8], pb[8];  // bf16 pairs: keys 8 r + 2 t4, +1 of hA / hB
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float x0 = __uint_as_float(sv[4 * r]), x1 = __uint_as_float(sv[4 * r + 1]);
+        const float y0 = __uint_as_float(sv[4 * r + 2]), y1 = __uint_as_float(sv[4 * r + 3]);
+        pa[r] = pack_bf16x2(x0 > -INFINITY ? ex2(x0 - mA) : 0.0f, x1 > -INFINITY ? ex2(x1 - mA) : 0.0f);
+        pb[r] = pack_bf16x2(y0 > -INFINITY ? ex2(y0 - mB) : 0.0f, y1 > -INFINITY ? ex2(y1 - mB) : 0.0f);
+        lA += __uint_as_float(pa[r] << 16) + __uint_as_float(pa[r] & 0xffff0000u);
+        lB += __uint_as_float(pb[r] << 16) + __uint_as_float(pb[r] & 0xffff0000u);
+      }
       // P and O are free once the O update of tile j - 1 is done.
       if (!bar_all(1, 128, j == 0 || mbar_wait(bar + kBarPvDone, (j - 1) & 1, abort_flag))) {
         ok = false;
@@ -537,23 +613,23 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
       }
       tc_fence_after();
       if (__any_sync(0xffffffffu, rescale)) {
-        const float a_lane = __shfl_sync(0xffffffffu, rescale ? alpha : 1.0f, lane & 15);
+        // O of hA / hB in lanes 16-31; 16-lane accesses leave Q and S alone.
 #pragma unroll 1
-        for (int c = 0; c < kV / 2; c += 32) {
-          uint32_t o[32];
-          tmem_ld32(tl + c, o);
+        for (int c = 0; c < kV; c += 32) {
+          uint32_t o[16];
+          tmem_ld16x256(tO + c, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * a_lane);
-          tmem_st32(tl + c, o);
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * ((i & 2) ? alB : alA));
+          tmem_st16x256(tO + c, o);
         }
         tmem_wait_st();
       }
-      if (owner) {
-        uint8_t* prow = smem + kSmemP;
+      uint8_t* prow = smem + kSmemP;
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(prow + sw_off(h, c)) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      for (int r = 0; r < 8; ++r) {
+        *reinterpret_cast<uint32_t*>(prow + sw_off(hA, r) + 4 * t4) = pa[r];
+        *reinterpret_cast<uint32_t*>(prow + sw_off(hB, r) + 4 * t4) = pb[r];
       }
       fence_proxy_async();
       tc_fence_before();
@@ -562,52 +638,66 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
     if (ok && n_tiles > 0 && !bar_all(1, 128, mbar_wait(bar + kBarPvDone, (n_tiles - 1) & 1, abort_flag))) ok = false;
     if (!ok) set_abort(abort_flag, p.status);
     tc_fence_after();
-    // Epilogue: lanes 0-15 hold latent 0-255 of head h, lanes 16-31 latent 256-511.
-    const float m_h = __shfl_sync(0xffffffffu, m_ref, lane & 15);
-    const float l_h = __shfl_sync(0xffffffffu, l_sum, lane & 15);
-    const int half = lane >> 4;
-    float oscale = 0.0f;
-    float* dst;
+    // Epilogue: the denominators sum the four threads' keys of each head.
+    lA += __shfl_xor_sync(0xffffffffu, lA, 1);
+    lA += __shfl_xor_sync(0xffffffffu, lA, 2);
+    lB += __shfl_xor_sync(0xffffffffu, lB, 1);
+    lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+    float scA = 0.0f, scB = 0.0f;
+    float *dA, *dB;
     if (p.n_splits > 1) {
-      const int64_t slot = ((int64_t)qi * p.n_splits + split) * kHeads + h;
-      dst = p.ws_o + slot * kV + half * (kV / 2);
-      if (owner) {
-        p.ws_ml[2 * slot] = m_h;
-        p.ws_ml[2 * slot + 1] = l_h;
+      const int64_t sA = ((int64_t)qi * p.n_splits + split) * kHeads + hA, sB = sA + 8;
+      dA = p.ws_o + sA * kV;
+      dB = p.ws_o + sB * kV;
+      if (t4 == 0) {
+        p.ws_ml[2 * sA] = mA;
+        p.ws_ml[2 * sA + 1] = lA;
+        p.ws_ml[2 * sB] = mB;
+        p.ws_ml[2 * sB + 1] = lB;
       }
-      oscale = 1.0f;
+      scA = scB = 1.0f;
     } else {
-      dst = p.out + ((int64_t)qi * kHeads + h) * kV + half * (kV / 2);
-      const float sink = p.sinks ? p.sinks[h] * 1.4426950408889634f : -INFINITY;
-      const float M = fmaxf(m_h, sink);
-      if (M > -INFINITY && M < INFINITY) {
-        const float wo = m_h > -INFINITY ? ex2(m_h - M) : 0.0f;
-        const float den = l_h * wo + (sink > -INFINITY ? ex2(sink - M) : 0.0f);
-        if (den > 0.0f && den < INFINITY) oscale = wo / den;
-      }
+      dA = p.out + ((int64_t)qi * kHeads + hA) * kV;
+      dB = p.out + ((int64_t)qi * kHeads + hB) * kV;
+      auto scale_of = [&](int h, float m, float l) {
+        const float sink = p.sinks ? p.sinks[h] * 1.4426950408889634f : -INFINITY;
+        const float M = fmaxf(m, sink);
+        float sc = 0.0f;
+        if (M > -INFINITY && M < INFINITY) {
+          const float wo = m > -INFINITY ? ex2(m - M) : 0.0f;
+          const float den = l * wo + (sink > -INFINITY ? ex2(sink - M) : 0.0f);
+          if (den > 0.0f && den < INFINITY) sc = wo / den;
+        }
+        return sc;
+      };
+      scA = scale_of(hA, mA, lA);
+      scB = scale_of(hB, mB, lB);
     }
     const bool have_o = ok && n_tiles > 0;
 #pragma unroll 1
-    for (int c = 0; c < kV / 2; c += 32) {
+    for (int c = 0; c < kV; c += 64) {
       uint32_t o[32];
       if (have_o) {
-        tmem_ld32(tl + c, o);
+        tmem_ld16x256x8(tO + c, o);
         tmem_wait_ld();
       }
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (have_o)
-          v = make_float4(__uint_as_float(o[i]) * oscale, __uint_as_float(o[i + 1]) * oscale,
-                          __uint_as_float(o[i + 2]) * oscale, __uint_as_float(o[i + 3]) * oscale);
-        *reinterpret_cast<float4*>(dst + c + i) = v;
+      for (int r = 0; r < 8; ++r) {
+        const int col = c + 8 * r + 2 * t4;
+        float2 va = make_float2(0.f, 0.f), vb = make_float2(0.f, 0.f);
+        if (have_o) {
+          va = make_float2(__uint_as_float(o[4 * r]) * scA, __uint_as_float(o[4 * r + 1]) * scA);
+          vb = make_float2(__uint_as_float(o[4 * r + 2]) * scB, __uint_as_float(o[4 * r + 3]) * scB);
+        }
+        *reinterpret_cast<float2*>(dA + col) = va;
+        *reinterpret_cast<float2*>(dB + col) = vb;
       }
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == kMmaWarp)
+  if (warp == kQkWarp)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
 }
 
