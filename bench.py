@@ -757,7 +757,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--only", choices=["all", "append", "gather", "sparse", "prefix"], default="all",
                     help="run one workload alone (profiling)")
-    ap.add_argument("--mla-splits", type=int, default=32,
+    ap.add_argument("--mla-splits", type=int, default=16,
                     help="page-range splits per query for the dense MLA decode phase")
     ap.add_argument("--small", action="store_true",
                     help="profiling sizes for the phases: 8 seqs / 1 layer (gather), 4 seqs / 1 layer (sparse)")
