@@ -546,6 +546,48 @@ def bench_sparse(args, dist: Dist, dev, peak) -> dict:
     return res
 
 
+def bench_kvc(args, dist: Dist, dev) -> dict:
+    """KVC file save and load (prefix persistence) of a config-5-sized prefix
+    (8229 tokens) over 61 layers: host-synchronous (device pack / unpack,
+    pinned copies, file IO), timed by wall clock; the loaded sequence's rows
+    are checked against the saved one."""
+    import tempfile
+
+    import rsllm_b200 as rk
+    from rsllm_b200 import synth
+    from rsllm_b200.prefix_pool import PrefixKvPool
+
+    n_tok, n_layers = (2048, 4) if args.small else (8229, N_LAYERS)
+    n_pages = 2 * ((n_tok + 63) // 64) + 2
+    pool = PrefixKvPool(n_pages, n_layers, device=dev)
+    seq = pool.create_sequence()
+    slots = torch.from_numpy(pool.reserve([seq], [n_tok])).to(dev)
+    rows = synth.kv_rows(n_tok, seed=77 + dist.rank, device=dev)
+    for layer in range(n_layers):
+        pool.kv.append_layer(layer, rows, slots)
+    pool.kv.check("kvc fill")
+    tokens = np.arange(n_tok, dtype=np.int32) + 1000 * dist.rank
+    page_bytes = n_layers * ((n_tok + 63) // 64) * rk.PAGE_BYTES
+    with tempfile.TemporaryDirectory() as d:
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        path = pool.save_kvc(seq, tokens, d)
+        t1 = time.perf_counter()
+        s2, _ = pool.load_kvc(path, insert_prefix=False)
+        torch.cuda.synchronize(dev)
+        t2 = time.perf_counter()
+        file_bytes = os.path.getsize(path)
+    pt1 = torch.from_numpy(pool.page_table(seq).reshape(1, -1)).to(dev)
+    pt2 = torch.from_numpy(pool.page_table(s2).reshape(1, -1)).to(dev)
+    cu = torch.tensor([0, n_tok], dtype=torch.int32, device=dev)
+    same = all(torch.equal(pool.kv.rows(layer, pt1, cu, n_tok), pool.kv.rows(layer, pt2, cu, n_tok))
+               for layer in (0, n_layers - 1))
+    return {"config": f"{n_tok} tokens x {n_layers} layers, one file ({file_bytes / 1e6:.1f} MB)",
+            "timing": "wall clock around the host-synchronous calls (includes file IO)",
+            "save_s": t1 - t0, "load_s": t2 - t1, "save_gbs": page_bytes / (t1 - t0) / GB,
+            "load_gbs": page_bytes / (t2 - t1) / GB, "loaded_rows_equal": bool(same)}
+
+
 # ---------------------------------------------------------------------------
 # config 5: prefix cache -- copy-on-write branches, LRU eviction, compaction
 # ---------------------------------------------------------------------------
@@ -750,12 +792,12 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--phases", default="gather,sparse,prefix",
-                    help="extra configs to measure (comma list of gather,sparse,prefix or 'none')")
+    ap.add_argument("--phases", default="gather,sparse,prefix,kvc",
+                    help="extra configs to measure (comma list of gather,sparse,prefix,kvc or 'none')")
     ap.add_argument("--phase-steps", type=int, default=3)
     ap.add_argument("--phase-warmup", type=int, default=1)
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
-    ap.add_argument("--only", choices=["all", "append", "gather", "sparse", "prefix"], default="all",
+    ap.add_argument("--only", choices=["all", "append", "gather", "sparse", "prefix", "kvc"], default="all",
                     help="run one workload alone (profiling)")
     ap.add_argument("--mla-splits", type=int, default=16,
                     help="page-range splits per query for the dense MLA decode phase")
@@ -788,6 +830,8 @@ def main():
             res = {"gather": g, "mla_decode_dense": m}
         elif args.only == "prefix":
             res = bench_prefix(args, dist, dev, peak)
+        elif args.only == "kvc":
+            res = bench_kvc(args, dist, dev)
         else:
             res = bench_sparse(args, dist, dev, peak)
         clocks.stop()
@@ -805,6 +849,8 @@ def main():
         phases.update(bench_sparse(args, dist, dev, peak))
     if "prefix" in wanted:
         phases["prefix_cow_evict_compact"] = bench_prefix(args, dist, dev, peak)
+    if "kvc" in wanted:
+        phases["kvc_save_load"] = bench_kvc(args, dist, dev)
     clk = clocks.stop()
 
     K, W = args.steps, args.warmup

@@ -298,6 +298,44 @@ RKV_API rkv_status rkv_pool_take_moves(rkv_pool* pool, int32_t* src, int32_t* ds
 /* Reads and clears the status bits of the pool's own device work (syncs). */
 RKV_API rkv_status rkv_pool_device_status(rkv_pool* pool, uint32_t* bits);
 
+/* ---- KVC on-disk format ---------------------------------------------------
+ * Prefix persistence after rsLLM's plan (docs/03-HLD.md:242-282; rsLLM has
+ * no implementation yet): the first n_tokens tokens of a pooled sequence,
+ * every layer, in file <dir>/<SHA1 of the token ids as little-endian u32>.kvc.
+ * Layout: a 48-byte header ("KVC", version 1, quant_bits 8, reason,
+ * token_count, ctx_size, created_at, payload_bytes, 4 zero bytes), the
+ * rendered text (u32 length + bytes), the engine payload ("DSV4" magic,
+ * version 1, vocab_size, n_layers, head_dim 576, page_tokens 64, n_pages,
+ * token ids, then every page of every layer as stored; rows past n_tokens are
+ * zero).  All integers little-endian. */
+#define RKV_KVC_HEADER_BYTES 48
+#define RKV_KVC_COLD 0
+#define RKV_KVC_CONTINUED 1
+#define RKV_KVC_EVICT 2
+#define RKV_KVC_SHUTDOWN 3
+typedef struct rkv_kvc_header {
+  uint32_t version, quant_bits, reason, reserved;
+  uint64_t token_count, ctx_size, created_at, payload_bytes;
+} rkv_kvc_header;
+/* out: the 40 hex digits of SHA1(token ids) followed by ".kvc" and a NUL. */
+RKV_API rkv_status rkv_kvc_name(const int32_t* token_ids, int64_t n_tokens, char out[46]);
+RKV_API rkv_status rkv_kvc_read_header(const char* path, rkv_kvc_header* out);
+/* Writes the file (through <name>.part, renamed when complete) and returns
+ * its path in path_out (may be NULL).  Synchronises stream.  Errors:
+ * SHAPE_MISMATCH if the sequence holds fewer than n_tokens tokens;
+ * INVALID_ARGUMENT for IO failures or a plan-only pool. */
+RKV_API rkv_status rkv_kvc_save(rkv_pool* pool, int64_t seq, const int32_t* token_ids, int64_t n_tokens,
+                                uint32_t reason, uint32_t vocab_size, const char* text, int64_t text_len,
+                                const char* dir, char* path_out, int64_t path_cap, rkv_stream_t stream);
+/* Creates a sequence holding the file's tokens (POOL_FULL if the pool has no
+ * room), uploads its pages, optionally registers it in the radix prefix store
+ * (rkv_prefix_insert), and returns it in seq_out; token_ids_out (capacity
+ * cap, may be NULL) receives the token ids and n_tokens_out their count.
+ * SHAPE_MISMATCH if the file's layer count or row layout differs from the
+ * pool's. */
+RKV_API rkv_status rkv_kvc_load(rkv_pool* pool, const char* path, int32_t* token_ids_out, int64_t cap,
+                                int64_t* n_tokens_out, int64_t* seq_out, int32_t insert_prefix, rkv_stream_t stream);
+
 /* ---- page moves without allocation -----------------------------------------
  * No counterpart in rsLLM: an addition of this library for callers that cannot
  * allocate device memory -- an engine that reserves all of its device memory
@@ -359,6 +397,19 @@ RKV_API rkv_status rkv_mla_decode_fp8(const rkv_pool_view* pool, int32_t layer, 
                                       const uint16_t* q, int32_t n_q, const int32_t* idx, int32_t k,
                                       const float* sinks, float softmax_scale, int32_t n_splits, void* workspace,
                                       float* out, uint32_t* d_status, rkv_stream_t stream);
+
+/* ---- page staging --------------------------------------------------------
+ * Contiguous copies of a page list (no rsLLM counterpart; the building block
+ * of host offload and of the KVC file format below).  pages: device int32
+ * [n]; the buffer is device memory of n_layers * n * RKV_PAGE_BYTES bytes laid
+ * out [layer][i][page bytes], 16-byte aligned.  pack: buffer <- pages of
+ * layers [layer0, layer0 + n_layers); unpack: pages <- buffer.  A page id
+ * outside the pool sets INDEX_OUT_OF_RANGE and that page is skipped. */
+RKV_API rkv_status rkv_pack_pages(const rkv_pool_view* pool, int32_t layer0, int32_t n_layers, const int32_t* pages,
+                                  int64_t n, void* dst, uint32_t* d_status, rkv_stream_t stream);
+RKV_API rkv_status rkv_unpack_pages(const rkv_pool_view* pool, int32_t layer0, int32_t n_layers,
+                                    const int32_t* pages, int64_t n, const void* src, uint32_t* d_status,
+                                    rkv_stream_t stream);
 
 /* ---- codec pin ---------------------------------------------------------------
  * out[i] = E4M3 code the append kernel stores for the f32 lane value whose

@@ -5,7 +5,7 @@ Loading fails loudly: there is no CPU fallback for any entry point.
 from __future__ import annotations
 
 import ctypes
-from ctypes import c_float, POINTER, Structure, c_char_p, c_int32, c_int64, c_uint8, c_uint16, c_uint32, c_void_p
+from ctypes import POINTER, Structure, c_char_p, c_float, c_int32, c_int64, c_uint8, c_uint16, c_uint32, c_uint64, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "librsllm_kv_cuda.so"
@@ -47,6 +47,17 @@ class PoolStats(Structure):
                 ("tick", c_int64), ("high_water", c_int64)]
 
 
+class KvcHeader(Structure):
+    """``rkv_kvc_header``."""
+
+    _fields_ = [("version", c_uint32), ("quant_bits", c_uint32), ("reason", c_uint32), ("reserved", c_uint32),
+                ("token_count", c_uint64), ("ctx_size", c_uint64), ("created_at", c_uint64),
+                ("payload_bytes", c_uint64)]
+
+
+KVC_COLD, KVC_CONTINUED, KVC_EVICT, KVC_SHUTDOWN = 0, 1, 2, 3
+KVC_HEADER_BYTES = 48
+
 PLAN_ONLY = -1
 
 _P = POINTER
@@ -69,6 +80,13 @@ SIGNATURES = {
     "rkv_copy_pages": (c_int32, [_P(PoolView), _i32p, _i32p, c_int64, _u32p, c_void_p]),
     "rkv_remap_pages": (c_int32, [_i32p, c_int64, _i32p, c_int64, _u32p, c_void_p]),
     "rkv_e4m3fn_code_range": (c_int32, [c_uint32, c_int64, _u8p, c_void_p]),
+    "rkv_pack_pages": (c_int32, [_P(PoolView), c_int32, c_int32, _i32p, c_int64, c_void_p, _u32p, c_void_p]),
+    "rkv_unpack_pages": (c_int32, [_P(PoolView), c_int32, c_int32, _i32p, c_int64, c_void_p, _u32p, c_void_p]),
+    "rkv_kvc_name": (c_int32, [_i32p, c_int64, c_char_p]),
+    "rkv_kvc_read_header": (c_int32, [c_char_p, _P(KvcHeader)]),
+    "rkv_kvc_save": (c_int32, [c_void_p, c_int64, _i32p, c_int64, c_uint32, c_uint32, c_char_p, c_int64, c_char_p,
+                               c_char_p, c_int64, c_void_p]),
+    "rkv_kvc_load": (c_int32, [c_void_p, c_char_p, _i32p, c_int64, _P(c_int64), _P(c_int64), c_int32, c_void_p]),
     "rkv_mla_decode_workspace_bytes": (c_int64, [c_int32, c_int32]),
     "rkv_mla_decode_fp8": (c_int32, [_P(PoolView), c_int32, _i32p, c_int64, _i32p, _i32p, _u16p, c_int32, _i32p,
                                      c_int32, _f32p, c_float, c_int32, c_void_p, _f32p, _u32p, c_void_p]),

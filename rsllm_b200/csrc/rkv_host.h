@@ -22,4 +22,9 @@ inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintp
 // Validates a pool view: non-null 256-byte aligned base, positive sizes.
 rkv_status check_pool(const rkv_pool_view* p, const char* what);
 
+// Internal accessors of a pool handle (rkv_pool.cpp): its device (RKV_PLAN_ONLY
+// for a plan-only pool) and its device status word.
+int pool_device(const rkv_pool* pool);
+uint32_t* pool_status_word(rkv_pool* pool);
+
 }  // namespace rkv

@@ -266,6 +266,11 @@ void remove_leaf(rkv_pool* P, int32_t id, int64_t* freed) {
 
 }  // namespace
 
+namespace rkv {
+int pool_device(const rkv_pool* pool) { return pool->device; }
+uint32_t* pool_status_word(rkv_pool* pool) { return pool->d_status; }
+}  // namespace rkv
+
 extern "C" {
 
 rkv_status rkv_pool_create(const rkv_pool_desc* desc, rkv_pool** out) {

@@ -8,6 +8,7 @@ returns the page moves it decides (``take_moves``) for the caller to apply.
 """
 from __future__ import annotations
 
+import ctypes
 from ctypes import byref, c_int64, c_uint32, c_void_p
 
 import numpy as np
@@ -168,3 +169,39 @@ class PrefixKvPool:
         b = c_uint32()
         check(self.lib.rkv_pool_device_status(self._h, byref(b)))
         return b.value
+
+    # -- KVC files (prefix persistence) -----------------------------------------
+    def save_kvc(self, seq: int, tokens, directory: str, reason: int = _abi.KVC_COLD, vocab_size: int = 0,
+                 text: bytes = b"", stream: torch.cuda.Stream | None = None) -> str:
+        """Writes the first ``len(tokens)`` tokens of ``seq`` (every layer) to
+        ``<directory>/<SHA1(tokens)>.kvc``; returns the path (see
+        ``rkv_kvc_save``)."""
+        t = _i32(tokens)
+        out = ctypes.create_string_buffer(len(directory.encode()) + 64)
+        check(self.lib.rkv_kvc_save(self._h, seq, _ptr(t), t.size, reason, vocab_size, text, len(text),
+                                    directory.encode(), out, len(out), _stream(stream)))
+        return out.value.decode()
+
+    def load_kvc(self, path: str, insert_prefix: bool = True,
+                 stream: torch.cuda.Stream | None = None) -> tuple[int, np.ndarray]:
+        """Loads a KVC file into a new sequence; returns (sequence, tokens)."""
+        h = read_kvc_header(path)
+        tokens = np.empty(h["token_count"], np.int32)
+        n, seq = c_int64(), c_int64()
+        check(self.lib.rkv_kvc_load(self._h, path.encode(), _ptr(tokens), tokens.size, byref(n), byref(seq),
+                                    int(insert_prefix), _stream(stream)))
+        return seq.value, tokens
+
+
+def kvc_name(tokens) -> str:
+    """File name of a token sequence: SHA1 of the ids as little-endian u32."""
+    t = _i32(tokens)
+    out = ctypes.create_string_buffer(46)
+    check(_abi.load().rkv_kvc_name(_ptr(t), t.size, out))
+    return out.value.decode()
+
+
+def read_kvc_header(path: str) -> dict:
+    h = _abi.KvcHeader()
+    check(_abi.load().rkv_kvc_read_header(path.encode(), byref(h)))
+    return {f: getattr(h, f) for f, _ in _abi.KvcHeader._fields_}
