@@ -546,6 +546,129 @@ def bench_sparse(args, dist: Dist, dev, peak) -> dict:
     return res
 
 
+def compress_bytes(n_tok: int, n_emit: int, ring_rows_written: int, ring_src_read: int) -> int:
+    """Algorithmic HBM bytes of one rkv_compress_append call (ratio 4, two
+    lanes of 576): every input (kv, score) row read once (9216 B), the ring
+    rows written for the next call (9216 B each), the ring half-rows the
+    emissions read (kv + score of one lane: 4608 B each) and the emitted
+    stored rows (672 B)."""
+    return n_tok * 9216 + ring_rows_written * 9216 + ring_src_read * 4608 + n_emit * 672
+
+
+def bench_compress(args, dist: Dist, dev, peak) -> dict:
+    """Compressor emission (rkv_compress_append, ratio 4, coff 2) as a decode
+    step -- one token of each of 256 sequences per layer, 61 layers, a quarter
+    of them emitting, the whole step captured in one CUDA graph -- and as a
+    prefill -- 8 sequences x 4096 tokens per layer call, 61 layers."""
+    import oracle
+    import rsllm_b200 as rk
+
+    res = {}
+    g = torch.Generator(device=dev)
+    g.manual_seed(500 + 7919 * dist.rank)
+    norm = (torch.rand(576, generator=g, device=dev) + 0.5).contiguous()
+    ape = torch.randn((4, 1152), generator=g, device=dev).contiguous()
+    stream = torch.cuda.Stream(device=dev)
+    n_layers = 1 if args.small else N_LAYERS
+
+    # -- decode step ---------------------------------------------------------------
+    n_seq, n_var, p0 = 256, 4, 8192
+    pool = rk.PagedKvPool(n_seq, n_layers, device=dev)
+    banks = rk.CompressorBank(4, n_seq * n_layers, device=dev, max_positions=p0 + 4096)
+    kv = torch.randn((n_var, n_layers, n_seq, 1152), generator=g, device=dev)
+    sc = torch.randn((n_var, n_layers, n_seq, 1152), generator=g, device=dev) * 3
+    seq = torch.arange(n_seq, dtype=torch.int32, device=dev)
+    sid = [(seq + layer * n_seq).contiguous() for layer in range(n_layers)]
+    n_pos_steps = args.phase_warmup + 3 + args.phase_steps + 2
+    pos = [(seq + p0 + j).contiguous() for j in range(n_pos_steps)]
+    slot = [(seq * 64 + ((seq + p0 + j + 1) // 4) % 64).to(torch.int32).contiguous() for j in range(n_pos_steps)]
+    state = {"j": 0}
+
+    def dstep(j):
+        for layer in range(n_layers):
+            banks.append(pool, layer, kv[j % n_var, layer], sc[j % n_var, layer], pos[j], sid[layer], slot[j], norm,
+                         ape, stream=stream)
+
+    # the positions advance every step, so the graph is captured per step index
+    for j in range(args.phase_warmup + 3):
+        dstep(j)
+    pool.check("compress decode", stream)
+    graphs = []
+    torch.cuda.synchronize(dev)
+    for j in range(args.phase_warmup + 3, args.phase_warmup + 3 + args.phase_steps):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            dstep(j)
+        graphs.append(gr)
+    dist.barrier()
+    flush_l2(dev)
+    ms = dist.max(events_time(lambda: [gr.replay() for gr in graphs], stream)) / args.phase_steps
+    pool.check("compress decode", stream)
+    one = events_time(lambda: banks.append(pool, 0, kv[0, 0], sc[0, 0], pos[-1], sid[0], slot[-1], norm, ape,
+                                           stream=stream), stream)
+    n_emit = n_seq // 4
+    per_layer = compress_bytes(n_seq, n_emit, n_seq, n_emit * 7)
+    t_layer = ms * 1e-3 / n_layers
+    res["compress_decode"] = {
+        "config": f"ratio 4 (two lanes of 576), {n_seq} sequences x 1 token x {n_layers} layers per step, "
+                  f"positions {p0}+i (a quarter emit), whole step in one CUDA graph",
+        "ms_per_step": ms, "tokens_per_s_per_gpu": n_seq * n_layers / (ms * 1e-3),
+        "emissions_per_s_per_gpu": n_emit * n_layers / (ms * 1e-3),
+        "algorithmic_bytes_per_layer": per_layer, "gbs_per_gpu": per_layer / t_layer / GB,
+        "frac_of_hbm_peak": per_layer / t_layer / GB / peak, "ms_per_layer_ungraphed": one,
+        "launches_per_step": 2 * n_layers}
+    del graphs, kv, sc, banks, pool
+    torch.cuda.empty_cache()
+
+    # -- prefill --------------------------------------------------------------------
+    n_seq, per = (2, 4096) if args.small else (8, 4096)
+    n_tok = n_seq * per
+    pool = rk.PagedKvPool(n_seq * per // 4 // 64, n_layers, device=dev)
+    banks = rk.CompressorBank(4, n_seq * n_layers, device=dev, max_positions=per)
+    kvp = torch.randn((n_tok, 1152), generator=g, device=dev)
+    scp = torch.randn((n_tok, 1152), generator=g, device=dev) * 3
+    posp = torch.arange(per, dtype=torch.int32, device=dev).repeat(n_seq).contiguous()
+    seqp = torch.arange(n_seq, dtype=torch.int32, device=dev).repeat_interleave(per)
+    slotp = (seqp * (per // 4) + (posp + 1) // 4 - 1).to(torch.int32).contiguous()
+    sidp = [(seqp + layer * n_seq).to(torch.int32).contiguous() for layer in range(n_layers)]
+
+    def pstep():
+        for layer in range(n_layers):
+            banks.append(pool, layer, kvp, scp, posp, sidp[layer], slotp, norm, ape, stream=stream)
+
+    for _ in range(args.phase_warmup):
+        pstep()
+    pool.check("compress prefill", stream)
+    dist.barrier()
+    msp = dist.max(events_time(lambda: [pstep() for _ in range(args.phase_steps)], stream)) / args.phase_steps
+    pool.check("compress prefill", stream)
+    onep = events_time(lambda: banks.append(pool, 0, kvp, scp, posp, sidp[0], slotp, norm, ape, stream=stream),
+                       stream)
+    n_emit = n_tok // 4
+    per_layer = compress_bytes(n_tok, n_emit, n_seq * 8, 0)
+    t_layer = msp * 1e-3 / n_layers
+    # CPU: the oracle (reference state machine, threads over sequences) on one layer's first 512 tokens per seq
+    cpu_per = 512
+    sel = (posp < cpu_per).cpu().numpy()
+    ref_pool = oracle.new_pool(pool.n_pages, 1)
+    kv_c, sc_c = kvp.cpu().numpy()[sel], scp.cpu().numpy()[sel]
+    args_c = (posp.cpu().numpy()[sel], seqp.cpu().numpy().astype(np.int32)[sel], slotp.cpu().numpy()[sel])
+    t0 = time.perf_counter()
+    oracle.compress_append(ref_pool, pool.n_pages, 1, 0, 4, oracle.compress_states(n_seq, 4), kv_c, sc_c, *args_c,
+                           ape.cpu().numpy(), norm.cpu().numpy())
+    cpu_s = time.perf_counter() - t0
+    res["compress_prefill"] = {
+        "config": f"ratio 4 (two lanes of 576), {n_seq} sequences x {per} tokens per layer call x {n_layers} layers",
+        "ms_per_step": msp, "tokens_per_s_per_gpu": n_tok * n_layers / (msp * 1e-3),
+        "algorithmic_bytes_per_layer": per_layer, "gbs_per_gpu": per_layer / t_layer / GB,
+        "frac_of_hbm_peak": per_layer / t_layer / GB / peak, "kernel_ms_per_layer": onep,
+        "cpu_baseline": {"tokens_per_s": n_seq * cpu_per / cpu_s, "cores": min(n_seq, oracle.threads()),
+                         "kind": "port", "sample": f"{n_seq} x {cpu_per} tokens of one layer, threads over sequences"}}
+    del kvp, scp, banks, pool
+    torch.cuda.empty_cache()
+    return res
+
+
 def bench_kvc(args, dist: Dist, dev) -> dict:
     """KVC file save and load (prefix persistence) of a config-5-sized prefix
     (8229 tokens) over 61 layers: host-synchronous (device pack / unpack,
@@ -792,12 +915,13 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--phases", default="gather,sparse,prefix,kvc",
-                    help="extra configs to measure (comma list of gather,sparse,prefix,kvc or 'none')")
+    ap.add_argument("--phases", default="gather,sparse,prefix,kvc,compress",
+                    help="extra configs to measure (comma list of gather,sparse,prefix,kvc,compress or 'none')")
     ap.add_argument("--phase-steps", type=int, default=3)
     ap.add_argument("--phase-warmup", type=int, default=1)
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
-    ap.add_argument("--only", choices=["all", "append", "gather", "sparse", "prefix", "kvc"], default="all",
+    ap.add_argument("--only", choices=["all", "append", "gather", "sparse", "prefix", "kvc", "compress"],
+                    default="all",
                     help="run one workload alone (profiling)")
     ap.add_argument("--mla-splits", type=int, default=16,
                     help="page-range splits per query for the dense MLA decode phase")
@@ -832,6 +956,8 @@ def main():
             res = bench_prefix(args, dist, dev, peak)
         elif args.only == "kvc":
             res = bench_kvc(args, dist, dev)
+        elif args.only == "compress":
+            res = bench_compress(args, dist, dev, peak)
         else:
             res = bench_sparse(args, dist, dev, peak)
         clocks.stop()
@@ -851,6 +977,8 @@ def main():
         phases["prefix_cow_evict_compact"] = bench_prefix(args, dist, dev, peak)
     if "kvc" in wanted:
         phases["kvc_save_load"] = bench_kvc(args, dist, dev)
+    if "compress" in wanted:
+        phases.update(bench_compress(args, dist, dev, peak))
     clk = clocks.stop()
 
     K, W = args.steps, args.warmup

@@ -411,6 +411,71 @@ RKV_API rkv_status rkv_unpack_pages(const rkv_pool_view* pool, int32_t layer0, i
                                     const int32_t* pages, int64_t n, const void* src, uint32_t* d_status,
                                     rkv_stream_t stream);
 
+/* ---- compressor emission: aggregate, RMSNorm, RoPE, quantize-on-append -----
+ * Replaces the per-token pool step of rsLLM's compressor
+ * (crates/rsllm-models/src/dsv4/compressor.rs:264-357 after the two
+ * projections: APE bias, CompressedKvPool::accumulate_wide and maybe_emit
+ * (crates/rsllm-kvcache/src/dsv4/compressed.rs:310-417), the per-dimension
+ * softmax aggregate (:481-554), RMSNorm with an f64 sum of squares, the YaRN
+ * RoPE of the 64 tail lanes at position pos + 1 - ratio
+ * (crates/rsllm-backend-cpu/src/ops/rope.rs:128-172 with
+ * compress_rope_params, compressor.rs:372-397) and
+ * fp8_kv_quantize_row_inplace(row, 576, 64)) for a batch of tokens, writing
+ * each emitted row into the pool in the stored format.
+ *
+ * Rows are 576 lanes (512 latent + 64 RoPE); coff = 2 for ratio 4 (two lanes
+ * per token: p = columns [0, 576), c = [576, 1152)) and 1 otherwise;
+ * width = coff * 576.  A token at position pos writes its row into the state
+ * of its sequence; when (pos + 1) % ratio == 0 it emits compressed row
+ * k = (pos + 1) / ratio - 1 from the window's c lanes (positions
+ * pos + 1 - ratio .. pos) and, for coff 2, the p lanes of the window before it
+ * (positions before 0 read as kv 0, score -inf: a fresh state).  This equals
+ * rsLLM's streaming state machine whenever its window counter equals
+ * pos % ratio (streaming decode, or after finish_prefill_state).
+ *
+ * states:        device f32, n_states * rkv_compress_state_bytes(ratio) bytes:
+ *                per state the last coff * ratio rows of kv, then of score
+ *                (APE added), [2][coff*ratio][width], row = pos % (coff*ratio).
+ *                Written by this call for the last coff * ratio tokens of each
+ *                state; no initialisation is needed.
+ * kv, score:     device f32 [n_tok][width] (the compressor projections),
+ *                16-byte aligned.  The tokens of one state must appear in
+ *                consecutive entries at consecutive positions, in order, and
+ *                continue the positions of the previous call for that state.
+ * pos, state_of_token, emit_slot: device int32 [n_tok]; emit_slot is the pool
+ *                slot (page * 64 + row) of the row a token emits, -1 to drop it.
+ * ape:           device f32 [ratio][width] (read at pos % ratio), or NULL.
+ * norm:          device f32 [576] RMSNorm weight.
+ * rope_table:    device f32 [rope_rows][32][2] from rkv_compress_rope_table.
+ * Device status: an out-of-range state, position or RoPE row, or an emit slot
+ * outside the pool sets INDEX_OUT_OF_RANGE (that token is skipped); an
+ * emitted row with a non-finite latent lane sets NON_FINITE_INPUT and is not
+ * written (rsLLM returns that error from the quantizer, remapped to
+ * ShapeMismatch by compressor.rs:351-356).
+ * Numerics: every f32 and f64 operation is rsLLM's, in its order and rounding
+ * (no contraction), and exp is glibc's expf, so emitted rows are bit-exact. */
+RKV_API int64_t rkv_compress_state_bytes(int32_t ratio);
+/* Host: cos/sin * mscale of the 32 RoPE pairs of compressed rows k = 0 ..
+ * n_rows - 1 (position k * ratio), out f32 [n_rows][32][2] (host memory),
+ * computed with the host's libm exactly as rope.rs:128-172 does. */
+RKV_API rkv_status rkv_compress_rope_table(int32_t ratio, int64_t n_rows, float* out);
+/* Builds the expf correction table of this process and uploads it to the
+ * current device (done by the first rkv_compress_append otherwise; call it
+ * before capturing a CUDA graph). */
+RKV_API rkv_status rkv_compress_prepare(void);
+RKV_API rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t layer, int32_t ratio, float* states,
+                                       int64_t n_states, const float* kv, const float* score, int64_t n_tok,
+                                       const int32_t* pos, const int32_t* state_of_token, const int32_t* emit_slot,
+                                       const float* ape, const float* norm, const float* rope_table,
+                                       int64_t rope_rows, uint32_t* d_status, rkv_stream_t stream);
+/* expf as the compressor kernel evaluates it, on the host (host != 0, x and
+ * out host memory) or on the current device (x, out device memory): a
+ * double-precision exp rounded to f32, corrected from a table wherever the
+ * host's expf rounds differently.  Exposed to check it against expf. */
+RKV_API rkv_status rkv_compress_expf(const float* x, float* out, int64_t n, int32_t host, rkv_stream_t stream);
+/* Number of table entries (x whose expf differs from the rounded double). */
+RKV_API int64_t rkv_compress_expf_table_size(void);
+
 /* ---- codec pin ---------------------------------------------------------------
  * out[i] = E4M3 code the append kernel stores for the f32 lane value whose
  * bit pattern is first_bits + i (already divided by its block scale), i < n:

@@ -67,6 +67,16 @@ def lib() -> ctypes.CDLL:
         "rkvo_copy_pages": (None, [P, c_int64, c_int32, P, P, c_int64]),
         "rkvo_mla_decode": (c_uint32, [P, c_int64, c_int32, c_int32, P, c_int64, P, P, P, c_int32, P, c_int32, P,
                                        c_float, P, c_int]),
+        "rkvo_per_dim_softmax_aggregate": (None, [P, P, c_int64, c_int64, c_int64, c_int64, P]),
+        "rkvo_compressor_accumulate": (c_int, [P, P, P, c_int64, c_int64, P, P, P]),
+        "rkvo_compressor_finish_prefill": (None, [P, P, P, c_int64, c_int64, c_int64]),
+        "rkvo_rope_yarn_tail": (None, [P, c_uint32, c_uint32, c_uint32, c_uint32, ctypes.c_uint64, c_float, c_float,
+                                       c_float, c_float, c_float, c_float, c_int]),
+        "rkvo_compressor_postprocess": (None, [P, c_int64, P, c_uint32]),
+        "rkvo_compress_rope": (None, [P, c_int64, c_uint32]),
+        "rkvo_compress_append": (c_uint32, [P, c_int64, c_int32, c_int32, c_int32, P, P, P, c_int64, P, P, c_int64,
+                                            P, P, P, P, P, c_int]),
+        "rkvo_expf_batch": (None, [P, P, c_int64, c_int]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -245,3 +255,98 @@ def mla_decode(pool: np.ndarray, n_pages: int, n_layers: int, layer: int, page_t
                                ip, k, None if sk is None else _p(sk), float(scale), _p(out),
                                n_threads or threads())
     return out, st
+
+
+# ---- compressor emission -----------------------------------------------------------
+
+class Compressor:
+    """One reference compressor window state (compressed.rs:76-120 layout):
+    kv and score [coff*ratio, coff*head_dim], initial kv 0 / score -inf."""
+
+    def __init__(self, ratio: int, head_dim: int = ROW_DIM):
+        self.ratio, self.head_dim = ratio, head_dim
+        self.coff = 2 if ratio == 4 else 1
+        self.width = self.coff * head_dim
+        self.kv = np.zeros((self.coff * ratio, self.width), np.float32)
+        self.score = np.full((self.coff * ratio, self.width), -np.inf, np.float32)
+        self.count = np.zeros(1, np.uint32)
+
+    def accumulate(self, kv: np.ndarray, score: np.ndarray) -> np.ndarray | None:
+        """accumulate_wide: the aggregate row when the window is full, else None."""
+        kv = np.ascontiguousarray(kv, np.float32)
+        score = np.ascontiguousarray(score, np.float32)
+        assert kv.shape == (self.width,) and score.shape == (self.width,)
+        out = np.zeros(self.head_dim, np.float32)
+        got = lib().rkvo_compressor_accumulate(_p(self.kv), _p(self.score), _p(self.count), self.ratio,
+                                               self.head_dim, _p(kv), _p(score), _p(out))
+        return out if got else None
+
+    def accumulate_narrow(self, kv: np.ndarray, score: np.ndarray) -> np.ndarray | None:
+        """accumulate (compressed.rs's head_dim-wide entry): the row replicated
+        into every lane."""
+        return self.accumulate(np.tile(np.asarray(kv, np.float32), self.coff),
+                               np.tile(np.asarray(score, np.float32), self.coff))
+
+    def finish_prefill(self, n_tokens: int) -> None:
+        lib().rkvo_compressor_finish_prefill(_p(self.kv), _p(self.score), _p(self.count), self.ratio, self.head_dim,
+                                             n_tokens)
+
+
+def rope_yarn_tail(x: np.ndarray, n_head: int, head_dim: int, n_rot: int, pos: int, n_ctx_orig: int = 65536,
+                   freq_base: float = 10000.0, freq_scale: float = 1.0, ext_factor: float = 0.0,
+                   attn_factor: float = 1.0, beta_fast: float = 32.0, beta_slow: float = 1.0,
+                   inverse: bool = False) -> None:
+    """rope.rs:128-172 in place on x float32 [n_head * head_dim]."""
+    assert x.dtype == np.float32 and x.flags["C_CONTIGUOUS"] and x.size == n_head * head_dim
+    lib().rkvo_rope_yarn_tail(_p(x), n_head, head_dim, n_rot, pos, n_ctx_orig, freq_base, freq_scale, ext_factor,
+                              attn_factor, beta_fast, beta_slow, int(inverse))
+
+
+def compressor_postprocess(row: np.ndarray, norm: np.ndarray, comp_pos: int) -> None:
+    """compressor.rs:284-330 in place: RMSNorm then the compressed-layer RoPE."""
+    assert row.dtype == np.float32 and row.flags["C_CONTIGUOUS"]
+    norm = np.ascontiguousarray(norm, np.float32)
+    assert norm.shape == row.shape
+    lib().rkvo_compressor_postprocess(_p(row), row.size, _p(norm), comp_pos)
+
+
+def compress_rope(row: np.ndarray, comp_pos: int) -> None:
+    """The compressed-layer YaRN rotation of the last 64 lanes, in place."""
+    assert row.dtype == np.float32 and row.flags["C_CONTIGUOUS"]
+    lib().rkvo_compress_rope(_p(row), row.size, comp_pos)
+
+
+def compress_states(n_states: int, ratio: int):
+    """Reference-layout states for compress_append: (kv, score, count)."""
+    coff = 2 if ratio == 4 else 1
+    shape = (n_states, coff * ratio, coff * ROW_DIM)
+    return np.zeros(shape, np.float32), np.full(shape, -np.inf, np.float32), np.zeros(n_states, np.uint32)
+
+
+def compress_append(pool: np.ndarray, n_pages: int, n_layers: int, layer: int, ratio: int, states,
+                    kv: np.ndarray, score: np.ndarray, pos: np.ndarray, state_of: np.ndarray,
+                    emit_slot: np.ndarray, ape: np.ndarray | None, norm: np.ndarray,
+                    n_threads: int | None = None) -> int:
+    """The compressor step of rkvo_compress_append (token order, reference
+    state machine); returns the status bits."""
+    skv, ssc, cnt = states
+    kv = np.ascontiguousarray(kv, np.float32)
+    score = np.ascontiguousarray(score, np.float32)
+    pos = np.ascontiguousarray(pos, np.int32)
+    state_of = np.ascontiguousarray(state_of, np.int32)
+    emit_slot = np.ascontiguousarray(emit_slot, np.int32)
+    norm = np.ascontiguousarray(norm, np.float32)
+    ape = None if ape is None else np.ascontiguousarray(ape, np.float32)
+    n_tok = kv.shape[0]
+    return lib().rkvo_compress_append(_p(pool), n_pages, n_layers, layer, ratio, _p(skv), _p(ssc), _p(cnt),
+                                      skv.shape[0], _p(kv), _p(score), n_tok, _p(pos), _p(state_of),
+                                      _p(emit_slot), None if ape is None else _p(ape), _p(norm),
+                                      n_threads or threads())
+
+
+def expf(x: np.ndarray, n_threads: int | None = None) -> np.ndarray:
+    """The host libm's expf over an array."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    lib().rkvo_expf_batch(_p(x), _p(out), x.size, n_threads or threads())
+    return out

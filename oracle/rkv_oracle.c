@@ -19,6 +19,13 @@
  *       page-table-indexed pool (the reference has no paged pool; its plan is
  *       docs/03-HLD.md:363-369).
  *   - sparse row read: crates/rsllm-models/src/dsv4/attention.rs:549-560.
+ *   - compressor emission: crates/rsllm-kvcache/src/dsv4/compressed.rs
+ *       accumulate_wide :310-343, maybe_emit :360-417, finish_prefill_state
+ *       :443-455, per_dim_softmax_aggregate :481-554; crates/rsllm-models/src/
+ *       dsv4/compressor.rs:264-357 (APE bias, RMSNorm with an f64 sum of
+ *       squares, RoPE at pos + 1 - ratio, quantize) with compress_rope_params
+ *       :372-397; crates/rsllm-backend-cpu/src/ops/rope.rs:28-172 (YaRN).
+ *       exp, log, pow, cos and sin are the host libm's, as in the reference.
  *
  * Parity pin: the reference is Rust and cannot be built here (no cargo or
  * rustc), so this restatement is pinned by the reference's own known-answer
@@ -804,4 +811,260 @@ uint32_t rkvo_mla_decode(const uint8_t* pool, int64_t n_pages, int32_t n_layers,
         st |= jobs[t].status;
     }
     return st;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Compressor emission: crates/rsllm-kvcache/src/dsv4/compressed.rs          */
+/* (window state, per-dimension softmax aggregate) and                       */
+/* crates/rsllm-models/src/dsv4/compressor.rs (APE bias, RMSNorm, RoPE,      */
+/* quantize), with crates/rsllm-backend-cpu/src/ops/rope.rs for the rotation. */
+/* ------------------------------------------------------------------------ */
+
+/* compressed.rs:481-554.  coff 2: lane p = state[r][j] (lower half), lane c =
+ * state[ratio + r][head_dim + j] (upper half), one softmax over both. */
+void rkvo_per_dim_softmax_aggregate(const float* state_kv, const float* state_score, int64_t ratio,
+                                    int64_t head_dim, int64_t coff, int64_t width, float* out) {
+    for (int64_t j = 0; j < head_dim; ++j) {
+        float max_s = -INFINITY;
+        if (coff == 2) {
+            for (int64_t r = 0; r < ratio; ++r) {
+                float sp = state_score[r * width + j];
+                float sc = state_score[(ratio + r) * width + head_dim + j];
+                if (sp > max_s) max_s = sp;
+                if (sc > max_s) max_s = sc;
+            }
+        } else {
+            for (int64_t r = 0; r < ratio; ++r) {
+                float s = state_score[r * width + j];
+                if (s > max_s) max_s = s;
+            }
+        }
+        if (max_s <= -INFINITY * 0.5f) { out[j] = 0.0f; continue; }
+        float denom = 0.0f, numer = 0.0f;
+        if (coff == 2) {
+            for (int64_t r = 0; r < ratio; ++r) {
+                int64_t off_p = r * width + j, off_c = (ratio + r) * width + head_dim + j;
+                float wp = expf(state_score[off_p] - max_s);
+                float wc = expf(state_score[off_c] - max_s);
+                denom += wp + wc;
+                numer += wp * state_kv[off_p] + wc * state_kv[off_c];
+            }
+        } else {
+            for (int64_t r = 0; r < ratio; ++r) {
+                int64_t off = r * width + j;
+                float w = expf(state_score[off] - max_s);
+                denom += w;
+                numer += w * state_kv[off];
+            }
+        }
+        out[j] = denom > 0.0f ? numer / denom : 0.0f;
+    }
+}
+
+static inline int64_t cmp_coff(int64_t ratio) { return ratio == 4 ? 2 : 1; }
+
+/* compressed.rs:310-343 (accumulate_wide) + :360-417 (maybe_emit) for a state
+ * of [coff*ratio][coff*head_dim] kv and score rows.  Returns 1 when the
+ * window is full and out[head_dim] holds the aggregate (the capacity check
+ * of the reference's row store is the caller's). */
+int rkvo_compressor_accumulate(float* state_kv, float* state_score, uint32_t* state_count, int64_t ratio,
+                               int64_t head_dim, const float* kv, const float* score, float* out) {
+    int64_t coff = cmp_coff(ratio), width = coff * head_dim, slot = *state_count;
+    int64_t row = coff == 2 ? ratio + slot : slot;
+    memcpy(state_kv + row * width, kv, (size_t)width * 4);
+    memcpy(state_score + row * width, score, (size_t)width * 4);
+    *state_count += 1;
+    if (*state_count < (uint32_t)ratio) return 0;
+    rkvo_per_dim_softmax_aggregate(state_kv, state_score, ratio, head_dim, coff, width, out);
+    if (coff == 2) {
+        for (int64_t r = 0; r < ratio; ++r) {
+            memmove(state_kv + r * width, state_kv + (ratio + r) * width, (size_t)width * 4);
+            memmove(state_score + r * width, state_score + (ratio + r) * width, (size_t)width * 4);
+        }
+        for (int64_t r = 0; r < ratio; ++r) {
+            memmove(state_kv + (ratio + r) * width, state_kv + r * width, (size_t)width * 4);
+            memmove(state_score + (ratio + r) * width, state_score + r * width, (size_t)width * 4);
+        }
+    } else {
+        for (int64_t i = 0; i < ratio * width; ++i) { state_kv[i] = 0.0f; state_score[i] = -INFINITY; }
+    }
+    *state_count = 0;
+    return 1;
+}
+
+/* compressed.rs:443-455. */
+void rkvo_compressor_finish_prefill(float* state_kv, float* state_score, uint32_t* state_count, int64_t ratio,
+                                    int64_t head_dim, int64_t n_tokens) {
+    int64_t coff = cmp_coff(ratio), width = coff * head_dim, rem = n_tokens % ratio;
+    for (int64_t row = coff == 2 ? ratio + rem : rem; row < coff * ratio; ++row)
+        for (int64_t j = 0; j < width; ++j) { state_kv[row * width + j] = 0.0f; state_score[row * width + j] = -INFINITY; }
+    *state_count = (uint32_t)rem;
+}
+
+/* rope.rs:28-31 */
+static float yarn_ramp(float low, float high, int32_t i0) {
+    float y = ((float)(i0 / 2) - low) / fmaxf(high - low, 0.001f);
+    y = y < 0.0f ? 0.0f : (y > 1.0f ? 1.0f : y);
+    return 1.0f - y;
+}
+
+/* rope.rs:37-39 (PI is f32 pi) */
+static float yarn_corr_dim(int32_t n_dims, uint64_t n_ctx_orig, float n_rot, float base) {
+    const float pi = 3.14159265358979323846f;
+    return ((float)n_dims * logf((float)n_ctx_orig / (n_rot * 2.0f * pi))) / (2.0f * logf(base));
+}
+
+/* rope.rs:128-172, x = [n_head][head_dim], the last n_rot lanes of each head
+ * rotated in pairs. */
+void rkvo_rope_yarn_tail(float* x, uint32_t n_head, uint32_t head_dim, uint32_t n_rot, uint32_t pos,
+                         uint64_t n_ctx_orig, float freq_base, float freq_scale, float ext_factor, float attn_factor,
+                         float beta_fast, float beta_slow, int inverse) {
+    uint32_t n_nope = head_dim - n_rot;
+    float theta_scale = powf(freq_base, -2.0f / (float)n_rot);
+    float sin_sign = inverse ? -1.0f : 1.0f;
+    float corr0 = 0.0f, corr1 = 0.0f;
+    if (ext_factor != 0.0f) {
+        corr0 = fmaxf(floorf(yarn_corr_dim((int32_t)n_rot, n_ctx_orig, beta_fast, freq_base)), 0.0f);
+        corr1 = fminf(ceilf(yarn_corr_dim((int32_t)n_rot, n_ctx_orig, beta_slow, freq_base)), (float)((int32_t)n_rot - 1));
+    }
+    for (uint32_t h = 0; h < n_head; ++h) {
+        float* tail = x + (size_t)h * head_dim + n_nope;
+        float theta_extrap = (float)pos;
+        for (uint32_t i = 0; i < n_rot; i += 2) {
+            float theta_interp = freq_scale * theta_extrap;
+            float theta = theta_interp;
+            float mscale = attn_factor;
+            if (ext_factor != 0.0f) {
+                float ramp_mix = yarn_ramp(corr0, corr1, (int32_t)i) * ext_factor;
+                theta = theta_interp * (1.0f - ramp_mix) + theta_extrap * ramp_mix;
+                mscale *= 1.0f + 0.1f * logf(1.0f / freq_scale);
+            }
+            float c = cosf(theta) * mscale;
+            float s = sin_sign * sinf(theta) * mscale;
+            float x0 = tail[i], x1 = tail[i + 1];
+            tail[i] = x0 * c - x1 * s;
+            tail[i + 1] = x0 * s + x1 * c;
+            theta_extrap *= theta_scale;
+        }
+    }
+}
+
+/* compressor.rs:284-330: RMSNorm with an f64 sum of squares (DSV4_RMS_EPS
+ * 1e-6), then the YaRN rotation of the last 64 lanes with
+ * compress_rope_params (compressor.rs:372-397) at comp_pos. */
+/* The compressed-layer rotation alone (compress_rope_params,
+ * compressor.rs:372-397) of the last 64 lanes of a head_dim row. */
+void rkvo_compress_rope(float* row, int64_t head_dim, uint32_t comp_pos) {
+    const float scale_factor = 16.0f, freq_scale = 1.0f / scale_factor;
+    const float attn_factor = 1.0f / (1.0f + 0.1f * logf(1.0f / freq_scale));
+    rkvo_rope_yarn_tail(row, 1, (uint32_t)head_dim, ROPE, comp_pos, 65536, 160000.0f, freq_scale, 1.0f, attn_factor,
+                        32.0f, 1.0f, 0);
+}
+
+void rkvo_compressor_postprocess(float* row, int64_t head_dim, const float* norm, uint32_t comp_pos) {
+    double ss = 0.0;
+    for (int64_t j = 0; j < head_dim; ++j) ss += (double)row[j] * (double)row[j];
+    float rms = 1.0f / sqrtf((float)(ss / (double)head_dim) + 1e-6f);
+    for (int64_t j = 0; j < head_dim; ++j) row[j] = row[j] * rms * norm[j];
+    rkvo_compress_rope(row, head_dim, comp_pos);
+}
+
+typedef struct {
+    uint8_t* pool; int64_t n_pages; int32_t n_layers; int32_t layer; int32_t ratio;
+    float* state_kv; float* state_score; uint32_t* state_count; int64_t n_states;
+    const float* kv; const float* score; int64_t n_tok; const int32_t* pos; const int32_t* state_of;
+    const int32_t* emit_slot; const float* ape; const float* norm;
+    int32_t t_id, n_workers; uint32_t status;
+} cmp_job;
+
+static void* cmp_worker(void* p) {
+    cmp_job* j = (cmp_job*)p;
+    int64_t coff = cmp_coff(j->ratio), width = coff * ROW_DIM, state_floats = coff * j->ratio * width;
+    float* sc = (float*)malloc((size_t)width * 4);
+    float row[ROW_DIM];
+    uint8_t codes[LATENT];
+    float scales[NBLK];
+    uint16_t rope[ROPE];
+    for (int64_t t = 0; t < j->n_tok; ++t) {
+        int32_t s = j->state_of[t], pos = j->pos[t];
+        if (s < 0 || s >= j->n_states || pos < 0) { if (j->t_id == 0) j->status |= 1u << RKVO_INDEX_OUT_OF_RANGE; continue; }
+        if (s % j->n_workers != j->t_id) continue;
+        /* compressor.rs:264-269: sc_cur += ape column pos % ratio */
+        memcpy(sc, j->score + t * width, (size_t)width * 4);
+        if (j->ape)
+            for (int64_t c = 0; c < width; ++c) sc[c] += j->ape[(int64_t)(pos % j->ratio) * width + c];
+        if (!rkvo_compressor_accumulate(j->state_kv + s * state_floats, j->state_score + s * state_floats,
+                                        j->state_count + s, j->ratio, ROW_DIM, j->kv + t * width, sc, row))
+            continue;
+        int32_t slot = j->emit_slot[t];
+        if (slot < 0) continue;
+        int64_t page = slot / PAGE_TOKENS, off = slot % PAGE_TOKENS;
+        if (page >= j->n_pages) { j->status |= 1u << RKVO_INDEX_OUT_OF_RANGE; continue; }
+        uint32_t comp_pos = (uint32_t)pos + 1 >= (uint32_t)j->ratio ? (uint32_t)pos + 1 - (uint32_t)j->ratio : 0;
+        rkvo_compressor_postprocess(row, ROW_DIM, j->norm, comp_pos);
+        int rc = rkvo_quantize_row_f32(row, ROW_DIM, ROPE, codes, scales, rope);
+        if (rc != RKVO_OK) { j->status |= 1u << rc; continue; }
+        uint8_t* pg = page_ptr(j->pool, j->n_pages, j->layer, page);
+        memcpy(pg + off * LATENT, codes, LATENT);
+        memcpy(pg + CODES_BYTES + off * NBLK * 4, scales, NBLK * 4);
+        memcpy(pg + CODES_BYTES + SCALES_BYTES + off * ROPE * 2, rope, ROPE * 2);
+    }
+    free(sc);
+    return NULL;
+}
+
+/* One compressor step for a batch of tokens (576-lane rows; kv, score
+ * [n_tok][coff*576]; ape [ratio][coff*576] or NULL; norm [576]), token by
+ * token in input order over the reference-layout states
+ * (state_kv/state_score [n_states][coff*ratio][coff*576], state_count
+ * [n_states]).  A row emitted by token t is post-processed, quantized and
+ * stored at emit_slot[t] (< 0: dropped).  States are split over threads. */
+uint32_t rkvo_compress_append(uint8_t* pool, int64_t n_pages, int32_t n_layers, int32_t layer, int32_t ratio,
+                              float* state_kv, float* state_score, uint32_t* state_count, int64_t n_states,
+                              const float* kv, const float* score, int64_t n_tok, const int32_t* pos,
+                              const int32_t* state_of, const int32_t* emit_slot, const float* ape, const float* norm,
+                              int n_threads) {
+    if (n_tok <= 0) return 0;
+    if (layer < 0 || layer >= n_layers) return 1u << RKVO_INVALID_LAYER;
+    if (ratio <= 0) return 1u << RKVO_SHAPE_MISMATCH;
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > 256) n_threads = 256;
+    if (n_states > 0 && n_threads > n_states) n_threads = (int)n_states;
+    pthread_t th[256];
+    cmp_job jobs[256];
+    for (int t = 0; t < n_threads; ++t) {
+        jobs[t] = (cmp_job){pool, n_pages, n_layers, layer, ratio, state_kv, state_score, state_count, n_states,
+                            kv, score, n_tok, pos, state_of, emit_slot, ape, norm, t, n_threads, 0};
+        if (n_threads == 1) cmp_worker(&jobs[t]);
+        else pthread_create(&th[t], NULL, cmp_worker, &jobs[t]);
+    }
+    uint32_t st = 0;
+    for (int t = 0; t < n_threads; ++t) {
+        if (n_threads > 1) pthread_join(th[t], NULL);
+        st |= jobs[t].status;
+    }
+    return st;
+}
+
+/* The host libm's expf over an array (the reference's f32::exp), for checking
+ * the product's expf rounding exhaustively. */
+typedef struct { const float* x; float* out; int64_t b, e; } expf_job;
+static void* expf_worker(void* p) {
+    expf_job* j = (expf_job*)p;
+    for (int64_t i = j->b; i < j->e; ++i) j->out[i] = expf(j->x[i]);
+    return NULL;
+}
+void rkvo_expf_batch(const float* x, float* out, int64_t n, int n_threads) {
+    if (n <= 0) return;
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > 256) n_threads = 256;
+    pthread_t th[256];
+    expf_job jobs[256];
+    for (int t = 0; t < n_threads; ++t) {
+        jobs[t] = (expf_job){x, out, n * t / n_threads, n * (t + 1) / n_threads};
+        if (n_threads == 1) expf_worker(&jobs[t]);
+        else pthread_create(&th[t], NULL, expf_worker, &jobs[t]);
+    }
+    if (n_threads > 1)
+        for (int t = 0; t < n_threads; ++t) pthread_join(th[t], NULL);
 }

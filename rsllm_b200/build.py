@@ -19,7 +19,7 @@ LIB = PKG / "librsllm_kv_cuda.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
-    "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2,-fvisibility=hidden",
+    "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2,-fvisibility=hidden,-ffp-contract=off",
     "--shared", "-cudart", "static", "-Xptxas", "-warn-spills",
 ]
 

@@ -1,0 +1,118 @@
+"""Compressor emission on the GPU, mirroring rsLLM's compressed-pool append path.
+
+rsLLM's compressor (crates/rsllm-models/src/dsv4/compressor.rs:223-362) turns
+every token into a (kv, score) row pair of ``width = coff * head_dim`` lanes,
+adds the APE bias to the score, and hands both to
+``CompressedKvPool::accumulate_wide`` (crates/rsllm-kvcache/src/dsv4/
+compressed.rs:310-343), which keeps a window state and, every ``ratio``
+tokens, emits one per-dimension softmax aggregate (:360-417, :481-554).  The
+emitted row is RMS-normalised, its 64 tail lanes are YaRN-rotated and it is
+FP8-quantized (compressor.rs:284-357).
+
+``CompressorBank`` holds the window states of many (sequence, layer)
+compressors of one ratio on the device and runs that whole step for a batch of
+tokens in one call (``rkv_compress_append``), writing each emitted row into a
+``PagedKvPool`` slot in the stored FP8 format.  Rows are 576 lanes here (512
+latent + 64 RoPE, the pool's row format); ratio 4 uses two lanes per token
+(coff 2) as rsLLM does.  Results are bit-exact with rsLLM's f32/f64
+arithmetic, including the host libm's expf and cos/sin.
+"""
+from __future__ import annotations
+
+from ctypes import byref
+
+import numpy as np
+import torch
+
+from . import _abi
+from ._abi import ROW_DIM
+from .kvcache import PagedKvPool, ShapeMismatch, _need, _ptr, _stream, check
+
+__all__ = ["CompressorBank", "compress_rope_table", "compress_expf", "compress_expf_table_size"]
+
+
+def compress_rope_table(ratio: int, n_rows: int) -> np.ndarray:
+    """cos/sin * mscale of the 32 RoPE pairs of compressed rows 0 .. n_rows-1
+    (position k * ratio): f32 [n_rows, 32, 2], computed on the host with its
+    libm as rope.rs:128-172 does with compress_rope_params."""
+    out = np.empty((n_rows, 32, 2), dtype=np.float32)
+    check(_abi.load().rkv_compress_rope_table(ratio, n_rows, out.ctypes.data), "compress_rope_table")
+    return out
+
+
+def compress_expf(x: torch.Tensor | np.ndarray) -> torch.Tensor | np.ndarray:
+    """The kernel's expf (the host libm's rounding) over f32 values: on the
+    device for a CUDA tensor, on the host for a numpy array."""
+    lib = _abi.load()
+    if isinstance(x, np.ndarray):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty_like(x)
+        check(lib.rkv_compress_expf(x.ctypes.data, out.ctypes.data, x.size, 1, None), "compress_expf")
+        return out
+    _need(x, torch.float32, "x", x.device)
+    out = torch.empty_like(x)
+    check(lib.rkv_compress_expf(_ptr(x), _ptr(out), x.numel(), 0, _stream(None)), "compress_expf")
+    return out
+
+
+def compress_expf_table_size() -> int:
+    """Entries of this process's expf correction table."""
+    return int(_abi.load().rkv_compress_expf_table_size())
+
+
+class CompressorBank:
+    """Window states of ``n_states`` compressors of one ratio (one per
+    sequence and layer, indexed by the caller), resident on one device.
+
+    ``max_positions`` bounds the token positions the bank serves: the RoPE
+    table holds the rows of compressed positions below it."""
+
+    def __init__(self, ratio: int, n_states: int, device: int | str | torch.device | None = None,
+                 max_positions: int = 1 << 17):
+        if ratio <= 0 or ratio > 128:
+            raise ShapeMismatch(f"CompressorBank: ratio {ratio} outside [1, 128]")
+        self.lib = _abi.load()
+        dev = torch.device("cuda", device) if isinstance(device, int) else \
+            torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
+        self.ratio = ratio
+        self.coff = 2 if ratio == 4 else 1
+        self.width = self.coff * ROW_DIM
+        self.n_states = n_states
+        nbytes = int(self.lib.rkv_compress_state_bytes(ratio))
+        self.states = torch.zeros((n_states, nbytes // 4), dtype=torch.float32, device=self.device)
+        rows = max_positions // ratio + 1
+        self.rope = torch.from_numpy(compress_rope_table(ratio, rows)).to(self.device)
+        with torch.cuda.device(self.device):
+            check(self.lib.rkv_compress_prepare(), "CompressorBank")
+
+    def append(self, pool: PagedKvPool, layer: int, kv: torch.Tensor, score: torch.Tensor, pos: torch.Tensor,
+               state_of_token: torch.Tensor, emit_slot: torch.Tensor, norm: torch.Tensor,
+               ape: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> None:
+        """One compressor step for ``n_tok`` tokens (``rkv_compress_append``):
+        kv, score f32 [n_tok, width]; pos, state_of_token, emit_slot int32
+        [n_tok]; norm f32 [576]; ape f32 [ratio, width] or None.  Tokens of one
+        state are consecutive entries at consecutive positions.  A token with
+        (pos + 1) % ratio == 0 writes its emitted row at ``emit_slot`` (< 0:
+        dropped).  Device-side errors land in ``pool.status``."""
+        for t, n in ((kv, "kv"), (score, "score"), (norm, "norm")):
+            _need(t, torch.float32, n, self.device)
+        for t, n in ((pos, "pos"), (state_of_token, "state_of_token"), (emit_slot, "emit_slot")):
+            _need(t, torch.int32, n, self.device)
+        n_tok = kv.shape[0] if kv.dim() == 2 else -1
+        if kv.dim() != 2 or kv.shape[1] != self.width or score.shape != kv.shape or \
+                pos.shape != (n_tok,) or state_of_token.shape != (n_tok,) or emit_slot.shape != (n_tok,) or \
+                norm.shape != (ROW_DIM,):
+            raise ShapeMismatch(f"CompressorBank.append: kv/score [n_tok, {self.width}], pos/state_of_token/"
+                                f"emit_slot [n_tok], norm [{ROW_DIM}]")
+        if ape is not None:
+            _need(ape, torch.float32, "ape", self.device)
+            if ape.shape != (self.ratio, self.width):
+                raise ShapeMismatch(f"CompressorBank.append: ape must be [{self.ratio}, {self.width}]")
+        check(self.lib.rkv_compress_append(byref(pool.view), layer, self.ratio, _ptr(self.states), self.n_states,
+                                           _ptr(kv), _ptr(score), n_tok, _ptr(pos), _ptr(state_of_token),
+                                           _ptr(emit_slot), _ptr(ape), _ptr(norm), _ptr(self.rope),
+                                           self.rope.shape[0], _ptr(pool.status), _stream(stream)),
+              "CompressorBank.append")
