@@ -21,15 +21,16 @@
 // it returns the neighbour of the correctly rounded value.  The kernel
 // evaluates exp in double precision (Tang's table-driven method: 2^(k/256)
 // from a 256-entry table times a cubic in the reduced argument, |r| <= ln2/512,
-// relative error about 2^-42), rounds to f32, and wherever the double lies
-// within 2^-7 f32 ulp of a rounding midpoint (about 1% of inputs, the only
-// place a libm within 0.51 ulp can round differently) looks x up in a table of
-// the inputs where the host's expf differs from that rounding.  The host
-// builds the table once per process by evaluating the identical double
-// algorithm (same IEEE operations) over every f32 in [-150, 0]; it is correct
-// by construction for inputs inside the band, and an exhaustive test checks
-// that no input outside the band differs.  RoPE cos/sin come from a host table
-// computed with the host's libm as rope.rs does.
+// relative error about 2^-42) and rounds it to f32.  Only where that double
+// lies within a narrow band around an f32 rounding midpoint can the libm round
+// the other way; there the kernel looks x up in a hash table of the inputs
+// where the host's expf differs from that rounding.  The host builds the table
+// once per process by evaluating the identical double algorithm (the same IEEE
+// operations) over every f32 in [-150, 0] and calling its expf wherever the
+// double lies within 2^-5 ulp of a midpoint; the band is the largest distance
+// at which it found a difference (2^-9.25 ulp for glibc 2.39, so about 0.4% of
+// inputs are looked up).  An exhaustive test checks every input.  RoPE cos/sin
+// come from a host table computed with the host's libm as rope.rs does.
 #include <math.h>
 #include <stdio.h>
 #include <string.h>
@@ -47,18 +48,17 @@ namespace rkv {
 
 // ---- exp: double evaluation shared by host and device --------------------------
 
-constexpr int kExpTableBits = 8;                       // 2^(j/256)
-constexpr uint32_t kExpMaxKey = 0x43160000u;           // |x| bits of 150.0f
-constexpr int kExpBucketShift = 14;
-constexpr int kExpBuckets = (int)(kExpMaxKey >> kExpBucketShift) + 2;
-constexpr int kExpMaxEntries = 1 << 18;
-constexpr uint32_t kExpBand = 1u << 22;               // 2^-7 f32 ulp, in units of the 29 dropped bits
+constexpr int kExpTableBits = 8;                 // 2^(j/256)
+constexpr uint32_t kExpMaxKey = 0x43160000u;     // |x| bits of 150.0f
+constexpr int kExpHashBits = 19;                 // 2 MB open-addressing table, load factor ~0.2
+constexpr uint32_t kExpScanWindow = 1u << 24;    // 2^-5 ulp, in units of the 29 dropped bits
 
 struct ExpConsts {
-  double inv_step;  // 256 / ln 2
+  float inv_step_f;  // 256 / ln 2 rounded to f32
   double step_hi;   // ln 2 / 256, 21 significant bits (k * step_hi is exact)
   double step_lo;   // ln 2 / 256 - step_hi
   double c2, c3;    // 1/2, 1/6
+  int64_t band;     // |dropped bits - 2^28| at or below which x is looked up
 };
 
 __host__ __device__ __forceinline__ double d_mul(double a, double b) {
@@ -101,26 +101,40 @@ __host__ __device__ __forceinline__ double d_from_bits(uint64_t b) {
 #endif
 }
 
+__host__ __device__ __forceinline__ float f_mul(float a, float b) {
+#ifdef __CUDA_ARCH__
+  return __fmul_rn(a, b);
+#else
+  return a * b;
+#endif
+}
+
 // exp(x) in double for x in [-150, 0]; the same IEEE operations on both sides.
+// k = rint(x * 256/ln2) is taken in f32 (any integer near the quotient
+// serves: r stays within 1.01 * ln2/512); the scaling by 2^(k/256) adds to the
+// exponent field (exact: every result is a normal double).
 __host__ __device__ __forceinline__ double exp_core(float xf, const ExpConsts& K, const double* T) {
   const double x = (double)xf;
-  const double shift = 6755399441055744.0;  // 1.5 * 2^52: adding it rounds to an integer
-  const double k = d_sub(d_add(d_mul(x, K.inv_step), shift), shift);
+  const float kf = rintf(f_mul(xf, K.inv_step_f));
+  const double k = (double)kf;
   const double r = d_sub(d_sub(x, d_mul(k, K.step_hi)), d_mul(k, K.step_lo));
   double p = d_add(d_mul(K.c3, r), K.c2);
   p = d_add(d_mul(p, r), 1.0);
   p = d_add(d_mul(p, r), 1.0);
-  const long long ki = (long long)k;
+  const int ki = (int)kf;
   const double y = d_mul(T[ki & ((1 << kExpTableBits) - 1)], p);
-  const double scale = d_from_bits((uint64_t)((ki >> kExpTableBits) + 1023) << 52);
-  return d_mul(y, scale);
+  return d_from_bits(d_bits(y) + ((uint64_t)(int64_t)(ki >> kExpTableBits) << 52));
 }
 
 // True where the rounding of d to f32 may differ from the host's expf.
-__host__ __device__ __forceinline__ bool exp_in_band(double d) {
+__host__ __device__ __forceinline__ bool exp_in_band(double d, int64_t band) {
   if (d < 1.1754943508222875e-38) return true;  // f32 subnormal results: always looked up
   const int64_t low = (int64_t)(d_bits(d) & ((1ull << 29) - 1)) - (1ll << 28);
-  return (low < 0 ? -low : low) <= (int64_t)kExpBand;
+  return (low < 0 ? -low : low) <= band;
+}
+
+__host__ __device__ __forceinline__ uint32_t exp_hash(uint32_t key) {
+  return (key * 0x9E3779B1u) >> (32 - kExpHashBits);
 }
 
 // ---- host table ------------------------------------------------------------------
@@ -128,8 +142,8 @@ __host__ __device__ __forceinline__ bool exp_in_band(double d) {
 struct ExpHost {
   ExpConsts K;
   double T[1 << kExpTableBits];
-  std::vector<uint32_t> entries;  // |x| bits ascending; bit 31: host expf = rounded + 1 ulp (else - 1)
-  std::vector<uint32_t> buckets;  // first entry of each key >> kExpBucketShift
+  std::vector<uint32_t> hash;  // |x| bits | (bit 31: host expf = rounded + 1 ulp, else - 1); 0 = empty
+  int64_t n_entries = 0;
   bool ok = false;
   char err[160] = {0};
 };
@@ -151,17 +165,19 @@ static uint32_t float_to_bits(float f) {
 static void build_exp_host() {
   ExpHost& E = g_exp;
   const long double ln2 = 0.693147180559945309417232121458176568L;
-  E.K.inv_step = (double)(256.0L / ln2);
+  E.K.inv_step_f = (float)(256.0L / ln2);
   const double step = (double)(ln2 / 256.0L);
   E.K.step_hi = d_from_bits(d_bits(step) & ~((1ull << 32) - 1));
   E.K.step_lo = (double)(ln2 / 256.0L - (long double)E.K.step_hi);
   E.K.c2 = 0.5;
   E.K.c3 = 1.0 / 6.0;
+  E.K.band = kExpScanWindow;
   for (int j = 0; j < (1 << kExpTableBits); ++j) E.T[j] = (double)exp2l((long double)j / 256.0L);
 
   unsigned nt = std::thread::hardware_concurrency();
   nt = nt < 1 ? 1 : (nt > 64 ? 64 : nt);
   std::vector<std::vector<uint32_t>> part(nt);
+  std::vector<int64_t> far(nt, 0);
   std::vector<int> bad(nt, 0);
   std::vector<std::thread> th;
   for (unsigned t = 0; t < nt; ++t)
@@ -171,37 +187,48 @@ static void build_exp_host() {
       for (uint32_t key = a; key < b; ++key) {
         const float x = bits_to_float(key | 0x80000000u);
         const double d = exp_core(x, E.K, E.T);
-        if (!exp_in_band(d)) continue;
+        if (!exp_in_band(d, kExpScanWindow)) continue;
         const uint32_t f = float_to_bits((float)d), g = float_to_bits(expf(x));
         if (f == g) continue;
         if (g != f + 1 && g + 1 != f) {
           bad[t] = 1;
           continue;
         }
+        if (d >= 1.1754943508222875e-38) {
+          const int64_t low = (int64_t)(d_bits(d) & ((1ull << 29) - 1)) - (1ll << 28);
+          far[t] = std::max(far[t], low < 0 ? -low : low);
+        }
         part[t].push_back(key | (g > f ? 0x80000000u : 0u));
       }
     });
   for (auto& x : th) x.join();
-  size_t total = 0;
+  int64_t band = 1;
   for (unsigned t = 0; t < nt; ++t) {
     if (bad[t]) {
       snprintf(E.err, sizeof E.err, "host expf differs from the double evaluation by more than one ulp");
       return;
     }
-    total += part[t].size();
+    band = std::max(band, far[t]);
+    E.n_entries += (int64_t)part[t].size();
   }
-  if (total > (size_t)kExpMaxEntries) {
-    snprintf(E.err, sizeof E.err, "expf correction table has %zu entries (capacity %d)", total, kExpMaxEntries);
+  if (band > (int64_t)kExpScanWindow / 2) {
+    snprintf(E.err, sizeof E.err, "host expf rounds differently %.4f ulp from a midpoint",
+             (double)band / (double)(1 << 29));
     return;
   }
-  E.entries.reserve(total);
-  for (unsigned t = 0; t < nt; ++t) E.entries.insert(E.entries.end(), part[t].begin(), part[t].end());
-  E.buckets.assign(kExpBuckets + 1, 0);
-  size_t e = 0;
-  for (int b = 0; b <= kExpBuckets; ++b) {
-    while (e < E.entries.size() && ((E.entries[e] & 0x7fffffffu) >> kExpBucketShift) < (uint32_t)b) ++e;
-    E.buckets[b] = (uint32_t)e;
+  if (E.n_entries > (1 << kExpHashBits) / 2) {
+    snprintf(E.err, sizeof E.err, "expf correction table has %lld entries", (long long)E.n_entries);
+    return;
   }
+  E.K.band = band;
+  E.hash.assign((size_t)1 << kExpHashBits, 0u);
+  const uint32_t mask = (1u << kExpHashBits) - 1;
+  for (unsigned t = 0; t < nt; ++t)
+    for (uint32_t v : part[t]) {
+      uint32_t h = exp_hash(v & 0x7fffffffu);
+      while (E.hash[h]) h = (h + 1) & mask;
+      E.hash[h] = v;
+    }
   E.ok = true;
 }
 
@@ -210,30 +237,35 @@ static const ExpHost* exp_host() {
   return g_exp.ok ? &g_exp : nullptr;
 }
 
-// Host-side lookup: the value the kernel produces.
+// The correction for an in-band x: +1, -1 or 0 ulp (table probe).
+__host__ __device__ __forceinline__ int exp_correction(uint32_t key, const uint32_t* hash) {
+  const uint32_t mask = (1u << kExpHashBits) - 1;
+  for (uint32_t h = exp_hash(key);; h = (h + 1) & mask) {
+    const uint32_t v = hash[h];
+    if (v == 0) return 0;
+    if ((v & 0x7fffffffu) == key) return (v >> 31) ? 1 : -1;
+  }
+}
+
+// Host-side evaluation: the value the kernel produces.
 static float expf_table_host(float x, const ExpHost& E) {
   if (x != x) return x;
   if (!(x >= -150.0f)) return 0.0f;
-  if (x > 0.0f) return (float)exp((double)x);  // outside the aggregate's domain
   const double d = exp_core(x, E.K, E.T);
   uint32_t f = float_to_bits((float)d);
-  if (exp_in_band(d)) {
-    const uint32_t key = float_to_bits(x) & 0x7fffffffu;
-    const uint32_t b = key >> kExpBucketShift;
-    for (uint32_t i = E.buckets[b]; i < E.buckets[b + 1]; ++i)
-      if ((E.entries[i] & 0x7fffffffu) == key) {
-        f = (E.entries[i] >> 31) ? f + 1 : f - 1;
-        break;
-      }
-  }
+  if (exp_in_band(d, E.K.band)) f += exp_correction(float_to_bits(x) & 0x7fffffffu, E.hash.data());
   return bits_to_float(f);
 }
 
 // ---- device copies of the table ------------------------------------------------
 
 static __device__ double g_exp_T[1 << kExpTableBits];
-static __device__ uint32_t g_exp_buckets[kExpBuckets + 1];
-static __device__ uint32_t g_exp_entries[kExpMaxEntries];
+static __device__ uint32_t g_exp_hash[1 << kExpHashBits];
+// Stand-ins for the rows of positions before a sequence's start (kv 0,
+// score -inf) and for "no APE" (adding +0.0 to a score changes at most the
+// sign of a zero, which no exp or comparison downstream can see).
+static __device__ float g_zero_row[2 * kRowDim];
+static __device__ float g_neginf_row[2 * kRowDim];
 
 constexpr int kMaxDevices = 64;
 static bool g_exp_uploaded[kMaxDevices];
@@ -249,39 +281,50 @@ static rkv_status prepare_device(const char* what) {
   std::lock_guard<std::mutex> lock(g_exp_mu);
   if (g_exp_uploaded[dev]) return RKV_OK;
   e = cudaMemcpyToSymbol(g_exp_T, E->T, sizeof E->T);
-  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_exp_buckets, E->buckets.data(), E->buckets.size() * 4);
-  if (e == cudaSuccess && !E->entries.empty())
-    e = cudaMemcpyToSymbol(g_exp_entries, E->entries.data(), E->entries.size() * 4);
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_exp_hash, E->hash.data(), E->hash.size() * 4);
+  if (e == cudaSuccess) {
+    std::vector<float> ninf(2 * kRowDim, -INFINITY);
+    e = cudaMemcpyToSymbol(g_neginf_row, ninf.data(), ninf.size() * 4);
+  }
   if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "%s: uploading the expf table: %s", what, cudaGetErrorString(e));
   g_exp_uploaded[dev] = true;
   return RKV_OK;
 }
 
-// expf as the host's libm rounds it, for the x = score - max of the aggregate
-// (x <= 0 or NaN).
-__device__ __forceinline__ float expf_host_rounding(float x, const ExpConsts& K) {
-  if (!(x >= -150.0f)) return x != x ? x : 0.0f;
-  if (x > 0.0f) return __double2float_rn(exp((double)x));  // outside the aggregate's domain
-  const double d = exp_core(x, K, g_exp_T);
-  uint32_t f = __float_as_uint(__double2float_rn(d));
-  if (exp_in_band(d)) {
-    const uint32_t key = __float_as_uint(x) & 0x7fffffffu;
-    const uint32_t b = key >> kExpBucketShift;
-    const uint32_t e1 = g_exp_buckets[b + 1];
-    for (uint32_t i = g_exp_buckets[b]; i < e1; ++i) {
-      const uint32_t v = g_exp_entries[i];
-      if ((v & 0x7fffffffu) == key) {
-        f = (v >> 31) ? f + 1 : f - 1;
-        break;
-      }
-    }
-  }
-  return __uint_as_float(f);
+// expf as the host's libm rounds it, in two steps so that a warp's table
+// probes can be gathered: exp_first gives the rounded double and whether x is
+// in the band; exp_fix applies the table.
+struct ExpVal {
+  float f;
+  bool probe;
+};
+
+// Branch-free so that a thread's exps interleave: x below -150 gives 0, NaN
+// gives NaN (x > 0 is outside the domain: the aggregate's x = score - max).
+__device__ __forceinline__ ExpVal exp_first(float x, const ExpConsts& K, const double* T) {
+  const bool in_range = x >= -150.0f;
+  const double d = exp_core(in_range ? x : 0.0f, K, T);
+  const float f = __double2float_rn(d);
+  return {in_range ? f : (x != x ? x : 0.0f), in_range && exp_in_band(d, K.band)};
+}
+
+__device__ __forceinline__ float exp_fix(float x, float f) {
+  return __uint_as_float(__float_as_uint(f) + exp_correction(__float_as_uint(x) & 0x7fffffffu, g_exp_hash));
+}
+
+// The 2 KB table of 2^(j/256), staged in shared memory by each CTA.
+__device__ __forceinline__ void load_exp_table(double* s_T) {
+  for (int i = threadIdx.x; i < (1 << kExpTableBits); i += blockDim.x) s_T[i] = g_exp_T[i];
+  __syncthreads();
 }
 
 __global__ void expf_map_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t n, ExpConsts K) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    out[i] = expf_host_rounding(x[i], K);
+  __shared__ double s_T[1 << kExpTableBits];
+  load_exp_table(s_T);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const ExpVal v = exp_first(x[i], K, s_T);
+    out[i] = v.probe ? exp_fix(x[i], v.f) : v.f;
+  }
 }
 
 // ---- RoPE table (host) ------------------------------------------------------------
@@ -319,10 +362,11 @@ static void rope_coeffs(uint32_t pos, float* out) {
 
 // ---- kernels ---------------------------------------------------------------------
 
-constexpr int kCmpWarps = 8;
+constexpr int kCmpThreads = 192;     // one emission per CTA at a time
 constexpr int kCmpMaxSources = 128;  // coff * ratio <= 128
 constexpr int kRowF = kRowDim;       // 576 lanes per compressed row
-constexpr int kDimIters = kRowF / 32;  // 18 dims per lane
+constexpr int kDimPerThread = kRowF / kCmpThreads;  // 3
+static_assert(kRowF % kCmpThreads == 0, "dims per thread");
 
 struct CmpArgs {
   rkv_pool_view pool;
@@ -350,19 +394,18 @@ __device__ __forceinline__ int source_of(const CmpArgs& a, int64_t t, int p, int
 }
 
 struct SrcPtr {
-  const float* kv;     // column 0 of the row (nullptr: kv 0, score -inf)
+  const float* kv;   // column 0 of the row
   const float* sc;
-  const float* ape;    // APE row to add to the score (input rows only), or nullptr
+  const float* ape;  // APE row added to the score (zeros for ring rows and when there is no APE)
 };
 
 __device__ __forceinline__ SrcPtr source_ptr(const CmpArgs& a, int code, int s, int q) {
-  SrcPtr r{nullptr, nullptr, nullptr};
-  if (code == -2) return r;
+  SrcPtr r{g_zero_row, g_neginf_row, g_zero_row};
   if (code >= 0) {
     r.kv = a.kv + (int64_t)code * a.width;
     r.sc = a.score + (int64_t)code * a.width;
-    r.ape = a.ape ? a.ape + (int64_t)(q % a.ratio) * a.width : nullptr;
-  } else {
+    if (a.ape) r.ape = a.ape + (int64_t)(q % a.ratio) * a.width;
+  } else if (code == -1) {
     const float* st = a.states + (int64_t)s * 2 * a.cr * a.width;
     r.kv = st + (int64_t)(q % a.cr) * a.width;
     r.sc = st + (int64_t)(a.cr + q % a.cr) * a.width;
@@ -371,142 +414,181 @@ __device__ __forceinline__ SrcPtr source_ptr(const CmpArgs& a, int code, int s, 
 }
 
 __device__ __forceinline__ void load_src(const SrcPtr& p, int col, float& kv, float& sc) {
-  if (!p.kv) {
-    kv = 0.0f;
-    sc = -INFINITY;
-    return;
-  }
   kv = __ldg(p.kv + col);
-  sc = __ldg(p.sc + col);
-  if (p.ape) sc = __fadd_rn(sc, __ldg(p.ape + col));
+  sc = __fadd_rn(__ldg(p.sc + col), __ldg(p.ape + col));
 }
 
-// One warp per emitting token.
-__global__ void __launch_bounds__(kCmpWarps * 32)
-compress_emit_kernel(const CmpArgs a, const ThresholdTable tab, const ExpConsts K) {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  __shared__ float s_row[kCmpWarps][kRowF];
-  __shared__ int s_src[kCmpWarps][kCmpMaxSources];
-  const unsigned FULL = 0xffffffffu;
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  float* row = s_row[w];
-  int* src = s_src[w];
-  const int64_t stride = (int64_t)gridDim.x * kCmpWarps;
-  for (int64_t t = (int64_t)blockIdx.x * kCmpWarps + w; t < a.n_tok; t += stride) {
-    const int p = __ldg(a.pos + t), s = __ldg(a.state_of + t), slot = __ldg(a.emit_slot + t);
-    if (p < 0 || s < 0 || (int64_t)s >= a.n_states) {
-      if (lane == 0) set_status(a.status, RKV_ERR_INDEX_OUT_OF_RANGE);
-      continue;
+// Applies the table to the lanes of x[] whose bit is set in `probes`: the
+// first probes of all of them are issued together, then the rare collisions
+// are walked.
+template <int N>
+__device__ __forceinline__ void exp_fix_n(const float (&x)[N], float (&f)[N], uint32_t probes) {
+  const uint32_t mask = (1u << kExpHashBits) - 1;
+  uint32_t h[N], v[N];
+#pragma unroll
+  for (int r = 0; r < N; ++r) {
+    h[r] = exp_hash(__float_as_uint(x[r]) & 0x7fffffffu);
+    v[r] = (probes >> r) & 1u ? g_exp_hash[h[r]] : 0u;
+  }
+#pragma unroll
+  for (int r = 0; r < N; ++r) {
+    if (!((probes >> r) & 1u)) continue;
+    const uint32_t key = __float_as_uint(x[r]) & 0x7fffffffu;
+    while (v[r] != 0u && (v[r] & 0x7fffffffu) != key) {
+      h[r] = (h[r] + 1) & mask;
+      v[r] = g_exp_hash[h[r]];
     }
-    if ((p + 1) % a.ratio != 0 || slot < 0) continue;
-    const int k = (p + 1) / a.ratio - 1;
-    if ((int64_t)k >= a.rope_rows) {
-      if (lane == 0) set_status(a.status, RKV_ERR_INDEX_OUT_OF_RANGE);
-      continue;
-    }
-    // Sources: coff 2: r < ratio the previous window (p lanes), then the
-    // current one (c lanes); coff 1: the current window.
-    const int q0 = p + 1 - a.cr;
-    for (int r = lane; r < a.cr; r += 32) src[r] = source_of(a, t, p, s, q0 + r);
-    __syncwarp();
+    if (v[r] != 0u) f[r] = __uint_as_float(__float_as_uint(f[r]) + ((v[r] >> 31) ? 1u : 0xffffffffu));
+  }
+}
 
-    if (a.coff == 2) {
-      // ratio 4: eight sources, pointers kept in registers.
-      SrcPtr sp[4], sc[4];
+// The emission of token t (position p, state s) by one CTA of kCmpThreads:
+// per-dimension aggregate into row[576] (shared, kDimPerThread dims per
+// thread), RMSNorm, RoPE, then quantize-on-append by warp 0.
+__device__ __forceinline__ void emit_row(const CmpArgs& a, const ThresholdTable& tab, const ExpConsts& K,
+                                         int64_t t, int p, int s, int slot, float* row, int* src, float* s_rms,
+                                         const double* s_T, double* sq) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int k = (p + 1) / a.ratio - 1;
+  if ((int64_t)k >= a.rope_rows) {
+    if (tid == 0) set_status(a.status, RKV_ERR_INDEX_OUT_OF_RANGE);
+    return;
+  }
+  // Sources: coff 2: r < ratio the previous window (p lanes), then the
+  // current one (c lanes); coff 1: the current window.
+  const int q0 = p + 1 - a.cr;
+  for (int r = tid; r < a.cr; r += kCmpThreads) src[r] = source_of(a, t, p, s, q0 + r);
+  __syncthreads();
+
+  if (a.coff == 2) {
+    SrcPtr sp[4], sc[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      sp[r] = source_ptr(a, src[r], s, q0 + r);
+      sc[r] = source_ptr(a, src[4 + r], s, q0 + 4 + r);
+    }
+    // All loads of the thread's dims first, then every exp, one table pass.
+    constexpr int D = kDimPerThread;
+    float kp[D][4], kc[D][4], x[D * 8], w[D * 8], m[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i)
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        sp[r] = source_ptr(a, src[r], s, q0 + r);
-        sc[r] = source_ptr(a, src[4 + r], s, q0 + 4 + r);
+        load_src(sp[r], tid + kCmpThreads * i, kp[i][r], x[8 * i + 2 * r]);
+        load_src(sc[r], kRowF + tid + kCmpThreads * i, kc[i][r], x[8 * i + 2 * r + 1]);
       }
-#pragma unroll 1
-      for (int i = 0; i < kDimIters; ++i) {
-        const int j = lane + 32 * i;
-        float kp[4], spv[4], kc[4], scv[4];
+    uint32_t probes = 0;
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          load_src(sp[r], j, kp[r], spv[r]);
-          load_src(sc[r], kRowF + j, kc[r], scv[r]);
-        }
-        float m = -INFINITY;
+    for (int i = 0; i < D; ++i) {
+      m[i] = -INFINITY;
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          if (spv[r] > m) m = spv[r];
-          if (scv[r] > m) m = scv[r];
-        }
-        float out = 0.0f;
-        if (!(m <= -INFINITY)) {
-          float den = 0.0f, num = 0.0f;
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const float wp = expf_host_rounding(__fsub_rn(spv[r], m), K);
-            const float wc = expf_host_rounding(__fsub_rn(scv[r], m), K);
-            den = __fadd_rn(den, __fadd_rn(wp, wc));
-            num = __fadd_rn(num, __fadd_rn(__fmul_rn(wp, kp[r]), __fmul_rn(wc, kc[r])));
-          }
-          out = den > 0.0f ? __fdiv_rn(num, den) : 0.0f;
-        }
-        row[j] = out;
+      for (int r = 0; r < 4; ++r) {
+        if (x[8 * i + 2 * r] > m[i]) m[i] = x[8 * i + 2 * r];
+        if (x[8 * i + 2 * r + 1] > m[i]) m[i] = x[8 * i + 2 * r + 1];
       }
-    } else {
-#pragma unroll 1
-      for (int i = 0; i < kDimIters; ++i) {
-        const int j = lane + 32 * i;
-        float m = -INFINITY;
-#pragma unroll 4
-        for (int r = 0; r < a.cr; ++r) {
-          float kv, sv;
-          load_src(source_ptr(a, src[r], s, q0 + r), j, kv, sv);
-          if (sv > m) m = sv;
-        }
-        float out = 0.0f;
-        if (!(m <= -INFINITY)) {
-          float den = 0.0f, num = 0.0f;
-#pragma unroll 4
-          for (int r = 0; r < a.cr; ++r) {
-            float kv, sv;
-            load_src(source_ptr(a, src[r], s, q0 + r), j, kv, sv);
-            const float wgt = expf_host_rounding(__fsub_rn(sv, m), K);
-            den = __fadd_rn(den, wgt);
-            num = __fadd_rn(num, __fmul_rn(wgt, kv));
-          }
-          out = den > 0.0f ? __fdiv_rn(num, den) : 0.0f;
-        }
-        row[j] = out;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        x[8 * i + r] = __fsub_rn(x[8 * i + r], m[i]);
+        const ExpVal e = exp_first(x[8 * i + r], K, s_T);
+        w[8 * i + r] = e.f;
+        probes |= (uint32_t)e.probe << (8 * i + r);
       }
     }
-    __syncwarp();
-
-    // RMSNorm: sequential f64 sum of squares (compressor.rs:292-296).
-    float rms = 0.0f;
-    if (lane == 0) {
-      double ss = 0.0;
+    if (probes) exp_fix_n<D * 8>(x, w, probes);
+#pragma unroll
+    for (int i = 0; i < D; ++i) {
+      float out = 0.0f;
+      if (!(m[i] <= -INFINITY)) {
+        float den = 0.0f, num = 0.0f;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          den = __fadd_rn(den, __fadd_rn(w[8 * i + 2 * r], w[8 * i + 2 * r + 1]));
+          num = __fadd_rn(num, __fadd_rn(__fmul_rn(w[8 * i + 2 * r], kp[i][r]),
+                                         __fmul_rn(w[8 * i + 2 * r + 1], kc[i][r])));
+        }
+        out = den > 0.0f ? __fdiv_rn(num, den) : 0.0f;
+      }
+      row[tid + kCmpThreads * i] = out;
+    }
+  } else {
+#pragma unroll 1
+    for (int i = 0; i < kDimPerThread; ++i) {
+      const int j = tid + kCmpThreads * i;
+      float m = -INFINITY;
 #pragma unroll 8
-      for (int j = 0; j < kRowF; ++j) {
-        const double v = (double)row[j];
-        ss = __dadd_rn(ss, __dmul_rn(v, v));
+      for (int r = 0; r < a.cr; ++r) {
+        float kv, sv;
+        load_src(source_ptr(a, src[r], s, q0 + r), j, kv, sv);
+        if (sv > m) m = sv;
       }
-      const float mean = __double2float_rn(__ddiv_rn(ss, (double)kRowF));
-      rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
-    }
-    rms = __shfl_sync(FULL, rms, 0);
+      float out = 0.0f;
+      if (!(m <= -INFINITY)) {
+        float den = 0.0f, num = 0.0f;
+#pragma unroll 1
+        for (int r0 = 0; r0 < a.cr; r0 += 8) {
+          float x[8], w[8], kv[8];
+          uint32_t probes = 0;
 #pragma unroll
-    for (int i = 0; i < kDimIters; ++i) {
-      const int j = lane + 32 * i;
-      row[j] = __fmul_rn(__fmul_rn(row[j], rms), __ldg(a.norm + j));
+          for (int r = 0; r < 8; ++r) {
+            float sv = -INFINITY;
+            kv[r] = 0.0f;
+            if (r0 + r < a.cr) load_src(source_ptr(a, src[r0 + r], s, q0 + r0 + r), j, kv[r], sv);
+            x[r] = __fsub_rn(sv, m);
+          }
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            const ExpVal e = exp_first(x[r], K, s_T);
+            w[r] = e.f;
+            probes |= (uint32_t)e.probe << r;
+          }
+          if (probes) exp_fix_n<8>(x, w, probes);
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            if (r0 + r < a.cr) {
+              den = __fadd_rn(den, w[r]);
+              num = __fadd_rn(num, __fmul_rn(w[r], kv[r]));
+            }
+          }
+        }
+        out = den > 0.0f ? __fdiv_rn(num, den) : 0.0f;
+      }
+      row[j] = out;
     }
-    __syncwarp();
+  }
+  // The squares (exact in f64) are formed by every thread; one thread adds
+  // them in order.
+#pragma unroll
+  for (int i = 0; i < kDimPerThread; ++i) {
+    const double v = (double)row[tid + kCmpThreads * i];
+    sq[tid + kCmpThreads * i] = __dmul_rn(v, v);
+  }
+  __syncthreads();
 
+  // RMSNorm: sequential f64 sum of squares (compressor.rs:292-296).
+  if (tid == 0) {
+    double ss = 0.0;
+#pragma unroll 16
+    for (int j = 0; j < kRowF; ++j) ss = __dadd_rn(ss, sq[j]);
+    const float mean = __double2float_rn(__ddiv_rn(ss, (double)kRowF));
+    *s_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
+  }
+  __syncthreads();
+  const float rms = *s_rms;
+#pragma unroll
+  for (int i = 0; i < kDimPerThread; ++i) {
+    const int j = tid + kCmpThreads * i;
+    row[j] = __fmul_rn(__fmul_rn(row[j], rms), __ldg(a.norm + j));
+  }
+  __syncthreads();
+
+  if (tid < 32) {
     // RoPE of the tail pairs (rope.rs:163-168), lane = pair.
-    {
-      const float c = __ldg(a.rope + (int64_t)k * 64 + 2 * lane);
-      const float sn = __ldg(a.rope + (int64_t)k * 64 + 2 * lane + 1);
-      const float x0 = row[kLatent + 2 * lane], x1 = row[kLatent + 2 * lane + 1];
-      row[kLatent + 2 * lane] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
-      row[kLatent + 2 * lane + 1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
-    }
+    const float c = __ldg(a.rope + (int64_t)k * 64 + 2 * lane);
+    const float sn = __ldg(a.rope + (int64_t)k * 64 + 2 * lane + 1);
+    const float x0 = row[kLatent + 2 * lane], x1 = row[kLatent + 2 * lane + 1];
+    row[kLatent + 2 * lane] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+    row[kLatent + 2 * lane + 1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
     __syncwarp();
-
     // Quantize-on-append (dsv4_quant.rs:316-362) into the emit slot.
     RowF32 x;
 #pragma unroll
@@ -521,7 +603,49 @@ compress_emit_kernel(const CmpArgs a, const ThresholdTable tab, const ExpConsts 
     }
     x.slot = slot;
     append_row_f32(a.pool, a.layer, x, tab, a.status, lane);
-    __syncwarp();
+  }
+  __syncthreads();
+}
+
+// Each CTA takes groups of `ratio` consecutive tokens (a group inside one
+// sequence's run holds exactly one emitting token), lists the emitting ones
+// and emits them one after another.
+__global__ void __launch_bounds__(kCmpThreads, 3)
+compress_emit_kernel(const CmpArgs a, const ThresholdTable tab, const ExpConsts K) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ float s_row[kRowF];
+  __shared__ int s_src[kCmpMaxSources];
+  __shared__ int s_list[kCmpMaxSources][4];
+  __shared__ int s_count;
+  __shared__ float s_rms;
+  __shared__ double s_T[1 << kExpTableBits];
+  __shared__ double s_sq[kRowF];
+  load_exp_table(s_T);
+  const int tid = threadIdx.x;
+  const int64_t n_groups = (a.n_tok + a.ratio - 1) / a.ratio;
+  for (int64_t g = blockIdx.x; g < n_groups; g += gridDim.x) {
+    if (tid == 0) s_count = 0;
+    __syncthreads();
+    for (int r = tid; r < a.ratio; r += kCmpThreads) {
+      const int64_t t = g * a.ratio + r;
+      if (t >= a.n_tok) break;
+      const int p = __ldg(a.pos + t), s = __ldg(a.state_of + t), slot = __ldg(a.emit_slot + t);
+      if (p < 0 || s < 0 || (int64_t)s >= a.n_states) {
+        set_status(a.status, RKV_ERR_INDEX_OUT_OF_RANGE);
+      } else if ((p + 1) % a.ratio == 0 && slot >= 0) {
+        const int i = atomicAdd(&s_count, 1);
+        s_list[i][0] = r;
+        s_list[i][1] = p;
+        s_list[i][2] = s;
+        s_list[i][3] = slot;
+      }
+    }
+    __syncthreads();
+    const int n = s_count;
+    for (int i = 0; i < n; ++i)
+      emit_row(a, tab, K, g * a.ratio + s_list[i][0], s_list[i][1], s_list[i][2], s_list[i][3], s_row, s_src,
+               &s_rms, s_T, s_sq);
   }
 }
 
@@ -581,7 +705,7 @@ extern "C" rkv_status rkv_compress_prepare(void) {
 
 extern "C" int64_t rkv_compress_expf_table_size(void) {
   const rkv::ExpHost* E = rkv::exp_host();
-  return E ? (int64_t)E->entries.size() : -1;
+  return E ? E->n_entries : -1;
 }
 
 extern "C" rkv_status rkv_compress_expf(const float* x, float* out, int64_t n, int32_t host, rkv_stream_t stream) {
@@ -668,11 +792,11 @@ extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t lay
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t need = (n_tok + kCmpWarps - 1) / kCmpWarps;
+  const int64_t need = (n_tok + ratio - 1) / ratio;  // token groups
   const int64_t cap = (int64_t)sms * 8;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(need < cap ? need : cap));
-  cfg.blockDim = dim3(kCmpWarps * 32);
+  cfg.blockDim = dim3(kCmpThreads);
   cfg.stream = (cudaStream_t)stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
