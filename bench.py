@@ -676,6 +676,72 @@ def bench_compress(args, dist: Dist, dev, peak) -> dict:
     return res
 
 
+FP32_OPS_PER_S = 35.79e12  # FMUL/FADD lane operations per second, measured on this pool's B200 (1965 MHz)
+
+
+def bench_indexer(args, dist: Dist, dev, peak) -> dict:
+    """Indexer scoring + top-k (rkv_indexer_topk_f32) as a decode step: one
+    query per sequence for 32 sequences (config 4's count) at context 131072,
+    i.e. 32768 compressed indexer rows each (ratio 4), k = 512 (rsLLM's
+    DSV4_N_INDEXER_TOP_K), one launch pair per layer over the same rows (537 MB,
+    read from HBM every layer)."""
+    import oracle
+    import rsllm_b200 as rk
+
+    n_seq, n_rows, k = (8, 32768, 512) if args.small else (32, 32768, 512)
+    n_layers = 1 if args.small else N_LAYERS
+    g = torch.Generator(device=dev)
+    g.manual_seed(700 + 7919 * dist.rank)
+    rows = torch.randn((n_seq * n_rows, 128), generator=g, device=dev)
+    row_start = (torch.arange(n_seq, device=dev, dtype=torch.int64) * n_rows).contiguous()
+    seq_rows = torch.full((n_seq,), n_rows, dtype=torch.int32, device=dev)
+    q = torch.randn((n_seq, 64, 128), generator=g, device=dev)
+    w = (torch.randn((n_seq, 64), generator=g, device=dev) / 8192 ** 0.5).contiguous()
+    sq = torch.arange(n_seq, dtype=torch.int32, device=dev)
+    nv = torch.full((n_seq,), n_rows, dtype=torch.int32, device=dev)
+    scores = torch.empty((n_seq, n_rows), dtype=torch.float32, device=dev)
+    out = torch.empty((n_seq, k), dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def one():
+        rk.indexer_select_top_k(rows, row_start, seq_rows, q, w, sq, nv, n_rows, k, scores=scores, out=out,
+                                status=status, stream=stream)
+
+    def score_only():
+        rk.indexer_scores(rows, row_start, seq_rows, q, w, sq, nv, n_rows, out=scores, status=status, stream=stream)
+
+    for _ in range(args.phase_warmup):
+        for _ in range(n_layers):
+            one()
+    stream.synchronize()
+    dist.barrier()
+    ms = dist.max(events_time(lambda: [one() for _ in range(args.phase_steps * n_layers)], stream)) / args.phase_steps
+    score_ms = events_time(score_only, stream)
+    assert int(status.item()) == 0
+    ops = 2.0 * n_seq * n_rows * 64 * 128      # one multiply and one add per lane per head
+    nbytes = n_seq * n_rows * 512 + n_seq * (64 * 128 * 4 + 64 * 4) + n_seq * n_rows * 4 + n_seq * k * 4
+    t_layer = ms * 1e-3 / n_layers
+    # CPU: the oracle's scoring (threads over queries) on 2048 rows of every sequence, then its selection
+    sample_rows = 2048
+    rows_c = rows.view(n_seq, n_rows, 128)[:, :sample_rows].reshape(-1, 128).cpu().numpy()
+    t0 = time.perf_counter()
+    sc_c, _ = oracle.indexer_scores(rows_c, np.arange(n_seq) * sample_rows, np.full(n_seq, sample_rows), q.cpu().numpy(),
+                                    w.cpu().numpy(), np.arange(n_seq), np.full(n_seq, sample_rows), sample_rows)
+    oracle.topk_batch(sc_c, np.full(n_seq, sample_rows, np.int32), k)
+    cpu_s = time.perf_counter() - t0
+    return {"config": f"{n_seq} decode queries x {n_rows} indexer rows (64 heads x 128, f32) x {n_layers} layers, "
+                      f"k = {k}",
+            "ms_per_step": ms, "ms_per_layer": ms / n_layers, "score_kernel_ms_per_layer": score_ms,
+            "rows_scored_per_s_per_gpu": n_seq * n_rows / t_layer,
+            "fp32_ops_per_s": ops / t_layer, "frac_of_fp32_issue_peak": ops / t_layer / FP32_OPS_PER_S,
+            "fp32_peak_source": "measured FMUL/FADD-rate micro-benchmark, 35.79 T lane-ops/s",
+            "gbs_per_gpu": nbytes / t_layer / GB, "frac_of_hbm_peak": nbytes / t_layer / GB / peak,
+            "roofline_bound": "fp32 (bit-exact lane-by-lane f32 dots: no tensor cores, no FMA)",
+            "cpu_baseline": {"rows_scored_per_s": n_seq * sample_rows / cpu_s, "cores": min(n_seq, oracle.threads()),
+                             "kind": "port", "sample": f"{n_seq} queries x {sample_rows} rows, scoring + selection"}}
+
+
 def bench_kvc(args, dist: Dist, dev) -> dict:
     """KVC file save and load (prefix persistence) of a config-5-sized prefix
     (8229 tokens) over 61 layers: host-synchronous (device pack / unpack,
@@ -922,12 +988,13 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--phases", default="gather,sparse,prefix,kvc,compress",
-                    help="extra configs to measure (comma list of gather,sparse,prefix,kvc,compress or 'none')")
+    ap.add_argument("--phases", default="gather,sparse,prefix,kvc,compress,indexer",
+                    help="extra configs to measure (comma list of gather,sparse,prefix,kvc,compress,indexer or "
+                         "'none')")
     ap.add_argument("--phase-steps", type=int, default=3)
     ap.add_argument("--phase-warmup", type=int, default=1)
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
-    ap.add_argument("--only", choices=["all", "append", "gather", "sparse", "prefix", "kvc", "compress"],
+    ap.add_argument("--only", choices=["all", "append", "gather", "sparse", "prefix", "kvc", "compress", "indexer"],
                     default="all",
                     help="run one workload alone (profiling)")
     ap.add_argument("--mla-splits", type=int, default=16,
@@ -965,6 +1032,8 @@ def main():
             res = bench_kvc(args, dist, dev)
         elif args.only == "compress":
             res = bench_compress(args, dist, dev, peak)
+        elif args.only == "indexer":
+            res = bench_indexer(args, dist, dev, peak)
         else:
             res = bench_sparse(args, dist, dev, peak)
         clocks.stop()
@@ -986,6 +1055,8 @@ def main():
         phases["kvc_save_load"] = bench_kvc(args, dist, dev)
     if "compress" in wanted:
         phases.update(bench_compress(args, dist, dev, peak))
+    if "indexer" in wanted:
+        phases["indexer_score_topk"] = bench_indexer(args, dist, dev, peak)
     clk = clocks.stop()
 
     K, W = args.steps, args.warmup

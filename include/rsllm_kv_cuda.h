@@ -476,6 +476,42 @@ RKV_API rkv_status rkv_compress_expf(const float* x, float* out, int64_t n, int3
 /* Number of table entries (x whose expf differs from the rounded double). */
 RKV_API int64_t rkv_compress_expf_table_size(void);
 
+/* ---- indexer scoring + top-k ----------------------------------------------------
+ * Replaces the scoring half of IndexerPool::select_top_k
+ * (crates/rsllm-kvcache/src/dsv4/indexer.rs:198-216): for query q and each
+ * visible compressed indexer row c of its sequence,
+ *   score[c] = sum over heads h (in order) of relu(dot(row_c, q_h)) * w_h,
+ *   dot = sum over the 128 lanes (in order) of row_c[i] * q_h[i],
+ * with f32 products and sums rounded one at a time (no contraction), as rsLLM
+ * computes them -- so scores and the selection are bit-exact.
+ *
+ * rows:       device f32 [*][128]: the indexer rows of sequence s start at row
+ *             row_start[s] (int64 [n_seq]) and number seq_rows[s] (int32).
+ * q:          device f32 [n_q][64][128] (the rotated, QAT'd indexer queries).
+ * w:          device f32 [n_q][64] (per-head weights, already scaled by
+ *             1/sqrt(64 * 128) as attention.rs does).
+ * seq_of_query, n_visible: device int32 [n_q]: query q scores rows
+ *             [0, n_visible[q]) of its sequence (n_visible <= seq_rows).
+ * scores:     device f32 [n_q][ld], 16-byte aligned, ld % 4 == 0 and
+ *             ld >= max_visible >= every n_visible; entries past n_visible
+ *             are left untouched.
+ * rows, q: 16-byte aligned.  A query whose sequence or n_visible is out of
+ * range sets INDEX_OUT_OF_RANGE and scores nothing. */
+RKV_API rkv_status rkv_indexer_scores_f32(const float* rows, const int64_t* row_start, const int32_t* seq_rows,
+                                          int64_t n_seq, const float* q, const float* w,
+                                          const int32_t* seq_of_query, const int32_t* n_visible, int32_t n_q,
+                                          int32_t max_visible, float* scores, int64_t ld, uint32_t* d_status,
+                                          rkv_stream_t stream);
+/* The whole IndexerPool::select_top_k (indexer.rs:169-236) for a batch of
+ * queries: rkv_indexer_scores_f32 into the caller's scores workspace, then
+ * rkv_topk_select_f32 (effective_k = min(k, n_visible), the reference's order
+ * and fill rules) into out_idx [n_q][k]. */
+RKV_API rkv_status rkv_indexer_topk_f32(const float* rows, const int64_t* row_start, const int32_t* seq_rows,
+                                        int64_t n_seq, const float* q, const float* w, const int32_t* seq_of_query,
+                                        const int32_t* n_visible, int32_t n_q, int32_t max_visible, int32_t k,
+                                        float* scores, int64_t ld, int32_t* out_idx, uint32_t* d_status,
+                                        rkv_stream_t stream);
+
 /* ---- codec pin ---------------------------------------------------------------
  * out[i] = E4M3 code the append kernel stores for the f32 lane value whose
  * bit pattern is first_bits + i (already divided by its block scale), i < n:

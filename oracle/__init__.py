@@ -77,6 +77,8 @@ def lib() -> ctypes.CDLL:
         "rkvo_compress_append": (c_uint32, [P, c_int64, c_int32, c_int32, c_int32, P, P, P, c_int64, P, P, c_int64,
                                             P, P, P, P, P, c_int]),
         "rkvo_expf_batch": (None, [P, P, c_int64, c_int]),
+        "rkvo_indexer_score_row": (c_float, [P, P, P]),
+        "rkvo_indexer_scores": (c_uint32, [P, P, P, c_int64, P, P, P, P, c_int32, P, c_int64, c_int]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -350,3 +352,24 @@ def expf(x: np.ndarray, n_threads: int | None = None) -> np.ndarray:
     out = np.empty_like(x)
     lib().rkvo_expf_batch(_p(x), _p(out), x.size, n_threads or threads())
     return out
+
+
+# ---- indexer scoring -------------------------------------------------------------
+
+def indexer_scores(rows: np.ndarray, row_start: np.ndarray, seq_rows: np.ndarray, q: np.ndarray, w: np.ndarray,
+                   seq_of_query: np.ndarray, n_visible: np.ndarray, ld: int, n_threads: int | None = None):
+    """indexer.rs:198-216 for a batch of queries: rows f32 [*, 128]; q f32
+    [n_q, 64, 128]; w f32 [n_q, 64]; returns (scores f32 [n_q, ld] with
+    -inf past n_visible, status bits)."""
+    rows = np.ascontiguousarray(rows, np.float32)
+    rs = np.ascontiguousarray(row_start, np.int64)
+    sr = np.ascontiguousarray(seq_rows, np.int32)
+    q = np.ascontiguousarray(q, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    sq = np.ascontiguousarray(seq_of_query, np.int32)
+    nv = np.ascontiguousarray(n_visible, np.int32)
+    n_q = q.shape[0]
+    out = np.full((n_q, ld), -np.inf, np.float32)
+    st = lib().rkvo_indexer_scores(_p(rows), _p(rs), _p(sr), rs.size, _p(q), _p(w), _p(sq), _p(nv), n_q, _p(out), ld,
+                                   n_threads or threads())
+    return out, st

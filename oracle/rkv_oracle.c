@@ -26,6 +26,8 @@
  *       squares, RoPE at pos + 1 - ratio, quantize) with compress_rope_params
  *       :372-397; crates/rsllm-backend-cpu/src/ops/rope.rs:28-172 (YaRN).
  *       exp, log, pow, cos and sin are the host libm's, as in the reference.
+ *   - indexer scoring: crates/rsllm-kvcache/src/dsv4/indexer.rs:198-216
+ *       (ReLU of per-head dots, weighted sum), scale_factor :scale.
  *
  * Parity pin: the reference is Rust and cannot be built here (no cargo or
  * rustc), so this restatement is pinned by the reference's own known-answer
@@ -1067,4 +1069,70 @@ void rkvo_expf_batch(const float* x, float* out, int64_t n, int n_threads) {
     }
     if (n_threads > 1)
         for (int t = 0; t < n_threads; ++t) pthread_join(th[t], NULL);
+}
+
+/* ------------------------------------------------------------------------ */
+/* indexer.rs:198-216, the scoring of compressed indexer rows                */
+/* ------------------------------------------------------------------------ */
+
+#define IDX_HEADS 64
+#define IDX_DIM 128
+
+/* score of one 128-lane row against q [64][128] and w [64]: per head a dot
+ * accumulated lane by lane, ReLU, then the weighted sum head by head, f32
+ * throughout (no contraction). */
+float rkvo_indexer_score_row(const float* row, const float* q, const float* w) {
+    float s = 0.0f;
+    for (int h = 0; h < IDX_HEADS; ++h) {
+        const float* qh = q + h * IDX_DIM;
+        float dot = 0.0f;
+        for (int i = 0; i < IDX_DIM; ++i) dot += row[i] * qh[i];
+        if (dot > 0.0f) s += dot * w[h];
+    }
+    return s;
+}
+
+typedef struct {
+    const float* rows; const int64_t* row_start; const int32_t* seq_rows; int64_t n_seq;
+    const float* q; const float* w; const int32_t* seq_of_query; const int32_t* n_visible;
+    float* scores; int64_t ld; int32_t q0, q1; uint32_t status;
+} idx_job;
+
+static void* idx_worker(void* p) {
+    idx_job* j = (idx_job*)p;
+    for (int32_t qi = j->q0; qi < j->q1; ++qi) {
+        int32_t s = j->seq_of_query[qi], nv = j->n_visible[qi];
+        if (s < 0 || s >= j->n_seq || nv < 0 || nv > j->seq_rows[s]) { j->status |= 1u << RKVO_INDEX_OUT_OF_RANGE; continue; }
+        const float* base = j->rows + j->row_start[s] * IDX_DIM;
+        for (int32_t c = 0; c < nv; ++c)
+            j->scores[(int64_t)qi * j->ld + c] =
+                rkvo_indexer_score_row(base + (int64_t)c * IDX_DIM, j->q + (int64_t)qi * IDX_HEADS * IDX_DIM,
+                                       j->w + (int64_t)qi * IDX_HEADS);
+    }
+    return NULL;
+}
+
+/* Scores of a batch of queries (rkv_indexer_scores_f32's contract), threads
+ * over queries; returns the status bits. */
+uint32_t rkvo_indexer_scores(const float* rows, const int64_t* row_start, const int32_t* seq_rows, int64_t n_seq,
+                             const float* q, const float* w, const int32_t* seq_of_query, const int32_t* n_visible,
+                             int32_t n_q, float* scores, int64_t ld, int n_threads) {
+    if (n_q <= 0) return 0;
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > 256) n_threads = 256;
+    if (n_threads > n_q) n_threads = n_q;
+    pthread_t th[256];
+    idx_job jobs[256];
+    for (int t = 0; t < n_threads; ++t) {
+        jobs[t] = (idx_job){rows, row_start, seq_rows, n_seq, q, w, seq_of_query, n_visible, scores, ld,
+                            (int32_t)((int64_t)n_q * t / n_threads), (int32_t)((int64_t)n_q * (t + 1) / n_threads), 0};
+        if (n_threads == 1) idx_worker(&jobs[t]);
+        else pthread_create(&th[t], NULL, idx_worker, &jobs[t]);
+    }
+    uint32_t st = 0;
+    for (int t = 0; t < n_threads; ++t) {
+        if (n_threads > 1) pthread_join(th[t], NULL);
+        st |= jobs[t].status;
+    }
+    return st;
 }

@@ -97,6 +97,10 @@ SIGNATURES = {
                                       _i32p, _i32p, _f32p, _f32p, _f32p, c_int64, _u32p, c_void_p]),
     "rkv_compress_expf": (c_int32, [_f32p, _f32p, c_int64, c_int32, c_void_p]),
     "rkv_compress_expf_table_size": (c_int64, []),
+    "rkv_indexer_scores_f32": (c_int32, [_f32p, c_void_p, _i32p, c_int64, _f32p, _f32p, _i32p, _i32p, c_int32,
+                                         c_int32, _f32p, c_int64, _u32p, c_void_p]),
+    "rkv_indexer_topk_f32": (c_int32, [_f32p, c_void_p, _i32p, c_int64, _f32p, _f32p, _i32p, _i32p, c_int32,
+                                       c_int32, c_int32, _f32p, c_int64, _i32p, _u32p, c_void_p]),
     "rkv_pool_create": (c_int32, [_P(PoolDesc), _P(c_void_p)]),
     "rkv_pool_destroy": (None, [c_void_p]),
     "rkv_pool_get_view": (c_int32, [c_void_p, _P(PoolView)]),

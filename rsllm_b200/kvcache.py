@@ -292,6 +292,67 @@ def select_top_k(scores: torch.Tensor, n_visible: torch.Tensor, k: int, out: tor
     return out
 
 
+def _indexer_args(rows, row_start, seq_rows, q, w, seq_of_query, n_visible):
+    dev = q.device
+    for t, n in ((rows, "rows"), (q, "q"), (w, "w")):
+        _need(t, torch.float32, n, dev)
+    _need(row_start, torch.int64, "row_start", dev)
+    for t, n in ((seq_rows, "seq_rows"), (seq_of_query, "seq_of_query"), (n_visible, "n_visible")):
+        _need(t, torch.int32, n, dev)
+    n_q = q.shape[0] if q.dim() == 3 else -1
+    if rows.dim() != 2 or rows.shape[1] != 128 or q.shape[1:] != (64, 128) or w.shape != (n_q, 64) or \
+            seq_of_query.shape != (n_q,) or n_visible.shape != (n_q,) or row_start.shape != seq_rows.shape:
+        raise ShapeMismatch("indexer: rows [*, 128], q [n_q, 64, 128], w [n_q, 64], seq_of_query / n_visible "
+                            "[n_q], row_start / seq_rows [n_seq]")
+    return dev, n_q
+
+
+def indexer_scores(rows: torch.Tensor, row_start: torch.Tensor, seq_rows: torch.Tensor, q: torch.Tensor,
+                   w: torch.Tensor, seq_of_query: torch.Tensor, n_visible: torch.Tensor, max_visible: int,
+                   out: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                   stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """Indexer scores (``rkv_indexer_scores_f32``, the scoring of
+    IndexerPool::select_top_k, indexer.rs:198-216): f32 [n_q, ld], entries
+    [0, n_visible[q]) written.  Device errors go to ``status`` (int32 [1]);
+    without one the call synchronises and raises."""
+    lib = _abi.load()
+    dev, n_q = _indexer_args(rows, row_start, seq_rows, q, w, seq_of_query, n_visible)
+    if out is None:
+        out = torch.empty((n_q, (max_visible + 3) // 4 * 4), dtype=torch.float32, device=dev)
+    _need(out, torch.float32, "out", dev)
+    st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=dev)
+    check(lib.rkv_indexer_scores_f32(_ptr(rows), _ptr(row_start), _ptr(seq_rows), row_start.shape[0], _ptr(q),
+                                     _ptr(w), _ptr(seq_of_query), _ptr(n_visible), n_q, max_visible, _ptr(out),
+                                     out.shape[1], _ptr(st), _stream(stream)), "indexer_scores")
+    if status is None:
+        raise_status_bits(int(st.item()), "indexer_scores")
+    return out
+
+
+def indexer_select_top_k(rows: torch.Tensor, row_start: torch.Tensor, seq_rows: torch.Tensor, q: torch.Tensor,
+                         w: torch.Tensor, seq_of_query: torch.Tensor, n_visible: torch.Tensor, max_visible: int,
+                         k: int, scores: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                         status: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """IndexerPool::select_top_k for a batch of queries
+    (``rkv_indexer_topk_f32``): int32 [n_q, k], the first min(k, n_visible)
+    entries in the reference's order, -1 after."""
+    lib = _abi.load()
+    dev, n_q = _indexer_args(rows, row_start, seq_rows, q, w, seq_of_query, n_visible)
+    if scores is None:
+        scores = torch.empty((n_q, (max_visible + 3) // 4 * 4), dtype=torch.float32, device=dev)
+    if out is None:
+        out = torch.empty((n_q, k), dtype=torch.int32, device=dev)
+    _need(scores, torch.float32, "scores", dev)
+    _need(out, torch.int32, "out", dev)
+    st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=dev)
+    check(lib.rkv_indexer_topk_f32(_ptr(rows), _ptr(row_start), _ptr(seq_rows), row_start.shape[0], _ptr(q), _ptr(w),
+                                   _ptr(seq_of_query), _ptr(n_visible), n_q, max_visible, k, _ptr(scores),
+                                   scores.shape[1], _ptr(out), _ptr(st), _stream(stream)), "indexer_select_top_k")
+    if status is None:
+        raise_status_bits(int(st.item()), "indexer_select_top_k")
+    return out
+
+
 def remap_pages(page_table: torch.Tensor, remap: torch.Tensor, status: torch.Tensor | None = None,
                 stream: torch.cuda.Stream | None = None) -> None:
     """In place: every entry >= 0 becomes remap[entry]."""
@@ -317,6 +378,7 @@ def pool_bytes(n_pages: int, n_layers: int) -> int:
 
 __all__ = [
     "KvError", "ShapeMismatch", "IndexOutOfRange", "InvalidLayer", "PoolFull", "NonFiniteInput", "InvalidArgument",
-    "CudaError", "BackendCapability", "CudaBackend", "PagedKvPool", "select_top_k", "remap_pages",
+    "CudaError", "BackendCapability", "CudaBackend", "PagedKvPool", "select_top_k", "indexer_scores",
+    "indexer_select_top_k", "remap_pages",
     "e4m3fn_code_range", "pool_bytes", "PAGE_TOKENS", "PAGE_BYTES", "ROW_DIM",
 ]
