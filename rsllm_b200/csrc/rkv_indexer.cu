@@ -7,10 +7,13 @@
 // each product and sum rounded on its own; the kernel does exactly that (an
 // f32 dot product on tensor cores or with fused multiply-adds would round
 // differently), so the scores -- and therefore the selected indices -- are
-// bit-exact.  Layout: one CTA of 128 threads per (query, 128 rows); the query
-// (32 KB) and its weights are staged in shared memory and read as broadcast
-// 16-byte loads; each thread holds its row in 128 registers and runs four
-// head chains at a time (four independent add chains hide the add latency).
+// bit-exact.  (Packed mul.rn.f32x2 / add.rn.f32x2 pairs are not used: in a
+// loop ptxas was measured to contract them into fused multiply-adds on this
+// B200, which changes the rounding.)  Layout: one CTA of 128 threads per
+// (query, 128 rows); the query (32 KB) and its weights are staged in shared
+// memory and read as broadcast 16-byte loads; each thread holds its row in 128
+// registers and runs four head chains at a time (four independent add chains
+// hide the add latency).
 // The work is 8192 multiplies and 8192 adds per (query, row): CUDA-core
 // bound, not HBM bound.
 #include "rkv_common.cuh"
