@@ -463,11 +463,16 @@ RKV_API rkv_status rkv_compress_rope_table(int32_t ratio, int64_t n_rows, float*
  * current device (done by the first rkv_compress_append otherwise; call it
  * before capturing a CUDA graph). */
 RKV_API rkv_status rkv_compress_prepare(void);
+/* workspace: device memory, 256-byte aligned, of at least
+ * rkv_compress_workspace_bytes(ratio, n_tok, n_states) bytes (the emitted rows
+ * between the aggregate and the finishing kernel). */
+RKV_API int64_t rkv_compress_workspace_bytes(int32_t ratio, int64_t n_tok, int64_t n_states);
 RKV_API rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t layer, int32_t ratio, float* states,
                                        int64_t n_states, const float* kv, const float* score, int64_t n_tok,
                                        const int32_t* pos, const int32_t* state_of_token, const int32_t* emit_slot,
                                        const float* ape, const float* norm, const float* rope_table,
-                                       int64_t rope_rows, uint32_t* d_status, rkv_stream_t stream);
+                                       int64_t rope_rows, void* workspace, int64_t workspace_bytes,
+                                       uint32_t* d_status, rkv_stream_t stream);
 /* expf as the compressor kernel evaluates it, on the host (host != 0, x and
  * out host memory) or on the current device (x, out device memory): a
  * double-precision exp rounded to f32, corrected from a table wherever the

@@ -85,6 +85,7 @@ class CompressorBank:
         self.states = torch.zeros((n_states, nbytes // 4), dtype=torch.float32, device=self.device)
         rows = max_positions // ratio + 1
         self.rope = torch.from_numpy(compress_rope_table(ratio, rows)).to(self.device)
+        self.workspace: torch.Tensor | None = None  # grown to the largest call (rkv_compress_workspace_bytes)
         with torch.cuda.device(self.device):
             check(self.lib.rkv_compress_prepare(), "CompressorBank")
 
@@ -111,8 +112,12 @@ class CompressorBank:
             _need(ape, torch.float32, "ape", self.device)
             if ape.shape != (self.ratio, self.width):
                 raise ShapeMismatch(f"CompressorBank.append: ape must be [{self.ratio}, {self.width}]")
+        need = int(self.lib.rkv_compress_workspace_bytes(self.ratio, n_tok, self.n_states))
+        if self.workspace is None or self.workspace.numel() < need:
+            self.workspace = torch.empty(need, dtype=torch.uint8, device=self.device)
         check(self.lib.rkv_compress_append(byref(pool.view), layer, self.ratio, _ptr(self.states), self.n_states,
                                            _ptr(kv), _ptr(score), n_tok, _ptr(pos), _ptr(state_of_token),
                                            _ptr(emit_slot), _ptr(ape), _ptr(norm), _ptr(self.rope),
-                                           self.rope.shape[0], _ptr(pool.status), _stream(stream)),
+                                           self.rope.shape[0], _ptr(self.workspace), self.workspace.numel(),
+                                           _ptr(pool.status), _stream(stream)),
               "CompressorBank.append")

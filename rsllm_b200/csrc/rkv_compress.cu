@@ -10,10 +10,13 @@
 // dimension (:481-554); the emitted row is RMS-normalised with an f64 sum of
 // squares, its 64 tail lanes are rotated (crates/rsllm-backend-cpu/src/ops/
 // rope.rs:128-172 at position pos + 1 - ratio) and it is FP8-quantized
-// (dsv4_quant.rs:316-362).  Here a batch of tokens is one launch: each warp
-// takes one emitting token and reads the window's rows straight from this
-// call's input or, for positions of earlier calls, from a per-state ring of
-// the last coff * ratio rows; a second launch then writes the ring.
+// (dsv4_quant.rs:316-362).  Here a batch of tokens is two launches: the
+// aggregate kernel (one CTA of 576 threads per emission, one output dimension
+// per thread) reads the window's rows straight from this call's input or, for
+// positions of earlier calls, from a per-state ring of the last coff * ratio
+// rows, and leaves each aggregate row in a workspace; the finishing kernel
+// (one warp per row: the in-order f64 sum of squares, RMSNorm, RoPE,
+// quantize-on-append) also writes the rings for the next call.
 //
 // Bit-exactness.  Every f32/f64 operation is rsLLM's, in its order, with
 // explicit round-to-nearest intrinsics (no contraction).  rsLLM's exp is the
@@ -362,11 +365,10 @@ static void rope_coeffs(uint32_t pos, float* out) {
 
 // ---- kernels ---------------------------------------------------------------------
 
-constexpr int kCmpThreads = 192;     // one emission per CTA at a time
 constexpr int kCmpMaxSources = 128;  // coff * ratio <= 128
 constexpr int kRowF = kRowDim;       // 576 lanes per compressed row
-constexpr int kDimPerThread = kRowF / kCmpThreads;  // 3
-static_assert(kRowF % kCmpThreads == 0, "dims per thread");
+constexpr int kAggThreads = kRowF;   // aggregate: one thread per output dimension
+constexpr int kFinWarps = 8;         // finish: one warp per emitted row
 
 struct CmpArgs {
   rkv_pool_view pool;
@@ -442,220 +444,148 @@ __device__ __forceinline__ void exp_fix_n(const float (&x)[N], float (&f)[N], ui
   }
 }
 
-// The emission of token t (position p, state s) by one CTA of kCmpThreads:
-// per-dimension aggregate into row[576] (shared, kDimPerThread dims per
-// thread), RMSNorm, RoPE, then quantize-on-append by warp 0.
-__device__ __forceinline__ void emit_row(const CmpArgs& a, const ThresholdTable& tab, const ExpConsts& K,
-                                         int64_t t, int p, int s, int slot, float* row, int* src, float* s_rms,
-                                         const double* s_T, double* sq) {
-  const int tid = threadIdx.x, lane = tid & 31;
-  const int k = (p + 1) / a.ratio - 1;
-  if ((int64_t)k >= a.rope_rows) {
-    if (tid == 0) set_status(a.status, RKV_ERR_INDEX_OUT_OF_RANGE);
-    return;
-  }
-  // Sources: coff 2: r < ratio the previous window (p lanes), then the
-  // current one (c lanes); coff 1: the current window.
-  const int q0 = p + 1 - a.cr;
-  for (int r = tid; r < a.cr; r += kCmpThreads) src[r] = source_of(a, t, p, s, q0 + r);
-  __syncthreads();
-
-  if (a.coff == 2) {
-    SrcPtr sp[4], sc[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      sp[r] = source_ptr(a, src[r], s, q0 + r);
-      sc[r] = source_ptr(a, src[4 + r], s, q0 + 4 + r);
-    }
-    // All loads of the thread's dims first, then every exp, one table pass.
-    constexpr int D = kDimPerThread;
-    float kp[D][4], kc[D][4], x[D * 8], w[D * 8], m[D];
-#pragma unroll
-    for (int i = 0; i < D; ++i)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        load_src(sp[r], tid + kCmpThreads * i, kp[i][r], x[8 * i + 2 * r]);
-        load_src(sc[r], kRowF + tid + kCmpThreads * i, kc[i][r], x[8 * i + 2 * r + 1]);
-      }
-    uint32_t probes = 0;
-#pragma unroll
-    for (int i = 0; i < D; ++i) {
-      m[i] = -INFINITY;
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        if (x[8 * i + 2 * r] > m[i]) m[i] = x[8 * i + 2 * r];
-        if (x[8 * i + 2 * r + 1] > m[i]) m[i] = x[8 * i + 2 * r + 1];
-      }
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        x[8 * i + r] = __fsub_rn(x[8 * i + r], m[i]);
-        const ExpVal e = exp_first(x[8 * i + r], K, s_T);
-        w[8 * i + r] = e.f;
-        probes |= (uint32_t)e.probe << (8 * i + r);
-      }
-    }
-    if (probes) exp_fix_n<D * 8>(x, w, probes);
-#pragma unroll
-    for (int i = 0; i < D; ++i) {
-      float out = 0.0f;
-      if (!(m[i] <= -INFINITY)) {
-        float den = 0.0f, num = 0.0f;
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          den = __fadd_rn(den, __fadd_rn(w[8 * i + 2 * r], w[8 * i + 2 * r + 1]));
-          num = __fadd_rn(num, __fadd_rn(__fmul_rn(w[8 * i + 2 * r], kp[i][r]),
-                                         __fmul_rn(w[8 * i + 2 * r + 1], kc[i][r])));
-        }
-        out = den > 0.0f ? __fdiv_rn(num, den) : 0.0f;
-      }
-      row[tid + kCmpThreads * i] = out;
-    }
-  } else {
-#pragma unroll 1
-    for (int i = 0; i < kDimPerThread; ++i) {
-      const int j = tid + kCmpThreads * i;
-      float m = -INFINITY;
-#pragma unroll 8
-      for (int r = 0; r < a.cr; ++r) {
-        float kv, sv;
-        load_src(source_ptr(a, src[r], s, q0 + r), j, kv, sv);
-        if (sv > m) m = sv;
-      }
-      float out = 0.0f;
-      if (!(m <= -INFINITY)) {
-        float den = 0.0f, num = 0.0f;
-#pragma unroll 1
-        for (int r0 = 0; r0 < a.cr; r0 += 8) {
-          float x[8], w[8], kv[8];
-          uint32_t probes = 0;
-#pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            float sv = -INFINITY;
-            kv[r] = 0.0f;
-            if (r0 + r < a.cr) load_src(source_ptr(a, src[r0 + r], s, q0 + r0 + r), j, kv[r], sv);
-            x[r] = __fsub_rn(sv, m);
-          }
-#pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            const ExpVal e = exp_first(x[r], K, s_T);
-            w[r] = e.f;
-            probes |= (uint32_t)e.probe << r;
-          }
-          if (probes) exp_fix_n<8>(x, w, probes);
-#pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            if (r0 + r < a.cr) {
-              den = __fadd_rn(den, w[r]);
-              num = __fadd_rn(num, __fmul_rn(w[r], kv[r]));
-            }
-          }
-        }
-        out = den > 0.0f ? __fdiv_rn(num, den) : 0.0f;
-      }
-      row[j] = out;
-    }
-  }
-  // The squares (exact in f64) are formed by every thread; one thread adds
-  // them in order.
-#pragma unroll
-  for (int i = 0; i < kDimPerThread; ++i) {
-    const double v = (double)row[tid + kCmpThreads * i];
-    sq[tid + kCmpThreads * i] = __dmul_rn(v, v);
-  }
-  __syncthreads();
-
-  // RMSNorm: sequential f64 sum of squares (compressor.rs:292-296).
-  if (tid == 0) {
-    double ss = 0.0;
-#pragma unroll 16
-    for (int j = 0; j < kRowF; ++j) ss = __dadd_rn(ss, sq[j]);
-    const float mean = __double2float_rn(__ddiv_rn(ss, (double)kRowF));
-    *s_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
-  }
-  __syncthreads();
-  const float rms = *s_rms;
-#pragma unroll
-  for (int i = 0; i < kDimPerThread; ++i) {
-    const int j = tid + kCmpThreads * i;
-    row[j] = __fmul_rn(__fmul_rn(row[j], rms), __ldg(a.norm + j));
-  }
-  __syncthreads();
-
-  if (tid < 32) {
-    // RoPE of the tail pairs (rope.rs:163-168), lane = pair.
-    const float c = __ldg(a.rope + (int64_t)k * 64 + 2 * lane);
-    const float sn = __ldg(a.rope + (int64_t)k * 64 + 2 * lane + 1);
-    const float x0 = row[kLatent + 2 * lane], x1 = row[kLatent + 2 * lane + 1];
-    row[kLatent + 2 * lane] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
-    row[kLatent + 2 * lane + 1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
-    __syncwarp();
-    // Quantize-on-append (dsv4_quant.rs:316-362) into the emit slot.
-    RowF32 x;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      x.a[i] = __float_as_uint(row[16 * lane + i]);
-      x.b[i] = __float_as_uint(row[16 * lane + 8 + i]);
-      x.rope[i] = 0u;
-    }
-    if (lane < 8) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) x.rope[i] = __float_as_uint(row[kLatent + 8 * lane + i]);
-    }
-    x.slot = slot;
-    append_row_f32(a.pool, a.layer, x, tab, a.status, lane);
-  }
-  __syncthreads();
-}
-
+// Stage 1 of an emission: the per-dimension softmax aggregate of the window
+// (compressed.rs:481-554), one thread per output dimension (576 threads).
 // Each CTA takes groups of `ratio` consecutive tokens (a group inside one
-// sequence's run holds exactly one emitting token), lists the emitting ones
-// and emits them one after another.
-__global__ void __launch_bounds__(kCmpThreads, 3)
-compress_emit_kernel(const CmpArgs a, const ThresholdTable tab, const ExpConsts K) {
+// sequence's run holds exactly one emitting token), lists the emitting ones,
+// reserves workspace rows for them with one atomic and writes each aggregate
+// row (f32 [576]) and its (slot, compressed row) pair there.
+__global__ void __launch_bounds__(kAggThreads, 2)
+compress_aggregate_kernel(const CmpArgs a, const ExpConsts K, float* __restrict__ ws_rows,
+                          int2* __restrict__ ws_meta, int* __restrict__ ws_count, int64_t ws_cap) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  __shared__ float s_row[kRowF];
-  __shared__ int s_src[kCmpMaxSources];
-  __shared__ int s_list[kCmpMaxSources][4];
-  __shared__ int s_count;
-  __shared__ float s_rms;
   __shared__ double s_T[1 << kExpTableBits];
-  __shared__ double s_sq[kRowF];
+  __shared__ SrcPtr s_ptr[kCmpMaxSources];  // the window's source rows, resolved once per emission
+  __shared__ int s_list[kCmpMaxSources][4];
+  __shared__ int s_count, s_base;
   load_exp_table(s_T);
-  const int tid = threadIdx.x;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int tid = threadIdx.x, j = tid;
   const int64_t n_groups = (a.n_tok + a.ratio - 1) / a.ratio;
   for (int64_t g = blockIdx.x; g < n_groups; g += gridDim.x) {
     if (tid == 0) s_count = 0;
     __syncthreads();
-    for (int r = tid; r < a.ratio; r += kCmpThreads) {
-      const int64_t t = g * a.ratio + r;
-      if (t >= a.n_tok) break;
-      const int p = __ldg(a.pos + t), s = __ldg(a.state_of + t), slot = __ldg(a.emit_slot + t);
-      if (p < 0 || s < 0 || (int64_t)s >= a.n_states) {
-        set_status(a.status, RKV_ERR_INDEX_OUT_OF_RANGE);
-      } else if ((p + 1) % a.ratio == 0 && slot >= 0) {
-        const int i = atomicAdd(&s_count, 1);
-        s_list[i][0] = r;
-        s_list[i][1] = p;
-        s_list[i][2] = s;
-        s_list[i][3] = slot;
+    if (tid < a.ratio) {
+      const int64_t t = g * a.ratio + tid;
+      if (t < a.n_tok) {
+        const int p = __ldg(a.pos + t), s = __ldg(a.state_of + t), slot = __ldg(a.emit_slot + t);
+        if (p < 0 || s < 0 || (int64_t)s >= a.n_states) {
+          set_status(a.status, RKV_ERR_INDEX_OUT_OF_RANGE);
+        } else if ((p + 1) % a.ratio == 0 && slot >= 0) {
+          if ((int64_t)((p + 1) / a.ratio - 1) >= a.rope_rows) {
+            set_status(a.status, RKV_ERR_INDEX_OUT_OF_RANGE);
+          } else {
+            const int i = atomicAdd(&s_count, 1);
+            s_list[i][0] = tid;
+            s_list[i][1] = p;
+            s_list[i][2] = s;
+            s_list[i][3] = slot;
+          }
+        }
       }
     }
     __syncthreads();
     const int n = s_count;
-    for (int i = 0; i < n; ++i)
-      emit_row(a, tab, K, g * a.ratio + s_list[i][0], s_list[i][1], s_list[i][2], s_list[i][3], s_row, s_src,
-               &s_rms, s_T, s_sq);
+    if (n == 0) continue;
+    if (tid == 0) s_base = atomicAdd(ws_count, n);
+    __syncthreads();
+    const int64_t base = s_base;
+    for (int e = 0; e < n; ++e) {
+      const int64_t t = g * a.ratio + s_list[e][0];
+      const int p = s_list[e][1], s = s_list[e][2];
+      const bool room = base + e < ws_cap;
+      // Sources: coff 2: r < ratio the previous window (p lanes), then the
+      // current one (c lanes); coff 1: the current window.
+      const int q0 = p + 1 - a.cr;
+      if (tid < a.cr) s_ptr[tid] = source_ptr(a, source_of(a, t, p, s, q0 + tid), s, q0 + tid);
+      __syncthreads();
+      float out = 0.0f;
+      if (a.coff == 2) {
+        float kp[4], kc[4], x[8], w[8];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          load_src(s_ptr[r], j, kp[r], x[2 * r]);
+          load_src(s_ptr[4 + r], kRowF + j, kc[r], x[2 * r + 1]);
+        }
+        float m = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+          if (x[r] > m) m = x[r];  // order p0, c0, p1, c1, ...: the reference's comparison sequence
+        if (!(m <= -INFINITY)) {
+          uint32_t probes = 0;
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            x[r] = __fsub_rn(x[r], m);
+            const ExpVal ev = exp_first(x[r], K, s_T);
+            w[r] = ev.f;
+            probes |= (uint32_t)ev.probe << r;
+          }
+          if (probes) exp_fix_n<8>(x, w, probes);
+          float den = 0.0f, num = 0.0f;
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            den = __fadd_rn(den, __fadd_rn(w[2 * r], w[2 * r + 1]));
+            num = __fadd_rn(num, __fadd_rn(__fmul_rn(w[2 * r], kp[r]), __fmul_rn(w[2 * r + 1], kc[r])));
+          }
+          out = den > 0.0f ? __fdiv_rn(num, den) : 0.0f;
+        }
+      } else {
+        float m = -INFINITY;
+#pragma unroll 8
+        for (int r = 0; r < a.cr; ++r) {
+          float kv, sv;
+          load_src(s_ptr[r], j, kv, sv);
+          if (sv > m) m = sv;
+        }
+        if (!(m <= -INFINITY)) {
+          float den = 0.0f, num = 0.0f;
+#pragma unroll 1
+          for (int r0 = 0; r0 < a.cr; r0 += 8) {
+            float x[8], w[8], kv[8];
+            uint32_t probes = 0;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+              float sv = -INFINITY;
+              kv[r] = 0.0f;
+              if (r0 + r < a.cr) load_src(s_ptr[r0 + r], j, kv[r], sv);
+              x[r] = __fsub_rn(sv, m);
+            }
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+              const ExpVal ev = exp_first(x[r], K, s_T);
+              w[r] = ev.f;
+              probes |= (uint32_t)ev.probe << r;
+            }
+            if (probes) exp_fix_n<8>(x, w, probes);
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+              if (r0 + r < a.cr) {
+                den = __fadd_rn(den, w[r]);
+                num = __fadd_rn(num, __fmul_rn(w[r], kv[r]));
+              }
+            }
+          }
+          out = den > 0.0f ? __fdiv_rn(num, den) : 0.0f;
+        }
+      }
+      if (room) {
+        ws_rows[(base + e) * kRowF + j] = out;
+        if (tid == 0) ws_meta[base + e] = make_int2(s_list[e][3], (p + 1) / a.ratio - 1);
+      } else if (tid == 0) {
+        set_status(a.status, RKV_ERR_SHAPE_MISMATCH);  // workspace smaller than the call's emissions
+      }
+      __syncthreads();  // s_ptr is rewritten for the next emission
+    }
   }
 }
 
 // The ring keeps the last coff * ratio rows of every state: a token is
 // written when no later token of its state is within coff * ratio of it.
-__global__ void __launch_bounds__(256) compress_ring_kernel(const CmpArgs a) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+// Warps [w0, w0 + n_warps) of the finishing grid do this after the aggregate
+// has read the rings.
+__device__ __forceinline__ void write_rings(const CmpArgs& a, int64_t w0, int64_t n_warps) {
   const int lane = threadIdx.x & 31;
-  const int64_t stride = (int64_t)gridDim.x * 8;
-  for (int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); t < a.n_tok; t += stride) {
+  for (int64_t t = w0; t < a.n_tok; t += n_warps) {
     const int p = __ldg(a.pos + t), s = __ldg(a.state_of + t);
     if (p < 0 || s < 0 || (int64_t)s >= a.n_states) continue;
     if (t + a.cr < a.n_tok && __ldg(a.state_of + t + a.cr) == s) continue;
@@ -674,6 +604,76 @@ __global__ void __launch_bounds__(256) compress_ring_kernel(const CmpArgs a) {
       }
       ds[v] = x;
     }
+  }
+}
+
+// Stage 2: one warp per aggregated row: RMSNorm with the f64 sum of squares
+// added in order by one lane (compressor.rs:292-296), the YaRN rotation of the
+// tail pairs (rope.rs:163-168) and the quantize-on-append into the slot
+// (dsv4_quant.rs:316-362).  Many warps per SM keep the sequential sums of
+// different rows running side by side.
+__global__ void __launch_bounds__(kFinWarps * 32)
+compress_finish_kernel(const CmpArgs a, const ThresholdTable tab, const float* __restrict__ ws_rows,
+                       const int2* __restrict__ ws_meta, const int* __restrict__ ws_count, int64_t ws_cap,
+                       int fin_blocks) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  __shared__ double s_sq[kFinWarps][kRowF];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const unsigned FULL = 0xffffffffu;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if ((int)blockIdx.x >= fin_blocks) {  // the ring writers
+    write_rings(a, (int64_t)(blockIdx.x - fin_blocks) * kFinWarps + w, (int64_t)(gridDim.x - fin_blocks) * kFinWarps);
+    return;
+  }
+  double* sq = s_sq[w];
+  float* row = reinterpret_cast<float*>(sq);  // reused for the finished row after the sum
+  const int64_t count = min((int64_t)*ws_count, ws_cap);
+  for (int64_t e = (int64_t)blockIdx.x * kFinWarps + w; e < count; e += (int64_t)fin_blocks * kFinWarps) {
+    const int2 meta = ws_meta[e];
+    float v[kRowF / 32];
+#pragma unroll
+    for (int i = 0; i < kRowF / 32; ++i) {
+      v[i] = ws_rows[e * kRowF + lane + 32 * i];
+      const double d = (double)v[i];
+      sq[lane + 32 * i] = __dmul_rn(d, d);
+    }
+    __syncwarp();
+    float rms = 0.0f;
+    if (lane == 0) {
+      double ss = 0.0;
+#pragma unroll 16
+      for (int i = 0; i < kRowF; ++i) ss = __dadd_rn(ss, sq[i]);
+      const float mean = __double2float_rn(__ddiv_rn(ss, (double)kRowF));
+      rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
+    }
+    rms = __shfl_sync(FULL, rms, 0);
+    __syncwarp();  // the sum has read sq; row[] overwrites it
+#pragma unroll
+    for (int i = 0; i < kRowF / 32; ++i)
+      row[lane + 32 * i] = __fmul_rn(__fmul_rn(v[i], rms), __ldg(a.norm + lane + 32 * i));
+    __syncwarp();
+    {
+      const float c = __ldg(a.rope + (int64_t)meta.y * 64 + 2 * lane);
+      const float sn = __ldg(a.rope + (int64_t)meta.y * 64 + 2 * lane + 1);
+      const float x0 = row[kLatent + 2 * lane], x1 = row[kLatent + 2 * lane + 1];
+      row[kLatent + 2 * lane] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+      row[kLatent + 2 * lane + 1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    }
+    __syncwarp();
+    RowF32 x;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      x.a[i] = __float_as_uint(row[16 * lane + i]);
+      x.b[i] = __float_as_uint(row[16 * lane + 8 + i]);
+      x.rope[i] = 0u;
+    }
+    if (lane < 8) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x.rope[i] = __float_as_uint(row[kLatent + 8 * lane + i]);
+    }
+    x.slot = meta.x;
+    append_row_f32(a.pool, a.layer, x, tab, a.status, lane);
+    __syncwarp();
   }
 }
 
@@ -738,12 +738,31 @@ extern "C" rkv_status rkv_compress_expf(const float* x, float* out, int64_t n, i
   return check_launch("rkv_compress_expf");
 }
 
+namespace rkv {
+
+// Workspace of one rkv_compress_append call: the emission count, then per
+// emission its (slot, compressed row) pair and its aggregate row.  A state's
+// run of L tokens emits at most L / ratio + 1 rows.
+static int64_t ws_cap_of(int32_t ratio, int64_t n_tok, int64_t n_states) {
+  return n_tok / ratio + (n_tok < n_states ? n_tok : n_states) + 1;
+}
+static int64_t ws_meta_off() { return 256; }
+static int64_t ws_rows_off(int64_t cap) { return (ws_meta_off() + cap * 8 + 255) / 256 * 256; }
+
+}  // namespace rkv
+
+extern "C" int64_t rkv_compress_workspace_bytes(int32_t ratio, int64_t n_tok, int64_t n_states) {
+  if (ratio <= 0 || n_tok < 0 || n_states < 0) return -1;
+  const int64_t cap = rkv::ws_cap_of(ratio, n_tok, n_states);
+  return rkv::ws_rows_off(cap) + cap * rkv::kRowF * 4;
+}
+
 extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t layer, int32_t ratio, float* states,
                                           int64_t n_states, const float* kv, const float* score, int64_t n_tok,
                                           const int32_t* pos, const int32_t* state_of_token,
                                           const int32_t* emit_slot, const float* ape, const float* norm,
-                                          const float* rope_table, int64_t rope_rows, uint32_t* d_status,
-                                          rkv_stream_t stream) {
+                                          const float* rope_table, int64_t rope_rows, void* workspace,
+                                          int64_t workspace_bytes, uint32_t* d_status, rkv_stream_t stream) {
   using namespace rkv;
   rkv_status st = check_pool(pool, "rkv_compress_append");
   if (st != RKV_OK) return st;
@@ -760,10 +779,15 @@ extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t lay
     return RKV_OK;
   }
   if (!states || !aligned(states, 16) || !kv || !aligned(kv, 16) || !score || !aligned(score, 16) || !pos ||
-      !state_of_token || !emit_slot || !norm || !rope_table || (ape && !aligned(ape, 16)) || !d_status)
+      !state_of_token || !emit_slot || !norm || !rope_table || (ape && !aligned(ape, 16)) || !d_status ||
+      !workspace || !aligned(workspace, 256))
     return fail(RKV_ERR_INVALID_ARGUMENT,
                 "rkv_compress_append: states, kv, score, ape (16-byte aligned), pos, state_of_token, emit_slot, "
-                "norm, rope_table and d_status are required");
+                "norm, rope_table, workspace (256-byte aligned) and d_status are required");
+  const int64_t cap = ws_cap_of(ratio, n_tok, n_states);
+  if (workspace_bytes < rkv_compress_workspace_bytes(ratio, n_tok, n_states))
+    return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_compress_append: workspace of %lld bytes, %lld needed",
+                (long long)workspace_bytes, (long long)rkv_compress_workspace_bytes(ratio, n_tok, n_states));
   st = prepare_device("rkv_compress_append");
   if (st != RKV_OK) return st;
   CmpArgs a;
@@ -788,27 +812,39 @@ extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t lay
   a.status = d_status;
   const ThresholdTable& tab = f32_threshold_table();
   const ExpConsts K = exp_host()->K;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* ws_count = reinterpret_cast<int*>(ws);
+  int2* ws_meta = reinterpret_cast<int2*>(ws + ws_meta_off());
+  float* ws_rows = reinterpret_cast<float*>(ws + ws_rows_off(cap));
 
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t need = (n_tok + ratio - 1) / ratio;  // token groups
-  const int64_t cap = (int64_t)sms * 8;
+  cudaError_t e = cudaMemsetAsync(ws_count, 0, 4, (cudaStream_t)stream);
+  if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_compress_append: %s", cudaGetErrorString(e));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(need < cap ? need : cap));
-  cfg.blockDim = dim3(kCmpThreads);
   cfg.stream = (cudaStream_t)stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, compress_emit_kernel, a, tab, K);
+  // 1. aggregate: one CTA per token group, two resident per SM
+  const int64_t groups = (n_tok + ratio - 1) / ratio;
+  const int64_t agg_cap = (int64_t)sms * 2;
+  cfg.gridDim = dim3((unsigned)(groups < agg_cap ? groups : agg_cap));
+  cfg.blockDim = dim3(kAggThreads);
+  e = cudaLaunchKernelEx(&cfg, compress_aggregate_kernel, a, K, ws_rows, ws_meta, ws_count, cap);
   if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_compress_append: launch failed: %s", cudaGetErrorString(e));
-  const int64_t need2 = (n_tok + 7) / 8;
-  cfg.gridDim = dim3((unsigned)(need2 < cap ? need2 : cap));
-  cfg.blockDim = dim3(256);
-  e = cudaLaunchKernelEx(&cfg, compress_ring_kernel, a);
+  // 2. finish (one warp per emitted row, at most cap of them) and, in the
+  // same grid, the rings for the next call (after the aggregate has read them)
+  const int64_t fin_need = (cap + kFinWarps - 1) / kFinWarps, fin_cap = (int64_t)sms * 6;
+  const int64_t fin_blocks = fin_need < fin_cap ? fin_need : fin_cap;
+  const int64_t ring_need = (n_tok + kFinWarps - 1) / kFinWarps, ring_cap = (int64_t)sms * 2;
+  cfg.gridDim = dim3((unsigned)(fin_blocks + (ring_need < ring_cap ? ring_need : ring_cap)));
+  cfg.blockDim = dim3(kFinWarps * 32);
+  e = cudaLaunchKernelEx(&cfg, compress_finish_kernel, a, tab, (const float*)ws_rows, (const int2*)ws_meta,
+                         (const int*)ws_count, cap, (int)fin_blocks);
   if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_compress_append: launch failed: %s", cudaGetErrorString(e));
   return check_launch("rkv_compress_append");
 }
