@@ -307,16 +307,14 @@ __device__ void bitonic_sort_desc(unsigned long long* a, uint32_t P) {
   }
 }
 
-// Appends the index of every score >= thr to the candidate buffer, warp by
-// warp; sm.n_cand counts all matches (even past the cap).  Per round a warp
+// Appends every score >= thr to the candidate buffer as its (key, ~index)
+// composite, warp by warp; sm.n_cand counts all matches (even past the cap).  Per round a warp
 // tests 1024 consecutive scores: each lane issues all of its loads (four
 // 256-bit loads when the row is 32-byte aligned, eight 128-bit loads when
 // 16-byte aligned; every load instruction covers 1 KB contiguous across the
 // warp) before testing them into a 32-bit mask, so 128 B per thread are in
-// flight.  A warp scan of the mask counts places the matches.  Only indices
-// are stored here; fill_keys() forms the keys afterwards with all of its
-// loads in flight at once, which keeps dependent loads out of this loop.
-// The loads keep the default L2 policy so that those re-reads mostly hit L2.
+// flight.  A warp scan of the mask counts places the matches; a match's score
+// is taken from the registers that loaded it (no second read of the row).
 // kVec: 2 = 32-byte aligned row, 1 = 16-byte aligned, 0 = scalar.
 template <int kVec>
 __device__ __forceinline__ void collect_at_least(TopkSmem& sm, const float* __restrict__ row, int n, float thr) {
@@ -329,30 +327,30 @@ __device__ __forceinline__ void collect_at_least(TopkSmem& sm, const float* __re
     const int chunk = c0 + w;
     const float* base = row + (size_t)chunk * kWarpChunk;
     uint32_t m = 0;
+    uint32_t u2[4][8], u1[8][4];
     if (chunk < n_chunks) {
       if (kVec == 2) {
-        uint32_t u[4][8];
 #pragma unroll
         for (int q = 0; q < 4; ++q)
           asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                       : "=r"(u[q][0]), "=r"(u[q][1]), "=r"(u[q][2]), "=r"(u[q][3]), "=r"(u[q][4]), "=r"(u[q][5]),
-                         "=r"(u[q][6]), "=r"(u[q][7])
+                       : "=r"(u2[q][0]), "=r"(u2[q][1]), "=r"(u2[q][2]), "=r"(u2[q][3]), "=r"(u2[q][4]),
+                         "=r"(u2[q][5]), "=r"(u2[q][6]), "=r"(u2[q][7])
                        : "l"(base + q * 256 + lane * 8));
 #pragma unroll
         for (int q = 0; q < 4; ++q)
 #pragma unroll
-          for (int j = 0; j < 8; ++j) m |= (__uint_as_float(u[q][j]) >= thr ? 1u : 0u) << (q * 8 + j);
+          for (int j = 0; j < 8; ++j) m |= (__uint_as_float(u2[q][j]) >= thr ? 1u : 0u) << (q * 8 + j);
       } else {
-        float4 v[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) v[q] = __ldg(reinterpret_cast<const float4*>(base + q * 128) + lane);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          m |= (v[q].x >= thr ? 1u : 0u) << (q * 4);
-          m |= (v[q].y >= thr ? 1u : 0u) << (q * 4 + 1);
-          m |= (v[q].z >= thr ? 1u : 0u) << (q * 4 + 2);
-          m |= (v[q].w >= thr ? 1u : 0u) << (q * 4 + 3);
+          const float4 v = __ldg(reinterpret_cast<const float4*>(base + q * 128) + lane);
+          u1[q][0] = __float_as_uint(v.x), u1[q][1] = __float_as_uint(v.y);
+          u1[q][2] = __float_as_uint(v.z), u1[q][3] = __float_as_uint(v.w);
         }
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) m |= (__uint_as_float(u1[q][j]) >= thr ? 1u : 0u) << (q * 4 + j);
       }
     }
     const uint32_t c = __popc(m);
@@ -369,38 +367,23 @@ __device__ __forceinline__ void collect_at_least(TopkSmem& sm, const float* __re
     while (m) {
       const int b = __ffs(m) - 1;
       m &= m - 1;
-      // bit b of lane `lane`: piece b/8 (b/4) of the lane, element b%8 (b%4)
+      // bit b of lane `lane`: piece b/8 (b/4) of the lane, element b%8 (b%4);
+      // its score is picked from the registers with a select chain (static
+      // indices keep the loaded values in registers)
       const int off = kVec == 2 ? (b >> 3) * 256 + lane * 8 + (b & 7) : (b >> 2) * 128 + lane * 4 + (b & 3);
-      if (pos < (uint32_t)kCandCap) sm.cand[pos] = (unsigned long long)(uint32_t)(chunk * kWarpChunk + off);
+      uint32_t bits = 0u;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) bits = (b == i) ? (kVec == 2 ? u2[i >> 3][i & 7] : u1[i >> 2][i & 3]) : bits;
+      if (pos < (uint32_t)kCandCap)
+        sm.cand[pos] = composite(topk_key(__uint_as_float(bits)), (uint32_t)(chunk * kWarpChunk + off));
       ++pos;
     }
   }
   for (int i = n_chunks * kWarpChunk + threadIdx.x; i < n; i += kTopkThreads) {
-    if (__ldg(row + i) >= thr) {
+    const float v = __ldg(row + i);
+    if (v >= thr) {
       const uint32_t pos = atomicAdd(&sm.n_cand, 1u);
-      if (pos < (uint32_t)kCandCap) sm.cand[pos] = (unsigned long long)(uint32_t)i;
-    }
-  }
-}
-
-// The collection pass stores indices only; this forms every candidate's key
-// with all of a thread's score loads issued together (mostly L2 hits).
-__device__ __forceinline__ void fill_keys(TopkSmem& sm, const float* __restrict__ row, uint32_t m) {
-  constexpr int U = 8;
-  for (uint32_t base = 0; base < m; base += U * kTopkThreads) {
-    uint32_t idx[U];
-    float v[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const uint32_t i = base + u * kTopkThreads + threadIdx.x;
-      idx[u] = i < m ? (uint32_t)sm.cand[i] : 0u;
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) v[u] = __ldg(row + idx[u]);
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const uint32_t i = base + u * kTopkThreads + threadIdx.x;
-      if (i < m) sm.cand[i] = composite(topk_key(v[u]), idx[u]);
+      if (pos < (uint32_t)kCandCap) sm.cand[pos] = composite(topk_key(v), (uint32_t)i);
     }
   }
 }
@@ -561,8 +544,7 @@ topk_select_kernel(const float* __restrict__ scores, int64_t ld, const int32_t* 
     const float q = (float)kk * (float)kSample / (float)n;
     uint32_t rank = (uint32_t)ceilf(q + 3.5f * sqrtf(q) + 2.0f);
     rank = max(1u, min(rank, (uint32_t)kSample));
-    const uint32_t fit = (uint32_t)(0.75f * (float)kCandCap * (float)kSample / (float)n);
-    const uint32_t t = sample_select(sm, skeys, rank, max(fit, rank));
+    const uint32_t t = sample_select(sm, skeys, rank, rank);
     if (t != 0u) {
       if (tid == 0) sm.n_cand = 0u;
       __syncthreads();
@@ -574,10 +556,7 @@ topk_select_kernel(const float* __restrict__ scores, int64_t ld, const int32_t* 
       const uint32_t got = sm.n_cand;
       done = got >= (uint32_t)kk && got <= (uint32_t)kCandCap;
       __syncthreads();
-      if (done) {
-        fill_keys(sm, row, got);
-        __syncthreads();
-      }
+
     }
   }
 
