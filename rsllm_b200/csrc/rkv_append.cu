@@ -14,6 +14,8 @@
 // Semantics: crates/rsllm-backend-cpu/src/ops/dsv4_quant.rs:316-362 applied
 // per row (see rkv_common.cuh), row placement of crates/rsllm-kvcache/src/
 // dsv4/swa.rs:73-94 generalised to a slot mapping.
+#include <atomic>
+
 #include "rkv_common.cuh"
 #include "rkv_host.h"
 
@@ -127,13 +129,17 @@ extern "C" rkv_status rkv_append_quant_bf16(const rkv_pool_view* pool, int32_t l
   if (n_rows > (int64_t)INT32_MAX) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_append_quant_bf16: too many rows in one call");
   if (!rows || !aligned(rows, 32) || !slot_mapping || !aligned(slot_mapping, 4))
     return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_append_quant_bf16: rows (32-byte aligned) and slot_mapping are required");
-  static int resident = 0;  // CTAs of this kernel one wave holds on the device
+  // CTAs of this kernel one wave holds on the current device (cached per device)
+  static std::atomic<int> resident_of[kMaxDevicesCached];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int resident = (dev >= 0 && dev < kMaxDevicesCached) ? resident_of[dev].load(std::memory_order_relaxed) : 0;
   if (resident == 0) {
-    int dev = 0, sms = 0, per_sm = 0;
-    cudaGetDevice(&dev);
+    int sms = 0, per_sm = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, append_quant_kernel, kAppendWarps * 32, 0);
     resident = (sms > 0 && per_sm > 0) ? sms * per_sm : 148 * 4;
+    if (dev >= 0 && dev < kMaxDevicesCached) resident_of[dev].store(resident, std::memory_order_relaxed);
   }
   const int64_t need = (n_rows + kAppendWarps - 1) / kAppendWarps;
   const unsigned grid = (unsigned)(need < resident ? need : resident);

@@ -18,6 +18,7 @@
 // trip rounded to bf16 in every lane.
 #include <math.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "rkv_common.cuh"
@@ -104,13 +105,16 @@ extern "C" rkv_status rkv_append_quant_f32(const rkv_pool_view* pool, int32_t la
   if (!rows || !aligned(rows, 32) || !slot_mapping || !aligned(slot_mapping, 4))
     return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_append_quant_f32: rows (32-byte aligned) and slot_mapping are required");
   const ThresholdTable& tab = f32_threshold_table();
-  static int resident = 0;
+  static std::atomic<int> resident_of[kMaxDevicesCached];  // one wave of this kernel, per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int resident = (dev >= 0 && dev < kMaxDevicesCached) ? resident_of[dev].load(std::memory_order_relaxed) : 0;
   if (resident == 0) {
-    int dev = 0, sms = 0, per_sm = 0;
-    cudaGetDevice(&dev);
+    int sms = 0, per_sm = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, append_quant_f32_kernel, kF32Warps * 32, 0);
     resident = (sms > 0 && per_sm > 0) ? sms * per_sm : 148 * 4;
+    if (dev >= 0 && dev < kMaxDevicesCached) resident_of[dev].store(resident, std::memory_order_relaxed);
   }
   const int64_t need = (n_rows + kF32Warps - 1) / kF32Warps;
   cudaLaunchConfig_t cfg = {};

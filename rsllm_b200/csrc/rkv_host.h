@@ -17,6 +17,9 @@ void clear_error();
 // Maps a pending launch error (cudaGetLastError) to RKV_ERR_CUDA.
 rkv_status check_launch(const char* what);
 
+// Per-device caches of launch parameters cover devices [0, kMaxDevicesCached).
+constexpr int kMaxDevicesCached = 64;
+
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 // Validates a pool view: non-null 256-byte aligned base, positive sizes.

@@ -48,6 +48,8 @@
 // tensor memory and returns.
 #include <cmath>
 
+#include <atomic>
+
 #include "rkv_common.cuh"
 #include "rkv_host.h"
 
@@ -767,11 +769,14 @@ extern "C" rkv_status rkv_mla_decode_fp8(const rkv_pool_view* pool, int32_t laye
                 "aligned), out (16-byte aligned) and, with n_splits > 1, workspace are required");
   if (!std::isfinite(softmax_scale))
     return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_mla_decode_fp8: softmax_scale must be finite");
-  static bool attr_set = false;
-  if (!attr_set) {
+  // the shared-memory opt-in is per device
+  static std::atomic<bool> attr_set[kMaxDevicesCached];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevicesCached || !attr_set[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
     if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_mla_decode_fp8: %s", cudaGetErrorString(e));
-    attr_set = true;
+    if (dev >= 0 && dev < kMaxDevicesCached) attr_set[dev].store(true, std::memory_order_release);
   }
   Params prm;
   prm.pool = *pool;

@@ -18,6 +18,8 @@
 // or the same device from several threads) race on it -- order them.
 #include <algorithm>
 
+#include <atomic>
+
 #include "rkv_common.cuh"
 #include "rkv_host.h"
 
@@ -30,7 +32,7 @@ constexpr int64_t kStaticMaxMoves = RKV_STATIC_MAX_MOVES;
 static __device__ __align__(256) int32_t g_move_scratch[2 * kStaticMaxMoves];
 
 constexpr int kMaxDevices = 64;
-static int32_t* g_scratch_addr[kMaxDevices];  // device address of g_move_scratch, per device
+static std::atomic<int32_t*> g_scratch_addr[kMaxDevices];  // device address of g_move_scratch, per device
 
 // Page-table rewrite against the staged move list: an entry equal to some
 // src[i] becomes dst[i] (binary search of the ascending sources).
@@ -89,14 +91,14 @@ extern "C" rkv_status rkv_apply_page_moves_static(const rkv_pool_view* pool, con
   if (dev < 0 || dev >= kMaxDevices) return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_apply_page_moves_static: device %d", dev);
   // Once per device, with that device current: the device address of the
   // staging array (the symbol itself is only a host-side stand-in).
-  if (!g_scratch_addr[dev]) {
+  if (!g_scratch_addr[dev].load(std::memory_order_acquire)) {
     void* ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, g_move_scratch);
     if (e != cudaSuccess || !ptr)
       return fail(RKV_ERR_CUDA, "rkv_apply_page_moves_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_scratch_addr[dev] = static_cast<int32_t*>(ptr);
+    g_scratch_addr[dev].store(static_cast<int32_t*>(ptr), std::memory_order_release);
   }
-  int32_t* s_src = g_scratch_addr[dev];
+  int32_t* s_src = g_scratch_addr[dev].load(std::memory_order_acquire);
   int32_t* s_dst = s_src + kStaticMaxMoves;
   e = cudaMemcpyAsync(s_src, src, (size_t)n_moves * 4, cudaMemcpyHostToDevice, (cudaStream_t)stream);
   if (e == cudaSuccess)
