@@ -98,13 +98,13 @@ append_quant_kernel(rkv_pool_view pool, int layer0, uint32_t n_tokens, uint32_t 
 }
 
 // Exhaustive-check helper: the append kernel's lane conversion (packed
-// multiply by the inverse scale, here 1.0, + 0.0, saturating RNE) applied to
+// multiply by the inverse scale, here 1.0, -0.0 folded to +0.0, saturating RNE) applied to
 // raw f32 values that are already divided by their block scale.
 __global__ void e4m3_code_range_kernel(uint32_t first, int64_t n, uint8_t* __restrict__ out) {
   const unsigned long long one2 = 0x3f8000003f800000ull;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const unsigned long long x = first + (uint32_t)i;  // lane 0 = x, lane 1 = +0.0
-    const unsigned long long t = add_f32x2(mul_f32x2(x, one2), 0ull);
+    const unsigned long long t = clear_zero_sign2(mul_f32x2(x, one2));
     out[i] = (uint8_t)(cvt_e4m3x2(__uint_as_float((uint32_t)t), 0.0f) & 0xffu);
   }
 }

@@ -90,13 +90,24 @@ __device__ __forceinline__ unsigned long long add_f32x2(unsigned long long a, un
   return r;
 }
 
+// -0.0 -> +0.0 in both halves of a packed pair (the reference's code sign is
+// `x < 0`, so a zero, negative or not, gets code 0x00).  Done on the bits: an
+// `add.rn.f32x2` of +0.0 after the multiply can be contracted by ptxas into a
+// fused multiply-add, which keeps the sign of a product that underflows to 0.
+__device__ __forceinline__ unsigned long long clear_zero_sign2(unsigned long long t) {
+  uint32_t lo = (uint32_t)t, hi = (uint32_t)(t >> 32);
+  lo = (lo & 0x7fffffffu) ? lo : 0u;
+  hi = (hi & 0x7fffffffu) ? hi : 0u;
+  return ((unsigned long long)hi << 32) | lo;
+}
+
 // One bf16 pair -> two E4M3 codes (bits 0..15): t = v * 2^-e exactly as the
-// reference's v / 2^e (both correctly rounded), + 0.0 folds -0.0 into +0.0
-// (the reference's sign is `x < 0`), then RNE with saturation.  For bf16
-// inputs |t| <= 448 always holds, so the reference's clamp is the identity.
+// reference's v / 2^e (both correctly rounded), -0.0 folded into +0.0 (the
+// reference's sign is `x < 0`), then RNE with saturation.  For bf16 inputs
+// |t| <= 448 always holds, so the reference's clamp is the identity.
 __device__ __forceinline__ uint32_t quant_pair(uint32_t w, unsigned long long inv2) {
   const unsigned long long v = ((unsigned long long)(w & 0xffff0000u) << 32) | (unsigned long long)(w << 16);
-  const unsigned long long t = add_f32x2(mul_f32x2(v, inv2), 0ull);
+  const unsigned long long t = clear_zero_sign2(mul_f32x2(v, inv2));
   return cvt_e4m3x2(__uint_as_float((uint32_t)t), __uint_as_float((uint32_t)(t >> 32)));
 }
 

@@ -46,7 +46,7 @@ __device__ __forceinline__ void load_row_f32(const uint8_t* rows, const int32_t*
 
 __device__ __forceinline__ uint32_t quant_pair_f32(uint32_t lo, uint32_t hi, unsigned long long inv2) {
   const unsigned long long v = ((unsigned long long)hi << 32) | lo;
-  const unsigned long long t = add_f32x2(mul_f32x2(v, inv2), 0ull);
+  const unsigned long long t = clear_zero_sign2(mul_f32x2(v, inv2));
   return cvt_e4m3x2(__uint_as_float((uint32_t)t), __uint_as_float((uint32_t)(t >> 32)));
 }
 

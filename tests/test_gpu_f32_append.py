@@ -87,3 +87,37 @@ def test_bad_rows_write_nothing(cuda, orc):
     with pytest.raises(rk.NonFiniteInput):
         pool.append_layer(0, torch.from_numpy(rows[3:4]).to(cuda), i32(slots[3:4], cuda))
         pool.check("append")
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_tiny_lanes_next_to_huge_amax(cuda, orc, dtype):
+    """Lanes so small next to their block's amax that v / 2^e underflows: the
+    reference's f32 division gives -0.0 or +0.0 and the code is 0x00 either
+    way (sign = x < 0); subnormal and tiny negative quotients keep 0x80 where
+    they round to a zero magnitude of a negative value."""
+    rng = np.random.default_rng(9)
+    n_tok = 128
+    rows = rng.standard_normal((n_tok, 576)).astype(np.float32)
+    big = np.float32(3.0e38) if dtype == "f32" else np.float32(1.0e38)
+    for b in range(8):
+        blk = rows[:, 64 * b:64 * b + 64]
+        blk[:, 0] = big * (1 if b % 2 else -1)
+        blk[:, 1:9] = np.array([-1e-30, 1e-30, -1e-38, -1e-40, -1e-45, -3e-7, 2e-9, -2e-9], np.float32)
+        blk[:, 9:17] *= np.float32(1e-20)
+    if dtype == "bf16":
+        b16 = (rows.view(np.uint32) >> 16).astype(np.uint16)  # truncation keeps every class of value
+        rows_t = torch.from_numpy(b16.view(np.int16)).view(torch.bfloat16)
+        ref_rows = b16
+    else:
+        rows_t = torch.from_numpy(rows)
+        ref_rows = rows
+    slots = np.arange(n_tok, dtype=np.int32)
+    pool = rk.PagedKvPool(2, 1, device=cuda)
+    pool.storage.zero_()
+    pool.append_layer(0, rows_t.to(cuda), i32(slots, cuda))
+    pool.check("append")
+    ref = orc.new_pool(2, 1)
+    assert orc.append_rows(ref, 2, 1, 0, ref_rows, slots) == 0
+    got = pool.storage.cpu().numpy()
+    bad = np.nonzero(got != ref)[0]
+    assert bad.size == 0, f"{bad.size} pool bytes differ, first at byte {int(bad[0])}: {got[bad[:4]]} vs {ref[bad[:4]]}"
