@@ -476,7 +476,9 @@ RKV_API rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t layer,
 /* expf as the compressor kernel evaluates it, on the host (host != 0, x and
  * out host memory) or on the current device (x, out device memory): a
  * double-precision exp rounded to f32, corrected from a table wherever the
- * host's expf rounds differently.  Exposed to check it against expf. */
+ * host's expf rounds differently.  Domain: x <= 0, -inf and NaN (the
+ * aggregate's x = score - max); x > 0 is outside it.  Exposed to check it
+ * against expf. */
 RKV_API rkv_status rkv_compress_expf(const float* x, float* out, int64_t n, int32_t host, rkv_stream_t stream);
 /* Number of table entries (x whose expf differs from the rounded double). */
 RKV_API int64_t rkv_compress_expf_table_size(void);
