@@ -435,9 +435,11 @@ RKV_API rkv_status rkv_unpack_pages(const rkv_pool_view* pool, int32_t layer0, i
  *
  * states:        device f32, n_states * rkv_compress_state_bytes(ratio) bytes:
  *                per state the last coff * ratio rows of kv, then of score
- *                (APE added), [2][coff*ratio][width], row = pos % (coff*ratio).
- *                Written by this call for the last coff * ratio tokens of each
- *                state; no initialisation is needed.
+ *                (as given, without APE: the APE row is added when a row is
+ *                read, so every call on these states must pass the same ape),
+ *                [2][coff*ratio][width], row = pos % (coff*ratio).  Written by
+ *                this call for the last coff * ratio tokens of each state; no
+ *                initialisation is needed.
  * kv, score:     device f32 [n_tok][width] (the compressor projections),
  *                16-byte aligned.  The tokens of one state must appear in
  *                consecutive entries at consecutive positions, in order, and
@@ -463,16 +465,11 @@ RKV_API rkv_status rkv_compress_rope_table(int32_t ratio, int64_t n_rows, float*
  * current device (done by the first rkv_compress_append otherwise; call it
  * before capturing a CUDA graph). */
 RKV_API rkv_status rkv_compress_prepare(void);
-/* workspace: device memory, 256-byte aligned, of at least
- * rkv_compress_workspace_bytes(ratio, n_tok, n_states) bytes (the emitted rows
- * between the aggregate and the finishing kernel). */
-RKV_API int64_t rkv_compress_workspace_bytes(int32_t ratio, int64_t n_tok, int64_t n_states);
 RKV_API rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t layer, int32_t ratio, float* states,
                                        int64_t n_states, const float* kv, const float* score, int64_t n_tok,
                                        const int32_t* pos, const int32_t* state_of_token, const int32_t* emit_slot,
                                        const float* ape, const float* norm, const float* rope_table,
-                                       int64_t rope_rows, void* workspace, int64_t workspace_bytes,
-                                       uint32_t* d_status, rkv_stream_t stream);
+                                       int64_t rope_rows, uint32_t* d_status, rkv_stream_t stream);
 /* expf as the compressor kernel evaluates it, on the host (host != 0, x and
  * out host memory) or on the current device (x, out device memory): a
  * double-precision exp rounded to f32, corrected from a table wherever the

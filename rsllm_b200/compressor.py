@@ -85,7 +85,6 @@ class CompressorBank:
         self.states = torch.zeros((n_states, nbytes // 4), dtype=torch.float32, device=self.device)
         rows = max_positions // ratio + 1
         self.rope = torch.from_numpy(compress_rope_table(ratio, rows)).to(self.device)
-        self.workspace: torch.Tensor | None = None  # grown to the largest call (rkv_compress_workspace_bytes)
         with torch.cuda.device(self.device):
             check(self.lib.rkv_compress_prepare(), "CompressorBank")
 
@@ -94,7 +93,8 @@ class CompressorBank:
                ape: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> None:
         """One compressor step for ``n_tok`` tokens (``rkv_compress_append``):
         kv, score f32 [n_tok, width]; pos, state_of_token, emit_slot int32
-        [n_tok]; norm f32 [576]; ape f32 [ratio, width] or None.  Tokens of one
+        [n_tok]; norm f32 [576]; ape f32 [ratio, width] or None (the same on
+        every call: the states keep scores without it).  Tokens of one
         state are consecutive entries at consecutive positions.  A token with
         (pos + 1) % ratio == 0 writes its emitted row at ``emit_slot`` (< 0:
         dropped).  Device-side errors land in ``pool.status``."""
@@ -112,12 +112,8 @@ class CompressorBank:
             _need(ape, torch.float32, "ape", self.device)
             if ape.shape != (self.ratio, self.width):
                 raise ShapeMismatch(f"CompressorBank.append: ape must be [{self.ratio}, {self.width}]")
-        need = int(self.lib.rkv_compress_workspace_bytes(self.ratio, n_tok, self.n_states))
-        if self.workspace is None or self.workspace.numel() < need:
-            self.workspace = torch.empty(need, dtype=torch.uint8, device=self.device)
         check(self.lib.rkv_compress_append(byref(pool.view), layer, self.ratio, _ptr(self.states), self.n_states,
                                            _ptr(kv), _ptr(score), n_tok, _ptr(pos), _ptr(state_of_token),
                                            _ptr(emit_slot), _ptr(ape), _ptr(norm), _ptr(self.rope),
-                                           self.rope.shape[0], _ptr(self.workspace), self.workspace.numel(),
-                                           _ptr(pool.status), _stream(stream)),
+                                           self.rope.shape[0], _ptr(pool.status), _stream(stream)),
               "CompressorBank.append")

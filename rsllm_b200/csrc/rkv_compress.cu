@@ -11,12 +11,12 @@
 // squares, its 64 tail lanes are rotated (crates/rsllm-backend-cpu/src/ops/
 // rope.rs:128-172 at position pos + 1 - ratio) and it is FP8-quantized
 // (dsv4_quant.rs:316-362).  Here a batch of tokens is two launches: the
-// aggregate kernel (one CTA of 576 threads per emission, one output dimension
+// emission kernel (one CTA of 576 threads per emission, one output dimension
 // per thread) reads the window's rows straight from this call's input or, for
 // positions of earlier calls, from a per-state ring of the last coff * ratio
-// rows, and leaves each aggregate row in a workspace; the finishing kernel
-// (one warp per row: the in-order f64 sum of squares, RMSNorm, RoPE,
-// quantize-on-append) also writes the rings for the next call.
+// rows, aggregates, normalises, rotates and quantizes the row into its pool
+// slot, and writes the ring rows that no emission of the call still needs;
+// the ring kernel writes the rest once every emission has read the rings.
 //
 // Bit-exactness.  Every f32/f64 operation is rsLLM's, in its order, with
 // explicit round-to-nearest intrinsics (no contraction).  rsLLM's exp is the
@@ -32,13 +32,18 @@
 // operations) over every f32 in [-150, 0] and calling its expf wherever the
 // double lies within 2^-5 ulp of a midpoint; the band is the largest distance
 // at which it found a difference (2^-9.25 ulp for glibc 2.39, so about 0.4% of
-// inputs are looked up).  An exhaustive test checks every input.  RoPE cos/sin
-// come from a host table computed with the host's libm as rope.rs does.
+// inputs are looked up).  An exhaustive test checks every input.  The f64
+// sum of squares of RMSNorm is a tree sum whose mean is used wherever the
+// in-order sum provably rounds to the same f32; otherwise (about 1 row in
+// 2^16) one thread adds the squares in order.  RoPE cos/sin come from a host
+// table computed with the host's libm as rope.rs does.
 #include <math.h>
+#include <cmath>
 #include <stdio.h>
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <thread>
 #include <vector>
@@ -57,13 +62,21 @@ constexpr int kExpHashBits = 19;                 // 2 MB open-addressing table, 
 constexpr uint32_t kExpScanWindow = 1u << 24;    // 2^-5 ulp, in units of the 29 dropped bits
 
 struct ExpConsts {
-  float inv_step_f;  // 256 / ln 2 rounded to f32
-  double step_hi;   // ln 2 / 256, 21 significant bits (k * step_hi is exact)
-  double step_lo;   // ln 2 / 256 - step_hi
-  double c2, c3;    // 1/2, 1/6
-  int64_t band;     // |dropped bits - 2^28| at or below which x is looked up
+  double inv_step;     // 256 / ln 2
+  double magic;        // 1.5 * 2^52: fma(x, inv_step, magic) rounds x * inv_step to an integer
+  double neg_step_hi;  // -(ln 2 / 256), 21 significant bits
+  double neg_step_lo;  // -(ln 2 / 256 - step_hi)
+  double c2, c3;       // 1/2, 1/6
+  int32_t band;        // |dropped bits - 2^28| at or below which x is looked up
 };
 
+__host__ __device__ __forceinline__ double d_fma(double a, double b, double c) {
+#ifdef __CUDA_ARCH__
+  return __fma_rn(a, b, c);
+#else
+  return std::fma(a, b, c);
+#endif
+}
 __host__ __device__ __forceinline__ double d_mul(double a, double b) {
 #ifdef __CUDA_ARCH__
   return __dmul_rn(a, b);
@@ -112,28 +125,37 @@ __host__ __device__ __forceinline__ float f_mul(float a, float b) {
 #endif
 }
 
-// exp(x) in double for x in [-150, 0]; the same IEEE operations on both sides.
-// k = rint(x * 256/ln2) is taken in f32 (any integer near the quotient
-// serves: r stays within 1.01 * ln2/512); the scaling by 2^(k/256) adds to the
-// exponent field (exact: every result is a normal double).
+// exp(x) in double for x in [-150, 0]; the same IEEE operations on both sides
+// (fused multiply-adds are single correctly rounded operations on both).
+// k = round(x * 256/ln2) comes from the magic-constant addition, whose low
+// word is k itself; r = x - k ln2/256 in two steps (|r| <= ln2/512); the
+// scaling by 2^(k/256) adds to the exponent field (exact: every result is a
+// normal double).
 __host__ __device__ __forceinline__ double exp_core(float xf, const ExpConsts& K, const double* T) {
   const double x = (double)xf;
-  const float kf = rintf(f_mul(xf, K.inv_step_f));
-  const double k = (double)kf;
-  const double r = d_sub(d_sub(x, d_mul(k, K.step_hi)), d_mul(k, K.step_lo));
-  double p = d_add(d_mul(K.c3, r), K.c2);
-  p = d_add(d_mul(p, r), 1.0);
-  p = d_add(d_mul(p, r), 1.0);
-  const int ki = (int)kf;
+  const double t = d_fma(x, K.inv_step, K.magic);
+  const double k = d_sub(t, K.magic);
+  const int ki = (int)(uint32_t)d_bits(t);
+  const double r = d_fma(k, K.neg_step_lo, d_fma(k, K.neg_step_hi, x));
+  const double p = d_fma(d_fma(d_fma(K.c3, r, K.c2), r, 1.0), r, 1.0);
   const double y = d_mul(T[ki & ((1 << kExpTableBits) - 1)], p);
+#ifdef __CUDA_ARCH__
+  return __hiloint2double(__double2hiint(y) + ((ki >> kExpTableBits) << 20), __double2loint(y));
+#else
   return d_from_bits(d_bits(y) + ((uint64_t)(int64_t)(ki >> kExpTableBits) << 52));
+#endif
 }
 
-// True where the rounding of d to f32 may differ from the host's expf.
-__host__ __device__ __forceinline__ bool exp_in_band(double d, int64_t band) {
-  if (d < 1.1754943508222875e-38) return true;  // f32 subnormal results: always looked up
-  const int64_t low = (int64_t)(d_bits(d) & ((1ull << 29) - 1)) - (1ll << 28);
-  return (low < 0 ? -low : low) <= band;
+// Distance of the 29 bits that the rounding to f32 drops from their midpoint.
+__host__ __device__ __forceinline__ int32_t exp_mid_dist(double d) {
+  const int32_t low = (int32_t)((uint32_t)d_bits(d) & ((1u << 29) - 1)) - (1 << 28);
+  return low < 0 ? -low : low;
+}
+
+// True where the rounding of d to f32 (f) may differ from the host's expf:
+// near a rounding midpoint, or f32 results at or below the smallest normal.
+__host__ __device__ __forceinline__ bool exp_in_band(double d, uint32_t f_bits, int32_t band) {
+  return f_bits <= 0x00800000u || exp_mid_dist(d) <= band;
 }
 
 __host__ __device__ __forceinline__ uint32_t exp_hash(uint32_t key) {
@@ -168,13 +190,15 @@ static uint32_t float_to_bits(float f) {
 static void build_exp_host() {
   ExpHost& E = g_exp;
   const long double ln2 = 0.693147180559945309417232121458176568L;
-  E.K.inv_step_f = (float)(256.0L / ln2);
+  E.K.inv_step = (double)(256.0L / ln2);
+  E.K.magic = 6755399441055744.0;
   const double step = (double)(ln2 / 256.0L);
-  E.K.step_hi = d_from_bits(d_bits(step) & ~((1ull << 32) - 1));
-  E.K.step_lo = (double)(ln2 / 256.0L - (long double)E.K.step_hi);
+  const double step_hi = d_from_bits(d_bits(step) & ~((1ull << 32) - 1));
+  E.K.neg_step_hi = -step_hi;
+  E.K.neg_step_lo = -(double)(ln2 / 256.0L - (long double)step_hi);
   E.K.c2 = 0.5;
   E.K.c3 = 1.0 / 6.0;
-  E.K.band = kExpScanWindow;
+  E.K.band = (int32_t)kExpScanWindow;
   for (int j = 0; j < (1 << kExpTableBits); ++j) E.T[j] = (double)exp2l((long double)j / 256.0L);
 
   unsigned nt = std::thread::hardware_concurrency();
@@ -190,17 +214,15 @@ static void build_exp_host() {
       for (uint32_t key = a; key < b; ++key) {
         const float x = bits_to_float(key | 0x80000000u);
         const double d = exp_core(x, E.K, E.T);
-        if (!exp_in_band(d, kExpScanWindow)) continue;
-        const uint32_t f = float_to_bits((float)d), g = float_to_bits(expf(x));
+        const uint32_t f = float_to_bits((float)d);
+        if (!exp_in_band(d, f, (int32_t)kExpScanWindow)) continue;
+        const uint32_t g = float_to_bits(expf(x));
         if (f == g) continue;
         if (g != f + 1 && g + 1 != f) {
           bad[t] = 1;
           continue;
         }
-        if (d >= 1.1754943508222875e-38) {
-          const int64_t low = (int64_t)(d_bits(d) & ((1ull << 29) - 1)) - (1ll << 28);
-          far[t] = std::max(far[t], low < 0 ? -low : low);
-        }
+        if (f > 0x00800000u) far[t] = std::max(far[t], (int64_t)exp_mid_dist(d));
         part[t].push_back(key | (g > f ? 0x80000000u : 0u));
       }
     });
@@ -223,7 +245,7 @@ static void build_exp_host() {
     snprintf(E.err, sizeof E.err, "expf correction table has %lld entries", (long long)E.n_entries);
     return;
   }
-  E.K.band = band;
+  E.K.band = (int32_t)band;
   E.hash.assign((size_t)1 << kExpHashBits, 0u);
   const uint32_t mask = (1u << kExpHashBits) - 1;
   for (unsigned t = 0; t < nt; ++t)
@@ -256,7 +278,7 @@ static float expf_table_host(float x, const ExpHost& E) {
   if (!(x >= -150.0f)) return 0.0f;
   const double d = exp_core(x, E.K, E.T);
   uint32_t f = float_to_bits((float)d);
-  if (exp_in_band(d, E.K.band)) f += exp_correction(float_to_bits(x) & 0x7fffffffu, E.hash.data());
+  if (exp_in_band(d, f, E.K.band)) f += exp_correction(float_to_bits(x) & 0x7fffffffu, E.hash.data());
   return bits_to_float(f);
 }
 
@@ -267,8 +289,8 @@ static __device__ uint32_t g_exp_hash[1 << kExpHashBits];
 // Stand-ins for the rows of positions before a sequence's start (kv 0,
 // score -inf) and for "no APE" (adding +0.0 to a score changes at most the
 // sign of a zero, which no exp or comparison downstream can see).
-static __device__ float g_zero_row[2 * kRowDim];
-static __device__ float g_neginf_row[2 * kRowDim];
+static __device__ __align__(16) float g_zero_row[2 * kRowDim];
+static __device__ __align__(16) float g_neginf_row[2 * kRowDim];
 
 constexpr int kMaxDevices = 64;
 static bool g_exp_uploaded[kMaxDevices];
@@ -308,7 +330,7 @@ __device__ __forceinline__ ExpVal exp_first(float x, const ExpConsts& K, const d
   const bool in_range = x >= -150.0f;
   const double d = exp_core(in_range ? x : 0.0f, K, T);
   const float f = __double2float_rn(d);
-  return {in_range ? f : (x != x ? x : 0.0f), in_range && exp_in_band(d, K.band)};
+  return {in_range ? f : (x != x ? x : 0.0f), in_range && exp_in_band(d, __float_as_uint(f), K.band)};
 }
 
 __device__ __forceinline__ float exp_fix(float x, float f) {
@@ -368,7 +390,7 @@ static void rope_coeffs(uint32_t pos, float* out) {
 constexpr int kCmpMaxSources = 128;  // coff * ratio <= 128
 constexpr int kRowF = kRowDim;       // 576 lanes per compressed row
 constexpr int kAggThreads = kRowF;   // aggregate: one thread per output dimension
-constexpr int kFinWarps = 8;         // finish: one warp per emitted row
+constexpr int kFinWarps = 8;         // ring kernel: warps per CTA
 
 struct CmpArgs {
   rkv_pool_view pool;
@@ -398,7 +420,7 @@ __device__ __forceinline__ int source_of(const CmpArgs& a, int64_t t, int p, int
 struct SrcPtr {
   const float* kv;   // column 0 of the row
   const float* sc;
-  const float* ape;  // APE row added to the score (zeros for ring rows and when there is no APE)
+  const float* ape;  // APE row added to the score (zeros before the sequence start and when there is no APE)
 };
 
 __device__ __forceinline__ SrcPtr source_ptr(const CmpArgs& a, int code, int s, int q) {
@@ -411,6 +433,7 @@ __device__ __forceinline__ SrcPtr source_ptr(const CmpArgs& a, int code, int s, 
     const float* st = a.states + (int64_t)s * 2 * a.cr * a.width;
     r.kv = st + (int64_t)(q % a.cr) * a.width;
     r.sc = st + (int64_t)(a.cr + q % a.cr) * a.width;
+    if (a.ape) r.ape = a.ape + (int64_t)(q % a.ratio) * a.width;
   }
   return r;
 }
@@ -444,240 +467,742 @@ __device__ __forceinline__ void exp_fix_n(const float (&x)[N], float (&f)[N], ui
   }
 }
 
-// Stage 1 of an emission: the per-dimension softmax aggregate of the window
-// (compressed.rs:481-554), one thread per output dimension (576 threads).
-// Each CTA takes groups of `ratio` consecutive tokens (a group inside one
-// sequence's run holds exactly one emitting token), lists the emitting ones,
-// reserves workspace rows for them with one atomic and writes each aggregate
-// row (f32 [576]) and its (slot, compressed row) pair there.
+// exp of x[0..7] (x <= 0, -inf or NaN) as the host's expf rounds it.  When
+// all eight lie in [-87, 0] (no f32 subnormal results, no range or NaN
+// handling) the band test is the only check.  A per-lane branch, no warp
+// vote: callers may be divergent (dimensions whose scores are all -inf skip
+// the exps).
+__device__ __forceinline__ void exp8(float (&x)[8], float (&w)[8], const ExpConsts& K, const double* T) {
+  bool fast = true;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) fast = fast && x[r] >= -87.0f;
+  uint32_t probes = 0;
+  if (fast) {
+    const uint32_t lo_edge = (1u << 28) - (uint32_t)K.band, width = 2u * (uint32_t)K.band;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const double d = exp_core(x[r], K, T);
+      w[r] = __double2float_rn(d);
+      const uint32_t low = (uint32_t)__double2loint(d) & ((1u << 29) - 1);
+      probes |= (uint32_t)(low - lo_edge <= width) << r;
+    }
+  } else {
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const ExpVal ev = exp_first(x[r], K, T);
+      w[r] = ev.f;
+      probes |= (uint32_t)ev.probe << r;
+    }
+  }
+  if (probes) exp_fix_n<8>(x, w, probes);
+}
+
+// The per-dimension softmax aggregate of one emission's window
+// (compressed.rs:481-554) for output dimension j, from the window's source
+// rows listed in s_ptr (p lanes of the previous window, then c lanes of the
+// current one for coff 2).
+__device__ __forceinline__ float aggregate_dim(const CmpArgs& a, const ExpConsts& K, const double* s_T,
+                                               const SrcPtr* s_ptr, int j) {
+  float out = 0.0f;
+  if (a.coff == 2) {
+    float kp[4], kc[4], x[8], w[8];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      load_src(s_ptr[r], j, kp[r], x[2 * r]);
+      load_src(s_ptr[4 + r], kRowF + j, kc[r], x[2 * r + 1]);
+    }
+    float m = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      if (x[r] > m) m = x[r];  // order p0, c0, p1, c1, ...: the reference's comparison sequence
+    if (!(m <= -INFINITY)) {
+#pragma unroll
+      for (int r = 0; r < 8; ++r) x[r] = __fsub_rn(x[r], m);
+      exp8(x, w, K, s_T);
+      float den = 0.0f, num = 0.0f;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        den = __fadd_rn(den, __fadd_rn(w[2 * r], w[2 * r + 1]));
+        num = __fadd_rn(num, __fadd_rn(__fmul_rn(w[2 * r], kp[r]), __fmul_rn(w[2 * r + 1], kc[r])));
+      }
+      out = den > 0.0f ? __fdiv_rn(num, den) : 0.0f;
+    }
+  } else {
+    float m = -INFINITY;
+#pragma unroll 8
+    for (int r = 0; r < a.cr; ++r) {
+      float kv, sv;
+      load_src(s_ptr[r], j, kv, sv);
+      if (sv > m) m = sv;
+    }
+    if (!(m <= -INFINITY)) {
+      float den = 0.0f, num = 0.0f;
+#pragma unroll 1
+      for (int r0 = 0; r0 < a.cr; r0 += 8) {
+        float x[8], w[8], kv[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          float sv = -INFINITY;
+          kv[r] = 0.0f;
+          if (r0 + r < a.cr) load_src(s_ptr[r0 + r], j, kv[r], sv);
+          x[r] = __fsub_rn(sv, m);
+        }
+        exp8(x, w, K, s_T);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          if (r0 + r < a.cr) {
+            den = __fadd_rn(den, w[r]);
+            num = __fadd_rn(num, __fmul_rn(w[r], kv[r]));
+          }
+        }
+      }
+      out = den > 0.0f ? __fdiv_rn(num, den) : 0.0f;
+    }
+  }
+  return out;
+}
+
+// The ring keeps the last coff * ratio rows of every state: token t (of
+// state s) writes its kv row and its score row at pos % (coff * ratio) when
+// no later token of its state is within coff * ratio of it.  The score is kept
+// without the APE row, which is added when the row is read (the same rounded
+// sum rsLLM stores: APE is a per-layer constant).
+__device__ __forceinline__ bool ring_written(const CmpArgs& a, int64_t t, int s) {
+  return !(t + a.cr < a.n_tok && __ldg(a.state_of + t + a.cr) == s);
+}
+
+// Whether that write may happen while this call's emissions still read the
+// ring.  It overwrites position pos - coff*ratio.  For the first token of a
+// state's run every emission of the run reads only later positions; from the
+// (coff*ratio)-th token of the run on, the overwritten position lies inside
+// this call, where the emissions read the input rows.  Other ring writes (the
+// 2nd .. (coff*ratio)-th token of a run that is also among its last coff*ratio
+// tokens) wait for the ring kernel.
+__device__ __forceinline__ bool ring_write_now(const CmpArgs& a, int64_t t, int s) {
+  return t == 0 || __ldg(a.state_of + t - 1) != s || (t >= a.cr && __ldg(a.state_of + t - a.cr) == s);
+}
+
+// Copies token t's ring rows (kv, and the score as it came, without APE),
+// threads [i, i + n) of the caller.
+__device__ __forceinline__ void copy_ring_rows(const CmpArgs& a, int64_t t, int p, int s, int i, int n) {
+  float4* st = reinterpret_cast<float4*>(a.states + (int64_t)s * 2 * a.cr * a.width);
+  const float4* kv = reinterpret_cast<const float4*>(a.kv + t * a.width);
+  const float4* sc = reinterpret_cast<const float4*>(a.score + t * a.width);
+  const int n4 = a.width / 4;
+  float4* dk = st + (int64_t)(p % a.cr) * n4;
+  float4* ds = st + (int64_t)(a.cr + p % a.cr) * n4;
+  for (int v = i; v < 2 * n4; v += n) {
+    if (v < n4)
+      dk[v] = __ldg(kv + v);
+    else
+      ds[v - n4] = __ldg(sc + (v - n4));
+  }
+}
+
+constexpr int kEmitWarps = kAggThreads / 32;  // 18
+// The in-order f64 sum of squares is replaced by a tree sum unless the mean
+// lies within this many units of the 29 bits that its rounding to f32 drops
+// from a rounding midpoint: both sums are within 585 * 2^-53 of the exact sum
+// of the 576 non-negative squares (a tree of depth 10, and 575 roundings in
+// order), and the tree's mean (a product with the rounded 1/576) and the
+// reference's quotient differ by 3 more roundings, so the two means are
+// within 2^9.3 such units of each other and round alike outside the margin.
+constexpr int32_t kSumMargin = 1 << 11;
+
+// Barriers over the threads that work on one emission: the whole CTA
+// (compress_emit_kernel) or named barrier 1 over the consumer warps
+// (compress_emit_staged_kernel).
+template <bool kNamed>
+__device__ __forceinline__ void emit_bar() {
+  if (kNamed)
+    asm volatile("bar.sync 1, %0;" ::"n"(kAggThreads) : "memory");
+  else
+    __syncthreads();
+}
+template <bool kNamed>
+__device__ __forceinline__ bool emit_bar_or(bool v) {
+  if (!kNamed) return __syncthreads_or(v) != 0;
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(kAggThreads)
+      : "memory");
+  return r != 0;
+}
+
+struct EmitScratch {
+  double* sq;    // [576]
+  double* part;  // [18]
+  uint32_t* amax;  // [18]
+  double* ss;    // [1]
+};
+
+// The rest of an emission once thread j (of 576) holds the aggregate `out` of
+// dimension j: RMSNorm (compressor.rs:292-296: the f64 sum of squares, its
+// mean rounded to f32, 1/sqrt(mean + 1e-6), (v * rms) * w), the YaRN rotation
+// of the tail pairs (rope.rs:163-168; c, sn: this thread's pair coefficients)
+// and the quantize-on-append of the row (dsv4_quant.rs:316-362) into `slot`.
+template <bool kNamed>
+__device__ __forceinline__ void emit_finish(const CmpArgs& a, const ThresholdTable& tab, const EmitScratch& sc,
+                                            float out, float wn, float c, float sn, int slot) {
+  const unsigned FULL = 0xffffffffu;
+  const int j = threadIdx.x, lane = j & 31, w = j >> 5;
+  const double dv = (double)out;
+  const double sq = __dmul_rn(dv, dv);
+  sc.sq[j] = sq;
+  double ws = sq;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ws = __dadd_rn(ws, __shfl_xor_sync(FULL, ws, o));
+  if (lane == 0) sc.part[w] = ws;
+  emit_bar<kNamed>();
+  double ss = lane < kEmitWarps ? sc.part[lane] : 0.0;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(FULL, ss, o));
+  double qd = __dmul_rn(ss, 1.0 / (double)kRowF);
+  if (!(qd >= 0x1p-125 && qd < 0x1p127) || exp_mid_dist(qd) <= kSumMargin) {  // uniform over the emission's threads
+    if (j == 0) {
+      double s2 = 0.0;
+#pragma unroll 16
+      for (int i = 0; i < kRowF; ++i) s2 = __dadd_rn(s2, sc.sq[i]);
+      *sc.ss = s2;
+    }
+    emit_bar<kNamed>();
+    qd = __ddiv_rn(*sc.ss, (double)kRowF);
+  }
+  const float mean = __double2float_rn(qd);
+  const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
+  float v = __fmul_rn(__fmul_rn(out, rms), wn);
+  if (w >= kLatent / 32) {  // RoPE pairs (j, j ^ 1), warp-uniform
+    const float other = __shfl_xor_sync(FULL, v, 1);
+    v = (j & 1) ? __fadd_rn(__fmul_rn(other, sn), __fmul_rn(v, c)) : __fsub_rn(__fmul_rn(v, c), __fmul_rn(other, sn));
+  }
+
+  // quantize-on-append: block maxima, then one byte per latent lane
+  const uint32_t vb = __float_as_uint(v);
+  const uint32_t mag = j < kLatent ? (vb & 0x7fffffffu) : 0u;
+  const uint32_t wmax = __reduce_max_sync(FULL, mag);
+  if (lane == 0) sc.amax[w] = wmax;
+  if (emit_bar_or<kNamed>(mag >= 0x7f800000u)) {  // a non-finite latent lane rejects the row
+    if (j == 0) set_status(a.status, RKV_ERR_NON_FINITE_INPUT);
+    return;
+  }
+  uint8_t* pg = page_base(a.pool, a.layer, slot >> 6);
+  const int off = slot & 63;
+  if (j < kLatent) {
+    const int blk = j >> 6;
+    const int e = scale_exponent_f32(max(sc.amax[2 * blk], sc.amax[2 * blk + 1]), tab);
+    uint32_t tq = __float_as_uint(__fmul_rn(v, __uint_as_float((uint32_t)(127 - e) << 23)));
+    tq = (tq & 0x7fffffffu) ? tq : 0u;  // the reference's sign is x < 0
+    const float hi = __uint_as_float(__shfl_down_sync(FULL, tq, 1));
+    const uint32_t c2 = cvt_e4m3x2(__uint_as_float(tq), hi);  // lanes j, j + 1 (even j)
+    const uint32_t c4 = c2 | (__shfl_down_sync(FULL, c2, 2) << 16);
+    if ((j & 3) == 0) *reinterpret_cast<uint32_t*>(pg + codes_off(off) + j) = c4;
+    if ((j & 63) == 0) reinterpret_cast<uint32_t*>(pg + scales_off(off))[blk] = (uint32_t)(e + 127) << 23;
+  } else {
+    const uint32_t hi = __shfl_down_sync(FULL, vb, 1);
+    const uint32_t r2 = bf16x2_rn(vb, hi);
+    if ((j & 1) == 0) *reinterpret_cast<uint32_t*>(pg + rope_off(off) + 2 * (j - kLatent)) = r2;
+  }
+}
+
+// One emission per CTA iteration, one thread per output dimension: the
+// aggregate, RMSNorm (compressor.rs:292-296: the f64 sum of squares, its mean
+// rounded to f32, 1/sqrt(mean + 1e-6), (v * rms) * w), the YaRN rotation of
+// the tail pairs (rope.rs:163-168) and the quantize-on-append of the row
+// (dsv4_quant.rs:316-362) straight into its pool slot.  CTAs take groups of
+// `ratio` consecutive tokens; the ring rows of the group's tokens are written
+// here when ring_write_now allows it.
 __global__ void __launch_bounds__(kAggThreads, 2)
-compress_aggregate_kernel(const CmpArgs a, const ExpConsts K, float* __restrict__ ws_rows,
-                          int2* __restrict__ ws_meta, int* __restrict__ ws_count, int64_t ws_cap) {
+compress_emit_kernel(const CmpArgs a, const ExpConsts K, const ThresholdTable tab) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ double s_T[1 << kExpTableBits];
   __shared__ SrcPtr s_ptr[kCmpMaxSources];  // the window's source rows, resolved once per emission
-  __shared__ int s_list[kCmpMaxSources][4];
-  __shared__ int s_count, s_base;
+  __shared__ int4 s_tok[kCmpMaxSources];    // pos, state, slot of the group's tokens
+  __shared__ uint32_t s_bal[2][kCmpMaxSources / 32];  // emitting / ring-writing tokens of the group
+  __shared__ double s_sq[kRowF];
+  __shared__ double s_part[kEmitWarps];
+  __shared__ uint32_t s_amax[kEmitWarps];
+  __shared__ double s_ss;
+  const EmitScratch scr{s_sq, s_part, s_amax, &s_ss};
   load_exp_table(s_T);
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int tid = threadIdx.x, j = tid;
+  const unsigned FULL = 0xffffffffu;
+  const int tid = threadIdx.x, j = tid, lane = tid & 31, w = tid >> 5;
+  const float wn = __ldg(a.norm + j);
+  const int n_bal = (a.ratio + 31) >> 5;
   const int64_t n_groups = (a.n_tok + a.ratio - 1) / a.ratio;
   for (int64_t g = blockIdx.x; g < n_groups; g += gridDim.x) {
-    if (tid == 0) s_count = 0;
-    __syncthreads();
-    if (tid < a.ratio) {
+    __syncthreads();  // the previous group's s_tok and s_bal are consumed
+    if (w < n_bal) {
       const int64_t t = g * a.ratio + tid;
-      if (t < a.n_tok) {
+      bool em = false, rg = false;
+      if (tid < a.ratio && t < a.n_tok) {
         const int p = __ldg(a.pos + t), s = __ldg(a.state_of + t), slot = __ldg(a.emit_slot + t);
         if (p < 0 || s < 0 || (int64_t)s >= a.n_states) {
           set_status(a.status, RKV_ERR_INDEX_OUT_OF_RANGE);
-        } else if ((p + 1) % a.ratio == 0 && slot >= 0) {
-          if ((int64_t)((p + 1) / a.ratio - 1) >= a.rope_rows) {
-            set_status(a.status, RKV_ERR_INDEX_OUT_OF_RANGE);
-          } else {
-            const int i = atomicAdd(&s_count, 1);
-            s_list[i][0] = tid;
-            s_list[i][1] = p;
-            s_list[i][2] = s;
-            s_list[i][3] = slot;
+        } else {
+          if ((p + 1) % a.ratio == 0 && slot >= 0) {
+            if ((int64_t)((p + 1) / a.ratio - 1) >= a.rope_rows || (int64_t)(slot >> 6) >= a.pool.n_pages)
+              set_status(a.status, RKV_ERR_INDEX_OUT_OF_RANGE);
+            else
+              em = true;
           }
+          rg = ring_written(a, t, s) && ring_write_now(a, t, s);
+          s_tok[tid] = make_int4(p, s, slot, 0);
         }
+      }
+      const uint32_t be = __ballot_sync(FULL, em), br = __ballot_sync(FULL, rg);
+      if (lane == 0) {
+        s_bal[0][w] = be;
+        s_bal[1][w] = br;
       }
     }
     __syncthreads();
-    const int n = s_count;
-    if (n == 0) continue;
-    if (tid == 0) s_base = atomicAdd(ws_count, n);
-    __syncthreads();
-    const int64_t base = s_base;
-    for (int e = 0; e < n; ++e) {
-      const int64_t t = g * a.ratio + s_list[e][0];
-      const int p = s_list[e][1], s = s_list[e][2];
-      const bool room = base + e < ws_cap;
-      // Sources: coff 2: r < ratio the previous window (p lanes), then the
-      // current one (c lanes); coff 1: the current window.
-      const int q0 = p + 1 - a.cr;
-      if (tid < a.cr) s_ptr[tid] = source_ptr(a, source_of(a, t, p, s, q0 + tid), s, q0 + tid);
-      __syncthreads();
-      float out = 0.0f;
-      if (a.coff == 2) {
-        float kp[4], kc[4], x[8], w[8];
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          load_src(s_ptr[r], j, kp[r], x[2 * r]);
-          load_src(s_ptr[4 + r], kRowF + j, kc[r], x[2 * r + 1]);
+    for (int b = 0; b < n_bal; ++b) {
+      for (uint32_t bits = s_bal[0][b]; bits; bits &= bits - 1) {
+        const int tl = 32 * b + __ffs(bits) - 1;
+        const int64_t t = g * a.ratio + tl;
+        const int4 tk = s_tok[tl];
+        const int p = tk.x, s = tk.y, slot = tk.z;
+        // Sources: coff 2: r < ratio the previous window (p lanes), then the
+        // current one (c lanes); coff 1: the current window.
+        const int q0 = p + 1 - a.cr;
+        if (tid < a.cr) s_ptr[tid] = source_ptr(a, source_of(a, t, p, s, q0 + tid), s, q0 + tid);
+        __syncthreads();
+        const float out = aggregate_dim(a, K, s_T, s_ptr, j);
+
+        float c = 0.0f, sn = 0.0f;
+        if (j >= kLatent) {
+          const float* cs = a.rope + (int64_t)((p + 1) / a.ratio - 1) * 64 + ((j - kLatent) & ~1);
+          c = __ldg(cs);
+          sn = __ldg(cs + 1);
         }
-        float m = -INFINITY;
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-          if (x[r] > m) m = x[r];  // order p0, c0, p1, c1, ...: the reference's comparison sequence
-        if (!(m <= -INFINITY)) {
-          uint32_t probes = 0;
-#pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            x[r] = __fsub_rn(x[r], m);
-            const ExpVal ev = exp_first(x[r], K, s_T);
-            w[r] = ev.f;
-            probes |= (uint32_t)ev.probe << r;
-          }
-          if (probes) exp_fix_n<8>(x, w, probes);
-          float den = 0.0f, num = 0.0f;
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            den = __fadd_rn(den, __fadd_rn(w[2 * r], w[2 * r + 1]));
-            num = __fadd_rn(num, __fadd_rn(__fmul_rn(w[2 * r], kp[r]), __fmul_rn(w[2 * r + 1], kc[r])));
-          }
-          out = den > 0.0f ? __fdiv_rn(num, den) : 0.0f;
-        }
-      } else {
-        float m = -INFINITY;
-#pragma unroll 8
-        for (int r = 0; r < a.cr; ++r) {
-          float kv, sv;
-          load_src(s_ptr[r], j, kv, sv);
-          if (sv > m) m = sv;
-        }
-        if (!(m <= -INFINITY)) {
-          float den = 0.0f, num = 0.0f;
-#pragma unroll 1
-          for (int r0 = 0; r0 < a.cr; r0 += 8) {
-            float x[8], w[8], kv[8];
-            uint32_t probes = 0;
-#pragma unroll
-            for (int r = 0; r < 8; ++r) {
-              float sv = -INFINITY;
-              kv[r] = 0.0f;
-              if (r0 + r < a.cr) load_src(s_ptr[r0 + r], j, kv[r], sv);
-              x[r] = __fsub_rn(sv, m);
-            }
-#pragma unroll
-            for (int r = 0; r < 8; ++r) {
-              const ExpVal ev = exp_first(x[r], K, s_T);
-              w[r] = ev.f;
-              probes |= (uint32_t)ev.probe << r;
-            }
-            if (probes) exp_fix_n<8>(x, w, probes);
-#pragma unroll
-            for (int r = 0; r < 8; ++r) {
-              if (r0 + r < a.cr) {
-                den = __fadd_rn(den, w[r]);
-                num = __fadd_rn(num, __fmul_rn(w[r], kv[r]));
-              }
-            }
-          }
-          out = den > 0.0f ? __fdiv_rn(num, den) : 0.0f;
-        }
+        emit_finish<false>(a, tab, scr, out, wn, c, sn, slot);
       }
-      if (room) {
-        ws_rows[(base + e) * kRowF + j] = out;
-        if (tid == 0) ws_meta[base + e] = make_int2(s_list[e][3], (p + 1) / a.ratio - 1);
-      } else if (tid == 0) {
-        set_status(a.status, RKV_ERR_SHAPE_MISMATCH);  // workspace smaller than the call's emissions
+    }
+    for (int b = 0; b < n_bal; ++b) {
+      for (uint32_t bits = s_bal[1][b]; bits; bits &= bits - 1) {
+        const int tl = 32 * b + __ffs(bits) - 1;
+        copy_ring_rows(a, g * a.ratio + tl, s_tok[tl].x, s_tok[tl].y, tid, kAggThreads);
       }
-      __syncthreads();  // s_ptr is rewritten for the next emission
     }
   }
 }
 
-// The ring keeps the last coff * ratio rows of every state: a token is
-// written when no later token of its state is within coff * ratio of it.
-// Warps [w0, w0 + n_warps) of the finishing grid do this after the aggregate
-// has read the rings.
-__device__ __forceinline__ void write_rings(const CmpArgs& a, int64_t w0, int64_t n_warps) {
+// The ring writes that compress_emit_kernel left (ring_write_now false): one
+// warp per token, after every emission of the call has read the rings.
+__global__ void __launch_bounds__(kFinWarps * 32)
+compress_ring_kernel(const CmpArgs a) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = threadIdx.x & 31;
-  for (int64_t t = w0; t < a.n_tok; t += n_warps) {
+  const int64_t n_warps = (int64_t)gridDim.x * kFinWarps;
+  for (int64_t t = (int64_t)blockIdx.x * kFinWarps + (threadIdx.x >> 5); t < a.n_tok; t += n_warps) {
     const int p = __ldg(a.pos + t), s = __ldg(a.state_of + t);
     if (p < 0 || s < 0 || (int64_t)s >= a.n_states) continue;
-    if (t + a.cr < a.n_tok && __ldg(a.state_of + t + a.cr) == s) continue;
-    float* st = a.states + (int64_t)s * 2 * a.cr * a.width;
-    const float4* kv = reinterpret_cast<const float4*>(a.kv + t * a.width);
-    const float4* sc = reinterpret_cast<const float4*>(a.score + t * a.width);
-    const float4* ape = a.ape ? reinterpret_cast<const float4*>(a.ape + (int64_t)(p % a.ratio) * a.width) : nullptr;
-    float4* dk = reinterpret_cast<float4*>(st + (int64_t)(p % a.cr) * a.width);
-    float4* ds = reinterpret_cast<float4*>(st + (int64_t)(a.cr + p % a.cr) * a.width);
-    for (int v = lane; v < a.width / 4; v += 32) {
-      dk[v] = __ldg(kv + v);
-      float4 x = __ldg(sc + v);
-      if (ape) {
-        const float4 b = __ldg(ape + v);
-        x = make_float4(__fadd_rn(x.x, b.x), __fadd_rn(x.y, b.y), __fadd_rn(x.z, b.z), __fadd_rn(x.w, b.w));
-      }
-      ds[v] = x;
-    }
+    if (!ring_written(a, t, s) || ring_write_now(a, t, s)) continue;
+    copy_ring_rows(a, t, p, s, lane, 32);
   }
 }
 
-// Stage 2: one warp per aggregated row: RMSNorm with the f64 sum of squares
-// added in order by one lane (compressor.rs:292-296), the YaRN rotation of the
-// tail pairs (rope.rs:163-168) and the quantize-on-append into the slot
-// (dsv4_quant.rs:316-362).  Many warps per SM keep the sequential sums of
-// different rows running side by side.
-__global__ void __launch_bounds__(kFinWarps * 32)
-compress_finish_kernel(const CmpArgs a, const ThresholdTable tab, const float* __restrict__ ws_rows,
-                       const int2* __restrict__ ws_meta, const int* __restrict__ ws_count, int64_t ws_cap,
-                       int fin_blocks) {
+// ---- staged emission kernel (windows of at most 8 source rows) -------------------
+//
+// A producer warp walks the CTA's token groups one emission ahead of the 18
+// consumer warps: it loads the group's token metadata in one round trip,
+// resolves each emission's eight source rows with warp shuffles, and brings the
+// half-rows the aggregate reads (2 x 8 x 2304 B) into a shared-memory stage
+// with bulk asynchronous copies completing on the stage's mbarrier; it also
+// writes the group's ring rows where ring_write_now allows it.  Two stages:
+// the consumers aggregate, normalise and quantize one emission while the next
+// one's rows arrive.  Every wait is bounded (1 s); a timeout sets
+// RKV_ERR_CUDA in the status word and ends the CTA.
+
+constexpr int kStageRows = 8;                          // coff * ratio <= 8
+constexpr uint32_t kHalfBytes = kRowF * 4;             // one staged half-row (576 f32)
+constexpr int kConsumers = kAggThreads;                // 18 warps, one output dimension per thread
+constexpr int kStagedThreads = kConsumers + 32;        // + the producer warp
+constexpr uint64_t kStageTimeoutNs = 1000000000ull;
+
+struct StageDesc {
+  int kind;  // 1: an emission (its rows arrive on the stage's mbarrier), 2: ring rows only, 0: done
+  int p, slot, krow;
+  uint32_t ape_mask;  // sources that are real rows (their score gets the APE row)
+  int n_ring;         // ring rows to write after the emission (the group's last item carries them)
+  int pad[2];
+  int ring_t[kStageRows], ring_p[kStageRows], ring_s[kStageRows];
+};
+static_assert(sizeof(StageDesc) == 128, "stage descriptor layout");
+
+// Dynamic shared memory of the staged kernel.
+constexpr uint32_t kStKv = 0;                                         // f32 [2][8][576]
+constexpr uint32_t kStSc = kStKv + 2 * kStageRows * kHalfBytes;       // f32 [2][8][576]
+constexpr uint32_t kStT = kStSc + 2 * kStageRows * kHalfBytes;        // f64 [256]
+constexpr uint32_t kStSq = kStT + (1u << kExpTableBits) * 8;          // f64 [576]
+constexpr uint32_t kStPart = kStSq + kRowF * 8;                       // f64 [18]
+constexpr uint32_t kStAmax = kStPart + 160;                           // u32 [18]
+constexpr uint32_t kStDesc = kStAmax + 80;                            // StageDesc [2]
+constexpr uint32_t kStBar = kStDesc + 2 * sizeof(StageDesc);          // full[2], empty[2]
+constexpr uint32_t kStMisc = kStBar + 32;                             // f64 sum, abort flag
+constexpr uint32_t kStagedSmem = kStMisc + 16;
+
+__device__ __forceinline__ uint64_t st_now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool st_mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of the given parity; false on timeout or abort.
+__device__ __noinline__ bool st_mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (st_mbar_test(bar, parity)) return true;
+  const uint64_t t0 = st_now_ns();
+  while (!st_mbar_test(bar, parity)) {
+    if (*abort_flag) return false;
+    if (st_now_ns() - t0 > kStageTimeoutNs) return false;
+  }
+  return true;
+}
+// Barrier 1 over the consumer warps, AND of a predicate.
+__device__ __forceinline__ bool st_bar_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(kConsumers)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void st_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory"); }
+__device__ __forceinline__ void st_arrive_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void st_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// Global -> own shared memory bulk copy (no multicast), completing on bar.
+__device__ __forceinline__ void st_bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ uint32_t st_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// The aggregate of output dimension j from one stage: kvs / scs hold the
+// window's source half-rows [8][576] (for coff 2: sources 0..3 the previous
+// window's p lanes, 4..7 the current window's c lanes).  Source r reads APE
+// row r % ratio (q0 = pos + 1 - coff*ratio is a multiple of ratio).
+__device__ __forceinline__ float aggregate_staged(const CmpArgs& a, const ExpConsts& K, const double* s_T,
+                                                  const float* kvs, const float* scs, uint32_t ape_mask, int j) {
+  // The kv values stay in shared memory until the sums: fewer live registers.
+  float out = 0.0f;
+  if (a.coff == 2) {
+    float x[8], w[8];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      x[2 * r] = scs[r * kRowF + j];
+      x[2 * r + 1] = scs[(4 + r) * kRowF + j];
+    }
+    if (ape_mask) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        if ((ape_mask >> r) & 1u) x[2 * r] = __fadd_rn(x[2 * r], __ldg(a.ape + r * a.width + j));
+        if ((ape_mask >> (4 + r)) & 1u) x[2 * r + 1] = __fadd_rn(x[2 * r + 1], __ldg(a.ape + r * a.width + kRowF + j));
+      }
+    }
+    float m = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      if (x[r] > m) m = x[r];  // order p0, c0, p1, c1, ...: the reference's comparison sequence
+    if (!(m <= -INFINITY)) {
+#pragma unroll
+      for (int r = 0; r < 8; ++r) x[r] = __fsub_rn(x[r], m);
+      exp8(x, w, K, s_T);
+      float den = 0.0f, num = 0.0f;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        den = __fadd_rn(den, __fadd_rn(w[2 * r], w[2 * r + 1]));
+        num = __fadd_rn(num, __fadd_rn(__fmul_rn(w[2 * r], kvs[r * kRowF + j]),
+                                       __fmul_rn(w[2 * r + 1], kvs[(4 + r) * kRowF + j])));
+      }
+      out = den > 0.0f ? __fdiv_rn(num, den) : 0.0f;
+    }
+  } else {
+    float x[8], w[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      x[r] = -INFINITY;
+      if (r < a.cr) {
+        x[r] = scs[r * kRowF + j];
+        if ((ape_mask >> r) & 1u) x[r] = __fadd_rn(x[r], __ldg(a.ape + r * a.width + j));
+      }
+    }
+    float m = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      if (x[r] > m) m = x[r];
+    if (!(m <= -INFINITY)) {
+#pragma unroll
+      for (int r = 0; r < 8; ++r) x[r] = r < a.cr ? __fsub_rn(x[r], m) : 0.0f;  // padding: unused
+      exp8(x, w, K, s_T);
+      float den = 0.0f, num = 0.0f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        if (r < a.cr) {
+          den = __fadd_rn(den, w[r]);
+          num = __fadd_rn(num, __fmul_rn(w[r], kvs[r * kRowF + j]));
+        }
+      }
+      out = den > 0.0f ? __fdiv_rn(num, den) : 0.0f;
+    }
+  }
+  return out;
+}
+
+// Thread j of 576 copies its share of the ring rows listed in the stage
+// descriptor (token kv and score rows, one float4 at a time, four in flight).
+__device__ __forceinline__ void copy_ring_staged(const CmpArgs& a, const StageDesc* d, int n_ring, int j) {
+  const int n4 = a.width / 4, per = 2 * n4, total = n_ring * per;
+  for (int base = j; base < total; base += 4 * kAggThreads) {
+    float4 v[4];
+    float4* dst[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = base + k * kAggThreads;
+      dst[k] = nullptr;
+      if (i < total) {
+        const int e = i / per, x = i - e * per;
+        const int64_t t = d->ring_t[e];
+        const int p = d->ring_p[e], s = d->ring_s[e];
+        float4* st = reinterpret_cast<float4*>(a.states + (int64_t)s * 2 * a.cr * a.width);
+        if (x < n4) {
+          v[k] = __ldg(reinterpret_cast<const float4*>(a.kv) + t * n4 + x);
+          dst[k] = st + (int64_t)(p % a.cr) * n4 + x;
+        } else {
+          v[k] = __ldg(reinterpret_cast<const float4*>(a.score) + t * n4 + (x - n4));
+          dst[k] = st + (int64_t)(a.cr + p % a.cr) * n4 + (x - n4);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (dst[k]) *dst[k] = v[k];
+  }
+}
+
+__global__ void __launch_bounds__(kStagedThreads, 2)
+compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdTable tab) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  __shared__ double s_sq[kFinWarps][kRowF];
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  extern __shared__ __align__(16) uint8_t st_smem[];
+  float* s_kv = reinterpret_cast<float*>(st_smem + kStKv);
+  float* s_sc = reinterpret_cast<float*>(st_smem + kStSc);
+  double* s_T = reinterpret_cast<double*>(st_smem + kStT);
+  StageDesc* s_desc = reinterpret_cast<StageDesc*>(st_smem + kStDesc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(st_smem + kStMisc + 8);
+  const EmitScratch scr{reinterpret_cast<double*>(st_smem + kStSq), reinterpret_cast<double*>(st_smem + kStPart),
+                        reinterpret_cast<uint32_t*>(st_smem + kStAmax), reinterpret_cast<double*>(st_smem + kStMisc)};
+  const uint32_t bar_full = st_u32(st_smem + kStBar), bar_empty = bar_full + 16;  // [2] each, 8 B apart
   const unsigned FULL = 0xffffffffu;
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  if ((int)blockIdx.x >= fin_blocks) {  // the ring writers
-    write_rings(a, (int64_t)(blockIdx.x - fin_blocks) * kFinWarps + w, (int64_t)(gridDim.x - fin_blocks) * kFinWarps);
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  for (int i = tid; i < (1 << kExpTableBits); i += kStagedThreads) s_T[i] = g_exp_T[i];
+  if (tid == 0) {
+    for (int b = 0; b < 4; ++b)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_full + 8 * b) : "memory");
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  if (w == kConsumers / 32) {
+    // ---- producer warp ----
+    const int cr = a.cr, ratio = a.ratio, n_meta = 2 * cr + ratio;  // n_meta <= 24
+    const int64_t n_groups = (a.n_tok + ratio - 1) / ratio;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int64_t g = blockIdx.x; g < n_groups && ok; g += gridDim.x) {
+      // tokens t0 - cr .. t0 + ratio + cr - 1 around the group, one per lane
+      const int64_t t0 = g * ratio, tm = t0 - cr + lane;
+      int mp = -1, ms = -1, mslot = -1;
+      if (lane < n_meta && tm >= 0 && tm < a.n_tok) {
+        mp = __ldg(a.pos + tm);
+        ms = __ldg(a.state_of + tm);
+        mslot = __ldg(a.emit_slot + tm);
+      }
+      const bool in_group = lane >= cr && lane < cr + ratio && tm < a.n_tok;
+      const bool valid = mp >= 0 && ms >= 0 && (int64_t)ms < a.n_states;
+      if (in_group && !valid) set_status(a.status, RKV_ERR_INDEX_OUT_OF_RANGE);
+      const int s_prev = __shfl_sync(FULL, ms, (lane - 1) & 31);
+      const int s_back = __shfl_sync(FULL, ms, (lane - cr) & 31);
+      const int s_fwd = __shfl_sync(FULL, ms, (lane + cr) & 31);
+      bool em = false;
+      if (in_group && valid && (mp + 1) % ratio == 0 && mslot >= 0) {
+        if ((int64_t)((mp + 1) / ratio - 1) >= a.rope_rows || (int64_t)(mslot >> 6) >= a.pool.n_pages)
+          set_status(a.status, RKV_ERR_INDEX_OUT_OF_RANGE);
+        else
+          em = true;
+      }
+      // ring_written and ring_write_now from the neighbouring lanes
+      const bool rg = in_group && valid && s_fwd != ms && (s_prev != ms || s_back == ms);
+      const uint32_t emask = __ballot_sync(FULL, em), rmask = __ballot_sync(FULL, rg);
+      const int n_ring = __popc(rmask);
+      // items: one per emission, the last one carrying the ring rows; or one
+      // ring-only item
+      uint32_t items = emask ? emask : (rmask ? (rmask & (0u - rmask)) : 0u);
+      for (; items; items &= items - 1) {
+        const int L = __ffs(items) - 1;
+        const bool emission = emask != 0, last = (items & (items - 1)) == 0;
+        const uint32_t buf = it & 1;
+        if (it >= 2) {
+          bool got = true;
+          if (lane == 0) got = st_mbar_wait(bar_empty + 8 * buf, ((it >> 1) - 1) & 1, abort_flag);
+          if (!__shfl_sync(FULL, (int)got, 0)) {
+            ok = false;
+            break;
+          }
+        }
+        StageDesc* d = s_desc + buf;
+        const int nr = last ? n_ring : 0;
+        if (nr && rg) {
+          const int e = __popc(rmask & ((1u << lane) - 1));
+          d->ring_t[e] = (int)(t0 - cr + lane);
+          d->ring_p[e] = mp;
+          d->ring_s[e] = ms;
+        }
+        const uint32_t full = bar_full + 8 * buf;
+        if (!emission) {
+          __syncwarp();
+          if (lane == 0) {
+            d->kind = 2;
+            d->n_ring = nr;
+            st_arrive(full);
+          }
+          ++it;
+          continue;
+        }
+        const int p = __shfl_sync(FULL, mp, L), s = __shfl_sync(FULL, ms, L), slot = __shfl_sync(FULL, mslot, L);
+        const int64_t t = t0 - cr + L;
+        // source r = lane: position q = p + 1 - cr + r, input token u = t - cr + 1 + r
+        const int r = lane, q = p + 1 - cr + r;
+        const int lu = r < cr ? L - cr + 1 + r : L;
+        const int su = __shfl_sync(FULL, ms, lu), pu = __shfl_sync(FULL, mp, lu);
+        const int col = (a.coff == 2 && r >= ratio) ? kRowF : 0;
+        const float* skv = g_zero_row + col;
+        const float* ssc = g_neginf_row + col;
+        if (q >= 0 && su == s && pu == q) {
+          const int64_t u = t - cr + 1 + r;
+          skv = a.kv + u * a.width + col;
+          ssc = a.score + u * a.width + col;
+        } else if (q >= 0) {
+          const float* st = a.states + (int64_t)s * 2 * cr * a.width;
+          skv = st + (int64_t)(q % cr) * a.width + col;
+          ssc = st + (int64_t)(cr + q % cr) * a.width + col;
+        }
+        const uint32_t apem = __ballot_sync(FULL, r < cr && q >= 0 && a.ape != nullptr);
+        __syncwarp();
+        if (lane == 0) {
+          d->kind = 1;
+          d->p = p;
+          d->slot = slot;
+          d->krow = (p + 1) / ratio - 1;
+          d->ape_mask = apem;
+          d->n_ring = nr;
+          st_arrive_tx(full, 2u * cr * kHalfBytes);
+        }
+        __syncwarp();
+        if (r < cr) {
+          st_bulk_load(st_u32(s_kv + (buf * kStageRows + r) * kRowF), skv, kHalfBytes, full);
+          st_bulk_load(st_u32(s_sc + (buf * kStageRows + r) * kRowF), ssc, kHalfBytes, full);
+        }
+        ++it;
+      }
+    }
+    if (ok) {  // the end marker
+      const uint32_t buf = it & 1;
+      bool got = true;
+      if (it >= 2 && lane == 0) got = st_mbar_wait(bar_empty + 8 * buf, ((it >> 1) - 1) & 1, abort_flag);
+      ok = __shfl_sync(FULL, (int)got, 0) != 0;
+      if (ok && lane == 0) {
+        s_desc[buf].kind = 0;
+        st_arrive(bar_full + 8 * buf);
+      }
+    }
+    if (!ok && lane == 0) {
+      *abort_flag = 1;
+      set_status(a.status, RKV_ERR_CUDA);
+      // copies this CTA issued may still be in flight: wait for them (bounded)
+      // before the CTA's shared memory goes away
+      for (uint32_t i = it >= 2 ? it - 2 : 0; i < it; ++i) {
+        const uint32_t bar = bar_full + 8 * (i & 1), par = (i >> 1) & 1;
+        const uint64_t t0 = st_now_ns();
+        while (!st_mbar_test(bar, par) && st_now_ns() - t0 < kStageTimeoutNs) {
+        }
+      }
+    }
     return;
   }
-  double* sq = s_sq[w];
-  float* row = reinterpret_cast<float*>(sq);  // reused for the finished row after the sum
-  const int64_t count = min((int64_t)*ws_count, ws_cap);
-  for (int64_t e = (int64_t)blockIdx.x * kFinWarps + w; e < count; e += (int64_t)fin_blocks * kFinWarps) {
-    const int2 meta = ws_meta[e];
-    float v[kRowF / 32];
-#pragma unroll
-    for (int i = 0; i < kRowF / 32; ++i) {
-      v[i] = ws_rows[e * kRowF + lane + 32 * i];
-      const double d = (double)v[i];
-      sq[lane + 32 * i] = __dmul_rn(d, d);
+
+  // ---- consumer warps: thread j owns output dimension j ----
+  const int j = tid;
+  const float wn = __ldg(a.norm + j);
+  for (uint32_t it = 0;; ++it) {
+    const uint32_t buf = it & 1;
+    bool got = true;
+    if (j == 0) got = st_mbar_wait(bar_full + 8 * buf, (it >> 1) & 1, abort_flag);
+    if (!st_bar_and(got)) {
+      if (j == 0) {
+        *abort_flag = 1;
+        set_status(a.status, RKV_ERR_CUDA);
+      }
+      break;
     }
-    __syncwarp();
-    float rms = 0.0f;
-    if (lane == 0) {
-      double ss = 0.0;
-#pragma unroll 16
-      for (int i = 0; i < kRowF; ++i) ss = __dadd_rn(ss, sq[i]);
-      const float mean = __double2float_rn(__ddiv_rn(ss, (double)kRowF));
-      rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
+    const StageDesc* d = s_desc + buf;
+    const int kind = d->kind, n_ring = d->n_ring;
+    if (kind == 0) break;
+    if (kind == 1) {
+      const int slot = d->slot;
+      const uint32_t ape_mask = d->ape_mask;
+      float c = 0.0f, sn = 0.0f;
+      if (j >= kLatent) {
+        const float* cs = a.rope + (int64_t)d->krow * 64 + ((j - kLatent) & ~1);
+        c = __ldg(cs);
+        sn = __ldg(cs + 1);
+      }
+      const float out = aggregate_staged(a, K, s_T, s_kv + buf * kStageRows * kRowF,
+                                         s_sc + buf * kStageRows * kRowF, ape_mask, j);
+      emit_finish<true>(a, tab, scr, out, wn, c, sn, slot);
     }
-    rms = __shfl_sync(FULL, rms, 0);
-    __syncwarp();  // the sum has read sq; row[] overwrites it
-#pragma unroll
-    for (int i = 0; i < kRowF / 32; ++i)
-      row[lane + 32 * i] = __fmul_rn(__fmul_rn(v[i], rms), __ldg(a.norm + lane + 32 * i));
-    __syncwarp();
-    {
-      const float c = __ldg(a.rope + (int64_t)meta.y * 64 + 2 * lane);
-      const float sn = __ldg(a.rope + (int64_t)meta.y * 64 + 2 * lane + 1);
-      const float x0 = row[kLatent + 2 * lane], x1 = row[kLatent + 2 * lane + 1];
-      row[kLatent + 2 * lane] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
-      row[kLatent + 2 * lane + 1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    if (n_ring) {
+      copy_ring_staged(a, d, n_ring, j);
+      st_bar();  // every thread has read the descriptor
     }
-    __syncwarp();
-    RowF32 x;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      x.a[i] = __float_as_uint(row[16 * lane + i]);
-      x.b[i] = __float_as_uint(row[16 * lane + 8 + i]);
-      x.rope[i] = 0u;
-    }
-    if (lane < 8) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) x.rope[i] = __float_as_uint(row[kLatent + 8 * lane + i]);
-    }
-    x.slot = meta.x;
-    append_row_f32(a.pool, a.layer, x, tab, a.status, lane);
-    __syncwarp();
+    // the stage (rows, descriptor) is free once every thread is past its
+    // reads: the emission's barriers, or the one above
+    if (j == 0) st_arrive(bar_empty + 8 * buf);
   }
 }
 
 static int coff_of(int ratio) { return ratio == 4 ? 2 : 1; }
+
+// The staged kernel's shared-memory opt-in, once per device.
+static std::atomic<bool> g_staged_smem[kMaxDevices];
+
+static rkv_status staged_smem_opt_in(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_compress_append: device %d", dev);
+  if (g_staged_smem[dev].load(std::memory_order_acquire)) return RKV_OK;
+  const cudaError_t e =
+      cudaFuncSetAttribute(compress_emit_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStagedSmem);
+  if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_compress_append: %s", cudaGetErrorString(e));
+  g_staged_smem[dev].store(true, std::memory_order_release);
+  return RKV_OK;
+}
 
 }  // namespace rkv
 
@@ -738,31 +1263,12 @@ extern "C" rkv_status rkv_compress_expf(const float* x, float* out, int64_t n, i
   return check_launch("rkv_compress_expf");
 }
 
-namespace rkv {
-
-// Workspace of one rkv_compress_append call: the emission count, then per
-// emission its (slot, compressed row) pair and its aggregate row.  A state's
-// run of L tokens emits at most L / ratio + 1 rows.
-static int64_t ws_cap_of(int32_t ratio, int64_t n_tok, int64_t n_states) {
-  return n_tok / ratio + (n_tok < n_states ? n_tok : n_states) + 1;
-}
-static int64_t ws_meta_off() { return 256; }
-static int64_t ws_rows_off(int64_t cap) { return (ws_meta_off() + cap * 8 + 255) / 256 * 256; }
-
-}  // namespace rkv
-
-extern "C" int64_t rkv_compress_workspace_bytes(int32_t ratio, int64_t n_tok, int64_t n_states) {
-  if (ratio <= 0 || n_tok < 0 || n_states < 0) return -1;
-  const int64_t cap = rkv::ws_cap_of(ratio, n_tok, n_states);
-  return rkv::ws_rows_off(cap) + cap * rkv::kRowF * 4;
-}
-
 extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t layer, int32_t ratio, float* states,
                                           int64_t n_states, const float* kv, const float* score, int64_t n_tok,
                                           const int32_t* pos, const int32_t* state_of_token,
                                           const int32_t* emit_slot, const float* ape, const float* norm,
-                                          const float* rope_table, int64_t rope_rows, void* workspace,
-                                          int64_t workspace_bytes, uint32_t* d_status, rkv_stream_t stream) {
+                                          const float* rope_table, int64_t rope_rows, uint32_t* d_status,
+                                          rkv_stream_t stream) {
   using namespace rkv;
   rkv_status st = check_pool(pool, "rkv_compress_append");
   if (st != RKV_OK) return st;
@@ -779,15 +1285,10 @@ extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t lay
     return RKV_OK;
   }
   if (!states || !aligned(states, 16) || !kv || !aligned(kv, 16) || !score || !aligned(score, 16) || !pos ||
-      !state_of_token || !emit_slot || !norm || !rope_table || (ape && !aligned(ape, 16)) || !d_status ||
-      !workspace || !aligned(workspace, 256))
+      !state_of_token || !emit_slot || !norm || !rope_table || (ape && !aligned(ape, 16)) || !d_status)
     return fail(RKV_ERR_INVALID_ARGUMENT,
                 "rkv_compress_append: states, kv, score, ape (16-byte aligned), pos, state_of_token, emit_slot, "
-                "norm, rope_table, workspace (256-byte aligned) and d_status are required");
-  const int64_t cap = ws_cap_of(ratio, n_tok, n_states);
-  if (workspace_bytes < rkv_compress_workspace_bytes(ratio, n_tok, n_states))
-    return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_compress_append: workspace of %lld bytes, %lld needed",
-                (long long)workspace_bytes, (long long)rkv_compress_workspace_bytes(ratio, n_tok, n_states));
+                "norm, rope_table and d_status are required");
   st = prepare_device("rkv_compress_append");
   if (st != RKV_OK) return st;
   CmpArgs a;
@@ -812,16 +1313,10 @@ extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t lay
   a.status = d_status;
   const ThresholdTable& tab = f32_threshold_table();
   const ExpConsts K = exp_host()->K;
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  int* ws_count = reinterpret_cast<int*>(ws);
-  int2* ws_meta = reinterpret_cast<int2*>(ws + ws_meta_off());
-  float* ws_rows = reinterpret_cast<float*>(ws + ws_rows_off(cap));
 
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  cudaError_t e = cudaMemsetAsync(ws_count, 0, 4, (cudaStream_t)stream);
-  if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_compress_append: %s", cudaGetErrorString(e));
   cudaLaunchConfig_t cfg = {};
   cfg.stream = (cudaStream_t)stream;
   cudaLaunchAttribute attr[1];
@@ -829,22 +1324,30 @@ extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t lay
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  // 1. aggregate: one CTA per token group, two resident per SM
+  // 1. emissions and the ring writes that may happen alongside them: one CTA
+  // per token group, two resident per SM; windows of up to 8 rows go through
+  // the staged kernel
   const int64_t groups = (n_tok + ratio - 1) / ratio;
-  const int64_t agg_cap = (int64_t)sms * 2;
-  cfg.gridDim = dim3((unsigned)(groups < agg_cap ? groups : agg_cap));
-  cfg.blockDim = dim3(kAggThreads);
-  e = cudaLaunchKernelEx(&cfg, compress_aggregate_kernel, a, K, ws_rows, ws_meta, ws_count, cap);
+  const int64_t emit_cap = (int64_t)sms * 2;
+  cfg.gridDim = dim3((unsigned)(groups < emit_cap ? groups : emit_cap));
+  cudaError_t e;
+  if (a.cr <= kStageRows) {
+    st = staged_smem_opt_in(dev);
+    if (st != RKV_OK) return st;
+    cfg.blockDim = dim3(kStagedThreads);
+    cfg.dynamicSmemBytes = kStagedSmem;
+    e = cudaLaunchKernelEx(&cfg, compress_emit_staged_kernel, a, K, tab);
+    cfg.dynamicSmemBytes = 0;
+  } else {
+    cfg.blockDim = dim3(kAggThreads);
+    e = cudaLaunchKernelEx(&cfg, compress_emit_kernel, a, K, tab);
+  }
   if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_compress_append: launch failed: %s", cudaGetErrorString(e));
-  // 2. finish (one warp per emitted row, at most cap of them) and, in the
-  // same grid, the rings for the next call (after the aggregate has read them)
-  const int64_t fin_need = (cap + kFinWarps - 1) / kFinWarps, fin_cap = (int64_t)sms * 6;
-  const int64_t fin_blocks = fin_need < fin_cap ? fin_need : fin_cap;
+  // 2. the remaining ring writes, after every emission has read the rings
   const int64_t ring_need = (n_tok + kFinWarps - 1) / kFinWarps, ring_cap = (int64_t)sms * 2;
-  cfg.gridDim = dim3((unsigned)(fin_blocks + (ring_need < ring_cap ? ring_need : ring_cap)));
+  cfg.gridDim = dim3((unsigned)(ring_need < ring_cap ? ring_need : ring_cap));
   cfg.blockDim = dim3(kFinWarps * 32);
-  e = cudaLaunchKernelEx(&cfg, compress_finish_kernel, a, tab, (const float*)ws_rows, (const int2*)ws_meta,
-                         (const int*)ws_count, cap, (int)fin_blocks);
+  e = cudaLaunchKernelEx(&cfg, compress_ring_kernel, a);
   if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_compress_append: launch failed: %s", cudaGetErrorString(e));
   return check_launch("rkv_compress_append");
 }
