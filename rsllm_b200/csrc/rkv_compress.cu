@@ -790,19 +790,29 @@ compress_emit_kernel(const CmpArgs a, const ExpConsts K, const ThresholdTable ta
   }
 }
 
-// The ring writes that compress_emit_kernel left (ring_write_now false): one
-// warp per token, after every emission of the call has read the rings.
+// The ring writes that the emission kernels left (ring_write_now false), after
+// every emission of the call has read the rings: each warp tests 32 tokens
+// (one per lane) and copies the deferred ones together.
 __global__ void __launch_bounds__(kFinWarps * 32)
 compress_ring_kernel(const CmpArgs a) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  const unsigned FULL = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   const int64_t n_warps = (int64_t)gridDim.x * kFinWarps;
-  for (int64_t t = (int64_t)blockIdx.x * kFinWarps + (threadIdx.x >> 5); t < a.n_tok; t += n_warps) {
-    const int p = __ldg(a.pos + t), s = __ldg(a.state_of + t);
-    if (p < 0 || s < 0 || (int64_t)s >= a.n_states) continue;
-    if (!ring_written(a, t, s) || ring_write_now(a, t, s)) continue;
-    copy_ring_rows(a, t, p, s, lane, 32);
+  for (int64_t t0 = ((int64_t)blockIdx.x * kFinWarps + (threadIdx.x >> 5)) * 32; t0 < a.n_tok; t0 += n_warps * 32) {
+    const int64_t t = t0 + lane;
+    int p = -1, s = -1;
+    bool deferred = false;
+    if (t < a.n_tok) {
+      p = __ldg(a.pos + t);
+      s = __ldg(a.state_of + t);
+      deferred = p >= 0 && s >= 0 && (int64_t)s < a.n_states && ring_written(a, t, s) && !ring_write_now(a, t, s);
+    }
+    for (uint32_t bits = __ballot_sync(FULL, deferred); bits; bits &= bits - 1) {
+      const int L = __ffs(bits) - 1;
+      copy_ring_rows(a, t0 + L, __shfl_sync(FULL, p, L), __shfl_sync(FULL, s, L), lane, 32);
+    }
   }
 }
 
@@ -997,7 +1007,11 @@ __device__ __forceinline__ void copy_ring_staged(const CmpArgs& a, const StageDe
   }
 }
 
-__global__ void __launch_bounds__(kStagedThreads, 2)
+// kMinBlocks 2: two CTAs per SM (48 registers, some spilled) for calls with
+// more token groups than SMs; 1: one CTA per SM with no spills, the shorter
+// latency for decode-sized calls.
+template <int kMinBlocks>
+__global__ void __launch_bounds__(kStagedThreads, kMinBlocks)
 compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdTable tab) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ __align__(16) uint8_t st_smem[];
@@ -1191,14 +1205,17 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
 
 static int coff_of(int ratio) { return ratio == 4 ? 2 : 1; }
 
-// The staged kernel's shared-memory opt-in, once per device.
+// The staged kernels' shared-memory opt-in, once per device.
 static std::atomic<bool> g_staged_smem[kMaxDevices];
 
 static rkv_status staged_smem_opt_in(int dev) {
   if (dev < 0 || dev >= kMaxDevices) return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_compress_append: device %d", dev);
   if (g_staged_smem[dev].load(std::memory_order_acquire)) return RKV_OK;
-  const cudaError_t e =
-      cudaFuncSetAttribute(compress_emit_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStagedSmem);
+  cudaError_t e = cudaFuncSetAttribute(compress_emit_staged_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kStagedSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(compress_emit_staged_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kStagedSmem);
   if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_compress_append: %s", cudaGetErrorString(e));
   g_staged_smem[dev].store(true, std::memory_order_release);
   return RKV_OK;
@@ -1336,7 +1353,10 @@ extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t lay
     if (st != RKV_OK) return st;
     cfg.blockDim = dim3(kStagedThreads);
     cfg.dynamicSmemBytes = kStagedSmem;
-    e = cudaLaunchKernelEx(&cfg, compress_emit_staged_kernel, a, K, tab);
+    if (groups <= sms)
+      e = cudaLaunchKernelEx(&cfg, compress_emit_staged_kernel<1>, a, K, tab);
+    else
+      e = cudaLaunchKernelEx(&cfg, compress_emit_staged_kernel<2>, a, K, tab);
     cfg.dynamicSmemBytes = 0;
   } else {
     cfg.blockDim = dim3(kAggThreads);
@@ -1344,7 +1364,7 @@ extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t lay
   }
   if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_compress_append: launch failed: %s", cudaGetErrorString(e));
   // 2. the remaining ring writes, after every emission has read the rings
-  const int64_t ring_need = (n_tok + kFinWarps - 1) / kFinWarps, ring_cap = (int64_t)sms * 2;
+  const int64_t ring_need = (n_tok + 32 * kFinWarps - 1) / (32 * kFinWarps), ring_cap = (int64_t)sms * 2;
   cfg.gridDim = dim3((unsigned)(ring_need < ring_cap ? ring_need : ring_cap));
   cfg.blockDim = dim3(kFinWarps * 32);
   e = cudaLaunchKernelEx(&cfg, compress_ring_kernel, a);
