@@ -326,6 +326,11 @@ __device__ __forceinline__ void collect_at_least(TopkSmem& sm, const float* __re
   for (int c0 = 0; c0 < n_chunks; c0 += kTopkWarps) {
     const int chunk = c0 + w;
     const float* base = row + (size_t)chunk * kWarpChunk;
+    // the warp's next 4 KB chunk into L2 (one 128-byte line per lane) while
+    // this one is loaded and tested, so that the next round's loads do not pay
+    // the full HBM latency
+    if (chunk + kTopkWarps < n_chunks)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (size_t)kTopkWarps * kWarpChunk + lane * 32));
     uint32_t m = 0;
     uint32_t u2[4][8], u1[8][4];
     if (chunk < n_chunks) {
