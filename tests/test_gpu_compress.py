@@ -8,6 +8,7 @@ import numpy as np
 import pytest
 import torch
 
+import compress_cases as cc
 import rsllm_b200 as rk
 
 pytestmark = pytest.mark.gpu
@@ -151,3 +152,35 @@ def test_device_expf_matches_libm(cuda, orc):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
     sp = np.array([0.0, -0.0, -np.inf, -151.0, -1e30], np.float32)
     assert np.array_equal(rk.compress_expf(torch.from_numpy(sp).to(cuda)).cpu().numpy(), orc.expf(sp))
+
+
+@pytest.mark.parametrize("ratio", [4, 2, 128])
+def test_rms_mean_at_an_f32_midpoint(cuda, orc, ratio):
+    """An emitted row whose RMSNorm mean the kernels' tree sum would round to
+    the other f32 (tests/compress_cases.py), with a lane whose FP8 code tells
+    the two means apart: the kernels must redo the sum in rsLLM's order.  One
+    finite score per dimension makes the aggregate the row itself.  Ratio 4
+    (two lanes) and 2 run the staged kernel, 128 the generic one."""
+    width = (2 if ratio == 4 else 1) * 576
+    row = cc.sensitive_row(orc.quantize_rows_f32)
+    kv = np.zeros((ratio, width), np.float32)
+    sc = np.full((ratio, width), -np.inf, np.float32)
+    kv[0, width - 576:] = row  # the current window's lanes (the c lanes for ratio 4)
+    sc[0, width - 576:] = 0.0
+    pos = np.arange(ratio, dtype=np.int32)
+    st = np.zeros(ratio, np.int32)
+    slot = np.where(pos == ratio - 1, 5, -1).astype(np.int32)
+    norm = np.ones(576, np.float32)
+    n_pages = 4
+    pool = rk.PagedKvPool(n_pages, 2, device=cuda)
+    pool.storage.zero_()
+    bank = rk.CompressorBank(ratio, 1, device=cuda, max_positions=4 * ratio)
+    ref = orc.new_pool(n_pages, 2)
+    T = lambda a: torch.from_numpy(a).to(cuda)
+    bank.append(pool, 1, T(kv), T(sc), T(pos), T(st), T(slot), T(norm))
+    assert pool.take_status() == 0
+    assert orc.compress_append(ref, n_pages, 2, 1, ratio, orc.compress_states(1, ratio), kv, sc, pos, st, slot,
+                               None, norm) == 0
+    got = pool.storage.cpu().numpy()
+    assert np.array_equal(got, ref)
+    assert got.any()  # the row was written

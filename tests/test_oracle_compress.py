@@ -11,6 +11,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
+import compress_cases as cc
 import oracle
 import rsllm_b200 as rk
 
@@ -175,3 +176,24 @@ def test_batch_driver_matches_primitives():
                 slots.append(slot[t])
         assert oracle.append_rows(want, n_pages, 1, 0, np.array(rows, np.float32)[None], np.array(slots)) == 0
         assert np.array_equal(pool, want), ratio
+
+
+def test_midpoint_row_needs_the_in_order_sum():
+    """The constructed row (tests/compress_cases.py): the in-order f64 sum of
+    squares and the emission kernels' tree sum give f32 means on either side
+    of a rounding midpoint, the tree's mean lies inside the kernels' 2^11-unit
+    band (so they redo the sum in order), and the oracle's RMSNorm uses the
+    in-order mean."""
+    for off in (20, 56, 120):
+        row = cc.midpoint_row(off)
+        qs, qt = cc.means(row)
+        assert np.float32(qs) != np.float32(qt)
+        assert cc.mid_distance(qt) <= 1 << 11
+        x = row.copy()
+        oracle.compressor_postprocess(x, np.ones(576, np.float32), 0)
+        rms = np.float32(1.0) / np.sqrt(np.float32(qs) + np.float32(1e-6), dtype=np.float32)
+        assert np.array_equal(x[:512], (row[:512] * rms).astype(np.float32))
+    # the GPU test's row: one lane's FP8 code tells the two means apart
+    row = cc.sensitive_row(oracle.quantize_rows_f32)
+    qs, qt = cc.means(row)
+    assert np.float32(qs) != np.float32(qt) and cc.mid_distance(qt) <= 1 << 11
