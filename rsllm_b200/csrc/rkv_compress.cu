@@ -390,7 +390,7 @@ static void rope_coeffs(uint32_t pos, float* out) {
 constexpr int kCmpMaxSources = 128;  // coff * ratio <= 128
 constexpr int kRowF = kRowDim;       // 576 lanes per compressed row
 constexpr int kAggThreads = kRowF;   // aggregate: one thread per output dimension
-constexpr int kFinWarps = 8;         // ring kernel: warps per CTA
+constexpr int kRingWarps = 8;        // ring kernel: warps per CTA
 
 struct CmpArgs {
   rkv_pool_view pool;
@@ -793,14 +793,14 @@ compress_emit_kernel(const CmpArgs a, const ExpConsts K, const ThresholdTable ta
 // The ring writes that the emission kernels left (ring_write_now false), after
 // every emission of the call has read the rings: each warp tests 32 tokens
 // (one per lane) and copies the deferred ones together.
-__global__ void __launch_bounds__(kFinWarps * 32)
+__global__ void __launch_bounds__(kRingWarps * 32)
 compress_ring_kernel(const CmpArgs a) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const unsigned FULL = 0xffffffffu;
   const int lane = threadIdx.x & 31;
-  const int64_t n_warps = (int64_t)gridDim.x * kFinWarps;
-  for (int64_t t0 = ((int64_t)blockIdx.x * kFinWarps + (threadIdx.x >> 5)) * 32; t0 < a.n_tok; t0 += n_warps * 32) {
+  const int64_t n_warps = (int64_t)gridDim.x * kRingWarps;
+  for (int64_t t0 = ((int64_t)blockIdx.x * kRingWarps + (threadIdx.x >> 5)) * 32; t0 < a.n_tok; t0 += n_warps * 32) {
     const int64_t t = t0 + lane;
     int p = -1, s = -1;
     bool deferred = false;
@@ -1364,9 +1364,9 @@ extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t lay
   }
   if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_compress_append: launch failed: %s", cudaGetErrorString(e));
   // 2. the remaining ring writes, after every emission has read the rings
-  const int64_t ring_need = (n_tok + 32 * kFinWarps - 1) / (32 * kFinWarps), ring_cap = (int64_t)sms * 2;
+  const int64_t ring_need = (n_tok + 32 * kRingWarps - 1) / (32 * kRingWarps), ring_cap = (int64_t)sms * 2;
   cfg.gridDim = dim3((unsigned)(ring_need < ring_cap ? ring_need : ring_cap));
-  cfg.blockDim = dim3(kFinWarps * 32);
+  cfg.blockDim = dim3(kRingWarps * 32);
   e = cudaLaunchKernelEx(&cfg, compress_ring_kernel, a);
   if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_compress_append: launch failed: %s", cudaGetErrorString(e));
   return check_launch("rkv_compress_append");
