@@ -43,6 +43,10 @@ constexpr int kSampleChunks = 32;
 constexpr int kSample = kSampleChunks * kSampleChunk;     // 4096
 constexpr int kSamplePerThread = kSample / kTopkThreads;  // 8, held in registers
 constexpr int kBinsPerThread = 2048 / kTopkThreads;       // 4
+#ifndef RKV_TOPK_PREFETCH_ROUNDS
+#define RKV_TOPK_PREFETCH_ROUNDS 2
+#endif
+constexpr int kPrefetchRounds = RKV_TOPK_PREFETCH_ROUNDS;  // collection rounds prefetched ahead
 
 struct TopkSmem {
   uint32_t hist[2048];
@@ -326,11 +330,12 @@ __device__ __forceinline__ void collect_at_least(TopkSmem& sm, const float* __re
   for (int c0 = 0; c0 < n_chunks; c0 += kTopkWarps) {
     const int chunk = c0 + w;
     const float* base = row + (size_t)chunk * kWarpChunk;
-    // the warp's next 4 KB chunk into L2 (one 128-byte line per lane) while
-    // this one is loaded and tested, so that the next round's loads do not pay
-    // the full HBM latency
-    if (chunk + kTopkWarps < n_chunks)
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (size_t)kTopkWarps * kWarpChunk + lane * 32));
+    // the warp's chunk kPrefetchRounds rounds ahead into L2 (one 128-byte
+    // line per lane; the first rounds were prefetched while the sample was
+    // selected), so that the rounds' loads hit L2 instead of paying HBM latency
+    if (chunk + kPrefetchRounds * kTopkWarps < n_chunks)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (size_t)kPrefetchRounds * kTopkWarps * kWarpChunk +
+                                                         lane * 32));
     uint32_t m = 0;
     uint32_t u2[4][8], u1[8][4];
     if (chunk < n_chunks) {
@@ -549,6 +554,16 @@ topk_select_kernel(const float* __restrict__ scores, int64_t ld, const int32_t* 
     const float q = (float)kk * (float)kSample / (float)n;
     uint32_t rank = (uint32_t)ceilf(q + 3.5f * sqrtf(q) + 2.0f);
     rank = max(1u, min(rank, (uint32_t)kSample));
+    // the collection's first kPrefetchRounds rounds (a 4 KB chunk per warp each)
+    // into L2 while the threshold is selected
+    if (vec) {
+      const int w_ = tid >> 5;
+      for (int rr = 0; rr < kPrefetchRounds; ++rr) {
+        const int64_t chunk = (int64_t)rr * kTopkWarps + w_;
+        if ((chunk + 1) * 1024 <= n)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(row + chunk * 1024 + (tid & 31) * 32));
+      }
+    }
     const uint32_t t = sample_select(sm, skeys, rank, rank);
     if (t != 0u) {
       if (tid == 0) sm.n_cand = 0u;
