@@ -2,7 +2,7 @@
 against the oracle's restatement of rsLLM's streaming state machine: the pool
 bytes of every emitted row (FP8 codes, scales, bf16 RoPE lanes) are identical
 after every call, across prefill chunks, decode steps, states in any order,
-ratios 4 (two lanes), 128, 2 and 1, with and without the APE bias, masked
+ratios 4 (two lanes), 128, 16, 8, 3, 2 and 1, with and without the APE bias, masked
 (-inf) and NaN score lanes; errors land in the status word as the oracle's."""
 import numpy as np
 import pytest
@@ -80,8 +80,10 @@ def test_ratio128_prefill_then_decode(cuda, orc):
     _run(cuda, orc, 128, calls, seed=2, order="reversed")
 
 
-@pytest.mark.parametrize("ratio", [1, 2])
+@pytest.mark.parametrize("ratio", [1, 2, 3, 8, 16])
 def test_other_ratios(cuda, orc, ratio):
+    """Staged windows with padding (1, 2, 3), a full eight-row staged window
+    (8) and the first window too long to stage (16: the generic kernel)."""
     _run(cuda, orc, ratio, [[9, 4, 1]] + [[1, 1, 1]] * 5 + [[6, 0, 3]], seed=3 + ratio)
 
 
