@@ -1027,7 +1027,8 @@ def main():
             g, m = bench_gather(args, dist, dev, peak)
             res = {"gather": g, "mla_decode_dense": m}
         elif args.only == "prefix":
-            res = bench_prefix(args, dist, dev, peak)
+            res = {"prefix_cow_evict_compact": bench_prefix(args, dist, dev, peak),
+                   "prefix_cow_evict_compact_aligned": bench_prefix(args, dist, dev, peak, tail=0)}
         elif args.only == "kvc":
             res = bench_kvc(args, dist, dev)
         elif args.only == "compress":
@@ -1051,6 +1052,8 @@ def main():
         phases.update(bench_sparse(args, dist, dev, peak))
     if "prefix" in wanted:
         phases["prefix_cow_evict_compact"] = bench_prefix(args, dist, dev, peak)
+        # the literal config: a page-aligned 8192-token prefix, so copy-on-write has nothing to copy
+        phases["prefix_cow_evict_compact_aligned"] = bench_prefix(args, dist, dev, peak, tail=0)
     if "kvc" in wanted:
         phases["kvc_save_load"] = bench_kvc(args, dist, dev)
     if "compress" in wanted:
