@@ -1066,6 +1066,8 @@ def main():
     line = None
     if dist.rank == 0:
         cpu = cpu_append_sample(app["wl"], W, args.cpu_budget, threads=__import__("oracle").threads())
+        # the reference calls its quantiser single-threaded: the same port on one core, a shorter sample
+        cpu1 = cpu_append_sample(app["wl"], W, min(args.cpu_budget, 5.0), threads=1)
         value = app["gbs_per_gpu"] * dist.world
         traffic = NCU_TRAFFIC_PER_ROW["append"]
         rows_per_launch = N_LAYERS * N_SEQ_APPEND
@@ -1089,6 +1091,7 @@ def main():
                          "kernel": "append_quant_kernel", "algorithmic_bytes_per_launch": app["step_bytes"],
                          "traffic": None if traffic is None else traffic * rows_per_launch},
             "cpu_baseline": cpu,
+            "cpu_baseline_single_thread": cpu1,
             "e2e": {k: v for k, v in app["e2e"].items() if k in ("value", "unit", "h2d_bytes_per_step",
                                                                    "d2h_bytes_per_step")},
             "e2e_detail": app["e2e"],
