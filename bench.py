@@ -322,6 +322,77 @@ def cpu_append_sample(wl: AppendWorkload, W: int, budget_s: float, threads: int)
             "tokens_per_s": steps * N_SEQ_APPEND / t_total}
 
 
+def cpu_phase_samples(threads: int, seed: int = 11) -> dict:
+    """The oracle (C restatement of rsLLM's paths) on bounded samples of the
+    config-3/4/5 work, on `threads` host threads: a rate per phase in the
+    phase's own unit, which extrapolates linearly to the full configuration
+    (every unit -- row, query, page -- costs the same).
+      gather: 4 sequences x 32,768 rows of one layer, pages in seeded random
+        order (the c3 shape per sequence);
+      topk: 32 queries over 131,072 N(0,1) scores, k = 2048, the reference's
+        repeated strict-`>` scan (indexer.rs:218-236);
+      sparse_gather: 16 queries x 2048 selected rows of the gather sample;
+      page moves: 4096 pages copied (compaction, 2 x 43,008 B per page)."""
+    import oracle
+
+    def timed(fn, min_s: float = 0.5, max_reps: int = 200):
+        """Seconds per call of fn, repeated until min_s have passed."""
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            fn()
+            reps += 1
+            dt = time.perf_counter() - t0
+            if dt >= min_s or reps >= max_reps:
+                return dt / reps, reps
+
+    rng = np.random.default_rng(seed)
+    out = {}
+    n_seq, ctx = 4, 32768
+    ppseq = ctx // 64
+    n_pages = n_seq * ppseq + 4096
+    pool = oracle.new_pool(n_pages, 1)
+    perm = rng.permutation(n_seq * ppseq).astype(np.int32)
+    pt = perm.reshape(n_seq, ppseq)
+    rows = rng.standard_normal((n_seq * ctx, 576)).astype(np.float32)
+    bf = (rows.view(np.uint32) >> 16).astype(np.uint16)
+    slots = (pt[:, :, None] * 64 + np.arange(64)[None, None, :]).reshape(-1).astype(np.int32)
+    assert oracle.append_rows(pool, n_pages, 1, 0, bf, slots, n_threads=threads) == 0
+    cu = (np.arange(n_seq + 1) * ctx).astype(np.int32)
+    assert oracle.gather_rows(pool, n_pages, 1, 0, pt, cu, n_threads=threads)[1] == 0
+    dt, reps = timed(lambda: oracle.gather_rows(pool, n_pages, 1, 0, pt, cu, n_threads=threads))
+    out["gather"] = {"value": n_seq * ctx * GATHER_ROW_BYTES / dt / GB, "unit": "GB/s", "cores": threads,
+                     "kind": "port",
+                     "sample": f"{n_seq} sequences x {ctx} rows of one layer, {reps} x {dt * 1e3:.1f} ms"}
+
+    n_q, n_keys, k = 32, 131072, 2048
+    scores = rng.standard_normal((n_q, n_keys)).astype(np.float32)
+    nv = np.full(n_q, n_keys, np.int32)
+    t0 = time.perf_counter()
+    oracle.topk_batch(scores, nv, k, scan=True, n_threads=threads)
+    dt = time.perf_counter() - t0
+    out["topk"] = {"value": n_q * n_keys * 4 / dt / GB, "unit": "GB/s", "queries_per_s": n_q / dt,
+                   "cores": threads, "kind": "port",
+                   "sample": f"{n_q} queries x {n_keys} scores, k = {k}, repeated best scan, {dt:.2f} s"}
+
+    n_sq = 16
+    idx = np.stack([rng.choice(ctx, k, replace=False) for _ in range(n_sq)]).astype(np.int32)
+    sq = (np.arange(n_sq) % n_seq).astype(np.int32)
+    sl = np.full(n_seq, ctx, np.int32)
+    assert oracle.sparse_gather_rows(pool, n_pages, 1, 0, pt, sq, sl, idx, n_threads=threads)[1] == 0
+    dt, reps = timed(lambda: oracle.sparse_gather_rows(pool, n_pages, 1, 0, pt, sq, sl, idx, n_threads=threads))
+    out["sparse_gather"] = {"value": n_sq * k * (GATHER_ROW_BYTES + 8) / dt / GB, "unit": "GB/s",
+                            "cores": threads, "kind": "port",
+                            "sample": f"{n_sq} queries x {k} selected rows, {reps} x {dt * 1e3:.1f} ms"}
+
+    n_move = 4096
+    src = rng.permutation(n_seq * ppseq)[:n_move].astype(np.int32)
+    dst = (n_seq * ppseq + np.arange(n_move)).astype(np.int32)
+    dt, reps = timed(lambda: oracle.copy_pages(pool, n_pages, 1, src, dst))
+    out["page_moves"] = {"value": 2 * n_move * 43008 / dt / GB, "unit": "GB/s", "cores": 1, "kind": "port",
+                         "sample": f"{n_move} page moves, {reps} x {dt * 1e3:.1f} ms"}
+    return out
+
+
 # ---------------------------------------------------------------------------
 # config 3: paged gather + dequant; config 4: top-k + sparse gather
 # ---------------------------------------------------------------------------
@@ -1068,6 +1139,13 @@ def main():
         cpu = cpu_append_sample(app["wl"], W, args.cpu_budget, threads=__import__("oracle").threads())
         # the reference calls its quantiser single-threaded: the same port on one core, a shorter sample
         cpu1 = cpu_append_sample(app["wl"], W, min(args.cpu_budget, 5.0), threads=1)
+        if any(k in phases for k in ("gather", "topk", "sparse_gather", "prefix_cow_evict_compact")):
+            cpu_ph = cpu_phase_samples(__import__("oracle").threads())
+            for name, key in (("gather", "gather"), ("topk", "topk"), ("sparse_gather", "sparse_gather"),
+                              ("prefix_cow_evict_compact", "page_moves"),
+                              ("prefix_cow_evict_compact_aligned", "page_moves")):
+                if name in phases and isinstance(phases[name], dict):
+                    phases[name]["cpu_baseline"] = cpu_ph[key]
         value = app["gbs_per_gpu"] * dist.world
         traffic = NCU_TRAFFIC_PER_ROW["append"]
         rows_per_launch = N_LAYERS * N_SEQ_APPEND
