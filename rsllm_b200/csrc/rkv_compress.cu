@@ -84,13 +84,6 @@ __host__ __device__ __forceinline__ double d_mul(double a, double b) {
   return a * b;
 #endif
 }
-__host__ __device__ __forceinline__ double d_add(double a, double b) {
-#ifdef __CUDA_ARCH__
-  return __dadd_rn(a, b);
-#else
-  return a + b;
-#endif
-}
 __host__ __device__ __forceinline__ double d_sub(double a, double b) {
 #ifdef __CUDA_ARCH__
   return __dsub_rn(a, b);
@@ -117,13 +110,6 @@ __host__ __device__ __forceinline__ double d_from_bits(uint64_t b) {
 #endif
 }
 
-__host__ __device__ __forceinline__ float f_mul(float a, float b) {
-#ifdef __CUDA_ARCH__
-  return __fmul_rn(a, b);
-#else
-  return a * b;
-#endif
-}
 
 // exp(x) in double for x in [-150, 0]; the same IEEE operations on both sides
 // (fused multiply-adds are single correctly rounded operations on both).
