@@ -65,19 +65,6 @@ __device__ __forceinline__ int scale_exponent_bf16bits(uint32_t amax_bits) {
   return E - 8 + ((amax_bits & 0x7fu) > 96u ? 1 : 0);
 }
 
-// One quantised lane pair: t = v * 2^-e (equal to v / 2^e, both correctly
-// rounded), clamp to +-448, fold -0.0 into +0.0 (the reference's sign is
-// `x < 0`), convert.
-__device__ __forceinline__ float quant_lane(float v, float inv_scale) {
-  float t = __fmul_rn(v, inv_scale);
-  t = fminf(fmaxf(t, -448.0f), 448.0f);
-  return __fadd_rn(t, 0.0f);
-}
-
-// bf16 pair (packed u32, lo lane in bits 0..15) -> f32 lanes.
-__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
-
 // Packed f32x2 arithmetic (sm_100): lo lane in bits 0..31.
 __device__ __forceinline__ unsigned long long mul_f32x2(unsigned long long a, unsigned long long b) {
   unsigned long long r;
@@ -109,23 +96,6 @@ __device__ __forceinline__ uint32_t quant_pair(uint32_t w, unsigned long long in
   const unsigned long long v = ((unsigned long long)(w & 0xffff0000u) << 32) | (unsigned long long)(w << 16);
   const unsigned long long t = clear_zero_sign2(mul_f32x2(v, inv2));
   return cvt_e4m3x2(__uint_as_float((uint32_t)t), __uint_as_float((uint32_t)(t >> 32)));
-}
-
-// 8 bf16 lanes (one uint4) -> 8 codes (uint2), with the block's inverse scale.
-__device__ __forceinline__ uint2 quant8(const uint4& v, float inv) {
-  uint32_t c0 = cvt_e4m3x2(quant_lane(bf16lo(v.x), inv), quant_lane(bf16hi(v.x), inv));
-  uint32_t c1 = cvt_e4m3x2(quant_lane(bf16lo(v.y), inv), quant_lane(bf16hi(v.y), inv));
-  uint32_t c2 = cvt_e4m3x2(quant_lane(bf16lo(v.z), inv), quant_lane(bf16hi(v.z), inv));
-  uint32_t c3 = cvt_e4m3x2(quant_lane(bf16lo(v.w), inv), quant_lane(bf16hi(v.w), inv));
-  return make_uint2(c0 | (c1 << 16), c2 | (c3 << 16));
-}
-
-// Largest |bf16| magnitude bits in a uint4 of 8 lanes (0x7f80 and above means
-// inf or NaN).
-__device__ __forceinline__ uint32_t absmax_bits8(const uint4& v) {
-  uint32_t m = __vmaxu2(__vmaxu2(v.x & 0x7fff7fffu, v.y & 0x7fff7fffu),
-                        __vmaxu2(v.z & 0x7fff7fffu, v.w & 0x7fff7fffu));
-  return max(m & 0xffffu, m >> 16);
 }
 
 // ---- decode ---------------------------------------------------------------
@@ -237,9 +207,6 @@ __device__ __forceinline__ uint4 ld_stream16(const void* p) {
 __device__ __forceinline__ void st_stream16(void* p, const uint4& v) {
   asm volatile("st.global.L1::no_allocate.v4.u32 [%0], {%1,%2,%3,%4};"
                :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
-}
-__device__ __forceinline__ void st_stream8(void* p, const uint2& v) {
-  asm volatile("st.global.L1::no_allocate.v2.u32 [%0], {%1,%2};" :: "l"(p), "r"(v.x), "r"(v.y) : "memory");
 }
 
 }  // namespace rkv
