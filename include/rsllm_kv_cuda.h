@@ -465,6 +465,11 @@ RKV_API rkv_status rkv_compress_rope_table(int32_t ratio, int64_t n_rows, float*
  * current device (done by the first rkv_compress_append otherwise; call it
  * before capturing a CUDA graph). */
 RKV_API rkv_status rkv_compress_prepare(void);
+/* Test hook, no rsLLM counterpart: one thread waits, with the compressor
+ * kernel's bounded wait, on a barrier nothing arrives on; after the limit
+ * (1 s) it sets RKV_ERR_CUDA in the device status word and the kernel
+ * returns.  Shows that a stalled wait ends in a status, not a hang. */
+RKV_API rkv_status rkv_compress_wait_probe(uint32_t* d_status, rkv_stream_t stream);
 RKV_API rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t layer, int32_t ratio, float* states,
                                        int64_t n_states, const float* kv, const float* score, int64_t n_tok,
                                        const int32_t* pos, const int32_t* state_of_token, const int32_t* emit_slot,

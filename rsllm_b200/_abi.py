@@ -93,6 +93,7 @@ SIGNATURES = {
     "rkv_compress_state_bytes": (c_int64, [c_int32]),
     "rkv_compress_rope_table": (c_int32, [c_int32, c_int64, _f32p]),
     "rkv_compress_prepare": (c_int32, []),
+    "rkv_compress_wait_probe": (c_int32, [_u32p, c_void_p]),
     "rkv_compress_append": (c_int32, [_P(PoolView), c_int32, c_int32, _f32p, c_int64, _f32p, _f32p, c_int64, _i32p,
                                       _i32p, _i32p, _f32p, _f32p, _f32p, c_int64, _u32p, c_void_p]),
     "rkv_compress_expf": (c_int32, [_f32p, _f32p, c_int64, c_int32, c_void_p]),

@@ -1189,6 +1189,23 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
   }
 }
 
+// Test hook for the bounded waits: thread 0 waits, with the staged kernel's
+// st_mbar_wait, for a phase of an mbarrier that nothing arrives on.  The wait
+// gives up after kStageTimeoutNs, the kernel records RKV_ERR_CUDA in the
+// status word and returns -- the path every staged-kernel wait takes when its
+// producer or consumers stop -- and the context stays usable.
+__global__ void wait_probe_kernel(uint32_t* status) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(st_u32(&bar)) : "memory");
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !st_mbar_wait(st_u32(&bar), 0, &abort_flag)) set_status(status, RKV_ERR_CUDA);
+}
+
 static int coff_of(int ratio) { return ratio == 4 ? 2 : 1; }
 
 // The staged kernels' shared-memory opt-in, once per device.
@@ -1223,6 +1240,13 @@ extern "C" rkv_status rkv_compress_rope_table(int32_t ratio, int64_t n_rows, flo
   for (int64_t k = 0; k < n_rows; ++k) rope_coeffs((uint32_t)(k * ratio), out + k * 64);
   clear_error();
   return RKV_OK;
+}
+
+extern "C" rkv_status rkv_compress_wait_probe(uint32_t* d_status, rkv_stream_t stream) {
+  using namespace rkv;
+  if (!d_status) return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_compress_wait_probe: d_status is required");
+  wait_probe_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(d_status);
+  return check_launch("rkv_compress_wait_probe");
 }
 
 extern "C" rkv_status rkv_compress_prepare(void) {

@@ -186,3 +186,25 @@ def test_rms_mean_at_an_f32_midpoint(cuda, orc, ratio):
     got = pool.storage.cpu().numpy()
     assert np.array_equal(got, ref)
     assert got.any()  # the row was written
+
+
+def test_stalled_wait_ends_in_a_status(cuda):
+    """The compressor kernels' bounded wait (rkv_compress_wait_probe): a wait on
+    a barrier that nothing arrives on gives up after about a second, leaves
+    RKV_ERR_CUDA in the status word instead of hanging, and the context keeps
+    working afterwards."""
+    import time
+
+    from rsllm_b200 import _abi
+
+    lib = _abi.load()
+    st = torch.zeros(1, dtype=torch.int32, device=cuda)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    assert lib.rkv_compress_wait_probe(st.data_ptr(), None) == 0
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    assert int(st.item()) == 1 << _abi.RKV_ERR_CUDA
+    assert 0.5 < dt < 30.0
+    x = torch.arange(1024, dtype=torch.float32, device=cuda)
+    assert float(x.sum().item()) == 1023 * 1024 / 2
