@@ -87,6 +87,15 @@ def test_other_ratios(cuda, orc, ratio):
     _run(cuda, orc, ratio, [[9, 4, 1]] + [[1, 1, 1]] * 5 + [[6, 0, 3]], seed=3 + ratio)
 
 
+@pytest.mark.parametrize("ratio", [4, 2])
+def test_decode_sized_calls_with_multi_token_runs(cuda, orc, ratio):
+    """Small calls (at most n_states tokens) in which some states get two or
+    three tokens, so part of their ring rows must wait for the call's
+    emissions."""
+    calls = [[5, 3, 1, 2]] + [[2, 2, 0, 1], [1, 3, 2, 1], [2, 1, 1, 2]] * 4
+    _run(cuda, orc, ratio, calls, n_states=8, seed=11 + ratio)
+
+
 def test_masked_nan_and_underflowing_scores(cuda, orc):
     _run(cuda, orc, 4, [[40, 17, 64]] + [[1, 1, 1]] * 6, seed=7, specials=True)
     _run(cuda, orc, 128, [[256, 130]] + [[1, 1]] * 2, seed=8, specials=True)
