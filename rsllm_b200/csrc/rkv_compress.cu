@@ -840,7 +840,14 @@ constexpr uint32_t kStAmax = kStPart + 160;                           // u32 [18
 constexpr uint32_t kStDesc = kStAmax + 80;                            // StageDesc [2]
 constexpr uint32_t kStBar = kStDesc + 2 * sizeof(StageDesc);          // full[2], empty[2]
 constexpr uint32_t kStMisc = kStBar + 32;                             // f64 sum, abort flag
-constexpr uint32_t kStagedSmem = kStMisc + 16;
+constexpr uint32_t kStRingBar = kStMisc + 16;                         // ring staging barrier
+constexpr uint32_t kStagedSmem = kStRingBar + 16;                     // two CTAs per SM
+// One CTA per SM also stages a group's ring rows (at most ratio tokens x
+// 2 x width f32 = 36,864 B for every ratio <= 8) so that the producer moves
+// them with bulk copies while the consumers compute.
+constexpr uint32_t kStRing = (kStagedSmem + 127) & ~127u;
+constexpr uint32_t kRingStageBytes = kStageRows * 2 * kHalfBytes;
+constexpr uint32_t kStagedSmem1 = kStRing + kRingStageBytes;
 
 __device__ __forceinline__ uint64_t st_now_ns() {
   uint64_t t;
@@ -890,6 +897,11 @@ __device__ __forceinline__ void st_bulk_load(uint32_t dst, const void* src, uint
                : "memory");
 }
 __device__ __forceinline__ uint32_t st_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+// Own shared memory -> global bulk copy, in this thread's bulk async-group.
+__device__ __forceinline__ void st_bulk_store(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+}
 
 // The aggregate of output dimension j from one stage: kvs / scs hold the
 // window's source half-rows [8][576] (for coff 2: sources 0..3 the previous
@@ -1015,6 +1027,7 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
   if (tid == 0) {
     for (int b = 0; b < 4; ++b)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_full + 8 * b) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(st_u32(st_smem + kStRingBar)) : "memory");
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -1025,7 +1038,7 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
     // ---- producer warp ----
     const int cr = a.cr, ratio = a.ratio, n_meta = 2 * cr + ratio;  // n_meta <= 24
     const int64_t n_groups = (a.n_tok + ratio - 1) / ratio;
-    uint32_t it = 0;
+    uint32_t it = 0, ring_phase = 0;
     bool ok = true;
     for (int64_t g = blockIdx.x; g < n_groups && ok; g += gridDim.x) {
       // tokens t0 - cr .. t0 + ratio + cr - 1 around the group, one per lane
@@ -1052,10 +1065,11 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
       // ring_written and ring_write_now from the neighbouring lanes
       const bool rg = in_group && valid && s_fwd != ms && (s_prev != ms || s_back == ms);
       const uint32_t emask = __ballot_sync(FULL, em), rmask = __ballot_sync(FULL, rg);
-      const int n_ring = __popc(rmask);
+      // one CTA per SM: the producer writes the ring rows itself (below)
+      const int n_ring = kMinBlocks == 1 ? 0 : __popc(rmask);
       // items: one per emission, the last one carrying the ring rows; or one
       // ring-only item
-      uint32_t items = emask ? emask : (rmask ? (rmask & (0u - rmask)) : 0u);
+      uint32_t items = emask ? emask : (n_ring ? (rmask & (0u - rmask)) : 0u);
       for (; items; items &= items - 1) {
         const int L = __ffs(items) - 1;
         const bool emission = emask != 0, last = (items & (items - 1)) == 0;
@@ -1070,7 +1084,7 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
         }
         StageDesc* d = s_desc + buf;
         const int nr = last ? n_ring : 0;
-        if (nr && rg) {
+        if (nr && rg) {  // nr == 0 when the producer writes the ring rows
           const int e = __popc(rmask & ((1u << lane) - 1));
           d->ring_t[e] = (int)(t0 - cr + lane);
           d->ring_p[e] = mp;
@@ -1123,6 +1137,35 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
         }
         ++it;
       }
+      if (kMinBlocks == 1 && ok && rmask) {
+        // this group's ring rows (all safe to write now): bulk loads into the
+        // staging buffer, then bulk stores into the ring slots, while the
+        // consumers compute the group's emissions
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // earlier stores have read the buffer
+        __syncwarp();
+        const uint32_t rbar = st_u32(st_smem + kStRingBar), row_bytes = (uint32_t)a.width * 4u;
+        if (lane == 0) st_arrive_tx(rbar, (uint32_t)__popc(rmask) * 2u * row_bytes);
+        __syncwarp();
+        const uint32_t sbuf = st_u32(st_smem + kStRing) + (uint32_t)__popc(rmask & ((1u << lane) - 1u)) * 2u * row_bytes;
+        const int64_t t = t0 - cr + lane;
+        if (rg) {
+          st_bulk_load(sbuf, a.kv + t * a.width, row_bytes, rbar);
+          st_bulk_load(sbuf + row_bytes, a.score + t * a.width, row_bytes, rbar);
+        }
+        bool got = true;
+        if (lane == 0) got = st_mbar_wait(rbar, ring_phase & 1u, abort_flag);
+        if (!__shfl_sync(FULL, (int)got, 0)) {
+          ok = false;
+          break;
+        }
+        ++ring_phase;
+        if (rg) {
+          float* st = a.states + (int64_t)ms * 2 * cr * a.width;
+          st_bulk_store(st + (int64_t)(mp % cr) * a.width, sbuf, row_bytes);
+          st_bulk_store(st + (int64_t)(cr + mp % cr) * a.width, sbuf + row_bytes, row_bytes);
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+      }
     }
     if (ok) {  // the end marker
       const uint32_t buf = it & 1;
@@ -1145,7 +1188,13 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
         while (!st_mbar_test(bar, par) && st_now_ns() - t0 < kStageTimeoutNs) {
         }
       }
+      if (kMinBlocks == 1) {  // and the ring rows of an unfinished group
+        const uint64_t t0 = st_now_ns();
+        while (!st_mbar_test(st_u32(st_smem + kStRingBar), ring_phase & 1u) && st_now_ns() - t0 < kStageTimeoutNs) {
+        }
+      }
     }
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // this lane's ring stores are done
     return;
   }
 
@@ -1215,7 +1264,7 @@ static rkv_status staged_smem_opt_in(int dev) {
   if (dev < 0 || dev >= kMaxDevices) return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_compress_append: device %d", dev);
   if (g_staged_smem[dev].load(std::memory_order_acquire)) return RKV_OK;
   cudaError_t e = cudaFuncSetAttribute(compress_emit_staged_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kStagedSmem);
+                                       (int)kStagedSmem1);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(compress_emit_staged_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)kStagedSmem);
@@ -1362,11 +1411,13 @@ extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t lay
     st = staged_smem_opt_in(dev);
     if (st != RKV_OK) return st;
     cfg.blockDim = dim3(kStagedThreads);
-    cfg.dynamicSmemBytes = kStagedSmem;
-    if (groups <= sms)
+    if (groups <= sms) {
+      cfg.dynamicSmemBytes = kStagedSmem1;
       e = cudaLaunchKernelEx(&cfg, compress_emit_staged_kernel<1>, a, K, tab);
-    else
+    } else {
+      cfg.dynamicSmemBytes = kStagedSmem;
       e = cudaLaunchKernelEx(&cfg, compress_emit_staged_kernel<2>, a, K, tab);
+    }
     cfg.dynamicSmemBytes = 0;
   } else {
     cfg.blockDim = dim3(kAggThreads);
