@@ -842,10 +842,12 @@ constexpr uint32_t kStBar = kStDesc + 2 * sizeof(StageDesc);          // full[2]
 constexpr uint32_t kStMisc = kStBar + 32;                             // f64 sum, abort flag
 constexpr uint32_t kStRingBar = kStMisc + 16;                         // ring staging barrier
 constexpr uint32_t kStagedSmem = kStRingBar + 16;                     // two CTAs per SM
-// One CTA per SM also stages a group's ring rows (at most ratio tokens x
-// 2 x width f32 = 36,864 B for every ratio <= 8) so that the producer moves
-// them with bulk copies while the consumers compute.
-constexpr uint32_t kStRing = (kStagedSmem + 127) & ~127u;
+// One CTA per SM also keeps the APE table (f32 [ratio][width], at most 4608)
+// and stages a group's ring rows (at most ratio tokens x 2 x width f32 =
+// 36,864 B for every ratio <= 8) so that the producer moves them with bulk
+// copies while the consumers compute.
+constexpr uint32_t kStApe = kStagedSmem;
+constexpr uint32_t kStRing = (kStApe + kStageRows * kHalfBytes + 127) & ~127u;
 constexpr uint32_t kRingStageBytes = kStageRows * 2 * kHalfBytes;
 constexpr uint32_t kStagedSmem1 = kStRing + kRingStageBytes;
 
@@ -907,8 +909,13 @@ __device__ __forceinline__ void st_bulk_store(void* dst, uint32_t src, uint32_t 
 // window's source half-rows [8][576] (for coff 2: sources 0..3 the previous
 // window's p lanes, 4..7 the current window's c lanes).  Source r reads APE
 // row r % ratio (q0 = pos + 1 - coff*ratio is a multiple of ratio).
+// kApeShared: the APE table was staged in shared memory (s_ape); otherwise
+// it is read from global memory.
+template <bool kApeShared>
 __device__ __forceinline__ float aggregate_staged(const CmpArgs& a, const ExpConsts& K, const double* s_T,
-                                                  const float* kvs, const float* scs, uint32_t ape_mask, int j) {
+                                                  const float* kvs, const float* scs, const float* s_ape,
+                                                  uint32_t ape_mask, int j) {
+  auto ape_at = [&](int i) { return kApeShared ? s_ape[i] : __ldg(a.ape + i); };
   // The kv values stay in shared memory until the sums: fewer live registers.
   float out = 0.0f;
   if (a.coff == 2) {
@@ -921,8 +928,8 @@ __device__ __forceinline__ float aggregate_staged(const CmpArgs& a, const ExpCon
     if (ape_mask) {
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        if ((ape_mask >> r) & 1u) x[2 * r] = __fadd_rn(x[2 * r], __ldg(a.ape + r * a.width + j));
-        if ((ape_mask >> (4 + r)) & 1u) x[2 * r + 1] = __fadd_rn(x[2 * r + 1], __ldg(a.ape + r * a.width + kRowF + j));
+        if ((ape_mask >> r) & 1u) x[2 * r] = __fadd_rn(x[2 * r], ape_at(r * a.width + j));
+        if ((ape_mask >> (4 + r)) & 1u) x[2 * r + 1] = __fadd_rn(x[2 * r + 1], ape_at(r * a.width + kRowF + j));
       }
     }
     float m = -INFINITY;
@@ -949,7 +956,7 @@ __device__ __forceinline__ float aggregate_staged(const CmpArgs& a, const ExpCon
       x[r] = -INFINITY;
       if (r < a.cr) {
         x[r] = scs[r * kRowF + j];
-        if ((ape_mask >> r) & 1u) x[r] = __fadd_rn(x[r], __ldg(a.ape + r * a.width + j));
+        if ((ape_mask >> r) & 1u) x[r] = __fadd_rn(x[r], ape_at(r * a.width + j));
       }
     }
     float m = -INFINITY;
@@ -1201,6 +1208,12 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
   // ---- consumer warps: thread j owns output dimension j ----
   const int j = tid;
   const float wn = __ldg(a.norm + j);
+  // one CTA per SM (decode): the APE table into shared memory while the
+  // first stage is on its way (the stage-ready barrier below orders these
+  // writes before the reads)
+  float* s_ape = reinterpret_cast<float*>(st_smem + kStApe);
+  if (kMinBlocks == 1 && a.ape)
+    for (int i = j; i < a.ratio * a.width; i += kConsumers) s_ape[i] = __ldg(a.ape + i);
   for (uint32_t it = 0;; ++it) {
     const uint32_t buf = it & 1;
     bool got = true;
@@ -1224,8 +1237,8 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
         c = __ldg(cs);
         sn = __ldg(cs + 1);
       }
-      const float out = aggregate_staged(a, K, s_T, s_kv + buf * kStageRows * kRowF,
-                                         s_sc + buf * kStageRows * kRowF, ape_mask, j);
+      const float out = aggregate_staged<kMinBlocks == 1>(a, K, s_T, s_kv + buf * kStageRows * kRowF,
+                                         s_sc + buf * kStageRows * kRowF, s_ape, ape_mask, j);
       emit_finish<true>(a, tab, scr, out, wn, c, sn, slot);
     }
     if (n_ring) {
