@@ -1137,9 +1137,11 @@ def main():
     line = None
     if dist.rank == 0:
         cpu = cpu_append_sample(app["wl"], W, args.cpu_budget, threads=__import__("oracle").threads())
-        # the reference calls its quantiser single-threaded: the same port on one core, a shorter sample
-        cpu1 = cpu_append_sample(app["wl"], W, min(args.cpu_budget, 5.0), threads=1)
-        if any(k in phases for k in ("gather", "topk", "sparse_gather", "prefix_cow_evict_compact")):
+        # the reference calls its quantiser single-threaded: the same port on one core, a shorter
+        # sample; it and the per-phase samples are taken at N = 1 only
+        cpu1 = cpu_append_sample(app["wl"], W, min(args.cpu_budget, 5.0), threads=1) if dist.world == 1 else None
+        if dist.world == 1 and any(k in phases for k in ("gather", "topk", "sparse_gather",
+                                                         "prefix_cow_evict_compact")):
             cpu_ph = cpu_phase_samples(__import__("oracle").threads())
             for name, key in (("gather", "gather"), ("topk", "topk"), ("sparse_gather", "sparse_gather"),
                               ("prefix_cow_evict_compact", "page_moves"),
