@@ -73,7 +73,8 @@ def peaks() -> tuple[float, str]:
 class Dist:
     """One process per GPU (torchrun env vars); NCCL between GPUs, gloo when
     no GPU is present (the CPU tests of the multi-rank path).  Only used
-    outside timed regions: barriers and the max over ranks of a time."""
+    outside timed regions: barriers, the max over ranks of a time, every
+    rank's time, and the AND over ranks of a parity check."""
 
     def __init__(self, backend: str | None = None):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -108,6 +109,21 @@ class Dist:
         t = torch.tensor([x], dtype=torch.float64, device=self.dev)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
+
+    def all(self, x: float) -> list[float]:
+        """x of every rank, in rank order."""
+        if not self.pg:
+            return [x]
+        t = torch.tensor([x], dtype=torch.float64, device=self.dev)
+        out = [torch.zeros_like(t) for _ in range(self.world)]
+        self.pg.all_gather(out, t)
+        return [float(o.item()) for o in out]
+
+    def all_true(self, ok: bool | None) -> bool | None:
+        """AND over ranks (None -- not checked -- on any rank gives None)."""
+        v = -1.0 if ok is None else float(bool(ok))
+        vals = self.all(v)
+        return None if min(vals) < 0 else all(v > 0 for v in vals)
 
     def close(self):
         if self.pg:
@@ -167,11 +183,20 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.rows), "samples_under_load": loaded}
 
 
+# cycles of torch's sleep kernel queued ahead of a timed region (about 1 ms at
+# 1.9 GHz): the host enqueues the timed work while the GPU still sleeps, so the
+# start event is followed at once by the first timed kernel and the host's
+# launch latency (a graph launch, the first eager launches) stays outside
+LAUNCH_COVER_CYCLES = 2_000_000
+
+
 def events_time(fn, stream: torch.cuda.Stream) -> float:
     """Milliseconds of fn() on `stream`, by CUDA events recorded on it."""
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(LAUNCH_COVER_CYCLES)
     a.record(stream)
     fn()
     b.record(stream)
@@ -185,6 +210,20 @@ def flush_l2(dev):
     del buf
 
 
+def same_bytes(storage: torch.Tensor, ref: np.ndarray, chunk: int = 1 << 28) -> bool:
+    """Device bytes == host bytes, compared in chunks (no second host copy)."""
+    if storage.numel() != ref.size:
+        return False
+    for c0 in range(0, ref.size, chunk):
+        if not np.array_equal(storage[c0:c0 + chunk].cpu().numpy(), ref[c0:c0 + chunk]):
+            return False
+    return True
+
+
+def u16(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
 # ---------------------------------------------------------------------------
 # config 2: decode-step batched append
 # ---------------------------------------------------------------------------
@@ -193,43 +232,32 @@ class AppendWorkload:
     """Per-rank state of config 2: lengths, page table of the pages the run
     touches, per-step slot mappings, per-step input rows."""
 
-    def __init__(self, n_steps: int, seed: int, dev: torch.device | None, make_rows: bool = True):
+    def __init__(self, n_steps: int, seed: int, dev: torch.device | None, make_rows: bool = True,
+                 n_seq: int = N_SEQ_APPEND):
         from rsllm_b200 import synth
 
-        self.n_steps = n_steps
-        lens = synth.uniform_ints(N_SEQ_APPEND, *LEN_RANGE, seed=seed).numpy().astype(np.int64)
-        first = lens // 64
-        last = (lens + n_steps - 1) // 64
-        need = last - first + 1
-        off = np.concatenate([[0], np.cumsum(need)])
-        self.n_pages = int(off[-1])
-        phys = synth.permutation(self.n_pages, seed=seed + 1).numpy().astype(np.int64)
-        steps = np.arange(n_steps)[:, None]
-        pos = lens[None, :] + steps                          # [steps, seq]
-        local = pos // 64 - first[None, :]
-        page = phys[off[:-1][None, :] + local]
-        self.slots_np = (page * 64 + pos % 64).astype(np.int32)  # [steps, seq]
+        self.n_steps, self.n_seq, self.seed = n_steps, n_seq, seed
+        self.slots_np, self.n_pages, self.lens = synth.decode_slots(n_seq, n_steps, seed, LEN_RANGE)
+        pos = self.lens[None, :] + np.arange(n_steps)[:, None]
         self.new_pages_per_step = (pos % 64 == 0).sum(axis=1)
         self.rows = None
         if dev is not None:
             self.slots = torch.from_numpy(self.slots_np).to(dev)
             if make_rows:
-                n = N_LAYERS * N_SEQ_APPEND
-                self.rows = torch.empty((n_steps, N_LAYERS, N_SEQ_APPEND, 576), dtype=torch.bfloat16, device=dev)
+                n = N_LAYERS * n_seq
+                self.rows = torch.empty((n_steps, N_LAYERS, n_seq, 576), dtype=torch.bfloat16, device=dev)
                 for j in range(n_steps):
-                    self.rows[j].copy_(synth.kv_rows(n, seed=seed * 1000 + j, device=dev).view(N_LAYERS,
-                                                                                                N_SEQ_APPEND, 576))
+                    self.rows[j].copy_(synth.kv_rows(n, seed=seed * 1000 + j, device=dev).view(N_LAYERS, n_seq, 576))
 
-    @staticmethod
-    def bytes_per_step() -> int:
-        return N_LAYERS * N_SEQ_APPEND * APPEND_ROW_BYTES + N_SEQ_APPEND * 4
+    def bytes_per_step(self) -> int:
+        return N_LAYERS * self.n_seq * APPEND_ROW_BYTES + self.n_seq * 4
 
 
-def bench_append(args, dist: Dist, dev, peak) -> dict:
+def bench_append(args, dist: Dist, dev, peak, n_seq: int = N_SEQ_APPEND, e2e: bool = True) -> dict:
     import rsllm_b200 as rk
 
     W, K = args.warmup, args.steps
-    wl = AppendWorkload(W + K, seed=3 + 7919 * dist.rank, dev=dev)
+    wl = AppendWorkload(W + K, seed=3 + 7919 * dist.rank, dev=dev, n_seq=n_seq)
     pool = rk.PagedKvPool(wl.n_pages, N_LAYERS, device=dev)
     pool.storage.zero_()
     stream = torch.cuda.Stream(device=dev)
@@ -251,54 +279,115 @@ def bench_append(args, dist: Dist, dev, peak) -> dict:
     stream.synchronize()
     flush_l2(dev)
     dist.barrier()
-    ms = events_time(replay, stream)
+    ms_rank = events_time(replay, stream)
     dist.barrier()
     pool.check("append", stream)
-    ms = dist.max(ms)
+    per_rank = dist.all(ms_rank)
+    ms = max(per_rank)
+    # five more K-step replays (L2 flushed before each), every rank's time
+    # kept: the spread a single short window hides
+    reps = []
+    for _ in range(5):
+        flush_l2(dev)
+        dist.barrier()
+        reps.append(dist.all(events_time(replay, stream)))
     del graph
     step_bytes = wl.bytes_per_step()
     res = {
         "ms_per_step": ms / K,
         "gbs_per_gpu": step_bytes * K / (ms * 1e-3) / GB,
-        "tokens_per_s_per_gpu": N_SEQ_APPEND * K / (ms * 1e-3),
+        "tokens_per_s_per_gpu": n_seq * K / (ms * 1e-3),
         "step_bytes": step_bytes,
+        "per_rank_ms_per_step": [t / K for t in per_rank],
+        "repeats_max_over_ranks_ms_per_step": [max(r) / K for r in reps],
+        "repeats_median_rank_ms_per_step": [float(np.median(r)) / K for r in reps],
         "pool": pool,
         "wl": wl,
     }
-    # end to end through the public API: pinned host rows -> device, append,
-    # status word back, every step
-    res["e2e"] = bench_append_e2e(pool, wl, W, K, dist, dev)
+    # bit-exact check of the whole pool (W + K steps) against the oracle
+    res["parity"] = dist.all_true(append_parity(pool, wl))
+    if e2e:
+        # end to end through the public API: the host allocator reserves each
+        # step's slots, pinned host rows and slots go to the device, append,
+        # status word back, every step
+        res["e2e"] = bench_append_e2e(wl, W, K, dist, dev)
     return res
 
 
-def bench_append_e2e(pool, wl: AppendWorkload, W: int, K: int, dist: Dist, dev) -> dict:
+def append_parity(pool, wl: AppendWorkload) -> bool:
+    """The pool after every step of the run equals the oracle's pool after
+    the same appends (fp8_kv_quantize_row_inplace + slot-mapped append)."""
+    import oracle
+
+    ref = oracle.new_pool(wl.n_pages, N_LAYERS)
+    for j in range(wl.n_steps):
+        st = oracle.append_rows(ref, wl.n_pages, N_LAYERS, 0, u16(wl.rows[j]), wl.slots_np[j],
+                                n_threads=oracle.threads())
+        if st != 0:
+            return False
+    return same_bytes(pool.storage, ref)
+
+
+def bench_append_e2e(wl: AppendWorkload, W: int, K: int, dist: Dist, dev) -> dict:
+    """Config 2 through the public API, as an engine's decode step runs it:
+    ``rkv_seq_reserve`` (the host allocator: a slot per sequence, a new page
+    from the free list when a sequence crosses a page boundary) writes the
+    step's slots into a pinned buffer, the rows (pinned) and the slots go to
+    the device, ``rkv_append_quant_bf16`` quantises them into the pool, the
+    status word comes back.  The allocator's pool holds each sequence's
+    current page (filled to its length mod 64, the sequences created in a
+    seeded random order, so page ids are scattered) and the pages it grows
+    into; the earlier full pages of a context play no part in a decode step."""
+    from rsllm_b200.prefix_pool import PrefixKvPool
+
+    n_seq = wl.n_seq
+    steps = W + K
+    n_pages = n_seq * (2 + (64 + steps) // 64)
+    pool = PrefixKvPool(n_pages, N_LAYERS, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    order = np.random.default_rng(wl.seed).permutation(n_seq)
+    seqs = np.empty(n_seq, np.int64)
+    for i in order:
+        seqs[i] = pool.create_sequence()
+        r = int(wl.lens[i] % 64) or 64
+        pool.reserve([int(seqs[i])], [r], stream=stream)
+    ones = np.ones(n_seq, np.int64)
     n_host = min(K, 8)
     host_rows = [wl.rows[W + j].cpu().pin_memory() for j in range(n_host)]
-    host_slots = [torch.from_numpy(wl.slots_np[W + j].copy()).pin_memory() for j in range(K)]
+    host_slots = torch.empty((steps, n_seq), dtype=torch.int32).pin_memory()
+    host_slots_np = host_slots.numpy()
     dev_rows = [torch.empty_like(wl.rows[0]) for _ in range(2)]
-    dev_slots = [torch.empty(N_SEQ_APPEND, dtype=torch.int32, device=dev) for _ in range(2)]
-    status_host = torch.empty(K, dtype=torch.int32).pin_memory()
-    stream = torch.cuda.Stream(device=dev)
+    dev_slots = [torch.empty(n_seq, dtype=torch.int32, device=dev) for _ in range(2)]
+    status_host = torch.empty(steps, dtype=torch.int32).pin_memory()
+    kv = pool.kv
 
-    def run():
+    def run(j0, j1):
         with torch.cuda.stream(stream):
-            for j in range(K):
+            for j in range(j0, j1):
                 b = j & 1
+                pool.reserve(seqs, ones, stream=stream, out=host_slots_np[j])
                 dev_rows[b].copy_(host_rows[j % n_host], non_blocking=True)
                 dev_slots[b].copy_(host_slots[j], non_blocking=True)
-                pool.append_layer(0, dev_rows[b], dev_slots[b])
-                status_host[j:j + 1].copy_(pool.status, non_blocking=True)
+                kv.append_layer(0, dev_rows[b], dev_slots[b])
+                status_host[j:j + 1].copy_(kv.status, non_blocking=True)
 
-    run()  # warm
+    run(0, W)  # warm-up steps
     torch.cuda.synchronize()
-    pool.status.zero_()
+    kv.status.zero_()
     dist.barrier()
-    ms = dist.max(events_time(run, stream))
-    assert int(status_host.abs().sum()) == 0, "append reported device errors"
-    h2d = wl.rows[0].numel() * 2 + N_SEQ_APPEND * 4
-    return {"value": wl.bytes_per_step() * K / (ms * 1e-3) / GB, "unit": "GB/s",
-            "tokens_per_s_per_gpu": N_SEQ_APPEND * K / (ms * 1e-3),
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "ms_per_step": ms / K}
+    ms_rank = events_time(lambda: run(W, steps), stream)
+    per_rank = dist.all(ms_rank)
+    ms = max(per_rank)
+    assert int(status_host[W:].abs().sum()) == 0, "append reported device errors"
+    new_pages = int(sum(int(np.count_nonzero(host_slots_np[j] % 64 == 0)) for j in range(W, steps)))
+    pool.close()
+    h2d = wl.rows[0].numel() * 2 + n_seq * 4
+    return {"value": dist.world * wl.bytes_per_step() * K / (ms * 1e-3) / GB, "unit": "GB/s",
+            "tokens_per_s": dist.world * n_seq * K / (ms * 1e-3),
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "ms_per_step": ms / K,
+            "per_rank_ms_per_step": [t / K for t in per_rank],
+            "pages_allocated_in_timed_steps": new_pages,
+            "path": "rkv_seq_reserve -> pinned slots + rows H2D -> rkv_append_quant_bf16 -> status D2H, per step"}
 
 
 def cpu_append_sample(wl: AppendWorkload, W: int, budget_s: float, threads: int) -> dict:
@@ -308,18 +397,18 @@ def cpu_append_sample(wl: AppendWorkload, W: int, budget_s: float, threads: int)
     pool = oracle.new_pool(wl.n_pages, N_LAYERS)
     steps, t_total, done_bytes = 0, 0.0, 0
     while steps < wl.n_steps - W and (t_total < budget_s or steps == 0):
-        rows = wl.rows[W + steps].view(torch.int16).cpu().numpy().view(np.uint16)
+        rows = u16(wl.rows[W + steps])
         slots = wl.slots_np[W + steps]
         t0 = time.perf_counter()
         st = oracle.append_rows(pool, wl.n_pages, N_LAYERS, 0, rows, slots, n_threads=threads)
         t_total += time.perf_counter() - t0
         assert st == 0
         steps += 1
-        done_bytes += AppendWorkload.bytes_per_step()
+        done_bytes += wl.bytes_per_step()
     return {"value": done_bytes / t_total / GB, "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{steps} decode steps of config 2 ({steps * N_LAYERS * N_SEQ_APPEND} rows), "
+            "sample": f"{steps} decode steps of config 2 ({steps * N_LAYERS * wl.n_seq} rows), "
                       f"{t_total:.1f} s on {threads} threads",
-            "tokens_per_s": steps * N_SEQ_APPEND / t_total}
+            "tokens_per_s": steps * wl.n_seq / t_total}
 
 
 def cpu_phase_samples(threads: int, seed: int = 11) -> dict:
@@ -397,29 +486,60 @@ def cpu_phase_samples(threads: int, seed: int = 11) -> dict:
 # config 3: paged gather + dequant; config 4: top-k + sparse gather
 # ---------------------------------------------------------------------------
 
+FILL_CHUNK = 1 << 20
+
+
 def fill_pool(pool, n_layers_phys: int, slots_all: torch.Tensor, seed: int, dev):
     """Fills every slot of every backed layer through the append kernel, from
-    a seeded block of rows reused across chunks."""
+    a seeded block of rows reused across chunks (``fill_rows_of`` gives the
+    rows any position received)."""
     from rsllm_b200 import synth
 
-    chunk = 1 << 20
-    src = synth.kv_rows(chunk, seed=seed, device=dev)
+    src = synth.kv_rows(FILL_CHUNK, seed=seed, device=dev)
     n = slots_all.numel()
     for layer in range(n_layers_phys):
-        for c0 in range(0, n, chunk):
-            c1 = min(n, c0 + chunk)
-            rot = (layer * 7919 + c0) % chunk
+        for c0 in range(0, n, FILL_CHUNK):
+            c1 = min(n, c0 + FILL_CHUNK)
+            rot = (layer * 7919 + c0) % FILL_CHUNK
             rows = src[: c1 - c0] if rot == 0 else torch.roll(src, rot, 0)[: c1 - c0]
             pool.append_layer(layer, rows.contiguous(), slots_all[c0:c1])
     pool.check("fill")
     del src
 
 
-def bench_gather(args, dist: Dist, dev, peak) -> dict:
+def fill_rows_of(seed: int, dev, layer: int, start: int, count: int) -> np.ndarray:
+    """bf16 bits of the rows ``fill_pool`` appended at positions
+    [start, start + count) of ``slots_all`` for ``layer`` (one chunk)."""
+    from rsllm_b200 import synth
+
+    c0 = start // FILL_CHUNK * FILL_CHUNK
+    assert start + count <= c0 + FILL_CHUNK
+    rot = (layer * 7919 + c0) % FILL_CHUNK
+    src = synth.kv_rows(FILL_CHUNK, seed=seed, device=dev)
+    i = (torch.arange(start - c0, start - c0 + count, device=dev) - rot) % FILL_CHUNK
+    return u16(src[i])
+
+
+def oracle_sequence_pool(rows: np.ndarray):
+    """An oracle pool holding one sequence's rows in pages 0, 1, ... (its page
+    table is the identity)."""
+    import oracle
+
+    n = rows.shape[0]
+    n_pages = (n + 63) // 64
+    ref = oracle.new_pool(n_pages, 1)
+    assert oracle.append_rows(ref, n_pages, 1, 0, rows, np.arange(n, dtype=np.int32),
+                              n_threads=oracle.threads()) == 0
+    return ref, n_pages, np.arange(n_pages, dtype=np.int32).reshape(1, -1)
+
+
+def bench_gather(args, dist: Dist, dev, peak, n_seq: int | None = None, mla: bool = True):
+    import oracle
     import rsllm_b200 as rk
     from rsllm_b200 import synth
 
-    n_seq, ctx = (8, 32768) if args.small else (64, 32768)
+    ctx = 32768
+    n_seq = n_seq or (8 if args.small else 64)
     pages_per = ctx // 64
     n_pages = n_seq * pages_per
     free, _ = torch.cuda.mem_get_info(dev)
@@ -428,13 +548,14 @@ def bench_gather(args, dist: Dist, dev, peak) -> dict:
     n_layers = 1 if args.small else N_LAYERS
     l_phys = int(min(n_layers, (free - out_bytes - 8 * 2**30) // per_layer))
     if l_phys < 1:
-        return {"skipped": "not enough device memory"}
+        return {"skipped": "not enough device memory"}, None
     perm = synth.permutation(n_pages, seed=4 + 7919 * dist.rank).to(dev)
     pt = perm.view(n_seq, pages_per).contiguous()
     tok = torch.arange(ctx, device=dev, dtype=torch.int32)
     slots_all = (pt[:, tok // 64] * 64 + (tok % 64)).reshape(-1).contiguous()
+    fill_seed = 40 + dist.rank
     pool = rk.PagedKvPool(n_pages, l_phys, device=dev)
-    fill_pool(pool, l_phys, slots_all, seed=40 + dist.rank, dev=dev)
+    fill_pool(pool, l_phys, slots_all, seed=fill_seed, dev=dev)
     del slots_all
     cu = torch.arange(0, (n_seq + 1) * ctx, ctx, dtype=torch.int32, device=dev)
     out = torch.empty((n_seq * ctx, 576), dtype=torch.bfloat16, device=dev)
@@ -448,25 +569,43 @@ def bench_gather(args, dist: Dist, dev, peak) -> dict:
         step()
     pool.check("gather", stream)
     dist.barrier()
-    ms = dist.max(events_time(lambda: [step() for _ in range(args.phase_steps)], stream))
+    per_rank = dist.all(events_time(lambda: [step() for _ in range(args.phase_steps)], stream))
+    ms = max(per_rank)
     pool.check("gather", stream)
     # per-launch duration of the kernel alone
     one = events_time(lambda: pool.rows(0, pt, cu, ctx, out=out, stream=stream), stream)
+    # parity: the first and last sequence of the first and last backed layer,
+    # gathered by the timed launch shape, against the oracle's append + gather
+    # of the rows the fill put there
+    ok = True
+    for layer in sorted({0, l_phys - 1}):
+        pool.rows(layer, pt, cu, ctx, out=out, stream=stream)
+        pool.check("gather parity", stream)
+        for s in sorted({0, n_seq - 1}):
+            ref, rp, rpt = oracle_sequence_pool(fill_rows_of(fill_seed, dev, layer, s * ctx, ctx))
+            want, st = oracle.gather_rows(ref, rp, 1, 0, rpt, np.array([0, ctx], np.int32),
+                                          n_threads=oracle.threads())
+            ok = ok and st == 0 and np.array_equal(u16(out[s * ctx:(s + 1) * ctx]), want)
     rows = n_seq * ctx
     step_bytes = n_layers * (rows * GATHER_ROW_BYTES + n_pages * 4)
     res = {"config": f"c3: {n_seq} seqs x {ctx} ctx x {n_layers} layers, random page order",
            "layers_backed": l_phys, "ms_per_step": ms / args.phase_steps,
+           "per_rank_ms_per_step": [t / args.phase_steps for t in per_rank],
            "gbs_per_gpu": step_bytes * args.phase_steps / (ms * 1e-3) / GB,
            "frac_of_hbm_peak": None, "kernel_ms_per_layer": one,
-           "launches_per_step": n_layers}
+           "launches_per_step": n_layers, "step_bytes": step_bytes,
+           "parity": dist.all_true(ok),
+           "parity_sample": "sequences first + last of layers first + last backed, every lane vs the oracle"}
     res["frac_of_hbm_peak"] = res["gbs_per_gpu"] / peak
     del out
     torch.cuda.empty_cache()
-    seq_lens = torch.full((n_seq,), ctx, dtype=torch.int32, device=dev)
-    res_mla = bench_mla(args, dist, pool, pt, seq_lens, torch.arange(n_seq, dtype=torch.int32, device=dev), None,
-                        n_layers, l_phys, stream, peak,
-                        f"c3 shape: {n_seq} decode queries (one per sequence) x {ctx} rows x {n_layers} layers",
-                        n_splits=args.mla_splits)
+    res_mla = None
+    if mla:
+        seq_lens = torch.full((n_seq,), ctx, dtype=torch.int32, device=dev)
+        res_mla = bench_mla(args, dist, pool, pt, seq_lens, torch.arange(n_seq, dtype=torch.int32, device=dev),
+                            None, n_layers, l_phys, stream, peak,
+                            f"c3 shape: {n_seq} decode queries (one per sequence) x {ctx} rows x {n_layers} layers",
+                            n_splits=args.mla_splits)
     del pool
     torch.cuda.empty_cache()
     return res, res_mla
@@ -511,7 +650,8 @@ def bench_mla(args, dist: Dist, pool, pt, seq_lens, seq_of_query, idx, n_layers:
         step()
     pool.check("mla", stream)
     dist.barrier()
-    ms = dist.max(events_time(lambda: [step() for _ in range(args.phase_steps)], stream))
+    per_rank = dist.all(events_time(lambda: [step() for _ in range(args.phase_steps)], stream))
+    ms = max(per_rank)
     pool.check("mla", stream)
     kernel_ms = events_time(lambda: one(0), stream)
     if idx is None:
@@ -525,7 +665,8 @@ def bench_mla(args, dist: Dist, pool, pt, seq_lens, seq_of_query, idx, n_layers:
     t_layer = ms / args.phase_steps / n_layers * 1e-3
     t_ideal = max(nbytes_alg / (peak * GB), flops / (tc_peak * 1e12))
     return {"config": config, "layers_backed": l_phys, "n_splits": n_splits,
-            "ms_per_step": ms / args.phase_steps, "kernel_ms_per_layer": kernel_ms,
+            "ms_per_step": ms / args.phase_steps, "per_rank_ms_per_step": [t / args.phase_steps for t in per_rank],
+            "kernel_ms_per_layer": kernel_ms,
             "gbs_per_gpu": nbytes_alg / t_layer / GB, "tflops_per_gpu": flops / t_layer / 1e12,
             "frac_of_hbm_peak": nbytes_alg / t_layer / GB / peak,
             "frac_of_tensor_peak_sustained": flops / t_layer / 1e12 / tc_peak,
@@ -534,11 +675,13 @@ def bench_mla(args, dist: Dist, pool, pt, seq_lens, seq_of_query, idx, n_layers:
             "algorithmic_bytes_per_launch": nbytes_alg, "flops_per_launch": flops}
 
 
-def bench_sparse(args, dist: Dist, dev, peak) -> dict:
+def bench_sparse(args, dist: Dist, dev, peak, n_seq: int | None = None, mla: bool = True) -> dict:
+    import oracle
     import rsllm_b200 as rk
     from rsllm_b200 import synth
 
-    n_seq, ctx, n_qpos, k = (4 if args.small else 32), 131072, 64, 2048
+    ctx, n_qpos, k = 131072, 64, 2048
+    n_seq = n_seq or (4 if args.small else 32)
     pages_per = ctx // 64
     n_pages = n_seq * pages_per
     n_q = n_seq * n_qpos
@@ -556,8 +699,9 @@ def bench_sparse(args, dist: Dist, dev, peak) -> dict:
     pt = perm.view(n_seq, pages_per).contiguous()
     tok = torch.arange(ctx, device=dev, dtype=torch.int32)
     slots_all = (pt[:, tok // 64] * 64 + (tok % 64)).reshape(-1).contiguous()
+    fill_seed = 60 + dist.rank
     pool = rk.PagedKvPool(n_pages, l_phys, device=dev)
-    fill_pool(pool, l_phys, slots_all, seed=60 + dist.rank, dev=dev)
+    fill_pool(pool, l_phys, slots_all, seed=fill_seed, dev=dev)
     del slots_all
     torch.cuda.empty_cache()
     scores = [synth.scores(n_q, ctx, seed=500 + 31 * i + 7919 * dist.rank, device=dev) for i in range(n_score_mats)]
@@ -582,13 +726,33 @@ def bench_sparse(args, dist: Dist, dev, peak) -> dict:
         sparse_step()
     pool.check("sparse", stream)
     dist.barrier()
-    ms_topk = dist.max(events_time(lambda: [topk_step() for _ in range(args.phase_steps)], stream))
+    rank_topk = dist.all(events_time(lambda: [topk_step() for _ in range(args.phase_steps)], stream))
     dist.barrier()
-    ms_sparse = dist.max(events_time(lambda: [sparse_step() for _ in range(args.phase_steps)], stream))
+    rank_sparse = dist.all(events_time(lambda: [sparse_step() for _ in range(args.phase_steps)], stream))
+    ms_topk, ms_sparse = max(rank_topk), max(rank_sparse)
     pool.check("sparse", stream)
     one_topk = events_time(lambda: rk.select_top_k(scores[0], n_visible, k, out=idx[0], stream=stream), stream)
     one_sparse = events_time(lambda: pool.sparse_rows(0, pt, seq_of_query, seq_lens, idx[0], out=out,
                                                       stream=stream), stream)
+    pool.check("sparse", stream)
+    # parity on layer 0 (idx[0] and out now hold its selection and rows):
+    # sampled queries of the first and last sequence, every index against the
+    # oracle's selection and every gathered lane against the oracle's pool
+    sample = sorted({0, 1, n_qpos // 2, n_qpos - 1, n_q - n_qpos, n_q - 1})
+    nv_np = n_visible.cpu().numpy()
+    sc0 = scores[0][sample].cpu().numpy()
+    want_idx = oracle.topk_batch(sc0, nv_np[sample], k, n_threads=oracle.threads())
+    got_idx = idx[0][sample].cpu().numpy()
+    ok_topk = bool(np.array_equal(got_idx, want_idx))
+    ok_sparse = ok_topk
+    sq_np = seq_of_query.cpu().numpy()
+    for s in sorted({int(sq_np[q]) for q in sample}):
+        qs = [q for q in sample if int(sq_np[q]) == s]
+        ref, rp, rpt = oracle_sequence_pool(fill_rows_of(fill_seed, dev, 0, s * ctx, ctx))
+        want, st = oracle.sparse_gather_rows(ref, rp, 1, 0, rpt, np.zeros(len(qs), np.int32),
+                                             np.array([ctx], np.int32), idx[0][qs].cpu().numpy(),
+                                             n_threads=oracle.threads())
+        ok_sparse = ok_sparse and st == 0 and np.array_equal(u16(out[qs]), want)
     sel = n_q * k
     sparse_bytes = n_layers * sel * (GATHER_ROW_BYTES + 4 + 4)
     vis = int(n_visible.sum().item())
@@ -597,21 +761,29 @@ def bench_sparse(args, dist: Dist, dev, peak) -> dict:
     res = {
         "topk": {"config": f"c4: {n_q} queries ({n_seq} seqs x last 64 positions, causal) over 131072 keys, "
                            f"k=2048, {n_layers} layers cycling {n_score_mats} seeded N(0,1) score matrices",
-                 "ms_per_step": ms_topk / P, "gbs_per_gpu": topk_bytes * P / (ms_topk * 1e-3) / GB,
+                 "ms_per_step": ms_topk / P, "per_rank_ms_per_step": [t / P for t in rank_topk],
+                 "gbs_per_gpu": topk_bytes * P / (ms_topk * 1e-3) / GB,
                  "frac_of_hbm_peak": topk_bytes * P / (ms_topk * 1e-3) / GB / peak,
                  "queries_per_s_per_gpu": n_layers * n_q * P / (ms_topk * 1e-3),
-                 "kernel_ms_per_layer": one_topk},
+                 "kernel_ms_per_layer": one_topk, "step_bytes": topk_bytes,
+                 "parity": dist.all_true(ok_topk),
+                 "parity_sample": f"queries {sample} of layer 0: every index in order vs the oracle"},
         "sparse_gather": {"config": f"c4: {n_q} queries x 2048 selected rows x {n_layers} layers, random page order",
                           "layers_backed": l_phys, "ms_per_step": ms_sparse / P,
+                          "per_rank_ms_per_step": [t / P for t in rank_sparse],
                           "gbs_per_gpu": sparse_bytes * P / (ms_sparse * 1e-3) / GB,
                           "frac_of_hbm_peak": sparse_bytes * P / (ms_sparse * 1e-3) / GB / peak,
-                          "kernel_ms_per_layer": one_sparse},
+                          "kernel_ms_per_layer": one_sparse, "step_bytes": sparse_bytes,
+                          "parity": dist.all_true(ok_sparse),
+                          "parity_sample": f"queries {sample} of layer 0: every lane of their 2048 rows vs the "
+                                           "oracle"},
     }
     del out, scores
     torch.cuda.empty_cache()
-    res["mla_decode_sparse"] = bench_mla(
-        args, dist, pool, pt, seq_lens, seq_of_query, idx, n_layers, l_phys, stream, peak,
-        f"c4 shape: {n_q} queries x 2048 top-k rows (the indices above) x {n_layers} layers")
+    if mla:
+        res["mla_decode_sparse"] = bench_mla(
+            args, dist, pool, pt, seq_lens, seq_of_query, idx, n_layers, l_phys, stream, peak,
+            f"c4 shape: {n_q} queries x 2048 top-k rows (the indices above) x {n_layers} layers")
     del pool, idx
     torch.cuda.empty_cache()
     return res
@@ -859,7 +1031,7 @@ def bench_kvc(args, dist: Dist, dev) -> dict:
 # config 5: prefix cache -- copy-on-write branches, LRU eviction, compaction
 # ---------------------------------------------------------------------------
 
-def bench_prefix(args, dist: Dist, dev, peak, tail: int = 37) -> dict:
+def bench_prefix(args, dist: Dist, dev, peak, tail: int = 37, n_branch: int | None = None) -> dict:
     """Per GPU: a pool of 2^20 pages (1 layer) filled to 90% by released
     resident sequences (lengths U[1024, 32768], seeded), a shared prefix of
     8192 + tail tokens in the radix store, 512 branches that match it,
@@ -869,13 +1041,19 @@ def bench_prefix(args, dist: Dist, dev, peak, tail: int = 37) -> dict:
     work of each phase with CUDA events on the pool's stream -- for the
     copy-on-write copies and the compaction moves by replaying the same page
     moves (their sources are unchanged free or shared pages, and the remap is
-    idempotent), so no host planning time lands between the events."""
+    idempotent), so no host planning time lands between the events.
+    Parity: every branch's rows are gathered before the compaction and again
+    through the remapped device tables after it (equal bit for bit), and the
+    first and last branch's rows equal the oracle's append + gather of the
+    prefix rows followed by the branch's own."""
+    import oracle
     import rsllm_b200 as rk
     from rsllm_b200 import synth
     from rsllm_b200.prefix_pool import PrefixKvPool
 
     n_pages = 1 << 14 if args.small else 1 << 20
-    n_branch, new_tok = (16, 2048) if args.small else (512, 2048)
+    n_branch = n_branch or (16 if args.small else 512)
+    new_tok = 2048
     prefix_len = 8192 + tail
     stream = torch.cuda.Stream(device=dev)
     t0 = time.perf_counter()
@@ -896,8 +1074,8 @@ def bench_prefix(args, dist: Dist, dev, peak, tail: int = 37) -> dict:
     owner = pool.create_sequence()
     slots = pool.reserve([owner], [prefix_len], stream=stream)
     with torch.cuda.stream(stream):
-        rows = synth.kv_rows(prefix_len, seed=70 + dist.rank, device=dev)
-        pool.kv.append_layer(0, rows, torch.from_numpy(slots).to(dev))
+        prefix_rows = synth.kv_rows(prefix_len, seed=70 + dist.rank, device=dev)
+        pool.kv.append_layer(0, prefix_rows, torch.from_numpy(slots).to(dev))
     prefix_tokens = np.arange(prefix_len, dtype=np.int32)
     pool.insert_prefix(prefix_tokens, owner)
     pool.free(owner)
@@ -909,7 +1087,8 @@ def bench_prefix(args, dist: Dist, dev, peak, tail: int = 37) -> dict:
         return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
     # (A) branches: radix match and batched reserve with copy-on-write (host
-    # plan; the copies are enqueued), then 2048 rows appended per branch
+    # plan; the copies are enqueued), the copies timed by a replay, then 2048
+    # rows appended per branch
     dist.barrier()
     h0 = time.perf_counter()
     branches = []
@@ -922,13 +1101,6 @@ def bench_prefix(args, dist: Dist, dev, peak, tail: int = 37) -> dict:
     h1 = time.perf_counter()
     d_slots = torch.from_numpy(slots).to(dev)
     stream.synchronize()
-    a, b = ev_pair()
-    a.record(stream)
-    with torch.cuda.stream(stream):
-        pool.kv.append_layer(0, branch_rows, d_slots)
-    b.record(stream)
-    stream.synchronize()
-    append_ms = a.elapsed_time(b)
     cow_ms = None
     if tail:
         src = torch.full((n_branch,), shared_page, dtype=torch.int32, device=dev)
@@ -940,6 +1112,14 @@ def bench_prefix(args, dist: Dist, dev, peak, tail: int = 37) -> dict:
         b.record(stream)
         stream.synchronize()
         cow_ms = a.elapsed_time(b)
+    a, b = ev_pair()
+    a.record(stream)
+    with torch.cuda.stream(stream):
+        pool.kv.append_layer(0, branch_rows, d_slots)
+    b.record(stream)
+    stream.synchronize()
+    append_ms = a.elapsed_time(b)
+    pool.kv.check("prefix append", stream)
 
     # (B) LRU eviction of 30% of the used pages, then compaction with the
     # branches' device page table remapped in place
@@ -949,6 +1129,16 @@ def bench_prefix(args, dist: Dist, dev, peak, tail: int = 37) -> dict:
     for i, t in enumerate(tabs):
         pt[i, :len(t)] = t
     d_pt = torch.from_numpy(pt).to(dev)
+    L = prefix_len + new_tok
+    cu = torch.arange(0, (n_branch + 1) * L, L, dtype=torch.int32, device=dev)
+    pre = pool.kv.rows(0, d_pt, cu, L, stream=stream, total=n_branch * L)
+    pool.kv.check("prefix gather", stream)
+    ok_oracle = True
+    for i in sorted({0, n_branch - 1}):
+        rows = np.concatenate([u16(prefix_rows), u16(branch_rows[i * new_tok:(i + 1) * new_tok])])
+        ref, rp, rpt = oracle_sequence_pool(rows)
+        want, st = oracle.gather_rows(ref, rp, 1, 0, rpt, np.array([0, L], np.int32), n_threads=oracle.threads())
+        ok_oracle = ok_oracle and st == 0 and np.array_equal(u16(pre[i * L:(i + 1) * L]), want)
     used = pool.stats()["live_pages"]
     stream.synchronize()
     dist.barrier()
@@ -977,6 +1167,10 @@ def bench_prefix(args, dist: Dist, dev, peak, tail: int = 37) -> dict:
     st = pool.stats()
     ok_tables = all(np.array_equal(pool.page_table(x), d_pt[i, :len(tabs[i])].cpu().numpy())
                     for i, x in enumerate(branches))
+    post = pool.kv.rows(0, d_pt, cu, L, stream=stream, total=n_branch * L)
+    pool.kv.check("prefix gather after compaction", stream)
+    ok_same = bool(torch.equal(pre, post))
+    del pre, post
     moved_bytes = 2 * moved * rk.PAGE_BYTES
     res = {
         "config": f"c5: pool 2^{int(np.log2(n_pages))} pages x 1 layer at 90% (released residents), prefix "
@@ -992,6 +1186,11 @@ def bench_prefix(args, dist: Dist, dev, peak, tail: int = 37) -> dict:
         "compact_frac_of_hbm_peak": moved_bytes / (compact_copy_ms * 1e-3) / GB / peak if moved else None,
         "high_water_after": st["high_water"], "live_after": st["live_pages"],
         "device_tables_match_host": ok_tables,
+        "rows_equal_after_compaction": ok_same,
+        "branch_rows_match_oracle": ok_oracle,
+        "parity": dist.all_true(ok_tables and ok_same and ok_oracle),
+        "parity_sample": f"all {n_branch} branches x {L} rows equal before and after compaction; branches first + "
+                         "last vs the oracle; device tables vs the host allocator",
     }
     pool.close()
     del pool, branch_rows, d_pt
@@ -1002,6 +1201,9 @@ def bench_prefix(args, dist: Dist, dev, peak, tail: int = 37) -> dict:
 # ---------------------------------------------------------------------------
 # reference arm: the CPU restatement of rsLLM's path on the host cores
 # ---------------------------------------------------------------------------
+
+METRIC = "KV append GB/s (config 2 decode append: FP8 quantize-on-append into a paged pool)"
+
 
 def run_reference(args, dist: Dist) -> None:
     if dist.rank != 0:
@@ -1033,12 +1235,12 @@ def run_reference(args, dist: Dist) -> None:
         st = oracle.append_rows(pool, wl.n_pages, N_LAYERS, 0, r, wl.slots_np[j], n_threads=threads)
         t += time.perf_counter() - t0
         assert st == 0
-    value = AppendWorkload.bytes_per_step() * K / t / GB
+    value = wl.bytes_per_step() * K / t / GB
     line = {
-        "metric": "KV append GB/s (config 2 decode append; CPU restatement of rsLLM's codec + append)",
+        "metric": METRIC,
         "value": value, "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus, "steps": K, "warmup": W,
         "ms_per_step": t / K * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "u8", "data": "synthetic (seeded)",
+        "dtype": "u8", "data": "synthetic (seeded N(0,1) bf16 rows, 1% x20 outliers; seeded page tables)",
         "config": {"workload": "c2-decode-append", "sequences": N_SEQ_APPEND, "layers": N_LAYERS,
                    "page_tokens": 64, "row": "512 latent fp8 + 64 rope bf16"},
         "tokens_per_s": N_SEQ_APPEND * K / t,
@@ -1046,9 +1248,86 @@ def run_reference(args, dist: Dist) -> None:
                          "sample": f"{K} full decode steps of config 2 ({K * N_LAYERS * N_SEQ_APPEND} rows)"},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "rsLLM is Rust (no cargo/rustc here); this arm times the C restatement of its CPU path "
-                "(oracle/rkv_oracle.c) with the same loop structure, on all host threads",
+                "(oracle/rkv_oracle.c: binary-search snap per lane, as dsv4_quant.rs) on all host threads",
     }
     print(json.dumps(line), flush=True)
+
+
+def _r(x, nd: int = 3):
+    """A number rounded to nd significant digits (None passes through)."""
+    if x is None or isinstance(x, bool):
+        return x
+    return float(f"{x:.{nd}g}")
+
+
+def summary(app: dict, phases: dict, split: dict | None) -> dict:
+    """Compact per-phase figures (GB/s per GPU, fraction of the measured HBM
+    peak, kernel ms per layer, parity), printed last in the line."""
+    out = {"append_c2": {"gbs": _r(app["gbs_per_gpu"]), "frac": _r(app["frac"]), "us_step": _r(app["ms_per_step"] * 1e3),
+                         "parity": app["parity"]}}
+    keys = {"gather": "gather_c3", "topk": "topk_c4", "sparse_gather": "sparse_c4", "mla_decode_dense": "mla_c3",
+            "mla_decode_sparse": "mla_c4", "compress_decode": "cmp_dec", "compress_prefill": "cmp_pre",
+            "indexer_score_topk": "idx_c4"}
+    for name, short in keys.items():
+        p = phases.get(name)
+        if not isinstance(p, dict) or "skipped" in p:
+            continue
+        d = {"gbs": _r(p.get("gbs_per_gpu")), "frac": _r(p.get("roofline_frac", p.get("frac_of_hbm_peak")))}
+        ms = p.get("kernel_ms_per_layer", p.get("ms_per_layer_ungraphed", p.get("ms_per_layer")))
+        if ms is not None:
+            d["ms_l"] = _r(ms)
+        if "parity" in p:
+            d["parity"] = p["parity"]
+        out[short] = d
+    for name, short in (("prefix_cow_evict_compact", "prefix_c5"), ("prefix_cow_evict_compact_aligned", "prefix_c5a")):
+        p = phases.get(name)
+        if isinstance(p, dict):
+            out[short] = {"compact_gbs": _r(p.get("compact_gbs")), "frac": _r(p.get("compact_frac_of_hbm_peak")),
+                          "append_gbs": _r(p.get("append_gbs")), "parity": p.get("parity")}
+    if split:
+        out["split"] = {k: {"agg_gbs": _r(v.get("aggregate_gbs")), "parity": v.get("parity")}
+                        for k, v in split.items() if isinstance(v, dict)}
+    return out
+
+
+def bench_split(args, dist: Dist, dev, peak) -> dict:
+    """The configurations split over the ranks, as the multi-GPU plan states
+    them (strong scaling): config 2's 256 sequences, config 3's 64 and
+    config 4's 32 sequences and config 5's 512 branches, each divided evenly;
+    aggregate GB/s = all ranks' algorithmic bytes / the slowest rank's time."""
+    G = dist.world
+    out = {}
+    a = bench_append(args, dist, dev, peak, n_seq=max(1, N_SEQ_APPEND // G), e2e=False)
+    out["append_c2"] = {"sequences_per_gpu": a["wl"].n_seq, "ms_per_step": a["ms_per_step"],
+                        "per_rank_ms_per_step": a["per_rank_ms_per_step"],
+                        "aggregate_gbs": G * a["step_bytes"] / (a["ms_per_step"] * 1e-3) / GB,
+                        "parity": a["parity"]}
+    del a
+    torch.cuda.empty_cache()
+    wanted = [] if args.phases == "none" else args.phases.split(",")
+    if "gather" in wanted:
+        g, _ = bench_gather(args, dist, dev, peak, n_seq=max(1, 64 // G), mla=False)
+        if "skipped" not in g:
+            out["gather_c3"] = {"sequences_per_gpu": max(1, 64 // G), "ms_per_step": g["ms_per_step"],
+                                "per_rank_ms_per_step": g["per_rank_ms_per_step"],
+                                "aggregate_gbs": G * g["step_bytes"] / (g["ms_per_step"] * 1e-3) / GB,
+                                "parity": g["parity"]}
+    if "sparse" in wanted:
+        sp = bench_sparse(args, dist, dev, peak, n_seq=max(1, 32 // G), mla=False)
+        if "skipped" not in sp:
+            for name, short in (("topk", "topk_c4"), ("sparse_gather", "sparse_c4")):
+                p = sp[name]
+                out[short] = {"sequences_per_gpu": max(1, 32 // G), "ms_per_step": p["ms_per_step"],
+                              "per_rank_ms_per_step": p["per_rank_ms_per_step"],
+                              "aggregate_gbs": G * p["step_bytes"] / (p["ms_per_step"] * 1e-3) / GB,
+                              "parity": p["parity"]}
+    if "prefix" in wanted:
+        p = bench_prefix(args, dist, dev, peak, n_branch=max(1, 512 // G))
+        out["prefix_c5"] = {"branches_per_gpu": max(1, 512 // G), "pages_moved": p["pages_moved"],
+                            "device_compact_ms": p["device_compact_ms"],
+                            "aggregate_gbs": dist.world * p["compact_gbs"] if p["compact_gbs"] else None,
+                            "parity": p["parity"]}
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -1065,13 +1344,15 @@ def main():
     ap.add_argument("--phase-steps", type=int, default=3)
     ap.add_argument("--phase-warmup", type=int, default=1)
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
-    ap.add_argument("--only", choices=["all", "append", "gather", "sparse", "prefix", "kvc", "compress", "indexer"],
+    ap.add_argument("--only", choices=["all", "append", "gather", "sparse", "prefix", "kvc", "compress", "indexer",
+                                       "split"],
                     default="all",
                     help="run one workload alone (profiling)")
     ap.add_argument("--mla-splits", type=int, default=16,
                     help="page-range splits per query for the dense MLA decode phase")
     ap.add_argument("--small", action="store_true",
                     help="profiling sizes for the phases: 8 seqs / 1 layer (gather), 4 seqs / 1 layer (sparse)")
+    ap.add_argument("--no-split", action="store_true", help="skip the strong-split phases at N > 1")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         ap.error("--warmup must be >= 3")
@@ -1081,8 +1362,8 @@ def main():
         run_reference(args, dist)
         dist.close()
         return
-    import oracle  # noqa: F401  (cpu_baseline leg)
-    import rsllm_b200 as rk
+    import oracle  # noqa: F401  (cpu_baseline leg and parity checks)
+    import rsllm_b200 as rk  # noqa: F401
 
     dev = torch.device("cuda", dist.local if dist.world > 1 else torch.cuda.current_device())
     torch.cuda.set_device(dev)
@@ -1106,6 +1387,8 @@ def main():
             res = bench_compress(args, dist, dev, peak)
         elif args.only == "indexer":
             res = bench_indexer(args, dist, dev, peak)
+        elif args.only == "split":
+            res = bench_split(args, dist, dev, peak)
         else:
             res = bench_sparse(args, dist, dev, peak)
         clocks.stop()
@@ -1115,6 +1398,7 @@ def main():
         return
 
     app = bench_append(args, dist, dev, peak)
+    app["frac"] = app["gbs_per_gpu"] / peak
     phases = {}
     wanted = [] if args.phases == "none" else args.phases.split(",")
     if "gather" in wanted:
@@ -1131,6 +1415,7 @@ def main():
         phases.update(bench_compress(args, dist, dev, peak))
     if "indexer" in wanted:
         phases["indexer_score_topk"] = bench_indexer(args, dist, dev, peak)
+    split = bench_split(args, dist, dev, peak) if dist.world > 1 and not args.no_split else None
     clk = clocks.stop()
 
     K, W = args.steps, args.warmup
@@ -1151,9 +1436,9 @@ def main():
         value = app["gbs_per_gpu"] * dist.world
         traffic = NCU_TRAFFIC_PER_ROW["append"]
         rows_per_launch = N_LAYERS * N_SEQ_APPEND
+        e2e = app["e2e"]
         line = {
-            "metric": "KV append GB/s (config 2 decode append: FP8 quantize-on-append into paged pool); "
-                      "see phases for gather / top-k / sparse gather",
+            "metric": METRIC,
             "value": value, "unit": "GB/s", "n_gpus": dist.world, "steps": K, "warmup": W,
             "ms_per_step": app["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "u8", "data": "synthetic (seeded N(0,1) bf16 rows, 1% x20 outliers; seeded page tables)",
@@ -1161,27 +1446,32 @@ def main():
                        "seq_len": "U[1024,32768]", "page_tokens": 64, "row": "512 latent fp8 + 64 rope bf16",
                        "parallelism": f"request-sharded x{dist.world}, no collective",
                        "l2": "inputs larger than L2 (fresh rows every step, 1.9 GB total) + L2 flush before timing",
-                       "launch": "K steps captured in one CUDA graph (uploaded by an untimed replay)"},
+                       "launch": "K steps captured in one CUDA graph (uploaded by an untimed replay); a sleep "
+                                 "kernel queued before the start event covers the host's graph launch"},
             "tokens_per_s": app["tokens_per_s_per_gpu"] * dist.world,
             "rows_per_s": app["tokens_per_s_per_gpu"] * dist.world * N_LAYERS,
-            "frac_of_hbm_peak_per_gpu": app["gbs_per_gpu"] / peak,
+            "frac_of_hbm_peak_per_gpu": app["frac"],
+            "per_rank_ms_per_step": app["per_rank_ms_per_step"],
+            "repeats_max_over_ranks_ms_per_step": app["repeats_max_over_ranks_ms_per_step"],
+            "repeats_median_rank_ms_per_step": app["repeats_median_rank_ms_per_step"],
+            "parity": app["parity"],
             "roofline": {"bound": "hbm", "achieved": app["gbs_per_gpu"], "peak": peak, "unit": "GB/s",
-                         "frac": app["gbs_per_gpu"] / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                         "frac": app["frac"], "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                          if peak_kind == "measured" else "fallback 6650 GB/s",
                          "kernel": "append_quant_kernel", "algorithmic_bytes_per_launch": app["step_bytes"],
                          "traffic": None if traffic is None else traffic * rows_per_launch},
             "cpu_baseline": cpu,
             "cpu_baseline_single_thread": cpu1,
-            "e2e": {k: v for k, v in app["e2e"].items() if k in ("value", "unit", "h2d_bytes_per_step",
-                                                                   "d2h_bytes_per_step")},
-            "e2e_detail": app["e2e"],
+            "e2e": {k: v for k, v in e2e.items() if k in ("value", "unit", "h2d_bytes_per_step",
+                                                           "d2h_bytes_per_step")},
+            "e2e_detail": e2e,
             "gpu_launches": K,
             "phases": phases,
+            "split": split,
             "clocks": clk,
             "wall_s": time.time() - t_start,
         }
-        if dist.world > 1:
-            line["e2e"]["value"] = app["e2e"]["value"] * dist.world
+        line["summary"] = summary(app, phases, split)
     del app
     dist.close()
     if line is not None:

@@ -349,9 +349,15 @@ RKV_API rkv_status rkv_kvc_load(rkv_pool* pool, const char* path, int32_t* token
  * d_tables is given, rewrites its n_entries page ids (an id equal to src[i]
  * becomes dst[i]).
  * src: host int32 [n_moves], strictly ascending; dst: host int32 [n_moves],
- * no destination also a source (the moves of one compaction, e.g. from
- * rkv_pool_last_remap or rkv_pool_take_moves, sorted by source).  At most
- * RKV_STATIC_MAX_MOVES moves per call: more is SHAPE_MISMATCH.
+ * no destination also a source and no page the destination of two moves
+ * (the moves of one compaction, e.g. from rkv_pool_last_remap or
+ * rkv_pool_take_moves, sorted by source); a list that breaks either rule is
+ * INVALID_ARGUMENT and nothing is queued.  The call reads src and dst on the
+ * host and queues their copy to the device on `stream`: pageable arrays may
+ * be reused when the call returns, but pinned (page-locked) arrays are read
+ * by that copy later, so keep them unchanged until the stream has passed the
+ * call.  At most RKV_STATIC_MAX_MOVES moves per call: more is
+ * SHAPE_MISMATCH.
  * The first call on a device looks up the array's device address with that
  * device current (once per device); make that first call before any stream
  * capture.  Every call shares the array and leaves its contents behind; calls

@@ -19,6 +19,7 @@
 #include <algorithm>
 
 #include <atomic>
+#include <mutex>
 
 #include "rkv_common.cuh"
 #include "rkv_host.h"
@@ -33,6 +34,12 @@ static __device__ __align__(256) int32_t g_move_scratch[2 * kStaticMaxMoves];
 
 constexpr int kMaxDevices = 64;
 static std::atomic<int32_t*> g_scratch_addr[kMaxDevices];  // device address of g_move_scratch, per device
+
+// Host-side room to sort a copy of the destinations (the duplicate check),
+// fixed like the device array so that validation allocates nothing either;
+// calls from several host threads take turns on it.
+static int32_t g_dst_sorted[kStaticMaxMoves];
+static std::mutex g_dst_sorted_mutex;
 
 // Page-table rewrite against the staged move list: an entry equal to some
 // src[i] becomes dst[i] (binary search of the ascending sources).
@@ -84,6 +91,16 @@ extern "C" rkv_status rkv_apply_page_moves_static(const rkv_pool_view* pool, con
     if (hit != src + n_moves && *hit == dst[i])
       return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_apply_page_moves_static: page %d is both a source and a destination",
                   dst[i]);
+  }
+  {  // no two moves may write one page: the copies run in parallel, and the
+     // table rewrite would map two live pages onto it
+    std::lock_guard<std::mutex> lock(g_dst_sorted_mutex);
+    std::copy(dst, dst + n_moves, g_dst_sorted);
+    std::sort(g_dst_sorted, g_dst_sorted + n_moves);
+    const int32_t* dup = std::adjacent_find(g_dst_sorted, g_dst_sorted + n_moves);
+    if (dup != g_dst_sorted + n_moves)
+      return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_apply_page_moves_static: page %d is the destination of two moves",
+                  *dup);
   }
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -185,15 +185,20 @@ class PagedKvPool:
 
     # -- reads ----------------------------------------------------------------
     def rows(self, layer: int, page_table: torch.Tensor, cu_seqlens: torch.Tensor, max_seq_len: int,
-             out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+             out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None,
+             total: int | None = None) -> torch.Tensor:
         """Chronological bf16 rows of every sequence (``[total, 576]``):
-        row t of sequence s at ``out[cu_seqlens[s] + t]``."""
+        row t of sequence s at ``out[cu_seqlens[s] + t]``.  Pass ``out`` or
+        ``total`` (= cu_seqlens[-1]) to keep the call asynchronous; without
+        either the call reads cu_seqlens[-1] back from the device (a stream
+        synchronisation) to size the output."""
         _need(page_table, torch.int32, "page_table", self.device)
         _need(cu_seqlens, torch.int32, "cu_seqlens", self.device)
         if page_table.dim() != 2 or cu_seqlens.dim() != 1 or cu_seqlens.shape[0] != page_table.shape[0] + 1:
             raise ShapeMismatch("rows: page_table [n_seq, stride] and cu_seqlens [n_seq+1] required")
         if out is None:
-            total = int(cu_seqlens[-1].item())
+            if total is None:
+                total = int(cu_seqlens[-1].item())
             out = torch.empty((total, ROW_DIM), dtype=torch.bfloat16, device=self.device)
         _need(out, torch.bfloat16, "out", self.device)
         check(self.lib.rkv_gather_dequant_bf16(byref(self.view), layer, _ptr(page_table), page_table.shape[1],

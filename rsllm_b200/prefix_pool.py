@@ -72,16 +72,25 @@ class PrefixKvPool:
         check(self.lib.rkv_seq_fork(self._h, parent, n_tokens, byref(v)))
         return v.value
 
-    def reserve(self, seqs, n_tokens, stream: torch.cuda.Stream | None = None) -> np.ndarray:
+    def reserve(self, seqs, n_tokens, stream: torch.cuda.Stream | None = None,
+                out: np.ndarray | None = None) -> np.ndarray:
         """Slots (int32, sequence after sequence) for n_tokens[i] more tokens
-        of each seqs[i]; copy-on-write copies go on ``stream``."""
+        of each seqs[i]; copy-on-write copies go on ``stream``.  ``out`` (a
+        contiguous int32 array of sum(n_tokens) entries, e.g. a view of a
+        pinned host tensor) receives the slots instead of a new array."""
+        from .kvcache import ShapeMismatch
+
         s = np.ascontiguousarray(np.atleast_1d(seqs), dtype=np.int64)
         n = np.ascontiguousarray(np.atleast_1d(n_tokens), dtype=np.int64)
         if s.shape != n.shape:
-            from .kvcache import ShapeMismatch
-
             raise ShapeMismatch("reserve: seqs and n_tokens differ in length")
-        slots = np.empty(int(n.sum()), np.int32)
+        total = int(n.sum())
+        if out is None:
+            slots = np.empty(total, np.int32)
+        elif out.dtype != np.int32 or not out.flags["C_CONTIGUOUS"] or out.size != total:
+            raise ShapeMismatch(f"reserve: out must be a contiguous int32 array of {total} entries")
+        else:
+            slots = out
         st = c_void_p(0) if self.kv is None else _stream(stream)
         check(self.lib.rkv_seq_reserve(self._h, s.size, _ptr(s), _ptr(n), _ptr(slots), st))
         return slots

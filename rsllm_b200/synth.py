@@ -44,3 +44,23 @@ def uniform_ints(n: int, lo: int, hi: int, seed: int) -> torch.Tensor:
     g = torch.Generator()
     g.manual_seed(seed)
     return torch.randint(lo, hi + 1, (n,), generator=g, dtype=torch.int64).to(torch.int32)
+
+
+def decode_slots(n_seq: int, n_steps: int, seed: int, len_range: tuple[int, int] = (1024, 32768)):
+    """The slot mappings of ``n_steps`` decode steps of the benchmark's
+    config 2: ``n_seq`` sequences with current lengths uniform in
+    ``len_range`` (seed ``seed``) each append one token per step; the pages the
+    run touches (each sequence's current page and every page it crosses into)
+    get physical ids from a seeded permutation (seed ``seed + 1``).
+    Returns ``(slots int32 [n_steps, n_seq], n_pages, lens int64 [n_seq])``."""
+    import numpy as np
+
+    lens = uniform_ints(n_seq, *len_range, seed=seed).numpy().astype(np.int64)
+    first = lens // 64
+    need = (lens + n_steps - 1) // 64 - first + 1
+    off = np.concatenate([[0], np.cumsum(need)])
+    n_pages = int(off[-1])
+    phys = permutation(n_pages, seed=seed + 1).numpy().astype(np.int64)
+    pos = lens[None, :] + np.arange(n_steps)[:, None]
+    page = phys[off[:-1][None, :] + pos // 64 - first[None, :]]
+    return (page * 64 + pos % 64).astype(np.int32), n_pages, lens

@@ -96,3 +96,49 @@ def test_static_moves_rejects_too_many_and_bad_lists(cuda):
     src = np.array([3, 9], np.int32)
     assert lib.rkv_apply_page_moves_static(byref(view), c_void_p(src.ctypes.data), c_void_p(dst.ctypes.data), 2,
                                            null, 0, null, null) == _abi.RKV_ERR_INDEX_OUT_OF_RANGE
+    src = np.array([1, 2, 3], np.int32)
+    dst = np.array([6, 7, 6], np.int32)  # two moves write page 6
+    assert lib.rkv_apply_page_moves_static(byref(view), c_void_p(src.ctypes.data), c_void_p(dst.ctypes.data), 3,
+                                           null, 0, null, null) == _abi.RKV_ERR_INVALID_ARGUMENT
+    assert "two moves" in _abi.last_error()
+
+
+def _moves(rng, n_pages: int, n: int):
+    """n moves with ascending distinct sources and distinct destinations
+    outside the sources."""
+    pages = rng.permutation(n_pages)[:2 * n].astype(np.int32)
+    return np.sort(pages[:n]), pages[n:].copy()
+
+
+def test_static_moves_large_then_small_and_without_tables(cuda):
+    """A long move list, then short ones on the same stream (the staging
+    array's leftover entries from the long list must never be read), one of
+    them with no page table: pool bytes and tables equal those of
+    rkv_copy_pages + rkv_remap_pages applied to a twin of the pool."""
+    lib = _abi.load()
+    rng = np.random.default_rng(5)
+    n_pages, n_layers = 4096, 2
+    mine = torch.empty(rk.pool_bytes(n_pages, n_layers), dtype=torch.uint8, device=cuda).random_(0, 256)
+    twin = rk.PagedKvPool(n_pages, n_layers, device=cuda, storage=mine.clone())
+    view = _abi.PoolView(mine.data_ptr(), n_pages, n_layers, 0)
+    table = torch.from_numpy(rng.integers(-1, n_pages, 6000).astype(np.int32)).to(cuda)
+    table_twin = table.clone()
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    stream = torch.cuda.current_stream()
+    for n, with_table in ((1800, True), (7, True), (5, False)):
+        src, dst = _moves(rng, n_pages, n)
+        rc = lib.rkv_apply_page_moves_static(byref(view), c_void_p(src.ctypes.data), c_void_p(dst.ctypes.data), n,
+                                             c_void_p(table.data_ptr() if with_table else 0),
+                                             table.numel() if with_table else 0, c_void_p(status.data_ptr()),
+                                             c_void_p(stream.cuda_stream))
+        assert rc == 0, _abi.last_error()
+        twin.copy_pages(torch.from_numpy(src).to(cuda), torch.from_numpy(dst).to(cuda))
+        if with_table:
+            remap = np.arange(n_pages, dtype=np.int32)
+            remap[src] = dst
+            rk.remap_pages(table_twin, torch.from_numpy(remap).to(cuda))
+        torch.cuda.synchronize()
+        twin.check("twin moves")
+        assert int(status.item()) == 0
+        assert torch.equal(table, table_twin), f"{n} moves: page tables differ"
+        assert torch.equal(mine, twin.storage), f"{n} moves: pool bytes differ"
