@@ -50,11 +50,13 @@ GATHER_ROW_BYTES = ROW_OUT + ROW_IN  # stored row read + bf16 row written
 L2_BYTES = 126 * 2**20
 GB = 1e9
 
-# DRAM bytes (read + write) per row from one ncu capture of each kernel
+# DRAM bytes (read + write) per row from ncu captures of each kernel
 # (profiles/append_quant_c2.md, gather_dequant_c3_small.md,
-# topk_sparse_c4_small.md).  The append's page writes drain from L2 after the
-# launch, so its figure is the bf16 input read: 17,997,824 B / 15,616 rows.
-NCU_TRAFFIC_PER_ROW = {"append": 17997824 / 15616, "gather": (176206080 + 248001536) / 262144,
+# topk_sparse_c4_small.md).  The append's figure is the mean over four
+# consecutive launches captured without cache control, so each launch carries
+# the previous launch's page writes draining from L2: 17,992,640 B read +
+# 8,241,600 B written per 15,616-row launch.
+NCU_TRAFFIC_PER_ROW = {"append": (17992640 + 8241600) / 15616, "gather": (176206080 + 248001536) / 262144,
                        "sparse_gather": (335133696 + 548617728) / 524288}
 
 
@@ -261,14 +263,23 @@ def bench_append(args, dist: Dist, dev, peak, n_seq: int = N_SEQ_APPEND, e2e: bo
     pool = rk.PagedKvPool(wl.n_pages, N_LAYERS, device=dev)
     pool.storage.zero_()
     stream = torch.cuda.Stream(device=dev)
+
+    def capture(inputs_ready: bool):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                for j in range(W, W + K):
+                    pool.append_layer(0, wl.rows[j], wl.slots[j], inputs_ready=inputs_ready)
+        return g
+
+    # the step's rows and slots exist before the previous step's append runs,
+    # so the append may read them while that launch drains (inputs ready)
     with torch.cuda.stream(stream):
         for j in range(W):
-            pool.append_layer(0, wl.rows[j], wl.slots[j])
-        pool.check("append warm-up", stream)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for j in range(W, W + K):
-                pool.append_layer(0, wl.rows[j], wl.slots[j])
+            pool.append_layer(0, wl.rows[j], wl.slots[j], inputs_ready=True)
+    pool.check("append warm-up", stream)
+    graph = capture(True)
+
     def replay():
         with torch.cuda.stream(stream):
             graph.replay()
@@ -292,6 +303,16 @@ def bench_append(args, dist: Dist, dev, peak, n_seq: int = N_SEQ_APPEND, e2e: bo
         dist.barrier()
         reps.append(dist.all(events_time(replay, stream)))
     del graph
+    # the same steps with every read after the wait on the previous launch
+    # (rkv_append_quant_bf16, for inputs a preceding kernel may still write)
+    graph = capture(False)
+    replay()
+    stream.synchronize()
+    flush_l2(dev)
+    dist.barrier()
+    wait_first = dist.max(events_time(replay, stream))
+    pool.check("append wait-first", stream)
+    del graph
     step_bytes = wl.bytes_per_step()
     res = {
         "ms_per_step": ms / K,
@@ -301,6 +322,8 @@ def bench_append(args, dist: Dist, dev, peak, n_seq: int = N_SEQ_APPEND, e2e: bo
         "per_rank_ms_per_step": [t / K for t in per_rank],
         "repeats_max_over_ranks_ms_per_step": [max(r) / K for r in reps],
         "repeats_median_rank_ms_per_step": [float(np.median(r)) / K for r in reps],
+        "wait_first_ms_per_step": wait_first / K,
+        "wait_first_gbs_per_gpu": step_bytes * K / (wait_first * 1e-3) / GB,
         "pool": pool,
         "wl": wl,
     }
@@ -354,8 +377,10 @@ def bench_append_e2e(wl: AppendWorkload, W: int, K: int, dist: Dist, dev) -> dic
     ones = np.ones(n_seq, np.int64)
     n_host = min(K, 8)
     host_rows = [wl.rows[W + j].cpu().pin_memory() for j in range(n_host)]
-    host_slots = torch.empty((steps, n_seq), dtype=torch.int32).pin_memory()
-    host_slots_np = host_slots.numpy()
+    # one pinned tensor per step: copies out of slices of one pinned tensor
+    # measured ~45% slower per step on this path
+    host_slots = [torch.empty(n_seq, dtype=torch.int32).pin_memory() for _ in range(steps)]
+    host_slots_np = [t.numpy() for t in host_slots]
     dev_rows = [torch.empty_like(wl.rows[0]) for _ in range(2)]
     dev_slots = [torch.empty(n_seq, dtype=torch.int32, device=dev) for _ in range(2)]
     status_host = torch.empty(steps, dtype=torch.int32).pin_memory()
@@ -368,7 +393,7 @@ def bench_append_e2e(wl: AppendWorkload, W: int, K: int, dist: Dist, dev) -> dic
                 pool.reserve(seqs, ones, stream=stream, out=host_slots_np[j])
                 dev_rows[b].copy_(host_rows[j % n_host], non_blocking=True)
                 dev_slots[b].copy_(host_slots[j], non_blocking=True)
-                kv.append_layer(0, dev_rows[b], dev_slots[b])
+                kv.append_layer(0, dev_rows[b], dev_slots[b], inputs_ready=True)  # filled by the copies above
                 status_host[j:j + 1].copy_(kv.status, non_blocking=True)
 
     run(0, W)  # warm-up steps
@@ -1447,18 +1472,22 @@ def main():
                        "parallelism": f"request-sharded x{dist.world}, no collective",
                        "l2": "inputs larger than L2 (fresh rows every step, 1.9 GB total) + L2 flush before timing",
                        "launch": "K steps captured in one CUDA graph (uploaded by an untimed replay); a sleep "
-                                 "kernel queued before the start event covers the host's graph launch"},
+                                 "kernel queued before the start event covers the host's graph launch; appends "
+                                 "with RKV_APPEND_INPUTS_READY (each step's rows exist before the previous step's "
+                                 "append, so its reads overlap that launch's drain; wait_first_* beside it)"},
             "tokens_per_s": app["tokens_per_s_per_gpu"] * dist.world,
             "rows_per_s": app["tokens_per_s_per_gpu"] * dist.world * N_LAYERS,
             "frac_of_hbm_peak_per_gpu": app["frac"],
             "per_rank_ms_per_step": app["per_rank_ms_per_step"],
             "repeats_max_over_ranks_ms_per_step": app["repeats_max_over_ranks_ms_per_step"],
             "repeats_median_rank_ms_per_step": app["repeats_median_rank_ms_per_step"],
+            "wait_first_ms_per_step": app["wait_first_ms_per_step"],
+            "wait_first_gbs_per_gpu": app["wait_first_gbs_per_gpu"],
             "parity": app["parity"],
             "roofline": {"bound": "hbm", "achieved": app["gbs_per_gpu"], "peak": peak, "unit": "GB/s",
                          "frac": app["frac"], "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                          if peak_kind == "measured" else "fallback 6650 GB/s",
-                         "kernel": "append_quant_kernel", "algorithmic_bytes_per_launch": app["step_bytes"],
+                         "kernel": "append_quant_early_kernel", "algorithmic_bytes_per_launch": app["step_bytes"],
                          "traffic": None if traffic is None else traffic * rows_per_launch},
             "cpu_baseline": cpu,
             "cpu_baseline_single_thread": cpu1,

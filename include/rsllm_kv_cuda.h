@@ -120,6 +120,23 @@ RKV_API rkv_status rkv_append_quant_bf16(const rkv_pool_view* pool, int32_t laye
                                  const uint16_t* rows, int64_t n_tokens, const int32_t* slot_mapping,
                                  uint32_t* d_status, rkv_stream_t stream);
 
+/* rkv_append_quant_bf16 with launch flags (same rsLLM items replaced, same
+ * arguments, status rules and stored bytes).  The append is launched with
+ * programmatic dependent launch, so it may start while the kernel issued just
+ * before it on `stream` is still running; it waits for that kernel before any
+ * write.  flags = 0 also waits before reading its inputs (what
+ * rkv_append_quant_bf16 does).  RKV_APPEND_INPUTS_READY lets it read `rows`
+ * and `slot_mapping` before that wait, overlapping the previous kernel's
+ * drain: set it only when no kernel that can still be running when this call
+ * starts writes them -- e.g. they came from host copies, from a kernel with a
+ * stream synchronisation, event wait or memcpy after it, or are rows a decode
+ * step prepared before the previous append.  Other flag bits:
+ * INVALID_ARGUMENT. */
+#define RKV_APPEND_INPUTS_READY 1u
+RKV_API rkv_status rkv_append_quant_bf16_ex(const rkv_pool_view* pool, int32_t layer0, int32_t n_layers_in,
+                                            const uint16_t* rows, int64_t n_tokens, const int32_t* slot_mapping,
+                                            uint32_t flags, uint32_t* d_status, rkv_stream_t stream);
+
 /* The same append for f32 rows, rsLLM's own row type: the arguments, status
  * rules and stored form of rkv_append_quant_bf16, with rows f32
  * [n_layers_in][n_tokens][576] (32-byte aligned).  The block exponent is

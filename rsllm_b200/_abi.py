@@ -70,6 +70,8 @@ SIGNATURES = {
     "rkv_status_from_bits": (c_int32, [c_uint32]),
     "rkv_pool_bytes": (c_int64, [c_int64, c_int32]),
     "rkv_append_quant_bf16": (c_int32, [_P(PoolView), c_int32, c_int32, _u16p, c_int64, _i32p, _u32p, c_void_p]),
+    "rkv_append_quant_bf16_ex": (c_int32, [_P(PoolView), c_int32, c_int32, _u16p, c_int64, _i32p, c_uint32, _u32p,
+                                           c_void_p]),
     "rkv_append_quant_f32": (c_int32, [_P(PoolView), c_int32, c_int32, _f32p, c_int64, _i32p, _u32p, c_void_p]),
     "rkv_scale_threshold_table": (None, [_u32p]),
     "rkv_gather_dequant_bf16": (c_int32, [_P(PoolView), c_int32, _i32p, c_int64, _i32p, c_int32, c_int32, _u16p,
@@ -126,6 +128,7 @@ SIGNATURES = {
                                               c_void_p]),
 }
 STATIC_MAX_MOVES = 262144
+APPEND_INPUTS_READY = 1
 
 _lib = None
 

@@ -97,6 +97,83 @@ append_quant_kernel(rkv_pool_view pool, int layer0, uint32_t n_tokens, uint32_t 
   }
 }
 
+// The same append for callers whose inputs are ready before the previous
+// kernel on the stream ends (RKV_APPEND_INPUTS_READY): each warp loads its
+// first two rows -- 32 B of latent and 4 B of RoPE per lane, and the slot --
+// BEFORE griddepcontrol.wait, so those reads overlap the previous kernel's
+// drain; every store stays after the wait.  Rows are taken two at a time
+// (r, r + W, then r + 2W, r + 3W, ...), each buffer refilled right after its
+// row is stored.  46 registers: five 256-thread CTAs per SM.
+constexpr int kEarlyRows = 2;
+
+__device__ __forceinline__ void append_row_rope4(const rkv_pool_view& pool, int layer, int32_t slot,
+                                                 const uint32_t (&lat)[8], uint32_t rope, uint32_t* status,
+                                                 int lane) {
+  const unsigned FULL = 0xffffffffu;
+  if (slot < 0) return;  // padding token
+  const int64_t page = slot >> 6;
+  const int off = slot & 63;
+  uint32_t m = absmax_bits16(lat);
+  m = max(m, __shfl_xor_sync(FULL, m, 1));
+  m = max(m, __shfl_xor_sync(FULL, m, 2));
+  if (page >= pool.n_pages) {
+    if (lane == 0) set_status(status, RKV_ERR_INDEX_OUT_OF_RANGE);
+    return;
+  }
+  if (__any_sync(FULL, m >= 0x7f80u)) {  // a non-finite latent lane rejects the row before any write
+    if (lane == 0) set_status(status, RKV_ERR_NON_FINITE_INPUT);
+    return;
+  }
+  const int e = scale_exponent_bf16bits(m);
+  const uint4 codes = quant16(lat, __uint_as_float((uint32_t)(127 - e) << 23));
+  uint8_t* pg = page_base(pool, layer, page);
+  st_stream16(pg + codes_off(off) + lane * 16, codes);
+  const float sc = __shfl_sync(FULL, __uint_as_float((uint32_t)(e + 127) << 23), (lane & 7) * 4);
+  if (lane < 8) reinterpret_cast<float*>(pg + scales_off(off))[lane] = sc;
+  st_stream4(pg + rope_off(off) + lane * 4, rope);
+}
+
+__device__ __forceinline__ void load_row_rope4(const uint8_t* rows8, const int32_t* slots, uint32_t r,
+                                               uint32_t n_tokens, int lane, uint32_t (&lat)[8], uint32_t& rope,
+                                               int32_t& slot) {
+  const uint8_t* row = rows8 + (size_t)r * (kRowDim * 2);
+  ld_stream32(row + lane * 32, lat);
+  rope = ld_stream4(row + 1024 + lane * 4);
+  slot = __ldg(slots + r % n_tokens);
+}
+
+__global__ void __launch_bounds__(kAppendWarps * 32, 5)
+append_quant_early_kernel(rkv_pool_view pool, int layer0, uint32_t n_tokens, uint32_t n_rows,
+                          const uint16_t* __restrict__ rows, const int32_t* __restrict__ slots,
+                          uint32_t* __restrict__ status) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int lane = threadIdx.x & 31;
+  const uint32_t stride = gridDim.x * kAppendWarps;
+  const uint32_t r0 = blockIdx.x * kAppendWarps + (threadIdx.x >> 5);
+  const uint8_t* rows8 = reinterpret_cast<const uint8_t*>(rows);
+  uint32_t lat[kEarlyRows][8];
+  uint32_t rope[kEarlyRows];
+  int32_t slot[kEarlyRows];
+#pragma unroll
+  for (int i = 0; i < kEarlyRows; ++i) {
+    rope[i] = 0;
+    slot[i] = -1;
+    if (r0 + i * stride < n_rows) load_row_rope4(rows8, slots, r0 + i * stride, n_tokens, lane, lat[i], rope[i], slot[i]);
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  for (uint32_t r = r0; r < n_rows; r += kEarlyRows * stride) {
+#pragma unroll
+    for (int i = 0; i < kEarlyRows; ++i) {
+      const uint32_t ri = r + i * stride;
+      if (ri < n_rows) {
+        append_row_rope4(pool, layer0 + (int)(ri / n_tokens), slot[i], lat[i], rope[i], status, lane);
+        const uint32_t rn = ri + kEarlyRows * stride;
+        if (rn < n_rows) load_row_rope4(rows8, slots, rn, n_tokens, lane, lat[i], rope[i], slot[i]);
+      }
+    }
+  }
+}
+
 // Exhaustive-check helper: the append kernel's lane conversion (packed
 // multiply by the inverse scale, here 1.0, -0.0 folded to +0.0, saturating RNE) applied to
 // raw f32 values that are already divided by their block scale.
@@ -111,36 +188,48 @@ __global__ void e4m3_code_range_kernel(uint32_t first, int64_t n, uint8_t* __res
 
 }  // namespace rkv
 
-extern "C" rkv_status rkv_append_quant_bf16(const rkv_pool_view* pool, int32_t layer0, int32_t n_layers_in,
-                                            const uint16_t* rows, int64_t n_tokens, const int32_t* slot_mapping,
-                                            uint32_t* d_status, rkv_stream_t stream) {
-  using namespace rkv;
-  rkv_status st = check_pool(pool, "rkv_append_quant_bf16");
+namespace rkv {
+
+// CTAs of `kernel` one wave holds on the current device (cached per device).
+template <typename Kernel>
+static int resident_ctas(Kernel kernel, std::atomic<int> (&cache)[kMaxDevicesCached]) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int resident = (dev >= 0 && dev < kMaxDevicesCached) ? cache[dev].load(std::memory_order_relaxed) : 0;
+  if (resident == 0) {
+    int sms = 0, per_sm = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kAppendWarps * 32, 0);
+    resident = (sms > 0 && per_sm > 0) ? sms * per_sm : 148 * 4;
+    if (dev >= 0 && dev < kMaxDevicesCached) cache[dev].store(resident, std::memory_order_relaxed);
+  }
+  return resident;
+}
+
+static std::atomic<int> g_resident_append[kMaxDevicesCached];
+static std::atomic<int> g_resident_append_early[kMaxDevicesCached];
+
+static rkv_status append_bf16(const rkv_pool_view* pool, int32_t layer0, int32_t n_layers_in, const uint16_t* rows,
+                              int64_t n_tokens, const int32_t* slot_mapping, uint32_t flags, uint32_t* d_status,
+                              rkv_stream_t stream, const char* what) {
+  rkv_status st = check_pool(pool, what);
   if (st != RKV_OK) return st;
+  if (flags & ~RKV_APPEND_INPUTS_READY) return fail(RKV_ERR_INVALID_ARGUMENT, "%s: unknown flags 0x%x", what, flags);
   if (layer0 < 0 || n_layers_in < 0 || (int64_t)layer0 + n_layers_in > pool->n_layers)
-    return fail(RKV_ERR_INVALID_LAYER, "rkv_append_quant_bf16: layers [%d, %d) outside pool of %d layers", layer0,
+    return fail(RKV_ERR_INVALID_LAYER, "%s: layers [%d, %d) outside pool of %d layers", what, layer0,
                 layer0 + n_layers_in, pool->n_layers);
-  if (n_tokens < 0) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_append_quant_bf16: n_tokens < 0");
+  if (n_tokens < 0) return fail(RKV_ERR_SHAPE_MISMATCH, "%s: n_tokens < 0", what);
   const int64_t n_rows = n_tokens * (int64_t)n_layers_in;
   if (n_rows == 0) {
     clear_error();
     return RKV_OK;
   }
-  if (n_rows > (int64_t)INT32_MAX) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_append_quant_bf16: too many rows in one call");
+  if (n_rows > (int64_t)INT32_MAX) return fail(RKV_ERR_SHAPE_MISMATCH, "%s: too many rows in one call", what);
   if (!rows || !aligned(rows, 32) || !slot_mapping || !aligned(slot_mapping, 4))
-    return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_append_quant_bf16: rows (32-byte aligned) and slot_mapping are required");
-  // CTAs of this kernel one wave holds on the current device (cached per device)
-  static std::atomic<int> resident_of[kMaxDevicesCached];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  int resident = (dev >= 0 && dev < kMaxDevicesCached) ? resident_of[dev].load(std::memory_order_relaxed) : 0;
-  if (resident == 0) {
-    int sms = 0, per_sm = 0;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, append_quant_kernel, kAppendWarps * 32, 0);
-    resident = (sms > 0 && per_sm > 0) ? sms * per_sm : 148 * 4;
-    if (dev >= 0 && dev < kMaxDevicesCached) resident_of[dev].store(resident, std::memory_order_relaxed);
-  }
+    return fail(RKV_ERR_INVALID_ARGUMENT, "%s: rows (32-byte aligned) and slot_mapping are required", what);
+  const bool early = (flags & RKV_APPEND_INPUTS_READY) != 0;
+  const int resident = early ? resident_ctas(append_quant_early_kernel, g_resident_append_early)
+                             : resident_ctas(append_quant_kernel, g_resident_append);
   const int64_t need = (n_rows + kAppendWarps - 1) / kAppendWarps;
   const unsigned grid = (unsigned)(need < resident ? need : resident);
   cudaLaunchConfig_t cfg = {};
@@ -153,10 +242,28 @@ extern "C" rkv_status rkv_append_quant_bf16(const rkv_pool_view* pool, int32_t l
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, append_quant_kernel, pool_copy(*pool), (int)layer0, (uint32_t)n_tokens,
-                                     (uint32_t)n_rows, rows, slot_mapping, d_status);
-  if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_append_quant_bf16: launch failed: %s", cudaGetErrorString(e));
-  return check_launch("rkv_append_quant_bf16");
+  cudaError_t e = early ? cudaLaunchKernelEx(&cfg, append_quant_early_kernel, pool_copy(*pool), (int)layer0,
+                                             (uint32_t)n_tokens, (uint32_t)n_rows, rows, slot_mapping, d_status)
+                        : cudaLaunchKernelEx(&cfg, append_quant_kernel, pool_copy(*pool), (int)layer0,
+                                             (uint32_t)n_tokens, (uint32_t)n_rows, rows, slot_mapping, d_status);
+  if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return check_launch(what);
+}
+
+}  // namespace rkv
+
+extern "C" rkv_status rkv_append_quant_bf16(const rkv_pool_view* pool, int32_t layer0, int32_t n_layers_in,
+                                            const uint16_t* rows, int64_t n_tokens, const int32_t* slot_mapping,
+                                            uint32_t* d_status, rkv_stream_t stream) {
+  return rkv::append_bf16(pool, layer0, n_layers_in, rows, n_tokens, slot_mapping, 0u, d_status, stream,
+                          "rkv_append_quant_bf16");
+}
+
+extern "C" rkv_status rkv_append_quant_bf16_ex(const rkv_pool_view* pool, int32_t layer0, int32_t n_layers_in,
+                                               const uint16_t* rows, int64_t n_tokens, const int32_t* slot_mapping,
+                                               uint32_t flags, uint32_t* d_status, rkv_stream_t stream) {
+  return rkv::append_bf16(pool, layer0, n_layers_in, rows, n_tokens, slot_mapping, flags, d_status, stream,
+                          "rkv_append_quant_bf16_ex");
 }
 
 extern "C" rkv_status rkv_e4m3fn_code_range(uint32_t first_bits, int64_t n, uint8_t* out, rkv_stream_t stream) {

@@ -165,11 +165,14 @@ class PagedKvPool:
 
     # -- quantize-on-append ---------------------------------------------------
     def append_layer(self, layer0: int, rows: torch.Tensor, slot_mapping: torch.Tensor,
-                     stream: torch.cuda.Stream | None = None) -> None:
+                     stream: torch.cuda.Stream | None = None, inputs_ready: bool = False) -> None:
         """Quantise bf16 or f32 rows ``[n_layers_in, n_tokens, 576]`` (or
         ``[n_tokens, 576]`` for one layer) into the slots ``slot_mapping``
         (int32 ``[n_tokens]``, shared by the layers; negative = skip).  f32
-        rows take the reference's log2f exponent and store RoPE as bf16."""
+        rows take the reference's log2f exponent and store RoPE as bf16.
+        ``inputs_ready`` (bf16 rows): no kernel that may still be running on
+        the stream writes ``rows`` or ``slot_mapping``, so the append may read
+        them while the previous kernel drains (RKV_APPEND_INPUTS_READY)."""
         f32 = rows.dtype == torch.float32
         _need(rows, torch.float32 if f32 else torch.bfloat16, "rows", self.device)
         _need(slot_mapping, torch.int32, "slot_mapping", self.device)
@@ -179,6 +182,11 @@ class PagedKvPool:
             raise ShapeMismatch(f"append_layer: rows must be [..., {ROW_DIM}], got {tuple(rows.shape)}")
         if slot_mapping.dim() != 1 or slot_mapping.shape[0] != rows.shape[1]:
             raise ShapeMismatch("append_layer: slot_mapping must be [n_tokens]")
+        if inputs_ready and not f32:
+            check(self.lib.rkv_append_quant_bf16_ex(byref(self.view), layer0, rows.shape[0], _ptr(rows), rows.shape[1],
+                                                    _ptr(slot_mapping), _abi.APPEND_INPUTS_READY, _ptr(self.status),
+                                                    _stream(stream)))
+            return
         fn = self.lib.rkv_append_quant_f32 if f32 else self.lib.rkv_append_quant_bf16
         check(fn(byref(self.view), layer0, rows.shape[0], _ptr(rows), rows.shape[1], _ptr(slot_mapping),
                  _ptr(self.status), _stream(stream)))

@@ -65,7 +65,11 @@ def fill(pool: rk.PagedKvPool, ref: np.ndarray, orc, pt: np.ndarray, ctx: int, p
     pool.check("fill")
 
 
-def test_config2_decode_steps(cuda, orc):
+@pytest.mark.parametrize("inputs_ready", [False, True], ids=["wait_first", "inputs_ready"])
+def test_config2_decode_steps(cuda, orc, inputs_ready):
+    """Both launch forms of the append: loads after the wait on the previous
+    kernel, and loads before it (RKV_APPEND_INPUTS_READY), the steps queued
+    back to back on one stream so each launch overlaps the one before."""
     n_seq, n_steps = 256, 3
     slots, n_pages, lens = synth.decode_slots(n_seq, n_steps, seed=3)
     pos = lens[None, :] + np.arange(n_steps)[:, None]
@@ -73,10 +77,14 @@ def test_config2_decode_steps(cuda, orc):
     pool = rk.PagedKvPool(n_pages, N_LAYERS, device=cuda)
     pool.storage.zero_()
     ref = orc.new_pool(n_pages, N_LAYERS)
+    rows = [synth.kv_rows(N_LAYERS * n_seq, seed=3000 + j, device=cuda).view(N_LAYERS, n_seq, 576)
+            for j in range(n_steps)]
+    d_slots = [i32(slots[j], cuda) for j in range(n_steps)]
+    torch.cuda.synchronize()
     for j in range(n_steps):
-        rows = synth.kv_rows(N_LAYERS * n_seq, seed=3000 + j, device=cuda).view(N_LAYERS, n_seq, 576)
-        pool.append_layer(0, rows, i32(slots[j], cuda))
-        st = orc.append_rows(ref, n_pages, N_LAYERS, 0, u16(rows), slots[j], n_threads=orc.threads())
+        pool.append_layer(0, rows[j], d_slots[j], inputs_ready=inputs_ready)
+    for j in range(n_steps):
+        st = orc.append_rows(ref, n_pages, N_LAYERS, 0, u16(rows[j]), slots[j], n_threads=orc.threads())
         assert st == 0
     pool.check("config 2 append")
     bad = same_bytes(pool.storage, ref)
