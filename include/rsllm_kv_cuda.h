@@ -90,6 +90,30 @@ RKV_API const char* rkv_version(void);
 /* Message of the last failing call on this host thread ("" if none). */
 RKV_API const char* rkv_last_error(void);
 
+/* The data of the last failing call on this host thread, in the fields of
+ * rsLLM's error variants (crates/rsllm-kvcache/src/lib.rs:28-70):
+ *   SHAPE_MISMATCH     -> ShapeMismatch { what, expected, actual }
+ *   INDEX_OUT_OF_RANGE -> IndexOutOfRange { what, idx, len }
+ *   INVALID_LAYER      -> InvalidLayer { idx, max }
+ *   POOL_FULL          -> CompressedPoolFull { cap } (cap in token rows)
+ *   NON_FINITE_INPUT   -> NonFiniteInput(what)
+ * A field that does not apply is -1 (what: "").  `row` is the first failing
+ * row or entry for errors the device detects (set by the rkv_*_diagnose
+ * calls below), else -1.  After a call that succeeded status is RKV_OK. */
+typedef struct rkv_err_info {
+  int32_t status;
+  int32_t reserved;
+  char what[48];
+  int64_t idx;
+  int64_t len;
+  int64_t expected;
+  int64_t actual;
+  int64_t max;
+  int64_t cap;
+  int64_t row;
+} rkv_err_info;
+RKV_API rkv_status rkv_last_error_info(rkv_err_info* out);
+
 /* Highest-priority status in a device status word (0 -> RKV_OK).  Priority:
  * INVALID_ARGUMENT, INVALID_LAYER, SHAPE_MISMATCH, INDEX_OUT_OF_RANGE,
  * POOL_FULL, NON_FINITE_INPUT. */
@@ -205,6 +229,37 @@ RKV_API rkv_status rkv_sparse_gather_dequant_bf16(const rkv_pool_view* pool, int
                                           const int32_t* seq_of_query, const int32_t* seq_lens,
                                           const int32_t* idx, int32_t n_q, int32_t k, uint16_t* out,
                                           uint32_t* d_status, rkv_stream_t stream);
+
+/* ---- data of device-detected errors -----------------------------------------
+ * The kernels above report a bad slot, page id or position, or a non-finite
+ * row, as a bit of the status word and skip the row.  After seeing such a
+ * bit a caller passes the same inputs to the matching call below: it re-runs
+ * the kernel's checks on the host over copies of them (synchronous on
+ * `stream`; for the error path), in the kernel's row order, and returns the
+ * first failure's status, filling `out` (may be NULL) and the thread's last
+ * error (rkv_last_error_info) with rsLLM's fields (IndexOutOfRange { what,
+ * idx, len }, crates/rsllm-kvcache/src/lib.rs:28-70; NonFiniteInput(what),
+ * crates/rsllm-backend-cpu/src/error.rs:33) and `row`, the failing row's
+ * index.  RKV_OK (out->status 0) when every row passes.
+ *   append:        row = layer_in * n_tokens + token; a slot >= n_pages * 64
+ *                  -> what "slot_mapping", idx = slot, len = n_pages * 64; a
+ *                  non-finite latent lane -> NON_FINITE_INPUT, what "rows",
+ *                  idx = the lane.
+ *   gather:        row = the first output row of the bad page; what
+ *                  "page_table", idx = page id, len = n_pages.
+ *   sparse gather: row = q * k + j; what "seq_of_query" (idx outside
+ *                  [0, n_seq)), "idx" (position >= seq_lens, len = seq_len)
+ *                  or "page_table" (idx = page id, len = n_pages). */
+RKV_API rkv_status rkv_append_diagnose_bf16(const rkv_pool_view* pool, int32_t layer0, int32_t n_layers_in,
+                                            const uint16_t* rows, int64_t n_tokens, const int32_t* slot_mapping,
+                                            rkv_err_info* out, rkv_stream_t stream);
+RKV_API rkv_status rkv_gather_diagnose(const rkv_pool_view* pool, const int32_t* page_table, int64_t pt_stride,
+                                       const int32_t* cu_seqlens, int32_t n_seq, rkv_err_info* out,
+                                       rkv_stream_t stream);
+RKV_API rkv_status rkv_sparse_gather_diagnose(const rkv_pool_view* pool, const int32_t* page_table,
+                                              int64_t pt_stride, const int32_t* seq_of_query,
+                                              const int32_t* seq_lens, int32_t n_seq, const int32_t* idx,
+                                              int32_t n_q, int32_t k, rkv_err_info* out, rkv_stream_t stream);
 
 /* ---- page moves: copy-on-write and compaction -------------------------------
  * No rsLLM implementation exists; the planned design is refcounted shared

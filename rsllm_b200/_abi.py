@@ -40,6 +40,19 @@ class PoolDesc(Structure):
     _fields_ = [("n_pages", c_int64), ("n_layers", c_int32), ("device", c_int32), ("storage", c_void_p)]
 
 
+class ErrInfo(Structure):
+    """rkv_err_info: the fields of rsLLM's error variants."""
+
+    _fields_ = [("status", c_int32), ("reserved", c_int32), ("what", ctypes.c_char * 48), ("idx", c_int64),
+                ("len", c_int64), ("expected", c_int64), ("actual", c_int64), ("max", c_int64), ("cap", c_int64),
+                ("row", c_int64)]
+
+    def as_dict(self) -> dict:
+        d = {f: getattr(self, f) for f, _ in self._fields_ if f != "reserved"}
+        d["what"] = self.what.decode("utf-8", "replace")
+        return d
+
+
 class PoolStats(Structure):
     """``rkv_pool_stats``."""
 
@@ -67,6 +80,12 @@ _u8p, _u16p, _u32p, _i32p, _f32p = c_void_p, c_void_p, c_void_p, c_void_p, c_voi
 SIGNATURES = {
     "rkv_version": (c_char_p, []),
     "rkv_last_error": (c_char_p, []),
+    "rkv_last_error_info": (c_int32, [c_void_p]),
+    "rkv_append_diagnose_bf16": (c_int32, [_P(PoolView), c_int32, c_int32, _u16p, c_int64, _i32p, c_void_p,
+                                           c_void_p]),
+    "rkv_gather_diagnose": (c_int32, [_P(PoolView), _i32p, c_int64, _i32p, c_int32, c_void_p, c_void_p]),
+    "rkv_sparse_gather_diagnose": (c_int32, [_P(PoolView), _i32p, c_int64, _i32p, _i32p, c_int32, _i32p, c_int32,
+                                             c_int32, c_void_p, c_void_p]),
     "rkv_status_from_bits": (c_int32, [c_uint32]),
     "rkv_pool_bytes": (c_int64, [c_int64, c_int32]),
     "rkv_append_quant_bf16": (c_int32, [_P(PoolView), c_int32, c_int32, _u16p, c_int64, _i32p, _u32p, c_void_p]),
@@ -155,6 +174,13 @@ def load() -> ctypes.CDLL:
 
 def last_error() -> str:
     return load().rkv_last_error().decode("utf-8", "replace")
+
+
+def last_error_info() -> dict:
+    """rkv_last_error_info as a dict (fields that do not apply are -1)."""
+    info = ErrInfo()
+    load().rkv_last_error_info(ctypes.byref(info))
+    return info.as_dict()
 
 
 def header_functions() -> list[str]:

@@ -9,16 +9,90 @@
 namespace rkv {
 
 static thread_local char g_last_error[512] = {0};
+static thread_local rkv_err_info g_last_info = {RKV_OK, 0, {0}, -1, -1, -1, -1, -1, -1, -1};
+
+rkv_err_info blank_info(rkv_status st) {
+  rkv_err_info e = {st, 0, {0}, -1, -1, -1, -1, -1, -1, -1};
+  return e;
+}
+
+static void set_what(rkv_err_info& e, const char* what) {
+  snprintf(e.what, sizeof(e.what), "%s", what ? what : "");
+}
+
+static rkv_status record(const rkv_err_info& info, const char* fmt, va_list ap) {
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  g_last_info = info;
+  return info.status;
+}
 
 rkv_status fail(rkv_status st, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
-  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  record(blank_info(st), fmt, ap);
   va_end(ap);
   return st;
 }
 
-void clear_error() { g_last_error[0] = 0; }
+rkv_status fail_shape(const char* what, int64_t expected, int64_t actual, const char* fmt, ...) {
+  rkv_err_info e = blank_info(RKV_ERR_SHAPE_MISMATCH);
+  set_what(e, what);
+  e.expected = expected;
+  e.actual = actual;
+  va_list ap;
+  va_start(ap, fmt);
+  record(e, fmt, ap);
+  va_end(ap);
+  return e.status;
+}
+
+rkv_status fail_index(const char* what, int64_t idx, int64_t len, const char* fmt, ...) {
+  rkv_err_info e = blank_info(RKV_ERR_INDEX_OUT_OF_RANGE);
+  set_what(e, what);
+  e.idx = idx;
+  e.len = len;
+  va_list ap;
+  va_start(ap, fmt);
+  record(e, fmt, ap);
+  va_end(ap);
+  return e.status;
+}
+
+rkv_status fail_layer(int64_t idx, int64_t max, const char* fmt, ...) {
+  rkv_err_info e = blank_info(RKV_ERR_INVALID_LAYER);
+  set_what(e, "layer");
+  e.idx = idx;
+  e.max = max;
+  va_list ap;
+  va_start(ap, fmt);
+  record(e, fmt, ap);
+  va_end(ap);
+  return e.status;
+}
+
+rkv_status fail_full(int64_t cap, const char* fmt, ...) {
+  rkv_err_info e = blank_info(RKV_ERR_POOL_FULL);
+  set_what(e, "pool");
+  e.cap = cap;
+  va_list ap;
+  va_start(ap, fmt);
+  record(e, fmt, ap);
+  va_end(ap);
+  return e.status;
+}
+
+rkv_status fail_info(const rkv_err_info& info, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  record(info, fmt, ap);
+  va_end(ap);
+  return info.status;
+}
+
+void clear_error() {
+  g_last_error[0] = 0;
+  g_last_info = blank_info(RKV_OK);
+}
 
 rkv_status check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
@@ -45,6 +119,12 @@ extern "C" {
 const char* rkv_version(void) { return "0.1.0"; }
 
 const char* rkv_last_error(void) { return rkv::g_last_error; }
+
+rkv_status rkv_last_error_info(rkv_err_info* out) {
+  if (!out) return RKV_ERR_INVALID_ARGUMENT;
+  *out = rkv::g_last_info;
+  return RKV_OK;
+}
 
 rkv_status rkv_status_from_bits(uint32_t bits) {
   static const rkv_status order[] = {RKV_ERR_INVALID_ARGUMENT, RKV_ERR_INVALID_LAYER,  RKV_ERR_SHAPE_MISMATCH,

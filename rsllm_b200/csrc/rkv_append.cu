@@ -216,15 +216,17 @@ static rkv_status append_bf16(const rkv_pool_view* pool, int32_t layer0, int32_t
   if (st != RKV_OK) return st;
   if (flags & ~RKV_APPEND_INPUTS_READY) return fail(RKV_ERR_INVALID_ARGUMENT, "%s: unknown flags 0x%x", what, flags);
   if (layer0 < 0 || n_layers_in < 0 || (int64_t)layer0 + n_layers_in > pool->n_layers)
-    return fail(RKV_ERR_INVALID_LAYER, "%s: layers [%d, %d) outside pool of %d layers", what, layer0,
-                layer0 + n_layers_in, pool->n_layers);
-  if (n_tokens < 0) return fail(RKV_ERR_SHAPE_MISMATCH, "%s: n_tokens < 0", what);
+    return fail_layer(layer0 < 0 || n_layers_in < 0 ? layer0 : (int64_t)layer0 + n_layers_in - 1, pool->n_layers,
+                      "%s: layers [%d, %d) outside pool of %d layers", what, layer0, layer0 + n_layers_in,
+                      pool->n_layers);
+  if (n_tokens < 0) return fail_shape("n_tokens", 0, n_tokens, "%s: n_tokens < 0", what);
   const int64_t n_rows = n_tokens * (int64_t)n_layers_in;
   if (n_rows == 0) {
     clear_error();
     return RKV_OK;
   }
-  if (n_rows > (int64_t)INT32_MAX) return fail(RKV_ERR_SHAPE_MISMATCH, "%s: too many rows in one call", what);
+  if (n_rows > (int64_t)INT32_MAX)
+    return fail_shape("rows", INT32_MAX, n_rows, "%s: too many rows in one call", what);
   if (!rows || !aligned(rows, 32) || !slot_mapping || !aligned(slot_mapping, 4))
     return fail(RKV_ERR_INVALID_ARGUMENT, "%s: rows (32-byte aligned) and slot_mapping are required", what);
   const bool early = (flags & RKV_APPEND_INPUTS_READY) != 0;

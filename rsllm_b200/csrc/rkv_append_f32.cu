@@ -93,15 +93,17 @@ extern "C" rkv_status rkv_append_quant_f32(const rkv_pool_view* pool, int32_t la
   rkv_status st = check_pool(pool, "rkv_append_quant_f32");
   if (st != RKV_OK) return st;
   if (layer0 < 0 || n_layers_in < 0 || (int64_t)layer0 + n_layers_in > pool->n_layers)
-    return fail(RKV_ERR_INVALID_LAYER, "rkv_append_quant_f32: layers [%d, %d) outside pool of %d layers", layer0,
-                layer0 + n_layers_in, pool->n_layers);
-  if (n_tokens < 0) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_append_quant_f32: n_tokens < 0");
+    return fail_layer(layer0 < 0 || n_layers_in < 0 ? layer0 : (int64_t)layer0 + n_layers_in - 1, pool->n_layers,
+                      "rkv_append_quant_f32: layers [%d, %d) outside pool of %d layers", layer0,
+                      layer0 + n_layers_in, pool->n_layers);
+  if (n_tokens < 0) return fail_shape("n_tokens", 0, n_tokens, "rkv_append_quant_f32: n_tokens < 0");
   const int64_t n_rows = n_tokens * (int64_t)n_layers_in;
   if (n_rows == 0) {
     clear_error();
     return RKV_OK;
   }
-  if (n_rows > (int64_t)INT32_MAX) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_append_quant_f32: too many rows in one call");
+  if (n_rows > (int64_t)INT32_MAX)
+    return fail_shape("rows", INT32_MAX, n_rows, "rkv_append_quant_f32: too many rows in one call");
   if (!rows || !aligned(rows, 32) || !slot_mapping || !aligned(slot_mapping, 4))
     return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_append_quant_f32: rows (32-byte aligned) and slot_mapping are required");
   const ThresholdTable& tab = f32_threshold_table();

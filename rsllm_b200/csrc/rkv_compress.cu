@@ -1362,13 +1362,15 @@ extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t lay
   rkv_status st = check_pool(pool, "rkv_compress_append");
   if (st != RKV_OK) return st;
   if (layer < 0 || layer >= pool->n_layers)
-    return fail(RKV_ERR_INVALID_LAYER, "rkv_compress_append: layer %d outside pool of %d layers", layer,
-                pool->n_layers);
+    return fail_layer(layer, pool->n_layers, "rkv_compress_append: layer %d outside pool of %d layers", layer,
+                      pool->n_layers);
   if (ratio <= 0 || ratio > kCmpMaxSources)
-    return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_compress_append: ratio %d outside [1, %d]", ratio, kCmpMaxSources);
+    return fail_shape("ratio", kCmpMaxSources, ratio, "rkv_compress_append: ratio %d outside [1, %d]", ratio,
+                      kCmpMaxSources);
   if (n_tok < 0 || n_states < 0 || rope_rows < 0)
     return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_compress_append: negative sizes");
-  if (n_tok > (int64_t)INT32_MAX) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_compress_append: too many tokens");
+  if (n_tok > (int64_t)INT32_MAX)
+    return fail_shape("n_tokens", INT32_MAX, n_tok, "rkv_compress_append: too many tokens");
   if (n_tok == 0) {
     clear_error();
     return RKV_OK;

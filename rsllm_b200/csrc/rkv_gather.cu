@@ -169,18 +169,21 @@ extern "C" rkv_status rkv_gather_dequant_bf16(const rkv_pool_view* pool, int32_t
   rkv_status st = check_pool(pool, "rkv_gather_dequant_bf16");
   if (st != RKV_OK) return st;
   if (layer < 0 || layer >= pool->n_layers)
-    return fail(RKV_ERR_INVALID_LAYER, "rkv_gather_dequant_bf16: layer %d outside pool of %d layers", layer,
-                pool->n_layers);
-  if (n_seq < 0 || max_seq_len < 0) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_gather_dequant_bf16: negative sizes");
+    return fail_layer(layer, pool->n_layers, "rkv_gather_dequant_bf16: layer %d outside pool of %d layers", layer,
+                      pool->n_layers);
+  if (n_seq < 0 || max_seq_len < 0)
+    return fail_shape(n_seq < 0 ? "n_seq" : "max_seq_len", 0, n_seq < 0 ? n_seq : max_seq_len,
+                      "rkv_gather_dequant_bf16: negative sizes");
   if (n_seq == 0 || max_seq_len == 0) {
     clear_error();
     return RKV_OK;
   }
   const int64_t pages = (max_seq_len + kPageTokens - 1) / kPageTokens;
   if (pt_stride < pages)
-    return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_gather_dequant_bf16: pt_stride %lld < %lld pages", (long long)pt_stride,
-                (long long)pages);
-  if (n_seq > 65535) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_gather_dequant_bf16: at most 65535 sequences per call");
+    return fail_shape("pt_stride", pages, pt_stride, "rkv_gather_dequant_bf16: pt_stride %lld < %lld pages",
+                      (long long)pt_stride, (long long)pages);
+  if (n_seq > 65535)
+    return fail_shape("n_seq", 65535, n_seq, "rkv_gather_dequant_bf16: at most 65535 sequences per call");
   if (!page_table || !cu_seqlens || !out || !aligned(out, 32))
     return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_gather_dequant_bf16: page_table, cu_seqlens and a 32-byte aligned out are required");
   dim3 grid((unsigned)pages, (unsigned)n_seq);
@@ -198,9 +201,10 @@ extern "C" rkv_status rkv_sparse_gather_dequant_bf16(const rkv_pool_view* pool, 
   rkv_status st = check_pool(pool, "rkv_sparse_gather_dequant_bf16");
   if (st != RKV_OK) return st;
   if (layer < 0 || layer >= pool->n_layers)
-    return fail(RKV_ERR_INVALID_LAYER, "rkv_sparse_gather_dequant_bf16: layer %d outside pool of %d layers", layer,
-                pool->n_layers);
-  if (n_q < 0 || k < 0) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_sparse_gather_dequant_bf16: negative sizes");
+    return fail_layer(layer, pool->n_layers, "rkv_sparse_gather_dequant_bf16: layer %d outside pool of %d layers",
+                      layer, pool->n_layers);
+  if (n_q < 0 || k < 0)
+    return fail_shape(n_q < 0 ? "n_q" : "k", 0, n_q < 0 ? n_q : k, "rkv_sparse_gather_dequant_bf16: negative sizes");
   const int64_t n_sel = (int64_t)n_q * k;
   if (n_sel == 0) {
     clear_error();
@@ -211,7 +215,7 @@ extern "C" rkv_status rkv_sparse_gather_dequant_bf16(const rkv_pool_view* pool, 
                 "rkv_sparse_gather_dequant_bf16: page_table, seq_of_query, seq_lens, idx and a 32-byte aligned out are required");
   const int64_t per_cta = (int64_t)kSparseWarps * kSparseRows;
   const int64_t grid = (n_sel + per_cta - 1) / per_cta;
-  if (grid > INT32_MAX) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_sparse_gather_dequant_bf16: too many rows");
+  if (grid > INT32_MAX) return fail_shape("idx", INT32_MAX, n_sel, "rkv_sparse_gather_dequant_bf16: too many rows");
   sparse_gather_dequant_kernel<<<(unsigned)grid, kSparseWarps * 32, 0, (cudaStream_t)stream>>>(
       *pool, layer, page_table, pt_stride, seq_of_query, seq_lens, idx, n_sel, k, out, d_status);
   return check_launch("rkv_sparse_gather_dequant_bf16");

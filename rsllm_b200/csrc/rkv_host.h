@@ -9,7 +9,20 @@
 namespace rkv {
 
 // Records a printf-style message as this thread's last error; returns `st`.
+// The error data (rkv_last_error_info) carries only the status.
 rkv_status fail(rkv_status st, const char* fmt, ...);
+
+// The same, with the data of rsLLM's error variant (rkv_err_info):
+// ShapeMismatch { what, expected, actual }, IndexOutOfRange { what, idx, len },
+// InvalidLayer { idx, max }, CompressedPoolFull { cap } (token rows).
+rkv_status fail_shape(const char* what, int64_t expected, int64_t actual, const char* fmt, ...);
+rkv_status fail_index(const char* what, int64_t idx, int64_t len, const char* fmt, ...);
+rkv_status fail_layer(int64_t idx, int64_t max, const char* fmt, ...);
+rkv_status fail_full(int64_t cap, const char* fmt, ...);
+// Records a device-detected error found by a diagnosis: `info` and a message.
+rkv_status fail_info(const rkv_err_info& info, const char* fmt, ...);
+// An rkv_err_info with status `st` and every field "does not apply".
+rkv_err_info blank_info(rkv_status st);
 
 // Clears this thread's last error (a call that succeeds leaves "" behind).
 void clear_error();

@@ -96,8 +96,8 @@ extern "C" rkv_status rkv_indexer_scores_f32(const float* rows, const int64_t* r
   if (n_q < 0 || max_visible < 0 || n_seq < 0)
     return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_indexer_scores_f32: negative sizes");
   if (ld < max_visible)
-    return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_indexer_scores_f32: ld %lld < max_visible %d", (long long)ld,
-                max_visible);
+    return fail_shape("ld", max_visible, ld, "rkv_indexer_scores_f32: ld %lld < max_visible %d", (long long)ld,
+                      max_visible);
   if (n_q == 0 || max_visible == 0) {
     clear_error();
     return RKV_OK;

@@ -214,8 +214,8 @@ rkv_status rkv_kvc_save(rkv_pool* pool, int64_t seq, const int32_t* token_ids, i
   rkv_status st = rkv_seq_info(pool, seq, &len, &n_seq_pages);
   if (st != RKV_OK) return st;
   if (len < n_tokens)
-    return fail(RKV_ERR_SHAPE_MISMATCH, "%s: sequence %lld holds %lld tokens, %lld requested", what, (long long)seq,
-                (long long)len, (long long)n_tokens);
+    return fail_shape("n_tokens", len, n_tokens, "%s: sequence %lld holds %lld tokens, %lld requested", what,
+                      (long long)seq, (long long)len, (long long)n_tokens);
   std::vector<int32_t> table((size_t)n_seq_pages);
   st = rkv_seq_page_table(pool, seq, table.data(), n_seq_pages);
   if (st != RKV_OK) return st;

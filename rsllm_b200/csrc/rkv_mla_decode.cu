@@ -733,8 +733,8 @@ extern "C" rkv_status rkv_mla_decode_fp8(const rkv_pool_view* pool, int32_t laye
   rkv_status st = check_pool(pool, "rkv_mla_decode_fp8");
   if (st != RKV_OK) return st;
   if (layer < 0 || layer >= pool->n_layers)
-    return fail(RKV_ERR_INVALID_LAYER, "rkv_mla_decode_fp8: layer %d outside pool of %d layers", layer,
-                pool->n_layers);
+    return fail_layer(layer, pool->n_layers, "rkv_mla_decode_fp8: layer %d outside pool of %d layers", layer,
+                      pool->n_layers);
   if (n_q < 0 || n_splits < 1 || n_splits > 65535 || pt_stride < 1 || (idx && (k < 0 || n_splits != 1)))
     return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_mla_decode_fp8: n_q >= 0, pt_stride >= 1, 1 <= n_splits <= 65535 "
                 "(1 with an index list) and k >= 0 are required");
@@ -742,7 +742,7 @@ extern "C" rkv_status rkv_mla_decode_fp8(const rkv_pool_view* pool, int32_t laye
     clear_error();
     return RKV_OK;
   }
-  if (n_q > 65535) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_mla_decode_fp8: at most 65535 queries per call");
+  if (n_q > 65535) return fail_shape("n_q", 65535, n_q, "rkv_mla_decode_fp8: at most 65535 queries per call");
   if (!page_table || !seq_lens || !seq_of_query || !q || !aligned(q, 16) || !out || !aligned(out, 16) ||
       (n_splits > 1 && (!workspace || !aligned(workspace, 16))) || (idx && k > 0 && !aligned(idx, 4)))
     return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_mla_decode_fp8: page_table, seq_lens, seq_of_query, q (16-byte "

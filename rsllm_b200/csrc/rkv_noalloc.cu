@@ -73,8 +73,9 @@ extern "C" rkv_status rkv_apply_page_moves_static(const rkv_pool_view* pool, con
   if (st != RKV_OK) return st;
   if (n_moves < 0 || n_entries < 0) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_apply_page_moves_static: negative sizes");
   if (n_moves > kStaticMaxMoves)
-    return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_apply_page_moves_static: %lld moves exceed the %lld this entry point stages",
-                (long long)n_moves, (long long)kStaticMaxMoves);
+    return fail_shape("n_moves", kStaticMaxMoves, n_moves,
+                      "rkv_apply_page_moves_static: %lld moves exceed the %lld this entry point stages",
+                      (long long)n_moves, (long long)kStaticMaxMoves);
   if (n_moves == 0) {
     clear_error();
     return RKV_OK;
@@ -83,8 +84,11 @@ extern "C" rkv_status rkv_apply_page_moves_static(const rkv_pool_view* pool, con
   for (int64_t i = 0; i < n_moves; ++i) {
     if (i > 0 && src[i] <= src[i - 1])
       return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_apply_page_moves_static: src must be strictly ascending");
-    if (src[i] < 0 || src[i] >= pool->n_pages || dst[i] < 0 || dst[i] >= pool->n_pages)
-      return fail(RKV_ERR_INDEX_OUT_OF_RANGE, "rkv_apply_page_moves_static: move %lld outside the pool", (long long)i);
+    if (src[i] < 0 || src[i] >= pool->n_pages || dst[i] < 0 || dst[i] >= pool->n_pages) {
+      const bool bad_src = src[i] < 0 || src[i] >= pool->n_pages;
+      return fail_index(bad_src ? "src" : "dst", bad_src ? src[i] : dst[i], pool->n_pages,
+                        "rkv_apply_page_moves_static: move %lld outside the pool", (long long)i);
+    }
   }
   for (int64_t i = 0; i < n_moves; ++i) {  // destinations must not be sources (copies run in parallel)
     const int32_t* hit = std::lower_bound(src, src + n_moves, dst[i]);

@@ -60,7 +60,7 @@ extern "C" rkv_status rkv_copy_pages(const rkv_pool_view* pool, const int32_t* s
   using namespace rkv;
   rkv_status st = check_pool(pool, "rkv_copy_pages");
   if (st != RKV_OK) return st;
-  if (n < 0) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_copy_pages: n < 0");
+  if (n < 0) return fail_shape("n", 0, n, "rkv_copy_pages: n < 0");
   if (n == 0) {
     clear_error();
     return RKV_OK;
@@ -126,8 +126,9 @@ static rkv_status stage_pages(bool pack, const rkv_pool_view* pool, int32_t laye
   rkv_status st = check_pool(pool, what);
   if (st != RKV_OK) return st;
   if (layer0 < 0 || n_layers < 0 || (int64_t)layer0 + n_layers > pool->n_layers)
-    return fail(RKV_ERR_INVALID_LAYER, "%s: layers [%d, %d) outside pool of %d layers", what, layer0, layer0 + n_layers,
-                pool->n_layers);
+    return fail_layer(layer0 < 0 || n_layers < 0 ? layer0 : (int64_t)layer0 + n_layers - 1, pool->n_layers,
+                      "%s: layers [%d, %d) outside pool of %d layers", what, layer0, layer0 + n_layers,
+                      pool->n_layers);
   if (n < 0 || n > INT32_MAX || n_layers > 65535) return fail(RKV_ERR_SHAPE_MISMATCH, "%s: bad page count", what);
   if (n == 0 || n_layers == 0) {
     clear_error();

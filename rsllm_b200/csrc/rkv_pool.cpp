@@ -375,10 +375,10 @@ rkv_status rkv_seq_fork(rkv_pool* P, int64_t parent, int64_t n_tokens, int64_t* 
   using namespace rkv;
   if (!P || !child) return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_seq_fork: pool and child are required");
   Seq* s = find_seq(P, parent);
-  if (!s) return fail(RKV_ERR_INDEX_OUT_OF_RANGE, "rkv_seq_fork: no sequence %lld", (long long)parent);
+  if (!s) return fail_index("seq", parent, -1, "rkv_seq_fork: no sequence %lld", (long long)parent);
   if (n_tokens < 0 || n_tokens > s->len)
-    return fail(RKV_ERR_INDEX_OUT_OF_RANGE, "rkv_seq_fork: %lld tokens of a %lld-token sequence", (long long)n_tokens,
-                (long long)s->len);
+    return fail_index("n_tokens", n_tokens, s->len + 1, "rkv_seq_fork: %lld tokens of a %lld-token sequence",
+                      (long long)n_tokens, (long long)s->len);
   std::vector<int32_t> pages(s->pages.begin(), s->pages.begin() + page_end(n_tokens));
   for (int32_t p : pages) P->incref(p);
   s->last_use = ++P->tick;
@@ -402,8 +402,8 @@ rkv_status rkv_seq_reserve(rkv_pool* P, int64_t n_seqs, const int64_t* seqs, con
   std::unordered_map<int64_t, int64_t> seen;
   for (int64_t i = 0; i < n_seqs; ++i) {
     Seq* s = find_seq(P, seqs[i]);
-    if (!s) return fail(RKV_ERR_INDEX_OUT_OF_RANGE, "rkv_seq_reserve: no sequence %lld", (long long)seqs[i]);
-    if (n_tokens[i] < 0) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_seq_reserve: negative token count");
+    if (!s) return fail_index("seq", seqs[i], -1, "rkv_seq_reserve: no sequence %lld", (long long)seqs[i]);
+    if (n_tokens[i] < 0) return fail_shape("n_tokens", 0, n_tokens[i], "rkv_seq_reserve: negative token count");
     if (!seen.emplace(seqs[i], i).second)
       return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_seq_reserve: sequence %lld listed twice", (long long)seqs[i]);
     const int64_t L = s->len;
@@ -411,8 +411,8 @@ rkv_status rkv_seq_reserve(rkv_pool* P, int64_t n_seqs, const int64_t* seqs, con
     need += (cow ? 1 : 0) + page_end(L + n_tokens[i]) - page_end(L);
   }
   if (need > P->free.count())
-    return fail(RKV_ERR_POOL_FULL, "rkv_seq_reserve: %lld pages needed, %lld free", (long long)need,
-                (long long)P->free.count());
+    return fail_full((int64_t)P->n_pages * kPageTokens, "rkv_seq_reserve: %lld pages needed, %lld free", (long long)need,
+                     (long long)P->free.count());
   int64_t off = 0;
   for (int64_t i = 0; i < n_seqs; ++i) {
     reserve(P, *find_seq(P, seqs[i]), n_tokens[i], slots ? slots + off : nullptr);
@@ -429,7 +429,7 @@ rkv_status rkv_seq_reserve(rkv_pool* P, int64_t n_seqs, const int64_t* seqs, con
 rkv_status rkv_seq_release(rkv_pool* P, int64_t seq) {
   if (!P) return rkv::fail(RKV_ERR_INVALID_ARGUMENT, "rkv_seq_release: pool is required");
   Seq* s = find_seq(P, seq);
-  if (!s) return rkv::fail(RKV_ERR_INDEX_OUT_OF_RANGE, "rkv_seq_release: no sequence %lld", (long long)seq);
+  if (!s) return rkv::fail_index("seq", seq, -1, "rkv_seq_release: no sequence %lld", (long long)seq);
   s->released = true;
   return RKV_OK;
 }
@@ -437,7 +437,7 @@ rkv_status rkv_seq_release(rkv_pool* P, int64_t seq) {
 rkv_status rkv_seq_touch(rkv_pool* P, int64_t seq) {
   if (!P) return rkv::fail(RKV_ERR_INVALID_ARGUMENT, "rkv_seq_touch: pool is required");
   Seq* s = find_seq(P, seq);
-  if (!s) return rkv::fail(RKV_ERR_INDEX_OUT_OF_RANGE, "rkv_seq_touch: no sequence %lld", (long long)seq);
+  if (!s) return rkv::fail_index("seq", seq, -1, "rkv_seq_touch: no sequence %lld", (long long)seq);
   s->last_use = ++P->tick;
   return RKV_OK;
 }
@@ -445,7 +445,7 @@ rkv_status rkv_seq_touch(rkv_pool* P, int64_t seq) {
 rkv_status rkv_seq_free(rkv_pool* P, int64_t seq) {
   if (!P) return rkv::fail(RKV_ERR_INVALID_ARGUMENT, "rkv_seq_free: pool is required");
   auto it = P->seqs.find(seq);
-  if (it == P->seqs.end()) return rkv::fail(RKV_ERR_INDEX_OUT_OF_RANGE, "rkv_seq_free: no sequence %lld", (long long)seq);
+  if (it == P->seqs.end()) return rkv::fail_index("seq", seq, -1, "rkv_seq_free: no sequence %lld", (long long)seq);
   drop_seq_pages(P, it->second, nullptr);
   P->seqs.erase(it);
   return RKV_OK;
@@ -454,7 +454,7 @@ rkv_status rkv_seq_free(rkv_pool* P, int64_t seq) {
 rkv_status rkv_seq_info(const rkv_pool* P, int64_t seq, int64_t* len, int64_t* n_pages) {
   if (!P) return rkv::fail(RKV_ERR_INVALID_ARGUMENT, "rkv_seq_info: pool is required");
   auto it = P->seqs.find(seq);
-  if (it == P->seqs.end()) return rkv::fail(RKV_ERR_INDEX_OUT_OF_RANGE, "rkv_seq_info: no sequence %lld", (long long)seq);
+  if (it == P->seqs.end()) return rkv::fail_index("seq", seq, -1, "rkv_seq_info: no sequence %lld", (long long)seq);
   if (len) *len = it->second.len;
   if (n_pages) *n_pages = (int64_t)it->second.pages.size();
   return RKV_OK;
@@ -464,11 +464,12 @@ rkv_status rkv_seq_page_table(const rkv_pool* P, int64_t seq, int32_t* out, int6
   if (!P) return rkv::fail(RKV_ERR_INVALID_ARGUMENT, "rkv_seq_page_table: pool is required");
   auto it = P->seqs.find(seq);
   if (it == P->seqs.end())
-    return rkv::fail(RKV_ERR_INDEX_OUT_OF_RANGE, "rkv_seq_page_table: no sequence %lld", (long long)seq);
+    return rkv::fail_index("seq", seq, -1, "rkv_seq_page_table: no sequence %lld", (long long)seq);
   const std::vector<int32_t>& pg = it->second.pages;
   if (pg.empty()) return RKV_OK;
   if (!out || cap < (int64_t)pg.size())
-    return rkv::fail(RKV_ERR_SHAPE_MISMATCH, "rkv_seq_page_table: need room for %lld pages", (long long)pg.size());
+    return rkv::fail_shape("out", (int64_t)pg.size(), out ? cap : 0, "rkv_seq_page_table: need room for %lld pages",
+                           (long long)pg.size());
   std::copy(pg.begin(), pg.end(), out);
   return RKV_OK;
 }
@@ -477,10 +478,10 @@ rkv_status rkv_prefix_insert(rkv_pool* P, const int32_t* tokens, int64_t n, int6
   using namespace rkv;
   if (!P || (n > 0 && !tokens)) return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_prefix_insert: pool and tokens are required");
   Seq* s = find_seq(P, seq);
-  if (!s) return fail(RKV_ERR_INDEX_OUT_OF_RANGE, "rkv_prefix_insert: no sequence %lld", (long long)seq);
+  if (!s) return fail_index("seq", seq, -1, "rkv_prefix_insert: no sequence %lld", (long long)seq);
   if (n < 0 || n > s->len)
-    return fail(RKV_ERR_INDEX_OUT_OF_RANGE, "rkv_prefix_insert: %lld tokens of a %lld-token sequence", (long long)n,
-                (long long)s->len);
+    return fail_index("n_tokens", n, s->len + 1, "rkv_prefix_insert: %lld tokens of a %lld-token sequence",
+                      (long long)n, (long long)s->len);
   const uint64_t now = ++P->tick;
   int32_t cur = 0;
   int64_t pos = 0;
@@ -658,7 +659,7 @@ rkv_status rkv_pool_take_moves(rkv_pool* P, int32_t* src, int32_t* dst, int64_t 
   *n = m;
   if (m == 0 || (!src && !dst)) return RKV_OK;  // count query
   if (!src || !dst || cap < m)
-    return rkv::fail(RKV_ERR_SHAPE_MISMATCH, "rkv_pool_take_moves: need room for %lld moves", (long long)m);
+    return rkv::fail_shape("src/dst", m, cap, "rkv_pool_take_moves: need room for %lld moves", (long long)m);
   std::copy(P->planned_src.begin(), P->planned_src.end(), src);
   std::copy(P->planned_dst.begin(), P->planned_dst.end(), dst);
   P->planned_src.clear();

@@ -687,8 +687,8 @@ extern "C" rkv_status rkv_topk_select_f32(const float* scores, int64_t ld, int32
   using namespace rkv;
   if (n_q < 0 || k < 0 || ld < 0 || n_keys_max < 0)
     return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_topk_select_f32: negative sizes");
-  if (k > kTopkMaxK) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_topk_select_f32: k %d > %d", k, kTopkMaxK);
-  if (n_keys_max > ld) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_topk_select_f32: n_keys_max > ld");
+  if (k > kTopkMaxK) return fail_shape("k", kTopkMaxK, k, "rkv_topk_select_f32: k %d > %d", k, kTopkMaxK);
+  if (n_keys_max > ld) return fail_shape("n_keys_max", ld, n_keys_max, "rkv_topk_select_f32: n_keys_max > ld");
   if (n_q == 0 || k == 0) {
     clear_error();
     return RKV_OK;

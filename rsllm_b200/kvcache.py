@@ -28,7 +28,23 @@ from ._abi import PAGE_BYTES, PAGE_TOKENS, ROW_DIM
 
 
 class KvError(RuntimeError):
+    """A failed call.  ``info`` holds rkv_last_error_info's fields, the data
+    of rsLLM's error variant: ``what``, ``idx``, ``len`` (IndexOutOfRange),
+    ``expected``, ``actual`` (ShapeMismatch), ``max`` (InvalidLayer), ``cap``
+    (CompressedPoolFull) and ``row`` (device-detected errors, from the
+    diagnose calls); -1 where a field does not apply."""
+
     status = -1
+
+    def __init__(self, msg: str = "", info: dict | None = None):
+        super().__init__(msg)
+        self.info = dict(info or {})
+
+    def __getattr__(self, name):
+        info = self.__dict__.get("info", {})
+        if name in info:
+            return info[name]
+        raise AttributeError(name)
 
 
 class ShapeMismatch(KvError):
@@ -64,10 +80,17 @@ ERRORS = {c.status: c for c in (ShapeMismatch, IndexOutOfRange, InvalidLayer, Po
 
 
 def check(rc: int, what: str = "") -> None:
-    """Raises the rsLLM-named error for a non-zero status."""
+    """Raises the rsLLM-named error for a non-zero status, with its data."""
     if rc != 0:
         msg = _abi.last_error() or what
-        raise ERRORS.get(rc, KvError)(msg)
+        raise ERRORS.get(rc, KvError)(msg, _abi.last_error_info())
+
+
+def raise_for_info(info: dict, what: str = "") -> None:
+    """Raises the error a diagnose call found (nothing if status is 0)."""
+    rc = int(info.get("status", 0))
+    if rc != 0:
+        raise ERRORS.get(rc, KvError)(f"{what}: {_abi.last_error()}" if what else _abi.last_error(), info)
 
 
 def raise_status_bits(bits: int, what: str) -> None:
@@ -190,6 +213,36 @@ class PagedKvPool:
         fn = self.lib.rkv_append_quant_f32 if f32 else self.lib.rkv_append_quant_bf16
         check(fn(byref(self.view), layer0, rows.shape[0], _ptr(rows), rows.shape[1], _ptr(slot_mapping),
                  _ptr(self.status), _stream(stream)))
+
+    # -- data of device-detected errors -------------------------------------------
+    def diagnose_append(self, layer0: int, rows: torch.Tensor, slot_mapping: torch.Tensor,
+                        stream: torch.cuda.Stream | None = None) -> dict:
+        """The first row of an append (same arguments) that the kernel
+        rejects, as rkv_append_diagnose_bf16 finds it: a dict of
+        rkv_err_info's fields, status 0 when every row passes."""
+        if rows.dim() == 2:
+            rows = rows.unsqueeze(0)
+        info = _abi.ErrInfo()
+        self.lib.rkv_append_diagnose_bf16(byref(self.view), layer0, rows.shape[0], _ptr(rows), rows.shape[1],
+                                          _ptr(slot_mapping), byref(info), _stream(stream))
+        return info.as_dict()
+
+    def diagnose_rows(self, page_table: torch.Tensor, cu_seqlens: torch.Tensor,
+                      stream: torch.cuda.Stream | None = None) -> dict:
+        """The first bad page of a gather (rkv_gather_diagnose)."""
+        info = _abi.ErrInfo()
+        self.lib.rkv_gather_diagnose(byref(self.view), _ptr(page_table), page_table.shape[1], _ptr(cu_seqlens),
+                                     page_table.shape[0], byref(info), _stream(stream))
+        return info.as_dict()
+
+    def diagnose_sparse_rows(self, page_table: torch.Tensor, seq_of_query: torch.Tensor, seq_lens: torch.Tensor,
+                             idx: torch.Tensor, stream: torch.cuda.Stream | None = None) -> dict:
+        """The first bad selection of a sparse gather (rkv_sparse_gather_diagnose)."""
+        info = _abi.ErrInfo()
+        self.lib.rkv_sparse_gather_diagnose(byref(self.view), _ptr(page_table), page_table.shape[1],
+                                            _ptr(seq_of_query), _ptr(seq_lens), seq_lens.shape[0], _ptr(idx),
+                                            idx.shape[0], idx.shape[1], byref(info), _stream(stream))
+        return info.as_dict()
 
     # -- reads ----------------------------------------------------------------
     def rows(self, layer: int, page_table: torch.Tensor, cu_seqlens: torch.Tensor, max_seq_len: int,
@@ -390,7 +443,7 @@ def pool_bytes(n_pages: int, n_layers: int) -> int:
 
 
 __all__ = [
-    "KvError", "ShapeMismatch", "IndexOutOfRange", "InvalidLayer", "PoolFull", "NonFiniteInput", "InvalidArgument",
+    "KvError", "raise_for_info", "ShapeMismatch", "IndexOutOfRange", "InvalidLayer", "PoolFull", "NonFiniteInput", "InvalidArgument",
     "CudaError", "BackendCapability", "CudaBackend", "PagedKvPool", "select_top_k", "indexer_scores",
     "indexer_select_top_k", "remap_pages",
     "e4m3fn_code_range", "pool_bytes", "PAGE_TOKENS", "PAGE_BYTES", "ROW_DIM",

@@ -84,7 +84,7 @@ class PrefixKvPool:
         n = np.ascontiguousarray(np.atleast_1d(n_tokens), dtype=np.int64)
         if s.shape != n.shape:
             raise ShapeMismatch("reserve: seqs and n_tokens differ in length")
-        total = int(n.sum())
+        total = int(n[n > 0].sum())  # a negative count is the C call's ShapeMismatch
         if out is None:
             slots = np.empty(total, np.int32)
         elif out.dtype != np.int32 or not out.flags["C_CONTIGUOUS"] or out.size != total:
