@@ -553,6 +553,28 @@ RKV_API rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t layer,
                                        const int32_t* pos, const int32_t* state_of_token, const int32_t* emit_slot,
                                        const float* ape, const float* norm, const float* rope_table,
                                        int64_t rope_rows, uint32_t* d_status, rkv_stream_t stream);
+/* The indexer pool's compressor step.  rsLLM runs compressor_decode_one a
+ * second time per token on its indexer pool (crates/rsllm-models/src/dsv4/
+ * attention.rs:405-429, head_dim 128): the same APE bias, window state,
+ * per-dimension softmax aggregate, RMSNorm (f64 sum of squares) and RoPE of
+ * the last 64 lanes as rkv_compress_append, on 128-lane rows (width =
+ * coff * 128), then a Hadamard + FP4 QAT of the row (compressor.rs:343-348)
+ * that this library does not restate.  Emitted rows are written as f32 to
+ * out_rows[emit_row[t]] (f32 [n_out_rows][128], e.g. the packed indexer rows
+ * rkv_indexer_scores_f32 reads; < 0 drops the row).  states:
+ * rkv_indexer_compress_state_bytes(ratio) bytes per state, same rules as
+ * rkv_compress_append; ape [ratio][width] or NULL; norm [128]; rope_table as
+ * for rkv_compress_append (the rotation does not depend on the row width).
+ * Device status: an out-of-range state, position, RoPE row or emit row sets
+ * INDEX_OUT_OF_RANGE and skips the token.  Bit-exact with rsLLM's f32/f64
+ * arithmetic up to the QAT step. */
+RKV_API int64_t rkv_indexer_compress_state_bytes(int32_t ratio);
+RKV_API rkv_status rkv_indexer_compress_append(int32_t ratio, float* states, int64_t n_states, const float* kv,
+                                               const float* score, int64_t n_tok, const int32_t* pos,
+                                               const int32_t* state_of_token, const int32_t* emit_row,
+                                               const float* ape, const float* norm, const float* rope_table,
+                                               int64_t rope_rows, float* out_rows, int64_t n_out_rows,
+                                               uint32_t* d_status, rkv_stream_t stream);
 /* expf as the compressor kernel evaluates it, on the host (host != 0, x and
  * out host memory) or on the current device (x, out device memory): a
  * double-precision exp rounded to f32, corrected from a table wherever the

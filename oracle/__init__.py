@@ -77,6 +77,8 @@ def lib() -> ctypes.CDLL:
         "rkvo_compress_append": (c_uint32, [P, c_int64, c_int32, c_int32, c_int32, P, P, P, c_int64, P, P, c_int64,
                                             P, P, P, P, P, c_int]),
         "rkvo_expf_batch": (None, [P, P, c_int64, c_int]),
+        "rkvo_indexer_compress_append": (c_uint32, [P, c_int64, c_int32, P, P, P, c_int64, P, P, c_int64, P, P, P,
+                                                    P, P, c_int]),
         "rkvo_indexer_score_row": (c_float, [P, P, P]),
         "rkvo_indexer_scores": (c_uint32, [P, P, P, c_int64, P, P, P, P, c_int32, P, c_int64, c_int]),
     }
@@ -344,6 +346,34 @@ def compress_append(pool: np.ndarray, n_pages: int, n_layers: int, layer: int, r
                                       skv.shape[0], _p(kv), _p(score), n_tok, _p(pos), _p(state_of),
                                       _p(emit_slot), None if ape is None else _p(ape), _p(norm),
                                       n_threads or threads())
+
+
+def indexer_compress_states(n_states: int, ratio: int, head_dim: int = 128):
+    """Reference-layout states of the indexer compressor: (kv, score, count)."""
+    coff = 2 if ratio == 4 else 1
+    shape = (n_states, coff * ratio, coff * head_dim)
+    return np.zeros(shape, np.float32), np.full(shape, -np.inf, np.float32), np.zeros(n_states, np.uint32)
+
+
+def indexer_compress_append(out_rows: np.ndarray, ratio: int, states, kv: np.ndarray, score: np.ndarray,
+                            pos: np.ndarray, state_of: np.ndarray, emit_row: np.ndarray, ape: np.ndarray | None,
+                            norm: np.ndarray, n_threads: int | None = None) -> int:
+    """The indexer pool's compressor step (128-lane rows) in token order over
+    the reference state machine; emitted rows (after RMSNorm and RoPE, before
+    the FP4 QAT) go to out_rows f32 [n_out_rows, 128]; returns status bits."""
+    skv, ssc, cnt = states
+    assert out_rows.dtype == np.float32 and out_rows.flags["C_CONTIGUOUS"] and out_rows.shape[1:] == (128,)
+    kv = np.ascontiguousarray(kv, np.float32)
+    score = np.ascontiguousarray(score, np.float32)
+    pos = np.ascontiguousarray(pos, np.int32)
+    state_of = np.ascontiguousarray(state_of, np.int32)
+    emit_row = np.ascontiguousarray(emit_row, np.int32)
+    norm = np.ascontiguousarray(norm, np.float32)
+    ape = None if ape is None else np.ascontiguousarray(ape, np.float32)
+    return lib().rkvo_indexer_compress_append(_p(out_rows), out_rows.shape[0], ratio, _p(skv), _p(ssc), _p(cnt),
+                                              skv.shape[0], _p(kv), _p(score), kv.shape[0], _p(pos), _p(state_of),
+                                              _p(emit_row), None if ape is None else _p(ape), _p(norm),
+                                              n_threads or threads())
 
 
 def expf(x: np.ndarray, n_threads: int | None = None) -> np.ndarray:

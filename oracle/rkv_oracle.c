@@ -1048,6 +1048,75 @@ uint32_t rkvo_compress_append(uint8_t* pool, int64_t n_pages, int32_t n_layers, 
     return st;
 }
 
+/* The indexer pool's compressor step (attention.rs:405-429 calls
+ * compressor_decode_one on the indexer pool, head_dim 128): the same APE
+ * bias, accumulate_wide / maybe_emit window (compressed.rs:310-417), per-
+ * dimension softmax aggregate (:481-554), RMSNorm with an f64 sum of squares
+ * and RoPE of the last 64 lanes at pos + 1 - ratio (compressor.rs:284-330),
+ * for 128-lane rows (kv, score [n_tok][coff*128]; ape [ratio][coff*128] or
+ * NULL; norm [128]).  The row emitted by token t is written as f32 to
+ * out_rows[emit_row[t]] (< 0: dropped; >= n_out_rows: INDEX_OUT_OF_RANGE),
+ * before the indexer's Hadamard + FP4 QAT step (compressor.rs:343-348), which
+ * is not restated here.  States [n_states][coff*ratio][coff*128]. */
+#define IDX_DIM 128
+typedef struct {
+    float* out_rows; int64_t n_out_rows; int32_t ratio;
+    float* state_kv; float* state_score; uint32_t* state_count; int64_t n_states;
+    const float* kv; const float* score; int64_t n_tok; const int32_t* pos; const int32_t* state_of;
+    const int32_t* emit_row; const float* ape; const float* norm;
+    int32_t t_id, n_workers; uint32_t status;
+} icmp_job;
+
+static void* icmp_worker(void* p) {
+    icmp_job* j = (icmp_job*)p;
+    int64_t coff = cmp_coff(j->ratio), width = coff * IDX_DIM, state_floats = coff * j->ratio * width;
+    float sc[2 * IDX_DIM];
+    float row[IDX_DIM];
+    for (int64_t t = 0; t < j->n_tok; ++t) {
+        int32_t s = j->state_of[t], pos = j->pos[t];
+        if (s < 0 || s >= j->n_states || pos < 0) { if (j->t_id == 0) j->status |= 1u << RKVO_INDEX_OUT_OF_RANGE; continue; }
+        if (s % j->n_workers != j->t_id) continue;
+        memcpy(sc, j->score + t * width, (size_t)width * 4);
+        if (j->ape)
+            for (int64_t c = 0; c < width; ++c) sc[c] += j->ape[(int64_t)(pos % j->ratio) * width + c];
+        if (!rkvo_compressor_accumulate(j->state_kv + s * state_floats, j->state_score + s * state_floats,
+                                        j->state_count + s, j->ratio, IDX_DIM, j->kv + t * width, sc, row))
+            continue;
+        int32_t r = j->emit_row[t];
+        if (r < 0) continue;
+        if (r >= j->n_out_rows) { j->status |= 1u << RKVO_INDEX_OUT_OF_RANGE; continue; }
+        uint32_t comp_pos = (uint32_t)pos + 1 >= (uint32_t)j->ratio ? (uint32_t)pos + 1 - (uint32_t)j->ratio : 0;
+        rkvo_compressor_postprocess(row, IDX_DIM, j->norm, comp_pos);
+        memcpy(j->out_rows + (int64_t)r * IDX_DIM, row, sizeof(row));
+    }
+    return NULL;
+}
+
+uint32_t rkvo_indexer_compress_append(float* out_rows, int64_t n_out_rows, int32_t ratio, float* state_kv,
+                                      float* state_score, uint32_t* state_count, int64_t n_states, const float* kv,
+                                      const float* score, int64_t n_tok, const int32_t* pos, const int32_t* state_of,
+                                      const int32_t* emit_row, const float* ape, const float* norm, int n_threads) {
+    if (n_tok <= 0) return 0;
+    if (ratio <= 0 || cmp_coff(ratio) * ratio > 128) return 1u << RKVO_SHAPE_MISMATCH;
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > 256) n_threads = 256;
+    if (n_states > 0 && n_threads > n_states) n_threads = (int)n_states;
+    pthread_t th[256];
+    icmp_job jobs[256];
+    for (int t = 0; t < n_threads; ++t) {
+        jobs[t] = (icmp_job){out_rows, n_out_rows, ratio, state_kv, state_score, state_count, n_states, kv, score,
+                             n_tok, pos, state_of, emit_row, ape, norm, t, n_threads, 0};
+        if (n_threads == 1) icmp_worker(&jobs[t]);
+        else pthread_create(&th[t], NULL, icmp_worker, &jobs[t]);
+    }
+    uint32_t st = 0;
+    for (int t = 0; t < n_threads; ++t) {
+        if (n_threads > 1) pthread_join(th[t], NULL);
+        st |= jobs[t].status;
+    }
+    return st;
+}
+
 /* The host libm's expf over an array (the reference's f32::exp), for checking
  * the product's expf rounding exhaustively. */
 typedef struct { const float* x; float* out; int64_t b, e; } expf_job;

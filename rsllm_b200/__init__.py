@@ -9,4 +9,5 @@ ABI in ``include/rsllm_kv_cuda.h``.  ``rsllm_b200.kvcache`` and
 """
 from .kvcache import *  # noqa: F401,F403
 from .kvcache import __all__  # noqa: F401
-from .compressor import CompressorBank, compress_expf, compress_expf_table_size, compress_rope_table  # noqa: F401
+from .compressor import (CompressorBank, IndexerCompressorBank, compress_expf, compress_expf_table_size,  # noqa: F401
+                         compress_rope_table)

@@ -112,6 +112,9 @@ SIGNATURES = {
     "rkv_mla_decode_fp8": (c_int32, [_P(PoolView), c_int32, _i32p, c_int64, _i32p, _i32p, _u16p, c_int32, _i32p,
                                      c_int32, _f32p, c_float, c_int32, c_void_p, _f32p, _u32p, c_void_p]),
     "rkv_compress_state_bytes": (c_int64, [c_int32]),
+    "rkv_indexer_compress_state_bytes": (c_int64, [c_int32]),
+    "rkv_indexer_compress_append": (c_int32, [c_int32, _f32p, c_int64, _f32p, _f32p, c_int64, _i32p, _i32p, _i32p,
+                                              _f32p, _f32p, _f32p, c_int64, _f32p, c_int64, _u32p, c_void_p]),
     "rkv_compress_rope_table": (c_int32, [c_int32, c_int64, _f32p]),
     "rkv_compress_prepare": (c_int32, []),
     "rkv_compress_wait_probe": (c_int32, [_u32p, c_void_p]),

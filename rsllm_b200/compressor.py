@@ -28,7 +28,10 @@ from . import _abi
 from ._abi import ROW_DIM
 from .kvcache import PagedKvPool, ShapeMismatch, _need, _ptr, _stream, check
 
-__all__ = ["CompressorBank", "compress_rope_table", "compress_expf", "compress_expf_table_size"]
+__all__ = ["CompressorBank", "IndexerCompressorBank", "compress_rope_table", "compress_expf",
+           "compress_expf_table_size"]
+
+INDEXER_HEAD_DIM = 128  # rsLLM's DSV4_N_INDEXER_HEAD_DIM
 
 
 def compress_rope_table(ratio: int, n_rows: int) -> np.ndarray:
@@ -117,3 +120,72 @@ class CompressorBank:
                                            _ptr(emit_slot), _ptr(ape), _ptr(norm), _ptr(self.rope),
                                            self.rope.shape[0], _ptr(pool.status), _stream(stream)),
               "CompressorBank.append")
+
+
+class IndexerCompressorBank:
+    """Window states of the indexer pool's compressors (128-lane rows; rsLLM
+    runs compressor_decode_one on its indexer pool too, attention.rs:405-429).
+    ``append`` aggregates, RMS-normalises and rotates each emitted row like
+    ``CompressorBank`` and writes it as f32 into a row buffer (the rows
+    ``indexer_scores`` reads), stopping before rsLLM's Hadamard + FP4 QAT of
+    the indexer row (compressor.rs:343-348), which this library does not
+    restate."""
+
+    def __init__(self, ratio: int, n_states: int, device: int | str | torch.device | None = None,
+                 max_positions: int = 1 << 17):
+        coff = 2 if ratio == 4 else 1
+        if ratio <= 0 or coff * ratio > 128:
+            raise ShapeMismatch(f"IndexerCompressorBank: ratio {ratio} outside [1, 128]")
+        self.lib = _abi.load()
+        dev = torch.device("cuda", device) if isinstance(device, int) else \
+            torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
+        self.ratio, self.coff = ratio, coff
+        self.width = coff * INDEXER_HEAD_DIM
+        self.n_states = n_states
+        nbytes = int(self.lib.rkv_indexer_compress_state_bytes(ratio))
+        self.states = torch.zeros((n_states, nbytes // 4), dtype=torch.float32, device=self.device)
+        rows = max_positions // ratio + 1
+        self.rope = torch.from_numpy(compress_rope_table(ratio, rows)).to(self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        with torch.cuda.device(self.device):
+            check(self.lib.rkv_compress_prepare(), "IndexerCompressorBank")
+
+    def append(self, out_rows: torch.Tensor, kv: torch.Tensor, score: torch.Tensor, pos: torch.Tensor,
+               state_of_token: torch.Tensor, emit_row: torch.Tensor, norm: torch.Tensor,
+               ape: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> None:
+        """One indexer compressor step for ``n_tok`` tokens
+        (``rkv_indexer_compress_append``): kv, score f32 [n_tok, width]; pos,
+        state_of_token, emit_row int32 [n_tok]; norm f32 [128]; ape f32
+        [ratio, width] or None; a token with (pos + 1) % ratio == 0 writes its
+        row to ``out_rows[emit_row]`` (f32 [n_rows, 128]; < 0: dropped).
+        Device-side errors land in ``self.status``."""
+        for t, n in ((kv, "kv"), (score, "score"), (norm, "norm"), (out_rows, "out_rows")):
+            _need(t, torch.float32, n, self.device)
+        for t, n in ((pos, "pos"), (state_of_token, "state_of_token"), (emit_row, "emit_row")):
+            _need(t, torch.int32, n, self.device)
+        n_tok = kv.shape[0] if kv.dim() == 2 else -1
+        if kv.dim() != 2 or kv.shape[1] != self.width or score.shape != kv.shape or \
+                pos.shape != (n_tok,) or state_of_token.shape != (n_tok,) or emit_row.shape != (n_tok,) or \
+                norm.shape != (INDEXER_HEAD_DIM,) or out_rows.dim() != 2 or out_rows.shape[1] != INDEXER_HEAD_DIM:
+            raise ShapeMismatch(f"IndexerCompressorBank.append: kv/score [n_tok, {self.width}], pos/state_of_token/"
+                                f"emit_row [n_tok], norm [128], out_rows [n_rows, 128]")
+        if ape is not None:
+            _need(ape, torch.float32, "ape", self.device)
+            if ape.shape != (self.ratio, self.width):
+                raise ShapeMismatch(f"IndexerCompressorBank.append: ape must be [{self.ratio}, {self.width}]")
+        check(self.lib.rkv_indexer_compress_append(self.ratio, _ptr(self.states), self.n_states, _ptr(kv),
+                                                   _ptr(score), n_tok, _ptr(pos), _ptr(state_of_token),
+                                                   _ptr(emit_row), _ptr(ape), _ptr(norm), _ptr(self.rope),
+                                                   self.rope.shape[0], _ptr(out_rows), out_rows.shape[0],
+                                                   _ptr(self.status), _stream(stream)),
+              "IndexerCompressorBank.append")
+
+    def take_status(self, stream: torch.cuda.Stream | None = None) -> int:
+        """Synchronises, returns and clears the device status bits."""
+        (stream or torch.cuda.current_stream()).synchronize()
+        bits = int(self.status.item()) & 0xFFFFFFFF
+        self.status.zero_()
+        return bits

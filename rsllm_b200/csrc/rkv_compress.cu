@@ -381,6 +381,9 @@ constexpr int kRingWarps = 8;        // ring kernel: warps per CTA
 struct CmpArgs {
   rkv_pool_view pool;
   int layer, ratio, coff, cr, width;
+  int hd;                 // lanes of a compressed row: 576 (attention pool) or 128 (indexer pool)
+  float* out_rows;        // indexer pool: f32 [n_out_rows][128] emitted rows
+  int64_t n_out_rows;
   float* states;
   int64_t n_states, n_tok, rope_rows;
   const float* kv;
@@ -495,7 +498,7 @@ __device__ __forceinline__ float aggregate_dim(const CmpArgs& a, const ExpConsts
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       load_src(s_ptr[r], j, kp[r], x[2 * r]);
-      load_src(s_ptr[4 + r], kRowF + j, kc[r], x[2 * r + 1]);
+      load_src(s_ptr[4 + r], a.hd + j, kc[r], x[2 * r + 1]);
     }
     float m = -INFINITY;
 #pragma unroll
@@ -798,6 +801,122 @@ compress_ring_kernel(const CmpArgs a) {
     for (uint32_t bits = __ballot_sync(FULL, deferred); bits; bits &= bits - 1) {
       const int L = __ffs(bits) - 1;
       copy_ring_rows(a, t0 + L, __shfl_sync(FULL, p, L), __shfl_sync(FULL, s, L), lane, 32);
+    }
+  }
+}
+
+// ---- the indexer pool's emission (128-lane rows) ------------------------------------
+//
+// rsLLM runs the same compressor step on its indexer pool (attention.rs:405-429,
+// compressor_decode_one with head_dim 128): the aggregate, then RMSNorm and the
+// rotation of the last 64 lanes, then a Hadamard + FP4 QAT of the row
+// (compressor.rs:343-348) that this library does not restate.  The rows go to
+// an f32 row buffer (the rows rkv_indexer_scores_f32 reads) instead of the FP8
+// pool.  One CTA of 128 threads per token group, one output dimension per
+// thread, the window rows resolved and read as in compress_emit_kernel.
+
+constexpr int kIdxDim = 128;
+constexpr int kIdxWarps = kIdxDim / 32;
+
+__global__ void __launch_bounds__(kIdxDim)
+indexer_emit_kernel(const CmpArgs a, const ExpConsts K) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  __shared__ double s_T[1 << kExpTableBits];
+  __shared__ SrcPtr s_ptr[kCmpMaxSources];
+  __shared__ int4 s_tok[kCmpMaxSources];
+  __shared__ uint32_t s_bal[2][kCmpMaxSources / 32];
+  __shared__ double s_sq[kIdxDim];
+  __shared__ double s_part[kIdxWarps];
+  __shared__ double s_ss;
+  load_exp_table(s_T);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const unsigned FULL = 0xffffffffu;
+  const int tid = threadIdx.x, j = tid, lane = tid & 31, w = tid >> 5;
+  const float wn = __ldg(a.norm + j);
+  const int n_bal = (a.ratio + 31) >> 5;
+  const int64_t n_groups = (a.n_tok + a.ratio - 1) / a.ratio;
+  for (int64_t g = blockIdx.x; g < n_groups; g += gridDim.x) {
+    __syncthreads();  // the previous group's s_tok and s_bal are consumed
+    if (w < n_bal) {
+      const int64_t t = g * a.ratio + tid;
+      bool em = false, rg = false;
+      if (tid < a.ratio && t < a.n_tok) {
+        const int p = __ldg(a.pos + t), s = __ldg(a.state_of + t), row = __ldg(a.emit_slot + t);
+        if (p < 0 || s < 0 || (int64_t)s >= a.n_states) {
+          set_status(a.status, RKV_ERR_INDEX_OUT_OF_RANGE);
+        } else {
+          if ((p + 1) % a.ratio == 0 && row >= 0) {
+            if ((int64_t)((p + 1) / a.ratio - 1) >= a.rope_rows || (int64_t)row >= a.n_out_rows)
+              set_status(a.status, RKV_ERR_INDEX_OUT_OF_RANGE);
+            else
+              em = true;
+          }
+          rg = ring_written(a, t, s) && ring_write_now(a, t, s);
+          s_tok[tid] = make_int4(p, s, row, 0);
+        }
+      }
+      const uint32_t be = __ballot_sync(FULL, em), br = __ballot_sync(FULL, rg);
+      if (lane == 0) {
+        s_bal[0][w] = be;
+        s_bal[1][w] = br;
+      }
+    }
+    __syncthreads();
+    for (int b = 0; b < n_bal; ++b) {
+      for (uint32_t bits = s_bal[0][b]; bits; bits &= bits - 1) {
+        const int tl = 32 * b + __ffs(bits) - 1;
+        const int64_t t = g * a.ratio + tl;
+        const int4 tk = s_tok[tl];
+        const int p = tk.x, s = tk.y, row = tk.z;
+        const int q0 = p + 1 - a.cr;
+        if (tid < a.cr) s_ptr[tid] = source_ptr(a, source_of(a, t, p, s, q0 + tid), s, q0 + tid);
+        __syncthreads();
+        const float out = aggregate_dim(a, K, s_T, s_ptr, j);
+        // RMSNorm (compressor.rs:292-296): the f64 sum of squares as a tree,
+        // or in rsLLM's order where the two could round to different means
+        // (see kSumMargin; the 128-lane sums are even closer), then the mean
+        // rounded to f32, 1/sqrt(mean + 1e-6) and (v * rms) * w
+        const double dv = (double)out;
+        const double sq = __dmul_rn(dv, dv);
+        s_sq[j] = sq;
+        double ws = sq;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ws = __dadd_rn(ws, __shfl_xor_sync(FULL, ws, o));
+        if (lane == 0) s_part[w] = ws;
+        __syncthreads();
+        double ss = lane < kIdxWarps ? s_part[lane] : 0.0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(FULL, ss, o));
+        double qd = __dmul_rn(ss, 1.0 / (double)kIdxDim);  // exact: a power of two
+        if (!(qd >= 0x1p-125 && qd < 0x1p127) || exp_mid_dist(qd) <= kSumMargin) {  // uniform over the CTA
+          if (j == 0) {
+            double s2 = 0.0;
+#pragma unroll 16
+            for (int i = 0; i < kIdxDim; ++i) s2 = __dadd_rn(s2, s_sq[i]);
+            s_ss = s2;
+          }
+          __syncthreads();
+          qd = __ddiv_rn(s_ss, (double)kIdxDim);
+        }
+        const float mean = __double2float_rn(qd);
+        const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
+        float v = __fmul_rn(__fmul_rn(out, rms), wn);
+        if (w >= (kIdxDim - 64) / 32) {  // the 64 tail lanes: RoPE pairs (j, j ^ 1), warp-uniform
+          const float* cs = a.rope + (int64_t)((p + 1) / a.ratio - 1) * 64 + ((j - (kIdxDim - 64)) & ~1);
+          const float c = __ldg(cs), sn = __ldg(cs + 1);
+          const float other = __shfl_xor_sync(FULL, v, 1);
+          v = (j & 1) ? __fadd_rn(__fmul_rn(other, sn), __fmul_rn(v, c))
+                      : __fsub_rn(__fmul_rn(v, c), __fmul_rn(other, sn));
+        }
+        a.out_rows[(int64_t)row * kIdxDim + j] = v;
+        __syncthreads();  // s_ptr, s_sq and s_part are reused by the next emission
+      }
+    }
+    for (int b = 0; b < n_bal; ++b) {
+      for (uint32_t bits = s_bal[1][b]; bits; bits &= bits - 1) {
+        const int tl = 32 * b + __ffs(bits) - 1;
+        copy_ring_rows(a, g * a.ratio + tl, s_tok[tl].x, s_tok[tl].y, tid, kIdxDim);
+      }
     }
   }
 }
@@ -1389,6 +1508,9 @@ extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t lay
   a.coff = coff_of(ratio);
   a.cr = a.coff * ratio;
   a.width = a.coff * kRowF;
+  a.hd = kRowF;
+  a.out_rows = nullptr;
+  a.n_out_rows = 0;
   a.states = states;
   a.n_states = n_states;
   a.n_tok = n_tok;
@@ -1446,4 +1568,84 @@ extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t lay
   e = cudaLaunchKernelEx(&cfg, compress_ring_kernel, a);
   if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_compress_append: launch failed: %s", cudaGetErrorString(e));
   return check_launch("rkv_compress_append");
+}
+
+extern "C" int64_t rkv_indexer_compress_state_bytes(int32_t ratio) {
+  if (ratio <= 0 || ratio > rkv::kCmpMaxSources) return -1;
+  const int coff = rkv::coff_of(ratio);
+  if (coff * ratio > rkv::kCmpMaxSources) return -1;
+  return (int64_t)2 * coff * ratio * coff * rkv::kIdxDim * 4;
+}
+
+extern "C" rkv_status rkv_indexer_compress_append(int32_t ratio, float* states, int64_t n_states, const float* kv,
+                                                  const float* score, int64_t n_tok, const int32_t* pos,
+                                                  const int32_t* state_of_token, const int32_t* emit_row,
+                                                  const float* ape, const float* norm, const float* rope_table,
+                                                  int64_t rope_rows, float* out_rows, int64_t n_out_rows,
+                                                  uint32_t* d_status, rkv_stream_t stream) {
+  using namespace rkv;
+  const char* what = "rkv_indexer_compress_append";
+  if (ratio <= 0 || coff_of(ratio) * ratio > kCmpMaxSources)
+    return fail_shape("ratio", kCmpMaxSources, ratio, "%s: ratio %d outside [1, %d]", what, ratio, kCmpMaxSources);
+  if (n_tok < 0 || n_states < 0 || rope_rows < 0 || n_out_rows < 0)
+    return fail(RKV_ERR_SHAPE_MISMATCH, "%s: negative sizes", what);
+  if (n_tok > (int64_t)INT32_MAX) return fail_shape("n_tokens", INT32_MAX, n_tok, "%s: too many tokens", what);
+  if (n_tok == 0) {
+    clear_error();
+    return RKV_OK;
+  }
+  if (!states || !aligned(states, 16) || !kv || !aligned(kv, 16) || !score || !aligned(score, 16) || !pos ||
+      !state_of_token || !emit_row || !norm || !rope_table || (ape && !aligned(ape, 16)) || !out_rows ||
+      !d_status)
+    return fail(RKV_ERR_INVALID_ARGUMENT,
+                "%s: states, kv, score, ape (16-byte aligned), pos, state_of_token, emit_row, norm, rope_table, "
+                "out_rows and d_status are required", what);
+  rkv_status st = prepare_device(what);
+  if (st != RKV_OK) return st;
+  CmpArgs a = {};
+  a.ratio = ratio;
+  a.coff = coff_of(ratio);
+  a.cr = a.coff * ratio;
+  a.width = a.coff * kIdxDim;
+  a.hd = kIdxDim;
+  a.out_rows = out_rows;
+  a.n_out_rows = n_out_rows;
+  a.states = states;
+  a.n_states = n_states;
+  a.n_tok = n_tok;
+  a.rope_rows = rope_rows;
+  a.kv = kv;
+  a.score = score;
+  a.pos = pos;
+  a.state_of = state_of_token;
+  a.emit_slot = emit_row;
+  a.ape = ape;
+  a.norm = norm;
+  a.rope = rope_table;
+  a.status = d_status;
+  const ExpConsts K = exp_host()->K;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // 1. emissions (one 128-thread CTA per token group, many per SM) and the
+  // ring writes allowed alongside them; 2. the deferred ring writes
+  const int64_t groups = (n_tok + ratio - 1) / ratio;
+  const int64_t emit_cap = (int64_t)sms * 8;
+  cfg.gridDim = dim3((unsigned)(groups < emit_cap ? groups : emit_cap));
+  cfg.blockDim = dim3(kIdxDim);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, indexer_emit_kernel, a, K);
+  if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  const int64_t ring_need = (n_tok + 32 * kRingWarps - 1) / (32 * kRingWarps), ring_cap = (int64_t)sms * 2;
+  cfg.gridDim = dim3((unsigned)(ring_need < ring_cap ? ring_need : ring_cap));
+  cfg.blockDim = dim3(kRingWarps * 32);
+  e = cudaLaunchKernelEx(&cfg, compress_ring_kernel, a);
+  if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return check_launch(what);
 }

@@ -10,13 +10,16 @@
 // (0 = cannot win; -0.0 folded into +0.0 because `>` ties them), so "key >= t"
 // is "score >= float(t)".
 //  * n <= 8192: every key goes to the shared-memory candidate buffer.
-//  * Otherwise a 4096-key sample (32 contiguous chunks of 128, held in
-//    registers) gives a threshold t, the sample's r-th largest key, with r
-//    set from the sampling error so that effective_k to ~1.5 effective_k
-//    scores are expected at or above it.  One pass over the
+//  * Otherwise a 4096-key sample (32 contiguous chunks of 128) gives a
+//    threshold t, the sample's r-th largest key, with r set from the sampling
+//    error so that effective_k to ~1.5 effective_k scores are expected at or
+//    above it; a separate light kernel (128-thread CTAs, the sample in
+//    registers) picks every query's t before the selection kernel runs, so
+//    the selection streams its row from the start.  One pass over the
 //    scores appends every score >= t to the candidate buffer (8192 entries,
 //    warp-aggregated).  If that set holds at least effective_k and fits, it
-//    contains the exact top-k (the k-th largest score is >= t), ties included.
+//    contains the exact top-k (the k-th largest score is >= t, whatever t
+//    is), ties included.
 //  * Otherwise (a skewed sample, or fewer than effective_k scores beat -inf)
 //    an exact radix selection runs: 11 + 11 + 10-bit histogram passes until
 //    the keys at or above the selected bin fit, then a collection pass; keys
@@ -41,8 +44,6 @@ constexpr int kSortedCap = kTopkMaxK + kBucketMax;
 constexpr int kSampleChunk = 128;                         // keys per chunk: one float4 per lane
 constexpr int kSampleChunks = 32;
 constexpr int kSample = kSampleChunks * kSampleChunk;     // 4096
-constexpr int kSamplePerThread = kSample / kTopkThreads;  // 8, held in registers
-constexpr int kBinsPerThread = 2048 / kTopkThreads;       // 4
 #ifndef RKV_TOPK_PREFETCH_ROUNDS
 #define RKV_TOPK_PREFETCH_ROUNDS 2
 #endif
@@ -87,16 +88,19 @@ __device__ __forceinline__ void for_each_key(const float* __restrict__ row, int 
 }
 
 // Finds the bin b (of nbins <= 2048) with above(b) < rank <= above(b) +
-// hist[b], above(b) = sum of hist over bins > b.  Thread t owns the
-// kBinsPerThread bins counted down from nbins-1-t*kBinsPerThread.  Result in
-// sm.sel_bin / sm.sel_above (valid after a barrier).
-__device__ void select_bin(TopkSmem& sm, int nbins, uint32_t rank) {
+// hist[b], above(b) = sum of hist over bins > b, with NT threads: thread t
+// owns the 2048/NT bins counted down from nbins-1-t*(2048/NT).  Result in
+// *sel_bin / *sel_above (valid after a barrier).
+template <int NT>
+__device__ void select_bin_t(const uint32_t* hist, uint32_t* warp_sums, int nbins, uint32_t rank, uint32_t* sel_bin,
+                             uint32_t* sel_above) {
+  constexpr int kPer = 2048 / NT, kWarps = NT / 32;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const int top = nbins - 1 - tid * kBinsPerThread;
-  uint32_t h[kBinsPerThread], v = 0;
+  const int top = nbins - 1 - tid * kPer;
+  uint32_t h[kPer], v = 0;
 #pragma unroll
-  for (int j = 0; j < kBinsPerThread; ++j) {
-    h[j] = top - j >= 0 ? sm.hist[top - j] : 0u;
+  for (int j = 0; j < kPer; ++j) {
+    h[j] = top - j >= 0 ? hist[top - j] : 0u;
     v += h[j];
   }
   uint32_t incl = v;
@@ -105,27 +109,31 @@ __device__ void select_bin(TopkSmem& sm, int nbins, uint32_t rank) {
     const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
     if (lane >= o) incl += y;
   }
-  if (lane == 31) sm.warp_sums[w] = incl;
+  if (lane == 31) warp_sums[w] = incl;
   __syncthreads();
   if (w == 0) {
-    uint32_t x = lane < kTopkWarps ? sm.warp_sums[lane] : 0u, xi = x;
+    uint32_t x = lane < kWarps ? warp_sums[lane] : 0u, xi = x;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const uint32_t y = __shfl_up_sync(0xffffffffu, xi, o);
       if (lane >= o) xi += y;
     }
-    if (lane < kTopkWarps) sm.warp_sums[lane] = xi - x;  // exclusive
+    if (lane < kWarps) warp_sums[lane] = xi - x;  // exclusive
   }
   __syncthreads();
-  uint32_t above = sm.warp_sums[w] + incl - v;
+  uint32_t above = warp_sums[w] + incl - v;
 #pragma unroll
-  for (int j = 0; j < kBinsPerThread; ++j) {
+  for (int j = 0; j < kPer; ++j) {
     if (top - j >= 0 && above < rank && rank <= above + h[j]) {
-      sm.sel_bin = (uint32_t)(top - j);
-      sm.sel_above = above;
+      *sel_bin = (uint32_t)(top - j);
+      *sel_above = above;
     }
     above += h[j];
   }
+}
+
+__device__ __forceinline__ void select_bin(TopkSmem& sm, int nbins, uint32_t rank) {
+  select_bin_t<kTopkThreads>(sm.hist, sm.warp_sums, nbins, rank, &sm.sel_bin, &sm.sel_above);
 }
 
 // Exclusive block scan of a 0/1 flag; returns the position, total in *total.
@@ -185,36 +193,91 @@ __device__ uint32_t smem_select(TopkSmem& sm, int count, uint32_t rank, uint32_t
   return prefix;
 }
 
-// Radix selection over the kSample sample keys, kSamplePerThread of them in
-// each thread's registers: the lower bound of the narrowest bin (11, then 11,
-// then 10 bits) holding the rank-th largest sample key (rank >= 1), stopping
-// once the sample keys at or above the bin number at most `fit`.  Returns 0
-// when fewer than `rank` sample keys can win.
-__device__ uint32_t sample_select(TopkSmem& sm, const uint32_t (&keys)[kSamplePerThread], uint32_t rank,
-                                  uint32_t fit) {
-  const int tid = threadIdx.x;
-  uint32_t prefix = 0u, pmask = 0u, above_total = 0u;
-  for (int pass = 0; pass < 3; ++pass) {
-    const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
-    const uint32_t dmask = pass == 2 ? 0x3ffu : 0x7ffu;
-    for (int b = tid; b < 2048; b += kTopkThreads) sm.hist[b] = 0u;
-    __syncthreads();
+// The sample rank: expected scores at or above the sample's rank-th largest
+// key are rank * n / kSample, with a relative spread of about 1/sqrt(rank).
+// rank = q + 3.5 sqrt(q) + 2 (q = kk * kSample / n) keeps the count >= kk in
+// all but ~0.1% of rows and far under the 8192-entry buffer for k <= 2048.
+__device__ __forceinline__ uint32_t sample_rank(int kk, int n) {
+  const float q = (float)kk * (float)kSample / (float)n;
+  const uint32_t rank = (uint32_t)ceilf(q + 3.5f * sqrtf(q) + 2.0f);
+  return max(1u, min(rank, (uint32_t)kSample));
+}
+
+// Start of sample chunk c (of kSampleChunks, 128 consecutive scores each,
+// spread evenly over the row; 4-aligned when the row is vectorised).
+__device__ __forceinline__ int64_t sample_chunk_start(int c, int n, int vec) {
+  int64_t c0 = (int64_t)c * (n - kSampleChunk) / (kSampleChunks - 1);
+  return vec ? (c0 & ~(int64_t)3) : c0;
+}
+
+// The rank-th largest of the kSample sample keys, PER of them in each of
+// the NT threads' registers, by a bitwise search from the top bit down: bit b
+// is set when at least `rank` sample keys are >= the prefix with it set.  One
+// count (a warp reduction and a barrier) per bit, no shared-memory atomics.
+// Returns 0 when fewer than `rank` sample keys can win (key 0).
+template <int NT, int PER>
+__device__ uint32_t sample_kth_largest(const uint32_t (&keys)[PER], uint32_t rank, uint32_t (*part)[NT / 32]) {
+  static_assert(NT * PER == kSample, "sample size");
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  auto count_ge = [&](uint32_t x, int slot) {
+    uint32_t c = 0;
 #pragma unroll
-    for (int j = 0; j < kSamplePerThread; ++j)
-      if ((keys[j] & pmask) == prefix) atomicAdd(&sm.hist[(keys[j] >> shift) & dmask], 1u);
+    for (int j = 0; j < PER; ++j) c += keys[j] >= x ? 1u : 0u;
+    c = __reduce_add_sync(0xffffffffu, c);
+    if (lane == 0) part[slot][w] = c;
     __syncthreads();
-    if (pass == 0 && (uint32_t)kSample - sm.hist[0] < rank) return 0u;  // bin 0 holds only keys that cannot win
-    select_bin(sm, (int)dmask + 1, rank);
-    __syncthreads();
-    const uint32_t b = sm.sel_bin, above = sm.sel_above, in_bin = sm.hist[b];
-    __syncthreads();
-    rank -= above;
-    above_total += above;
-    prefix |= b << shift;
-    pmask |= dmask << shift;
-    if (above_total + in_bin <= fit) break;
+    uint32_t all = 0;
+#pragma unroll
+    for (int i = 0; i < NT / 32; ++i) all += part[slot][i];
+    return all;
+  };
+  if (count_ge(1u, 1) < rank) return 0u;  // slot 1; bit 31 uses slot 0, bit 30 slot 1, ...
+  uint32_t prefix = 0u;
+#pragma unroll 1
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t cand = prefix | (1u << bit);
+    if (count_ge(cand, (bit & 1) ^ 1) >= rank) prefix = cand;  // two slots: a slot is rewritten two counts later
   }
   return prefix;
+}
+
+// Per query with more than kCandCap visible scores: the collection threshold
+// (the sample's rank-th largest key, 0 when the sample cannot supply one)
+// written to out[q * k] -- the first entry of the query's own output row,
+// which topk_select_kernel reads before it writes any output.  One 128-thread
+// CTA per query, 32 sample keys per thread in registers; many CTAs per SM, so
+// a layer's queries take their latency-bound sample phases in about one wave
+// instead of inside the streaming kernel.
+constexpr int kThrThreads = 128;
+constexpr int kThrPerThread = kSample / kThrThreads;  // 32
+
+__global__ void __launch_bounds__(kThrThreads)
+topk_threshold_kernel(const float* __restrict__ scores, int64_t ld, const int32_t* __restrict__ n_visible, int k,
+                      int32_t* __restrict__ out, int vec) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  __shared__ uint32_t part[2][kThrThreads / 32];
+  const int q = blockIdx.x;
+  const int n = max(0, __ldg(n_visible + q));
+  const int kk = min(k, n);
+  if (n <= kCandCap || kk == 0) return;
+  const float* row = scores + (int64_t)q * ld;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t skeys[kThrPerThread];
+  constexpr int kChunksPerWarp = kSampleChunks / (kThrThreads / 32);  // 8
+#pragma unroll
+  for (int c = 0; c < kChunksPerWarp; ++c) {
+    const int64_t c0 = sample_chunk_start(w * kChunksPerWarp + c, n, vec);
+    if (vec) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(row + c0) + lane);
+      skeys[4 * c] = topk_key(v.x), skeys[4 * c + 1] = topk_key(v.y);
+      skeys[4 * c + 2] = topk_key(v.z), skeys[4 * c + 3] = topk_key(v.w);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) skeys[4 * c + j] = topk_key(__ldg(row + c0 + lane * 4 + j));
+    }
+  }
+  const uint32_t t = sample_kth_largest<kThrThreads, kThrPerThread>(skeys, sample_rank(kk, n), part);
+  if (threadIdx.x == 0) out[(int64_t)q * k] = (int32_t)t;
 }
 
 // One compare-exchange stage of a descending bitonic sort on the 64-element
@@ -512,6 +575,21 @@ topk_select_kernel(const float* __restrict__ scores, int64_t ld, const int32_t* 
   const int n = max(0, __ldg(n_visible + q));
   const int kk = min(k, n);
   int32_t* o = out + (int64_t)q * k;
+  // The scores are complete before topk_threshold_kernel (launched without
+  // programmatic overlap) starts, so the first collection rounds go into L2
+  // before waiting for its thresholds.
+  if (vec && n > kCandCap) {
+    const int w_ = tid >> 5;
+    for (int rr = 0; rr < kPrefetchRounds; ++rr) {
+      const int64_t chunk = (int64_t)rr * kTopkWarps + w_;
+      if ((chunk + 1) * 1024 <= n)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(row + chunk * 1024 + (tid & 31) * 32));
+    }
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // the threshold topk_threshold_kernel left in this row's first entry
+  const uint32_t t = (n > kCandCap && kk > 0) ? (uint32_t)o[0] : 0u;
+  __syncthreads();  // every thread has read o[0] before any output is written
   for (int i = kk + tid; i < k; i += kTopkThreads) o[i] = -1;
   if (kk == 0) return;
 
@@ -528,56 +606,15 @@ topk_select_kernel(const float* __restrict__ scores, int64_t ld, const int32_t* 
     __syncthreads();
     nsel = min(sm.n_cand, (uint32_t)kk);
     done = true;
-  } else {
-    // 4096 sample keys in registers: warp w reads chunks 2w, 2w+1 of 128
-    // consecutive scores spread evenly over the row
-    const int w = tid >> 5, lane = tid & 31;
-    uint32_t skeys[kSamplePerThread];
-#pragma unroll
-    for (int c = 0; c < kSampleChunks / kTopkWarps; ++c) {
-      const int chunk = w * (kSampleChunks / kTopkWarps) + c;
-      int64_t c0 = (int64_t)chunk * (n - kSampleChunk) / (kSampleChunks - 1);
-      if (vec) {
-        c0 &= ~(int64_t)3;
-        const float4 v = __ldg(reinterpret_cast<const float4*>(row + c0) + lane);
-        skeys[4 * c] = topk_key(v.x), skeys[4 * c + 1] = topk_key(v.y);
-        skeys[4 * c + 2] = topk_key(v.z), skeys[4 * c + 3] = topk_key(v.w);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) skeys[4 * c + j] = topk_key(__ldg(row + c0 + lane * 4 + j));
-      }
-    }
-    // Expected scores at or above the sample's rank-th largest key: rank * n /
-    // kSample, with a relative spread of about 1/sqrt(rank).  rank = q +
-    // 3.5 sqrt(q) + 2 (q = kk * kSample / n) keeps the count >= kk in all but
-    // ~0.1% of rows and far under the 8192-entry buffer for k <= 2048.
-    const float q = (float)kk * (float)kSample / (float)n;
-    uint32_t rank = (uint32_t)ceilf(q + 3.5f * sqrtf(q) + 2.0f);
-    rank = max(1u, min(rank, (uint32_t)kSample));
-    // the collection's first kPrefetchRounds rounds (a 4 KB chunk per warp each)
-    // into L2 while the threshold is selected
-    if (vec) {
-      const int w_ = tid >> 5;
-      for (int rr = 0; rr < kPrefetchRounds; ++rr) {
-        const int64_t chunk = (int64_t)rr * kTopkWarps + w_;
-        if ((chunk + 1) * 1024 <= n)
-          asm volatile("prefetch.global.L2 [%0];" ::"l"(row + chunk * 1024 + (tid & 31) * 32));
-      }
-    }
-    const uint32_t t = sample_select(sm, skeys, rank, rank);
-    if (t != 0u) {
-      if (tid == 0) sm.n_cand = 0u;
-      __syncthreads();
-      const float thr = key_to_float(t);
-      if (vec == 2) collect_at_least<2>(sm, row, n, thr);
-      else if (vec == 1) collect_at_least<1>(sm, row, n, thr);
-      else collect_at_least<0>(sm, row, n, thr);
-      __syncthreads();
-      const uint32_t got = sm.n_cand;
-      done = got >= (uint32_t)kk && got <= (uint32_t)kCandCap;
-      __syncthreads();
-
-    }
+  } else if (t != 0u) {
+    const float thr = key_to_float(t);
+    if (vec == 2) collect_at_least<2>(sm, row, n, thr);
+    else if (vec == 1) collect_at_least<1>(sm, row, n, thr);
+    else collect_at_least<0>(sm, row, n, thr);
+    __syncthreads();
+    const uint32_t got = sm.n_cand;
+    done = got >= (uint32_t)kk && got <= (uint32_t)kCandCap;
+    __syncthreads();
   }
 
   if (!done) {
@@ -700,7 +737,22 @@ extern "C" rkv_status rkv_topk_select_f32(const float* scores, int64_t ld, int32
   const int smem = (int)sizeof(TopkSmem);
   cudaError_t e = cudaFuncSetAttribute(topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_topk_select_f32: %s", cudaGetErrorString(e));
-  topk_select_kernel<<<(unsigned)n_q, kTopkThreads, smem, (cudaStream_t)stream>>>(scores, ld, n_visible, k, out_idx,
-                                                                                 vec);
+  // thresholds of the long rows first (into each row's first output entry),
+  // then the selection, launched to overlap the threshold kernel's tail
+  if (n_keys_max > kCandCap)
+    topk_threshold_kernel<<<(unsigned)n_q, kThrThreads, 0, (cudaStream_t)stream>>>(scores, ld, n_visible, k, out_idx,
+                                                                                   vec);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)n_q);
+  cfg.blockDim = dim3(kTopkThreads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = n_keys_max > kCandCap ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, topk_select_kernel, scores, ld, n_visible, (int)k, out_idx, vec);
+  if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_topk_select_f32: launch failed: %s", cudaGetErrorString(e));
   return check_launch("rkv_topk_select_f32");
 }

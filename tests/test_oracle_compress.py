@@ -197,3 +197,41 @@ def test_midpoint_row_needs_the_in_order_sum():
     row = cc.sensitive_row(oracle.quantize_rows_f32)
     qs, qt = cc.means(row)
     assert np.float32(qs) != np.float32(qt) and cc.mid_distance(qt) <= 1 << 11
+
+
+def test_indexer_batch_driver_matches_primitives():
+    """oracle.indexer_compress_append (the indexer pool's 128-lane step, rows
+    out as f32 before the FP4 QAT) equals the same window state machine +
+    RMSNorm + RoPE primitives composed token by token on 128-lane rows."""
+    rng = np.random.default_rng(12)
+    for ratio in (4, 128, 2, 1):
+        coff = 2 if ratio == 4 else 1
+        width = coff * 128
+        n_states = 3
+        lens = [2 * ratio + 3, ratio, 5 * ratio - 1]
+        states = oracle.indexer_compress_states(n_states, ratio)
+        kv = rng.standard_normal((sum(lens), width)).astype(np.float32)
+        score = (rng.standard_normal((sum(lens), width)) * 2).astype(np.float32)
+        ape = rng.standard_normal((ratio, width)).astype(np.float32)
+        norm = rng.uniform(0.5, 1.5, 128).astype(np.float32)
+        pos = np.concatenate([np.arange(n) for n in lens]).astype(np.int32)
+        state_of = np.concatenate([np.full(n, s) for s, n in enumerate(lens)]).astype(np.int32)
+        emit_row = np.arange(sum(lens), dtype=np.int32)[::-1].copy()
+        out = np.full((sum(lens), 128), 7.0, np.float32)
+        st = oracle.indexer_compress_append(out, ratio, states, kv, score, pos, state_of, emit_row, ape, norm)
+        assert st == 0
+        want = np.full_like(out, 7.0)
+        comps = [oracle.Compressor(ratio, head_dim=128) for _ in range(n_states)]
+        for t in range(sum(lens)):
+            r = comps[state_of[t]].accumulate(kv[t], score[t] + ape[pos[t] % ratio])
+            if r is not None:
+                oracle.compressor_postprocess(r, norm, int(pos[t]) + 1 - ratio)
+                want[emit_row[t]] = r
+        assert np.array_equal(out.view(np.uint32), want.view(np.uint32)), ratio
+    # an emit row past the buffer: INDEX_OUT_OF_RANGE, nothing written
+    states = oracle.indexer_compress_states(1, 1)
+    out = np.zeros((2, 128), np.float32)
+    st = oracle.indexer_compress_append(out, 1, states, np.ones((1, 128), np.float32), np.zeros((1, 128), np.float32),
+                                        np.zeros(1, np.int32), np.zeros(1, np.int32), np.array([2], np.int32), None,
+                                        np.ones(128, np.float32))
+    assert st == 1 << oracle.INDEX_OUT_OF_RANGE and not out.any()
