@@ -814,6 +814,30 @@ def bench_sparse(args, dist: Dist, dev, peak, n_seq: int | None = None, mla: boo
     return res
 
 
+def bench_topk_only(args, dist: Dist, dev, peak) -> dict:
+    """Config 4's top-k alone (no pool): 2048 queries (32 sequences x the last
+    64 positions, causal) over 131072 seeded N(0,1) scores, k = 2048, two
+    score matrices alternating -- about 1 GB on the device, a size for
+    profiling the two top-k kernels."""
+    import rsllm_b200 as rk
+    from rsllm_b200 import synth
+
+    n_seq, ctx, n_qpos, k = 32, 131072, 64, 2048
+    n_q = n_seq * n_qpos
+    scores = [synth.scores(n_q, ctx, seed=500 + 31 * i + 7919 * dist.rank, device=dev) for i in range(2)]
+    n_visible = (ctx - n_qpos + 1 + torch.arange(n_qpos, device=dev, dtype=torch.int32)).repeat(n_seq).contiguous()
+    out = torch.empty((n_q, k), dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    for i in range(args.phase_warmup):
+        rk.select_top_k(scores[i % 2], n_visible, k, out=out, stream=stream)
+    P = max(1, args.phase_steps)
+    ms = dist.max(events_time(lambda: [rk.select_top_k(scores[i % 2], n_visible, k, out=out, stream=stream)
+                                       for i in range(P)], stream)) / P
+    nbytes = int(n_visible.sum().item()) * 4 + n_q * k * 4
+    return {"config": f"c4 top-k: {n_q} queries x {ctx} keys (causal), k = {k}", "ms_per_call": ms,
+            "gbs_per_gpu": nbytes / (ms * 1e-3) / GB, "frac_of_hbm_peak": nbytes / (ms * 1e-3) / GB / peak}
+
+
 def compress_bytes(n_tok: int, n_emit: int, ring_rows_written: int, ring_src_read: int) -> int:
     """Algorithmic HBM bytes of one rkv_compress_append call (ratio 4, two
     lanes of 576): every input (kv, score) row read once (9216 B), the ring
@@ -1370,7 +1394,7 @@ def main():
     ap.add_argument("--phase-warmup", type=int, default=1)
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--only", choices=["all", "append", "gather", "sparse", "prefix", "kvc", "compress", "indexer",
-                                       "split"],
+                                       "split", "topk"],
                     default="all",
                     help="run one workload alone (profiling)")
     ap.add_argument("--mla-splits", type=int, default=16,
@@ -1414,6 +1438,8 @@ def main():
             res = bench_indexer(args, dist, dev, peak)
         elif args.only == "split":
             res = bench_split(args, dist, dev, peak)
+        elif args.only == "topk":
+            res = bench_topk_only(args, dist, dev, peak)
         else:
             res = bench_sparse(args, dist, dev, peak)
         clocks.stop()

@@ -211,10 +211,13 @@ __device__ __forceinline__ int64_t sample_chunk_start(int c, int n, int vec) {
 }
 
 // The rank-th largest of the kSample sample keys, PER of them in each of
-// the NT threads' registers, by a bitwise search from the top bit down: bit b
-// is set when at least `rank` sample keys are >= the prefix with it set.  One
-// count (a warp reduction and a barrier) per bit, no shared-memory atomics.
-// Returns 0 when fewer than `rank` sample keys can win (key 0).
+// the NT threads' registers, to its top 16 bits (the lower bound of the
+// 2^16-key bin that holds it), by a bitwise search from the top bit down: bit
+// b is set when at least `rank` sample keys are >= the prefix with it set.
+// One count (a warp reduction and a barrier) per bit, no shared-memory
+// atomics.  16 bits keep the sign, exponent and 7 mantissa bits of the score:
+// the bin adds well under 1% to the expected count at or above it.  Returns
+// 0 when fewer than `rank` sample keys can win (key 0).
 template <int NT, int PER>
 __device__ uint32_t sample_kth_largest(const uint32_t (&keys)[PER], uint32_t rank, uint32_t (*part)[NT / 32]) {
   static_assert(NT * PER == kSample, "sample size");
@@ -234,7 +237,7 @@ __device__ uint32_t sample_kth_largest(const uint32_t (&keys)[PER], uint32_t ran
   if (count_ge(1u, 1) < rank) return 0u;  // slot 1; bit 31 uses slot 0, bit 30 slot 1, ...
   uint32_t prefix = 0u;
 #pragma unroll 1
-  for (int bit = 31; bit >= 0; --bit) {
+  for (int bit = 31; bit >= 16; --bit) {
     const uint32_t cand = prefix | (1u << bit);
     if (count_ge(cand, (bit & 1) ^ 1) >= rank) prefix = cand;  // two slots: a slot is rewritten two counts later
   }
@@ -441,12 +444,24 @@ __device__ __forceinline__ void collect_at_least(TopkSmem& sm, const float* __re
       const int b = __ffs(m) - 1;
       m &= m - 1;
       // bit b of lane `lane`: piece b/8 (b/4) of the lane, element b%8 (b%4);
-      // its score is picked from the registers with a select chain (static
-      // indices keep the loaded values in registers)
+      // its score is picked from the registers that loaded it
       const int off = kVec == 2 ? (b >> 3) * 256 + lane * 8 + (b & 7) : (b >> 2) * 128 + lane * 4 + (b & 3);
-      uint32_t bits = 0u;
+      // element b of the 32 loaded values by a 5-level select tree (31
+      // selects on the bits of b; static register indices throughout)
+      uint32_t t16[16], t8[8], t4[4], t2[2];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) bits = (b == i) ? (kVec == 2 ? u2[i >> 3][i & 7] : u1[i >> 2][i & 3]) : bits;
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t e0 = kVec == 2 ? u2[(2 * i) >> 3][(2 * i) & 7] : u1[(2 * i) >> 2][(2 * i) & 3];
+        const uint32_t e1 = kVec == 2 ? u2[(2 * i + 1) >> 3][(2 * i + 1) & 7] : u1[(2 * i + 1) >> 2][(2 * i + 1) & 3];
+        t16[i] = (b & 1) ? e1 : e0;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) t8[i] = (b & 2) ? t16[2 * i + 1] : t16[2 * i];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) t4[i] = (b & 4) ? t8[2 * i + 1] : t8[2 * i];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) t2[i] = (b & 8) ? t4[2 * i + 1] : t4[2 * i];
+      const uint32_t bits = (b & 16) ? t2[1] : t2[0];
       if (pos < (uint32_t)kCandCap)
         sm.cand[pos] = composite(topk_key(__uint_as_float(bits)), (uint32_t)(chunk * kWarpChunk + off));
       ++pos;
