@@ -52,7 +52,7 @@ GB = 1e9
 
 # DRAM bytes (read + write) per row from ncu captures of each kernel
 # (profiles/append_quant_c2.md, gather_dequant_c3_small.md,
-# topk_sparse_c4_small.md).  The append's figure is the mean over four
+# sparse_gather_c4_small.md).  The append's figure is the mean over four
 # consecutive launches captured without cache control, so each launch carries
 # the previous launch's page writes draining from L2: 17,992,640 B read +
 # 8,241,600 B written per 15,616-row launch.
