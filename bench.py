@@ -876,10 +876,12 @@ def bench_compress(args, dist: Dist, dev, peak) -> dict:
     slot = [(seq * 64 + ((seq + p0 + j + 1) // 4) % 64).to(torch.int32).contiguous() for j in range(n_pos_steps)]
     state = {"j": 0}
 
-    def dstep(j):
+    def dstep(j, flags=True):
+        # a decode step: one token per state, metadata tensors made before the
+        # step (RKV_COMPRESS_INPUTS_READY | RKV_COMPRESS_ONE_TOKEN_PER_STATE)
         for layer in range(n_layers):
             banks.append(pool, layer, kv[j % n_var, layer], sc[j % n_var, layer], pos[j], sid[layer], slot[j], norm,
-                         ape, stream=stream)
+                         ape, stream=stream, inputs_ready=flags, one_token_per_state=flags)
 
     # the timed steps (positions advancing) are one CUDA graph; an untimed
     # replay uploads it (it recomputes the same rows into the same slots)
@@ -888,21 +890,28 @@ def bench_compress(args, dist: Dist, dev, peak) -> dict:
             dstep(j)
     pool.check("compress decode", stream)
     torch.cuda.synchronize(dev)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for j in range(args.phase_warmup + 3, args.phase_warmup + 3 + args.phase_steps):
-            dstep(j)
 
-    def replay():
-        with torch.cuda.stream(stream):
-            graph.replay()
+    def timed_graph(flags):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for j in range(args.phase_warmup + 3, args.phase_warmup + 3 + args.phase_steps):
+                dstep(j, flags)
 
-    replay()
-    stream.synchronize()
-    flush_l2(dev)
-    dist.barrier()
-    ms = dist.max(events_time(replay, stream)) / args.phase_steps
-    pool.check("compress decode", stream)
+        def replay():
+            with torch.cuda.stream(stream):
+                graph.replay()
+
+        replay()
+        stream.synchronize()
+        flush_l2(dev)
+        dist.barrier()
+        t = dist.max(events_time(replay, stream)) / args.phase_steps
+        pool.check("compress decode", stream)
+        del graph
+        return t
+
+    ms_plain = timed_graph(False)  # two launches per layer, every read after the wait
+    ms = timed_graph(True)
     one = events_time(lambda: banks.append(pool, 0, kv[0, 0], sc[0, 0], pos[-1], sid[0], slot[-1], norm, ape,
                                            stream=stream), stream)
     n_emit = n_seq // 4
@@ -914,9 +923,12 @@ def bench_compress(args, dist: Dist, dev, peak) -> dict:
         "ms_per_step": ms, "tokens_per_s_per_gpu": n_seq * n_layers / (ms * 1e-3),
         "emissions_per_s_per_gpu": n_emit * n_layers / (ms * 1e-3),
         "algorithmic_bytes_per_layer": per_layer, "gbs_per_gpu": per_layer / t_layer / GB,
-        "frac_of_hbm_peak": per_layer / t_layer / GB / peak, "ms_per_layer_ungraphed": one,
-        "launches_per_step": 2 * n_layers}
-    del graph, kv, sc, banks, pool
+        "frac_of_hbm_peak": per_layer / t_layer / GB / peak, "ms_per_layer": ms / n_layers,
+        "ms_per_layer_plain": ms_plain / n_layers, "ms_per_layer_ungraphed": one,
+        "launches_per_step": n_layers,
+        "flags": "RKV_COMPRESS_INPUTS_READY | RKV_COMPRESS_ONE_TOKEN_PER_STATE",
+        "ms_per_step_plain": ms_plain, "launches_per_step_plain": 2 * n_layers}
+    del kv, sc, banks, pool
     torch.cuda.empty_cache()
 
     # -- prefill --------------------------------------------------------------------
@@ -1322,7 +1334,7 @@ def summary(app: dict, phases: dict, split: dict | None) -> dict:
         if not isinstance(p, dict) or "skipped" in p:
             continue
         d = {"gbs": _r(p.get("gbs_per_gpu")), "frac": _r(p.get("roofline_frac", p.get("frac_of_hbm_peak")))}
-        ms = p.get("kernel_ms_per_layer", p.get("ms_per_layer_ungraphed", p.get("ms_per_layer")))
+        ms = p.get("kernel_ms_per_layer", p.get("ms_per_layer", p.get("ms_per_layer_ungraphed")))
         if ms is not None:
             d["ms_l"] = _r(ms)
         if "parity" in p:

@@ -575,6 +575,30 @@ RKV_API rkv_status rkv_indexer_compress_append(int32_t ratio, float* states, int
                                                const float* ape, const float* norm, const float* rope_table,
                                                int64_t rope_rows, float* out_rows, int64_t n_out_rows,
                                                uint32_t* d_status, rkv_stream_t stream);
+/* rkv_compress_append with launch flags (same rsLLM items, arguments, status
+ * rules and pool bytes).  The emission kernel is launched with programmatic
+ * dependent launch and may start while the kernel issued just before it on
+ * `stream` is still running.
+ *   RKV_COMPRESS_INPUTS_READY: pos, state_of_token, emit_slot, ape, norm and
+ *     rope_table are not written by any kernel that can still be running when
+ *     this call starts (e.g. static per-step metadata and weight tables); the
+ *     kernel reads them, resolves each window's rows and stages the APE table
+ *     before waiting for that kernel.  kv, score and the states are still read
+ *     only after the wait.
+ *   RKV_COMPRESS_ONE_TOKEN_PER_STATE: no state has more than one token in the
+ *     call (a decode step): the emission kernel writes every ring row and the
+ *     second launch (deferred ring writes) is skipped.  A call that breaks
+ *     this sets INVALID_ARGUMENT in the device status word (the affected ring
+ *     rows are then not written).
+ * Other flag bits: INVALID_ARGUMENT. */
+#define RKV_COMPRESS_INPUTS_READY 1u
+#define RKV_COMPRESS_ONE_TOKEN_PER_STATE 2u
+RKV_API rkv_status rkv_compress_append_ex(const rkv_pool_view* pool, int32_t layer, int32_t ratio, float* states,
+                                          int64_t n_states, const float* kv, const float* score, int64_t n_tok,
+                                          const int32_t* pos, const int32_t* state_of_token,
+                                          const int32_t* emit_slot, const float* ape, const float* norm,
+                                          const float* rope_table, int64_t rope_rows, uint32_t flags,
+                                          uint32_t* d_status, rkv_stream_t stream);
 /* expf as the compressor kernel evaluates it, on the host (host != 0, x and
  * out host memory) or on the current device (x, out device memory): a
  * double-precision exp rounded to f32, corrected from a table wherever the

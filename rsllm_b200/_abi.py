@@ -112,6 +112,9 @@ SIGNATURES = {
     "rkv_mla_decode_fp8": (c_int32, [_P(PoolView), c_int32, _i32p, c_int64, _i32p, _i32p, _u16p, c_int32, _i32p,
                                      c_int32, _f32p, c_float, c_int32, c_void_p, _f32p, _u32p, c_void_p]),
     "rkv_compress_state_bytes": (c_int64, [c_int32]),
+    "rkv_compress_append_ex": (c_int32, [_P(PoolView), c_int32, c_int32, _f32p, c_int64, _f32p, _f32p, c_int64,
+                                         _i32p, _i32p, _i32p, _f32p, _f32p, _f32p, c_int64, c_uint32, _u32p,
+                                         c_void_p]),
     "rkv_indexer_compress_state_bytes": (c_int64, [c_int32]),
     "rkv_indexer_compress_append": (c_int32, [c_int32, _f32p, c_int64, _f32p, _f32p, c_int64, _i32p, _i32p, _i32p,
                                               _f32p, _f32p, _f32p, c_int64, _f32p, c_int64, _u32p, c_void_p]),
@@ -151,6 +154,8 @@ SIGNATURES = {
 }
 STATIC_MAX_MOVES = 262144
 APPEND_INPUTS_READY = 1
+COMPRESS_INPUTS_READY = 1
+COMPRESS_ONE_TOKEN_PER_STATE = 2
 
 _lib = None
 

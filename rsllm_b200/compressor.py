@@ -93,14 +93,20 @@ class CompressorBank:
 
     def append(self, pool: PagedKvPool, layer: int, kv: torch.Tensor, score: torch.Tensor, pos: torch.Tensor,
                state_of_token: torch.Tensor, emit_slot: torch.Tensor, norm: torch.Tensor,
-               ape: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> None:
+               ape: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None,
+               inputs_ready: bool = False, one_token_per_state: bool = False) -> None:
         """One compressor step for ``n_tok`` tokens (``rkv_compress_append``):
         kv, score f32 [n_tok, width]; pos, state_of_token, emit_slot int32
         [n_tok]; norm f32 [576]; ape f32 [ratio, width] or None (the same on
         every call: the states keep scores without it).  Tokens of one
         state are consecutive entries at consecutive positions.  A token with
         (pos + 1) % ratio == 0 writes its emitted row at ``emit_slot`` (< 0:
-        dropped).  Device-side errors land in ``pool.status``."""
+        dropped).  Device-side errors land in ``pool.status``.
+        ``inputs_ready``: pos / state_of_token / emit_slot / ape / norm are not
+        written by a kernel that may still be running on the stream
+        (RKV_COMPRESS_INPUTS_READY); ``one_token_per_state``: no state has two
+        tokens in this call, e.g. a decode step
+        (RKV_COMPRESS_ONE_TOKEN_PER_STATE, one launch instead of two)."""
         for t, n in ((kv, "kv"), (score, "score"), (norm, "norm")):
             _need(t, torch.float32, n, self.device)
         for t, n in ((pos, "pos"), (state_of_token, "state_of_token"), (emit_slot, "emit_slot")):
@@ -115,10 +121,19 @@ class CompressorBank:
             _need(ape, torch.float32, "ape", self.device)
             if ape.shape != (self.ratio, self.width):
                 raise ShapeMismatch(f"CompressorBank.append: ape must be [{self.ratio}, {self.width}]")
-        check(self.lib.rkv_compress_append(byref(pool.view), layer, self.ratio, _ptr(self.states), self.n_states,
-                                           _ptr(kv), _ptr(score), n_tok, _ptr(pos), _ptr(state_of_token),
-                                           _ptr(emit_slot), _ptr(ape), _ptr(norm), _ptr(self.rope),
-                                           self.rope.shape[0], _ptr(pool.status), _stream(stream)),
+        flags = (_abi.COMPRESS_INPUTS_READY if inputs_ready else 0) | \
+            (_abi.COMPRESS_ONE_TOKEN_PER_STATE if one_token_per_state else 0)
+        if not flags:
+            check(self.lib.rkv_compress_append(byref(pool.view), layer, self.ratio, _ptr(self.states), self.n_states,
+                                               _ptr(kv), _ptr(score), n_tok, _ptr(pos), _ptr(state_of_token),
+                                               _ptr(emit_slot), _ptr(ape), _ptr(norm), _ptr(self.rope),
+                                               self.rope.shape[0], _ptr(pool.status), _stream(stream)),
+                  "CompressorBank.append")
+            return
+        check(self.lib.rkv_compress_append_ex(byref(pool.view), layer, self.ratio, _ptr(self.states), self.n_states,
+                                              _ptr(kv), _ptr(score), n_tok, _ptr(pos), _ptr(state_of_token),
+                                              _ptr(emit_slot), _ptr(ape), _ptr(norm), _ptr(self.rope),
+                                              self.rope.shape[0], flags, _ptr(pool.status), _stream(stream)),
               "CompressorBank.append")
 
 

@@ -384,6 +384,7 @@ struct CmpArgs {
   int hd;                 // lanes of a compressed row: 576 (attention pool) or 128 (indexer pool)
   float* out_rows;        // indexer pool: f32 [n_out_rows][128] emitted rows
   int64_t n_out_rows;
+  uint32_t flags;         // RKV_COMPRESS_INPUTS_READY, RKV_COMPRESS_ONE_TOKEN_PER_STATE
   float* states;
   int64_t n_states, n_tok, rope_rows;
   const float* kv;
@@ -738,6 +739,8 @@ compress_emit_kernel(const CmpArgs a, const ExpConsts K, const ThresholdTable ta
               em = true;
           }
           rg = ring_written(a, t, s) && ring_write_now(a, t, s);
+          if ((a.flags & RKV_COMPRESS_ONE_TOKEN_PER_STATE) && ring_written(a, t, s) && !ring_write_now(a, t, s))
+            set_status(a.status, RKV_ERR_INVALID_ARGUMENT);
           s_tok[tid] = make_int4(p, s, slot, 0);
         }
       }
@@ -852,6 +855,8 @@ indexer_emit_kernel(const CmpArgs a, const ExpConsts K) {
               em = true;
           }
           rg = ring_written(a, t, s) && ring_write_now(a, t, s);
+          if ((a.flags & RKV_COMPRESS_ONE_TOKEN_PER_STATE) && ring_written(a, t, s) && !ring_write_now(a, t, s))
+            set_status(a.status, RKV_ERR_INVALID_ARGUMENT);
           s_tok[tid] = make_int4(p, s, row, 0);
         }
       }
@@ -1158,14 +1163,21 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // With RKV_COMPRESS_INPUTS_READY the token metadata, the APE, norm and RoPE
+  // tables are complete before the previous kernel on the stream ends: the
+  // producer reads them and resolves the first window's sources, and the
+  // consumers stage the APE table, before waiting for that kernel (the
+  // producer waits before its first copy of a kv / score / ring row, and the
+  // consumers touch no other global memory before its copies arrive).
+  const bool early = (a.flags & RKV_COMPRESS_INPUTS_READY) != 0;
+  if (!early) asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (w == kConsumers / 32) {
     // ---- producer warp ----
     const int cr = a.cr, ratio = a.ratio, n_meta = 2 * cr + ratio;  // n_meta <= 24
     const int64_t n_groups = (a.n_tok + ratio - 1) / ratio;
     uint32_t it = 0, ring_phase = 0;
-    bool ok = true;
+    bool ok = true, waited = !early;
     for (int64_t g = blockIdx.x; g < n_groups && ok; g += gridDim.x) {
       // tokens t0 - cr .. t0 + ratio + cr - 1 around the group, one per lane
       const int64_t t0 = g * ratio, tm = t0 - cr + lane;
@@ -1190,6 +1202,10 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
       }
       // ring_written and ring_write_now from the neighbouring lanes
       const bool rg = in_group && valid && s_fwd != ms && (s_prev != ms || s_back == ms);
+      // a ring write left for the ring kernel, which RKV_COMPRESS_ONE_TOKEN_PER_STATE does not launch
+      if ((a.flags & RKV_COMPRESS_ONE_TOKEN_PER_STATE) && in_group && valid && s_fwd != ms && s_prev == ms &&
+          s_back != ms)
+        set_status(a.status, RKV_ERR_INVALID_ARGUMENT);
       const uint32_t emask = __ballot_sync(FULL, em), rmask = __ballot_sync(FULL, rg);
       // one CTA per SM: the producer writes the ring rows itself (below)
       const int n_ring = kMinBlocks == 1 ? 0 : __popc(rmask);
@@ -1218,6 +1234,10 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
         }
         const uint32_t full = bar_full + 8 * buf;
         if (!emission) {
+          if (early && !waited) {  // the consumers copy this call's kv / score rows into the ring
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            waited = true;
+          }
           __syncwarp();
           if (lane == 0) {
             d->kind = 2;
@@ -1257,6 +1277,10 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
           st_arrive_tx(full, 2u * cr * kHalfBytes);
         }
         __syncwarp();
+        if (early && !waited) {  // the rows may come from the previous kernel
+          asm volatile("griddepcontrol.wait;" ::: "memory");
+          waited = true;
+        }
         if (r < cr) {
           st_bulk_load(st_u32(s_kv + (buf * kStageRows + r) * kRowF), skv, kHalfBytes, full);
           st_bulk_load(st_u32(s_sc + (buf * kStageRows + r) * kRowF), ssc, kHalfBytes, full);
@@ -1267,6 +1291,10 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
         // this group's ring rows (all safe to write now): bulk loads into the
         // staging buffer, then bulk stores into the ring slots, while the
         // consumers compute the group's emissions
+        if (early && !waited) {
+          asm volatile("griddepcontrol.wait;" ::: "memory");
+          waited = true;
+        }
         asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // earlier stores have read the buffer
         __syncwarp();
         const uint32_t rbar = st_u32(st_smem + kStRingBar), row_bytes = (uint32_t)a.width * 4u;
@@ -1320,6 +1348,9 @@ compress_emit_staged_kernel(const CmpArgs a, const ExpConsts K, const ThresholdT
         }
       }
     }
+    // a CTA with nothing to copy still waits: this grid then completes only after
+    // the previous one, so later kernels' waits cover every grid before it
+    if (early && !waited) asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // this lane's ring stores are done
     return;
   }
@@ -1471,13 +1502,14 @@ extern "C" rkv_status rkv_compress_expf(const float* x, float* out, int64_t n, i
   return check_launch("rkv_compress_expf");
 }
 
-extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t layer, int32_t ratio, float* states,
-                                          int64_t n_states, const float* kv, const float* score, int64_t n_tok,
-                                          const int32_t* pos, const int32_t* state_of_token,
-                                          const int32_t* emit_slot, const float* ape, const float* norm,
-                                          const float* rope_table, int64_t rope_rows, uint32_t* d_status,
-                                          rkv_stream_t stream) {
-  using namespace rkv;
+namespace rkv {
+static rkv_status compress_append(const rkv_pool_view* pool, int32_t layer, int32_t ratio, float* states,
+                                  int64_t n_states, const float* kv, const float* score, int64_t n_tok,
+                                  const int32_t* pos, const int32_t* state_of_token, const int32_t* emit_slot,
+                                  const float* ape, const float* norm, const float* rope_table, int64_t rope_rows,
+                                  uint32_t flags, uint32_t* d_status, rkv_stream_t stream) {
+  if (flags & ~(RKV_COMPRESS_INPUTS_READY | RKV_COMPRESS_ONE_TOKEN_PER_STATE))
+    return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_compress_append_ex: unknown flags 0x%x", flags);
   rkv_status st = check_pool(pool, "rkv_compress_append");
   if (st != RKV_OK) return st;
   if (layer < 0 || layer >= pool->n_layers)
@@ -1511,6 +1543,7 @@ extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t lay
   a.hd = kRowF;
   a.out_rows = nullptr;
   a.n_out_rows = 0;
+  a.flags = flags;
   a.states = states;
   a.n_states = n_states;
   a.n_tok = n_tok;
@@ -1562,12 +1595,36 @@ extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t lay
   }
   if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_compress_append: launch failed: %s", cudaGetErrorString(e));
   // 2. the remaining ring writes, after every emission has read the rings
-  const int64_t ring_need = (n_tok + 32 * kRingWarps - 1) / (32 * kRingWarps), ring_cap = (int64_t)sms * 2;
-  cfg.gridDim = dim3((unsigned)(ring_need < ring_cap ? ring_need : ring_cap));
-  cfg.blockDim = dim3(kRingWarps * 32);
-  e = cudaLaunchKernelEx(&cfg, compress_ring_kernel, a);
-  if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_compress_append: launch failed: %s", cudaGetErrorString(e));
+  // (none when every state has at most one token in the call)
+  if (!(flags & RKV_COMPRESS_ONE_TOKEN_PER_STATE)) {
+    const int64_t ring_need = (n_tok + 32 * kRingWarps - 1) / (32 * kRingWarps), ring_cap = (int64_t)sms * 2;
+    cfg.gridDim = dim3((unsigned)(ring_need < ring_cap ? ring_need : ring_cap));
+    cfg.blockDim = dim3(kRingWarps * 32);
+    e = cudaLaunchKernelEx(&cfg, compress_ring_kernel, a);
+    if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_compress_append: launch failed: %s", cudaGetErrorString(e));
+  }
   return check_launch("rkv_compress_append");
+}
+}  // namespace rkv
+
+extern "C" rkv_status rkv_compress_append(const rkv_pool_view* pool, int32_t layer, int32_t ratio, float* states,
+                                          int64_t n_states, const float* kv, const float* score, int64_t n_tok,
+                                          const int32_t* pos, const int32_t* state_of_token,
+                                          const int32_t* emit_slot, const float* ape, const float* norm,
+                                          const float* rope_table, int64_t rope_rows, uint32_t* d_status,
+                                          rkv_stream_t stream) {
+  return rkv::compress_append(pool, layer, ratio, states, n_states, kv, score, n_tok, pos, state_of_token, emit_slot,
+                              ape, norm, rope_table, rope_rows, 0u, d_status, stream);
+}
+
+extern "C" rkv_status rkv_compress_append_ex(const rkv_pool_view* pool, int32_t layer, int32_t ratio, float* states,
+                                             int64_t n_states, const float* kv, const float* score, int64_t n_tok,
+                                             const int32_t* pos, const int32_t* state_of_token,
+                                             const int32_t* emit_slot, const float* ape, const float* norm,
+                                             const float* rope_table, int64_t rope_rows, uint32_t flags,
+                                             uint32_t* d_status, rkv_stream_t stream) {
+  return rkv::compress_append(pool, layer, ratio, states, n_states, kv, score, n_tok, pos, state_of_token, emit_slot,
+                              ape, norm, rope_table, rope_rows, flags, d_status, stream);
 }
 
 extern "C" int64_t rkv_indexer_compress_state_bytes(int32_t ratio) {

@@ -217,3 +217,64 @@ def test_stalled_wait_ends_in_a_status(cuda):
     assert 0.5 < dt < 30.0
     x = torch.arange(1024, dtype=torch.float32, device=cuda)
     assert float(x.sum().item()) == 1023 * 1024 / 2
+
+
+@pytest.mark.parametrize("ratio", [4, 2, 128])
+def test_decode_steps_with_launch_flags(cuda, orc, ratio):
+    """Decode steps through rkv_compress_append_ex with
+    RKV_COMPRESS_INPUTS_READY | RKV_COMPRESS_ONE_TOKEN_PER_STATE, queued back to
+    back on one stream over two pool layers (each call's metadata read while
+    the previous call's kernel still runs; one launch per call): the pool
+    bytes equal the oracle's after a prefill and every decode step."""
+    rng = np.random.default_rng(40 + ratio)
+    n_states, coff = 6, (2 if ratio == 4 else 1)
+    width = coff * 576
+    n_pages = n_states * SLOTS_PER_STATE // 64
+    pool = rk.PagedKvPool(n_pages, 2, device=cuda)
+    pool.storage.zero_()
+    banks = [rk.CompressorBank(ratio, n_states, device=cuda, max_positions=SLOTS_PER_STATE * ratio) for _ in range(2)]
+    ref = orc.new_pool(n_pages, 2)
+    ref_states = [orc.compress_states(n_states, ratio) for _ in range(2)]
+    ape = [rng.standard_normal((ratio, width)).astype(np.float32) for _ in range(2)]
+    norm = rng.uniform(0.5, 1.5, 576).astype(np.float32)
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
+    prefill = 3 * ratio + 1
+    stream = torch.cuda.Stream(device=cuda)
+    calls = []
+    for step in range(1 + 2 * ratio + 3):
+        n = prefill if step == 0 else 1
+        p0 = 0 if step == 0 else prefill + step - 1
+        pos = np.tile(np.arange(p0, p0 + n), n_states).astype(np.int32)
+        st = np.repeat(np.arange(n_states), n).astype(np.int32)
+        slot = np.where((pos + 1) % ratio == 0, st * SLOTS_PER_STATE + (pos + 1) // ratio - 1, -1).astype(np.int32)
+        for layer in range(2):
+            kv = rng.standard_normal((n * n_states, width)).astype(np.float32)
+            sc = (rng.standard_normal((n * n_states, width)) * 3).astype(np.float32)
+            calls.append((layer, kv, sc, pos, st, slot, step > 0))
+    dev_calls = [(layer, T(kv), T(sc), T(pos), T(st), T(slot), flags) for layer, kv, sc, pos, st, slot, flags in calls]
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for layer, kv, sc, pos, st, slot, decode in dev_calls:
+            banks[layer].append(pool, layer, kv, sc, pos, st, slot, T(norm), T(ape[layer]), stream=stream,
+                                inputs_ready=decode, one_token_per_state=decode)
+    assert pool.take_status(stream) == 0
+    for layer, kv, sc, pos, st, slot, _ in calls:
+        assert orc.compress_append(ref, n_pages, 2, layer, ratio, ref_states[layer], kv, sc, pos, st, slot,
+                                   ape[layer], norm) == 0
+    got = pool.storage.cpu().numpy()
+    assert np.array_equal(got, ref), f"{int((got != ref).sum())} bytes differ"
+
+
+def test_one_token_flag_reports_a_repeated_state(cuda):
+    """Two tokens of one state in a call made with
+    RKV_COMPRESS_ONE_TOKEN_PER_STATE: the deferred ring write is reported as
+    INVALID_ARGUMENT in the status word."""
+    pool = rk.PagedKvPool(4, 1, device=cuda)
+    bank = rk.CompressorBank(4, 2, device=cuda, max_positions=64)
+    kv = torch.randn((3, 1152), device=cuda)
+    sc = torch.randn((3, 1152), device=cuda)
+    pos = torch.tensor([0, 1, 0], dtype=torch.int32, device=cuda)
+    st = torch.tensor([0, 0, 1], dtype=torch.int32, device=cuda)
+    slot = torch.full((3,), -1, dtype=torch.int32, device=cuda)
+    bank.append(pool, 0, kv, sc, pos, st, slot, torch.ones(576, device=cuda), one_token_per_state=True)
+    assert pool.take_status() == 1 << rk.InvalidArgument.status
