@@ -7,15 +7,26 @@
 // each product and sum rounded on its own; the kernel does exactly that (an
 // f32 dot product on tensor cores or with fused multiply-adds would round
 // differently), so the scores -- and therefore the selected indices -- are
-// bit-exact.  (Packed mul.rn.f32x2 / add.rn.f32x2 pairs are not used: in a
-// loop ptxas was measured to contract them into fused multiply-adds on this
-// B200, which changes the rounding.)  Layout: one CTA of 128 threads per
-// (query, 128 rows); the query (32 KB) and its weights are staged in shared
-// memory and read as broadcast 16-byte loads; each thread holds its row in 128
-// registers and runs four head chains at a time (four independent add chains
-// hide the add latency).
+// bit-exact.
+//
+// Shape: the scoring is a (rows x heads) product with K = 128 lanes, so the
+// kernel is tiled like a register-blocked f32 GEMM, with a separately rounded
+// multiply and add (__fmul_rn / __fadd_rn, which the compiler never fuses) in
+// place of each fused multiply-add, and the lanes visited in ascending order
+// for every (row, head) pair.  One CTA of 128 threads takes 128 rows of one
+// query: the rows (64 KB) and the query (32 KB) are copied to shared memory
+// (cp.async, row stride padded to 132 floats); each thread then owns an
+// 8-row x 8-head tile of dot products, so one 16-byte shared load feeds 32
+// products (a thread holding one row and looping over heads needs one load
+// per 4 products, which leaves the kernel bound by shared-memory wavefronts
+// near 0.6 of the FP32 rate).  Finally the 128 x 64 dot products go through
+// shared memory once more, and each thread applies ReLU and the weighted sum
+// to one row, head by head in head order.
 // The work is 8192 multiplies and 8192 adds per (query, row): CUDA-core
-// bound, not HBM bound.
+// bound, not HBM bound.  (Packed f32x2 arithmetic was measured slower here:
+// on this part it does not raise the FP32 rate.)
+#include <atomic>
+
 #include "rkv_common.cuh"
 #include "rkv_host.h"
 
@@ -25,14 +36,26 @@ constexpr int kIdxHeads = 64;
 constexpr int kIdxDim = 128;
 constexpr int kIdxRows = 128;  // rows (threads) per CTA
 
-__global__ void __launch_bounds__(kIdxRows, 3)
+constexpr int kIdxStride = kIdxDim + 4;  // padded shared row, floats
+constexpr int kIdxDotStride = kIdxHeads + 1;  // the dot-product tile's row, floats
+constexpr int kIdxSmem = (kIdxRows + kIdxHeads) * kIdxStride * 4 + kIdxHeads * 4;
+static_assert(kIdxRows * kIdxDotStride <= kIdxRows * kIdxStride, "dot tile fits in the row tile");
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem) : "memory");
+}
+
+__global__ void __launch_bounds__(kIdxRows, 2)
 indexer_score_kernel(const float* __restrict__ rows, const int64_t* __restrict__ row_start,
                      const int32_t* __restrict__ seq_rows, int64_t n_seq, const float* __restrict__ q,
                      const float* __restrict__ w, const int32_t* __restrict__ seq_of_query,
                      const int32_t* __restrict__ n_visible, int32_t blocks_per_q, float* __restrict__ scores,
                      int64_t ld, uint32_t* __restrict__ status) {
-  __shared__ __align__(16) float s_q[kIdxHeads * kIdxDim];
-  __shared__ float s_w[kIdxHeads];
+  extern __shared__ __align__(16) float smem[];
+  float* s_kv = smem;                              // [kIdxRows][kIdxStride]
+  float* s_q = smem + kIdxRows * kIdxStride;       // [kIdxHeads][kIdxStride]
+  float* s_w = s_q + kIdxHeads * kIdxStride;       // [kIdxHeads]
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int tid = threadIdx.x;
   const int64_t qi = blockIdx.x / blocks_per_q;
@@ -44,45 +67,83 @@ indexer_score_kernel(const float* __restrict__ rows, const int64_t* __restrict__
   }
   const int r0 = rb * kIdxRows;
   if (r0 >= nv) return;
-  const float4* qg = reinterpret_cast<const float4*>(q + qi * (kIdxHeads * kIdxDim));
-#pragma unroll 4
-  for (int v = tid; v < kIdxHeads * kIdxDim / 4; v += kIdxRows) reinterpret_cast<float4*>(s_q)[v] = __ldg(qg + v);
-  if (tid < kIdxHeads) s_w[tid] = __ldg(w + qi * kIdxHeads + tid);
-  __syncthreads();
-  const int r = r0 + tid;
-  if (r >= nv) return;
+  const int n_rows = nv - r0 < kIdxRows ? nv - r0 : kIdxRows;
 
-  const float4* rg = reinterpret_cast<const float4*>(rows + (__ldg(row_start + s) + r) * kIdxDim);
-  float kv[kIdxDim];
-#pragma unroll
-  for (int v = 0; v < kIdxDim / 4; ++v) {
-    const float4 t = __ldg(rg + v);
-    kv[4 * v] = t.x;
-    kv[4 * v + 1] = t.y;
-    kv[4 * v + 2] = t.z;
-    kv[4 * v + 3] = t.w;
+  // stage: a warp copies one 512-byte row per step (coalesced reads,
+  // conflict-free shared stores); rows past the visible end are zero
+  const float* rg = rows + (__ldg(row_start + s) + r0) * kIdxDim;
+  const float* qg = q + qi * (kIdxHeads * kIdxDim);
+  constexpr int kVecPerRow = kIdxDim / 4;
+#pragma unroll 4
+  for (int v = tid; v < kIdxRows * kVecPerRow; v += kIdxRows) {
+    const int r = v / kVecPerRow, c = 4 * (v % kVecPerRow);
+    if (r < n_rows)
+      cp_async16(s_kv + r * kIdxStride + c, rg + (int64_t)r * kIdxDim + c);
+    else
+      *reinterpret_cast<float4*>(s_kv + r * kIdxStride + c) = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  float acc = 0.0f;
+#pragma unroll 4
+  for (int v = tid; v < kIdxHeads * kVecPerRow; v += kIdxRows) {
+    const int h = v / kVecPerRow, c = 4 * (v % kVecPerRow);
+    cp_async16(s_q + h * kIdxStride + c, qg + h * kIdxDim + c);
+  }
+  if (tid < kIdxHeads) s_w[tid] = __ldg(w + qi * kIdxHeads + tid);
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+
+  // the thread tile: rows warp*32 + rt + 4a and heads ht + 8b (a, b < 8);
+  // at a fixed a (b) the warp reads 4 (8) consecutive padded rows, which
+  // fall in distinct banks, the other lanes reading the same addresses
+  const int warp = tid >> 5, lane = tid & 31, rt = lane & 3, ht = lane >> 2;
+  const float* kvb = s_kv + (warp * 32 + rt) * kIdxStride;
+  const float* qb = s_q + ht * kIdxStride;
+  float d[8][8];
+#pragma unroll
+  for (int a = 0; a < 8; ++a)
+#pragma unroll
+    for (int b = 0; b < 8; ++b) d[a][b] = 0.0f;
 #pragma unroll 1
-  for (int h = 0; h < kIdxHeads; h += 4) {
-    const float* qh = s_q + h * kIdxDim;
-    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int i = 0; i < kIdxDim; i += 4) {
+    float4 kr[8], qh[8];
 #pragma unroll
-    for (int i = 0; i < kIdxDim; i += 4) {
+    for (int a = 0; a < 8; ++a) kr[a] = *reinterpret_cast<const float4*>(kvb + 4 * a * kIdxStride + i);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float4 qv = *reinterpret_cast<const float4*>(qh + j * kIdxDim + i);
-        d[j] = __fadd_rn(d[j], __fmul_rn(kv[i], qv.x));
-        d[j] = __fadd_rn(d[j], __fmul_rn(kv[i + 1], qv.y));
-        d[j] = __fadd_rn(d[j], __fmul_rn(kv[i + 2], qv.z));
-        d[j] = __fadd_rn(d[j], __fmul_rn(kv[i + 3], qv.w));
-      }
-    }
+    for (int b = 0; b < 8; ++b) qh[b] = *reinterpret_cast<const float4*>(qb + 8 * b * kIdxStride + i);
+    // lanes i, i+1, i+2, i+3 in order, as rsLLM's dot adds them
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      if (d[j] > 0.0f) acc = __fadd_rn(acc, __fmul_rn(d[j], s_w[h + j]));
+    for (int a = 0; a < 8; ++a)
+#pragma unroll
+      for (int b = 0; b < 8; ++b) d[a][b] = __fadd_rn(d[a][b], __fmul_rn(kr[a].x, qh[b].x));
+#pragma unroll
+    for (int a = 0; a < 8; ++a)
+#pragma unroll
+      for (int b = 0; b < 8; ++b) d[a][b] = __fadd_rn(d[a][b], __fmul_rn(kr[a].y, qh[b].y));
+#pragma unroll
+    for (int a = 0; a < 8; ++a)
+#pragma unroll
+      for (int b = 0; b < 8; ++b) d[a][b] = __fadd_rn(d[a][b], __fmul_rn(kr[a].z, qh[b].z));
+#pragma unroll
+    for (int a = 0; a < 8; ++a)
+#pragma unroll
+      for (int b = 0; b < 8; ++b) d[a][b] = __fadd_rn(d[a][b], __fmul_rn(kr[a].w, qh[b].w));
   }
-  scores[qi * ld + r] = acc;
+  __syncthreads();  // every thread is done reading the row tile
+  float* s_dot = s_kv;  // [kIdxRows][kIdxDotStride]
+#pragma unroll
+  for (int a = 0; a < 8; ++a)
+#pragma unroll
+    for (int b = 0; b < 8; ++b) s_dot[(warp * 32 + rt + 4 * a) * kIdxDotStride + ht + 8 * b] = d[a][b];
+  __syncthreads();
+  if (tid >= n_rows) return;
+  // ReLU and the weighted sum head by head, in head order
+  const float* dr = s_dot + tid * kIdxDotStride;
+  float acc = 0.0f;
+#pragma unroll 8
+  for (int h = 0; h < kIdxHeads; ++h) {
+    const float dh = dr[h];
+    if (dh > 0.0f) acc = __fadd_rn(acc, __fmul_rn(dh, s_w[h]));
+  }
+  scores[qi * ld + r0 + tid] = acc;
 }
 
 }  // namespace rkv
@@ -107,12 +168,22 @@ extern "C" rkv_status rkv_indexer_scores_f32(const float* rows, const int64_t* r
     return fail(RKV_ERR_INVALID_ARGUMENT,
                 "rkv_indexer_scores_f32: rows, q (16-byte aligned), w, row_start, seq_rows, seq_of_query, "
                 "n_visible, scores and d_status are required");
+  // the shared-memory opt-in is per device
+  static std::atomic<bool> attr_set[kMaxDevicesCached];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevicesCached || !attr_set[dev].load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(indexer_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kIdxSmem);
+    if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_indexer_scores_f32: %s", cudaGetErrorString(e));
+    if (dev >= 0 && dev < kMaxDevicesCached) attr_set[dev].store(true, std::memory_order_release);
+  }
   const int64_t per_q = (max_visible + kIdxRows - 1) / kIdxRows;
   const int64_t blocks = per_q * n_q;
   if (blocks > (int64_t)INT32_MAX) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_indexer_scores_f32: grid too large");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)blocks);
   cfg.blockDim = dim3(kIdxRows);
+  cfg.dynamicSmemBytes = kIdxSmem;
   cfg.stream = (cudaStream_t)stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
