@@ -14,12 +14,12 @@
 // multiply and add (__fmul_rn / __fadd_rn, which the compiler never fuses) in
 // place of each fused multiply-add, and the lanes visited in ascending order
 // for every (row, head) pair.  One CTA of 128 threads takes 128 rows of one
-// query: the rows (64 KB) and the query (32 KB) are copied to shared memory
-// (cp.async, row stride padded to 132 floats); each thread then owns an
-// 8-row x 8-head tile of dot products, so one 16-byte shared load feeds 32
-// products (a thread holding one row and looping over heads needs one load
-// per 4 products, which leaves the kernel bound by shared-memory wavefronts
-// near 0.6 of the FP32 rate).  Finally the 128 x 64 dot products go through
+// query: the rows (64 KB) and the query (32 KB) pass through shared memory in
+// four chunks of 32 lanes, double-buffered with cp.async (55 KB per CTA, so
+// three CTAs share an SM); each thread owns an 8-row x 8-head tile of dot
+// products, so one 16-byte shared load feeds 32 products (a thread holding
+// one row and looping over heads needs one load per 4 products, which leaves
+// the kernel bound by shared-memory wavefronts near 0.6 of the FP32 rate).  Finally the 128 x 64 dot products go through
 // shared memory once more, and each thread applies ReLU and the weighted sum
 // to one row, head by head in head order.
 // The work is 8192 multiplies and 8192 adds per (query, row): CUDA-core
@@ -36,80 +36,56 @@ constexpr int kIdxHeads = 64;
 constexpr int kIdxDim = 128;
 constexpr int kIdxRows = 128;  // rows (threads) per CTA
 
-constexpr int kIdxStride = kIdxDim + 4;  // padded shared row, floats
-constexpr int kIdxDotStride = kIdxHeads + 1;  // the dot-product tile's row, floats
-constexpr int kIdxSmem = (kIdxRows + kIdxHeads) * kIdxStride * 4 + kIdxHeads * 4;
-static_assert(kIdxRows * kIdxDotStride <= kIdxRows * kIdxStride, "dot tile fits in the row tile");
+constexpr int kIdxChunk = 32;                  // lanes per staged chunk
+constexpr int kIdxChunks = kIdxDim / kIdxChunk;
+constexpr int kIdxStride = kIdxChunk + 4;      // padded shared row of a chunk, floats
+constexpr int kIdxBuf = (kIdxRows + kIdxHeads) * kIdxStride;  // one chunk buffer, floats
+constexpr int kIdxDotStride = kIdxHeads + 4;   // the dot-product tile's row, floats
+constexpr int kIdxSmem = (2 * kIdxBuf + kIdxHeads) * 4;
+static_assert(kIdxRows * kIdxDotStride <= 2 * kIdxBuf, "dot tile fits in the chunk buffers");
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem);
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem) : "memory");
 }
 
-__global__ void __launch_bounds__(kIdxRows, 2)
-indexer_score_kernel(const float* __restrict__ rows, const int64_t* __restrict__ row_start,
-                     const int32_t* __restrict__ seq_rows, int64_t n_seq, const float* __restrict__ q,
-                     const float* __restrict__ w, const int32_t* __restrict__ seq_of_query,
-                     const int32_t* __restrict__ n_visible, int32_t blocks_per_q, float* __restrict__ scores,
-                     int64_t ld, uint32_t* __restrict__ status) {
-  extern __shared__ __align__(16) float smem[];
-  float* s_kv = smem;                              // [kIdxRows][kIdxStride]
-  float* s_q = smem + kIdxRows * kIdxStride;       // [kIdxHeads][kIdxStride]
-  float* s_w = s_q + kIdxHeads * kIdxStride;       // [kIdxHeads]
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int tid = threadIdx.x;
-  const int64_t qi = blockIdx.x / blocks_per_q;
-  const int rb = (int)(blockIdx.x % blocks_per_q);
-  const int s = __ldg(seq_of_query + qi), nv = __ldg(n_visible + qi);
-  if (s < 0 || (int64_t)s >= n_seq || nv < 0 || nv > __ldg(seq_rows + s)) {
-    if (rb == 0 && tid == 0) set_status(status, RKV_ERR_INDEX_OUT_OF_RANGE);
-    return;
-  }
-  const int r0 = rb * kIdxRows;
-  if (r0 >= nv) return;
-  const int n_rows = nv - r0 < kIdxRows ? nv - r0 : kIdxRows;
-
-  // stage: a warp copies one 512-byte row per step (coalesced reads,
-  // conflict-free shared stores); rows past the visible end are zero
-  const float* rg = rows + (__ldg(row_start + s) + r0) * kIdxDim;
-  const float* qg = q + qi * (kIdxHeads * kIdxDim);
-  constexpr int kVecPerRow = kIdxDim / 4;
+// Copies lanes [32 ch, 32 ch + 32) of the CTA's rows and of the query into a
+// chunk buffer as one cp.async group: a warp copies 4 rows x 128 bytes per
+// step (coalesced reads, conflict-free shared stores); rows past the visible
+// end are left alone (the buffer's zeroed rows stay zero).
+__device__ __forceinline__ void stage_chunk(float* buf, const float* rg, const float* qg, int n_rows, int ch,
+                                            int tid) {
+  constexpr int kVec = kIdxChunk / 4;
+  float* s_kv = buf;
+  float* s_q = buf + kIdxRows * kIdxStride;
 #pragma unroll 4
-  for (int v = tid; v < kIdxRows * kVecPerRow; v += kIdxRows) {
-    const int r = v / kVecPerRow, c = 4 * (v % kVecPerRow);
-    if (r < n_rows)
-      cp_async16(s_kv + r * kIdxStride + c, rg + (int64_t)r * kIdxDim + c);
-    else
-      *reinterpret_cast<float4*>(s_kv + r * kIdxStride + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int v = tid; v < kIdxRows * kVec; v += kIdxRows) {
+    const int r = v / kVec, c = 4 * (v % kVec);
+    if (r < n_rows) cp_async16(s_kv + r * kIdxStride + c, rg + (int64_t)r * kIdxDim + ch * kIdxChunk + c);
   }
 #pragma unroll 4
-  for (int v = tid; v < kIdxHeads * kVecPerRow; v += kIdxRows) {
-    const int h = v / kVecPerRow, c = 4 * (v % kVecPerRow);
-    cp_async16(s_q + h * kIdxStride + c, qg + h * kIdxDim + c);
+  for (int v = tid; v < kIdxHeads * kVec; v += kIdxRows) {
+    const int h = v / kVec, c = 4 * (v % kVec);
+    cp_async16(s_q + h * kIdxStride + c, qg + h * kIdxDim + ch * kIdxChunk + c);
   }
-  if (tid < kIdxHeads) s_w[tid] = __ldg(w + qi * kIdxHeads + tid);
-  asm volatile("cp.async.wait_all;" ::: "memory");
-  __syncthreads();
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
 
-  // the thread tile: rows warp*32 + rt + 4a and heads ht + 8b (a, b < 8);
-  // at a fixed a (b) the warp reads 4 (8) consecutive padded rows, which
-  // fall in distinct banks, the other lanes reading the same addresses
-  const int warp = tid >> 5, lane = tid & 31, rt = lane & 3, ht = lane >> 2;
-  const float* kvb = s_kv + (warp * 32 + rt) * kIdxStride;
-  const float* qb = s_q + ht * kIdxStride;
-  float d[8][8];
-#pragma unroll
-  for (int a = 0; a < 8; ++a)
-#pragma unroll
-    for (int b = 0; b < 8; ++b) d[a][b] = 0.0f;
+// The thread tile over one staged chunk: rows warp*32 + rt + 4a and heads
+// ht + 8b (a, b < 8); at a fixed a (b) the warp reads 4 (8) consecutive
+// padded rows, which fall in distinct banks, the other lanes reading the
+// same addresses.  The lanes are added in ascending order, as rsLLM's dot
+// adds them.
+__device__ __forceinline__ void dot_chunk(float (&d)[8][8], const float* buf, int warp, int rt, int ht) {
+  const float* kvb = buf + (warp * 32 + rt) * kIdxStride;
+  const float* qb = buf + kIdxRows * kIdxStride + ht * kIdxStride;
 #pragma unroll 1
-  for (int i = 0; i < kIdxDim; i += 4) {
+  for (int i = 0; i < kIdxChunk; i += 4) {
     float4 kr[8], qh[8];
 #pragma unroll
     for (int a = 0; a < 8; ++a) kr[a] = *reinterpret_cast<const float4*>(kvb + 4 * a * kIdxStride + i);
 #pragma unroll
     for (int b = 0; b < 8; ++b) qh[b] = *reinterpret_cast<const float4*>(qb + 8 * b * kIdxStride + i);
-    // lanes i, i+1, i+2, i+3 in order, as rsLLM's dot adds them
 #pragma unroll
     for (int a = 0; a < 8; ++a)
 #pragma unroll
@@ -127,8 +103,70 @@ indexer_score_kernel(const float* __restrict__ rows, const int64_t* __restrict__
 #pragma unroll
       for (int b = 0; b < 8; ++b) d[a][b] = __fadd_rn(d[a][b], __fmul_rn(kr[a].w, qh[b].w));
   }
-  __syncthreads();  // every thread is done reading the row tile
-  float* s_dot = s_kv;  // [kIdxRows][kIdxDotStride]
+}
+
+__global__ void __launch_bounds__(kIdxRows, 3)
+indexer_score_kernel(const float* __restrict__ rows, const int64_t* __restrict__ row_start,
+                     const int32_t* __restrict__ seq_rows, int64_t n_seq, const float* __restrict__ q,
+                     const float* __restrict__ w, const int32_t* __restrict__ seq_of_query,
+                     const int32_t* __restrict__ n_visible, int32_t blocks_per_q, float* __restrict__ scores,
+                     int64_t ld, uint32_t* __restrict__ status) {
+  extern __shared__ __align__(16) float smem[];
+  float* buf0 = smem;
+  float* buf1 = smem + kIdxBuf;
+  float* s_w = smem + 2 * kIdxBuf;  // [kIdxHeads]
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int tid = threadIdx.x;
+  const int64_t qi = blockIdx.x / blocks_per_q;
+  const int rb = (int)(blockIdx.x % blocks_per_q);
+  const int s = __ldg(seq_of_query + qi), nv = __ldg(n_visible + qi);
+  if (s < 0 || (int64_t)s >= n_seq || nv < 0 || nv > __ldg(seq_rows + s)) {
+    if (rb == 0 && tid == 0) set_status(status, RKV_ERR_INDEX_OUT_OF_RANGE);
+    return;
+  }
+  const int r0 = rb * kIdxRows;
+  if (r0 >= nv) return;
+  const int n_rows = nv - r0 < kIdxRows ? nv - r0 : kIdxRows;
+  const float* rg = rows + (__ldg(row_start + s) + r0) * kIdxDim;
+  const float* qg = q + qi * (kIdxHeads * kIdxDim);
+
+  // rows past the visible end read as zero in both buffers
+  for (int v = tid; v < (kIdxRows - n_rows) * (kIdxChunk / 4); v += kIdxRows) {
+    const int r = n_rows + v / (kIdxChunk / 4), c = 4 * (v % (kIdxChunk / 4));
+    *reinterpret_cast<float4*>(buf0 + r * kIdxStride + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+    *reinterpret_cast<float4*>(buf1 + r * kIdxStride + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  stage_chunk(buf0, rg, qg, n_rows, 0, tid);
+  stage_chunk(buf1, rg, qg, n_rows, 1, tid);
+  if (tid < kIdxHeads) s_w[tid] = __ldg(w + qi * kIdxHeads + tid);
+
+  const int warp = tid >> 5, lane = tid & 31, rt = lane & 3, ht = lane >> 2;
+  float d[8][8];
+#pragma unroll
+  for (int a = 0; a < 8; ++a)
+#pragma unroll
+    for (int b = 0; b < 8; ++b) d[a][b] = 0.0f;
+  // two buffers: chunk ch + 2 is copied while chunk ch + 1 is multiplied
+  static_assert(kIdxChunks == 4, "the pipeline below covers four chunks");
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+  __syncthreads();
+  dot_chunk(d, buf0, warp, rt, ht);
+  __syncthreads();  // buffer 0 is free
+  stage_chunk(buf0, rg, qg, n_rows, 2, tid);
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+  __syncthreads();
+  dot_chunk(d, buf1, warp, rt, ht);
+  __syncthreads();  // buffer 1 is free
+  stage_chunk(buf1, rg, qg, n_rows, 3, tid);
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+  __syncthreads();
+  dot_chunk(d, buf0, warp, rt, ht);
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  dot_chunk(d, buf1, warp, rt, ht);
+  __syncthreads();  // every thread is done reading the buffers
+
+  float* s_dot = smem;  // [kIdxRows][kIdxDotStride]
 #pragma unroll
   for (int a = 0; a < 8; ++a)
 #pragma unroll
@@ -136,12 +174,15 @@ indexer_score_kernel(const float* __restrict__ rows, const int64_t* __restrict__
   __syncthreads();
   if (tid >= n_rows) return;
   // ReLU and the weighted sum head by head, in head order
-  const float* dr = s_dot + tid * kIdxDotStride;
+  const float4* dr = reinterpret_cast<const float4*>(s_dot + tid * kIdxDotStride);
   float acc = 0.0f;
-#pragma unroll 8
-  for (int h = 0; h < kIdxHeads; ++h) {
-    const float dh = dr[h];
-    if (dh > 0.0f) acc = __fadd_rn(acc, __fmul_rn(dh, s_w[h]));
+#pragma unroll 4
+  for (int h = 0; h < kIdxHeads; h += 4) {
+    const float4 d4 = dr[h / 4];
+    if (d4.x > 0.0f) acc = __fadd_rn(acc, __fmul_rn(d4.x, s_w[h]));
+    if (d4.y > 0.0f) acc = __fadd_rn(acc, __fmul_rn(d4.y, s_w[h + 1]));
+    if (d4.z > 0.0f) acc = __fadd_rn(acc, __fmul_rn(d4.z, s_w[h + 2]));
+    if (d4.w > 0.0f) acc = __fadd_rn(acc, __fmul_rn(d4.w, s_w[h + 3]));
   }
   scores[qi * ld + r0 + tid] = acc;
 }
