@@ -329,6 +329,36 @@ def bench_append(args, dist: Dist, dev, peak, n_seq: int = N_SEQ_APPEND, e2e: bo
     }
     # bit-exact check of the whole pool (W + K steps) against the oracle
     res["parity"] = dist.all_true(append_parity(pool, wl))
+    # the append's own traffic as a plain copy (rkv_copy_floor_bf16: the same
+    # grid, reads before the wait and launch arrangement, no codec), K steps
+    # in one graph after an L2 flush like the append: the ceiling the append
+    # is set against.  It overwrites the pool's rows, so it runs after the
+    # parity check.
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        for j in range(W):
+            pool.copy_floor_layer(0, wl.rows[j], wl.slots[j])
+        with torch.cuda.graph(g, stream=stream):
+            for j in range(W, W + K):
+                pool.copy_floor_layer(0, wl.rows[j], wl.slots[j])
+    graph = g
+
+    def replay_floor():
+        with torch.cuda.stream(stream):
+            graph.replay()
+
+    replay_floor()
+    stream.synchronize()
+    floor = []
+    for _ in range(3):
+        flush_l2(dev)
+        dist.barrier()
+        floor.append(dist.max(events_time(replay_floor, stream)))
+    del graph, g
+    floor_ms = min(floor)
+    res["copy_floor_ms_per_step"] = floor_ms / K
+    res["copy_floor_gbs_per_gpu"] = step_bytes * K / (floor_ms * 1e-3) / GB
+    res["append_speed_of_copy_floor"] = floor_ms / ms
     if e2e:
         # end to end through the public API: the host allocator reserves each
         # step's slots, pinned host rows and slots go to the device, append,
@@ -1326,6 +1356,9 @@ def summary(app: dict, phases: dict, split: dict | None) -> dict:
     peak, kernel ms per layer, parity), printed last in the line."""
     out = {"append_c2": {"gbs": _r(app["gbs_per_gpu"]), "frac": _r(app["frac"]), "us_step": _r(app["ms_per_step"] * 1e3),
                          "parity": app["parity"]}}
+    if app.get("copy_floor_ms_per_step") is not None:
+        out["append_c2"]["floor_us_step"] = _r(app["copy_floor_ms_per_step"] * 1e3)
+        out["append_c2"]["of_floor"] = _r(app["append_speed_of_copy_floor"])
     keys = {"gather": "gather_c3", "topk": "topk_c4", "sparse_gather": "sparse_c4", "mla_decode_dense": "mla_c3",
             "mla_decode_sparse": "mla_c4", "compress_decode": "cmp_dec", "compress_prefill": "cmp_pre",
             "indexer_score_topk": "idx_c4"}
@@ -1521,6 +1554,13 @@ def main():
             "repeats_median_rank_ms_per_step": app["repeats_median_rank_ms_per_step"],
             "wait_first_ms_per_step": app["wait_first_ms_per_step"],
             "wait_first_gbs_per_gpu": app["wait_first_gbs_per_gpu"],
+            "copy_floor": {"kernel": "copy_floor_kernel (rkv_copy_floor_bf16: the append's bytes, same launch, "
+                                     "no codec)",
+                           "ms_per_step": app.get("copy_floor_ms_per_step"),
+                           "gbs_per_gpu": app.get("copy_floor_gbs_per_gpu"),
+                           "frac_of_hbm_peak": None if app.get("copy_floor_gbs_per_gpu") is None
+                           else app["copy_floor_gbs_per_gpu"] / peak,
+                           "append_speed_of_copy_floor": app.get("append_speed_of_copy_floor")},
             "parity": app["parity"],
             "roofline": {"bound": "hbm", "achieved": app["gbs_per_gpu"], "peak": peak, "unit": "GB/s",
                          "frac": app["frac"], "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"

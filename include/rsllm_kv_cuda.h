@@ -161,6 +161,19 @@ RKV_API rkv_status rkv_append_quant_bf16_ex(const rkv_pool_view* pool, int32_t l
                                             const uint16_t* rows, int64_t n_tokens, const int32_t* slot_mapping,
                                             uint32_t flags, uint32_t* d_status, rkv_stream_t stream);
 
+/* Measurement reference, not a replacement of any rsLLM item: moves exactly
+ * the bytes rkv_append_quant_bf16_ex(..., RKV_APPEND_INPUTS_READY, ...) moves
+ * -- every row read, 672 B written to its slot's code, scale and RoPE
+ * regions -- with the same grid, the same reads before the wait on the
+ * previous kernel and the same programmatic dependent launch, but without the
+ * codec: it stores bytes of the input row, so the pool rows it writes are NOT
+ * valid FP8 rows.  A benchmark times it beside the append to show the
+ * append's distance from a plain copy of its own traffic.  Same host errors
+ * as the append; no device status. */
+RKV_API rkv_status rkv_copy_floor_bf16(const rkv_pool_view* pool, int32_t layer0, int32_t n_layers_in,
+                                       const uint16_t* rows, int64_t n_tokens, const int32_t* slot_mapping,
+                                       rkv_stream_t stream);
+
 /* The same append for f32 rows, rsLLM's own row type: the arguments, status
  * rules and stored form of rkv_append_quant_bf16, with rows f32
  * [n_layers_in][n_tokens][576] (32-byte aligned).  The block exponent is

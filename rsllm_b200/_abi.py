@@ -91,6 +91,7 @@ SIGNATURES = {
     "rkv_append_quant_bf16": (c_int32, [_P(PoolView), c_int32, c_int32, _u16p, c_int64, _i32p, _u32p, c_void_p]),
     "rkv_append_quant_bf16_ex": (c_int32, [_P(PoolView), c_int32, c_int32, _u16p, c_int64, _i32p, c_uint32, _u32p,
                                            c_void_p]),
+    "rkv_copy_floor_bf16": (c_int32, [_P(PoolView), c_int32, c_int32, _u16p, c_int64, _i32p, c_void_p]),
     "rkv_append_quant_f32": (c_int32, [_P(PoolView), c_int32, c_int32, _f32p, c_int64, _i32p, _u32p, c_void_p]),
     "rkv_scale_threshold_table": (None, [_u32p]),
     "rkv_gather_dequant_bf16": (c_int32, [_P(PoolView), c_int32, _i32p, c_int64, _i32p, c_int32, c_int32, _u16p,

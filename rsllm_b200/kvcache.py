@@ -214,6 +214,23 @@ class PagedKvPool:
         check(fn(byref(self.view), layer0, rows.shape[0], _ptr(rows), rows.shape[1], _ptr(slot_mapping),
                  _ptr(self.status), _stream(stream)))
 
+    def copy_floor_layer(self, layer0: int, rows: torch.Tensor, slot_mapping: torch.Tensor,
+                         stream: torch.cuda.Stream | None = None) -> None:
+        """Measurement reference (rkv_copy_floor_bf16): moves the bytes
+        ``append_layer(..., inputs_ready=True)`` moves, with the same launch,
+        but without the codec -- the rows it leaves in the slots are NOT valid
+        FP8 rows.  For timing the append against a plain copy of its traffic
+        on a pool whose contents no longer matter."""
+        _need(rows, torch.bfloat16, "rows", self.device)
+        _need(slot_mapping, torch.int32, "slot_mapping", self.device)
+        if rows.dim() == 2:
+            rows = rows.unsqueeze(0)
+        if rows.dim() != 3 or rows.shape[-1] != ROW_DIM or slot_mapping.dim() != 1 \
+                or slot_mapping.shape[0] != rows.shape[1]:
+            raise ShapeMismatch("copy_floor_layer: rows [..., n_tokens, 576] and slot_mapping [n_tokens] required")
+        check(self.lib.rkv_copy_floor_bf16(byref(self.view), layer0, rows.shape[0], _ptr(rows), rows.shape[1],
+                                           _ptr(slot_mapping), _stream(stream)))
+
     # -- data of device-detected errors -------------------------------------------
     def diagnose_append(self, layer0: int, rows: torch.Tensor, slot_mapping: torch.Tensor,
                         stream: torch.cuda.Stream | None = None) -> dict:
