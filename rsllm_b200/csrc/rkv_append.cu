@@ -105,10 +105,11 @@ append_quant_kernel(rkv_pool_view pool, int layer0, uint32_t n_tokens, uint32_t 
 // (r, r + W, then r + 2W, r + 3W, ...), each buffer refilled right after its
 // row is stored.  46 registers: five 256-thread CTAs per SM.
 constexpr int kEarlyRows = 2;
+constexpr unsigned long long kNegZero2 = 0x8000000080000000ull;  // -0.0 in both halves, a kernel argument
 
 __device__ __forceinline__ void append_row_rope4(const rkv_pool_view& pool, int layer, int32_t slot,
                                                  const uint32_t (&lat)[8], uint32_t rope, uint32_t* status,
-                                                 int lane) {
+                                                 int lane, unsigned long long nz2) {
   const unsigned FULL = 0xffffffffu;
   if (slot < 0) return;  // padding token
   const int64_t page = slot >> 6;
@@ -125,7 +126,7 @@ __device__ __forceinline__ void append_row_rope4(const rkv_pool_view& pool, int 
     return;
   }
   const int e = scale_exponent_bf16bits(m);
-  const uint4 codes = quant16(lat, __uint_as_float((uint32_t)(127 - e) << 23));
+  const uint4 codes = quant16_nz(lat, __uint_as_float((uint32_t)(127 - e) << 23), nz2);
   uint8_t* pg = page_base(pool, layer, page);
   st_stream16(pg + codes_off(off) + lane * 16, codes);
   const float sc = __shfl_sync(FULL, __uint_as_float((uint32_t)(e + 127) << 23), (lane & 7) * 4);
@@ -145,7 +146,7 @@ __device__ __forceinline__ void load_row_rope4(const uint8_t* rows8, const int32
 __global__ void __launch_bounds__(kAppendWarps * 32, 5)
 append_quant_early_kernel(rkv_pool_view pool, int layer0, uint32_t n_tokens, uint32_t n_rows,
                           const uint16_t* __restrict__ rows, const int32_t* __restrict__ slots,
-                          uint32_t* __restrict__ status) {
+                          uint32_t* __restrict__ status, unsigned long long nz2) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int lane = threadIdx.x & 31;
   const uint32_t stride = gridDim.x * kAppendWarps;
@@ -166,7 +167,7 @@ append_quant_early_kernel(rkv_pool_view pool, int layer0, uint32_t n_tokens, uin
     for (int i = 0; i < kEarlyRows; ++i) {
       const uint32_t ri = r + i * stride;
       if (ri < n_rows) {
-        append_row_rope4(pool, layer0 + (int)(ri / n_tokens), slot[i], lat[i], rope[i], status, lane);
+        append_row_rope4(pool, layer0 + (int)(ri / n_tokens), slot[i], lat[i], rope[i], status, lane, nz2);
         const uint32_t rn = ri + kEarlyRows * stride;
         if (rn < n_rows) load_row_rope4(rows8, slots, rn, n_tokens, lane, lat[i], rope[i], slot[i]);
       }
@@ -245,7 +246,8 @@ static rkv_status append_bf16(const rkv_pool_view* pool, int32_t layer0, int32_t
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = early ? cudaLaunchKernelEx(&cfg, append_quant_early_kernel, pool_copy(*pool), (int)layer0,
-                                             (uint32_t)n_tokens, (uint32_t)n_rows, rows, slot_mapping, d_status)
+                                             (uint32_t)n_tokens, (uint32_t)n_rows, rows, slot_mapping, d_status,
+                                             kNegZero2)
                         : cudaLaunchKernelEx(&cfg, append_quant_kernel, pool_copy(*pool), (int)layer0,
                                              (uint32_t)n_tokens, (uint32_t)n_rows, rows, slot_mapping, d_status);
   if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));

@@ -98,6 +98,27 @@ __device__ __forceinline__ uint32_t quant_pair(uint32_t w, unsigned long long in
   return cvt_e4m3x2(__uint_as_float((uint32_t)t), __uint_as_float((uint32_t)(t >> 32)));
 }
 
+// The same pair -> codes in two packed instructions instead of the bit-wise
+// clear: the product as fma.rn.f32x2(v, inv, nz) with nz = -0.0 in both
+// halves, passed in at run time -- exactly the rounded product, sign included
+// -- then add.rn.f32x2 of +0.0, which turns a zero of either sign into +0.0
+// and leaves every other value as it is.  An add cannot be fused into an fma,
+// so the product is rounded before the add (a multiply followed by that add
+// can be contracted into one fused multiply-add, which keeps the sign of a
+// product that underflows to zero; so can an fma whose -0.0 addend the
+// compiler sees).
+__device__ __forceinline__ unsigned long long fma_f32x2(unsigned long long a, unsigned long long b,
+                                                        unsigned long long c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint32_t quant_pair_nz(uint32_t w, unsigned long long inv2, unsigned long long nz2) {
+  const unsigned long long v = ((unsigned long long)(w & 0xffff0000u) << 32) | (unsigned long long)(w << 16);
+  const unsigned long long t = add_f32x2(fma_f32x2(v, inv2, nz2), 0ull);
+  return cvt_e4m3x2(__uint_as_float((uint32_t)t), __uint_as_float((uint32_t)(t >> 32)));
+}
+
 // ---- decode ---------------------------------------------------------------
 
 // Two E4M3 bytes -> f16x2 (exact: every E4M3 value is an f16 normal or zero).
@@ -165,6 +186,15 @@ __device__ __forceinline__ uint4 quant16(const uint32_t (&w)[8], float inv) {
   uint32_t c[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) c[i] = quant_pair(w[i], inv2);
+  return make_uint4(c[0] | (c[1] << 16), c[2] | (c[3] << 16), c[4] | (c[5] << 16), c[6] | (c[7] << 16));
+}
+
+// quant16 through quant_pair_nz (nz2: -0.0 in both halves, a run-time value).
+__device__ __forceinline__ uint4 quant16_nz(const uint32_t (&w)[8], float inv, unsigned long long nz2) {
+  const unsigned long long inv2 = ((unsigned long long)__float_as_uint(inv) << 32) | __float_as_uint(inv);
+  uint32_t c[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) c[i] = quant_pair_nz(w[i], inv2, nz2);
   return make_uint4(c[0] | (c[1] << 16), c[2] | (c[3] << 16), c[4] | (c[5] << 16), c[6] | (c[7] << 16));
 }
 

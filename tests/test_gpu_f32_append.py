@@ -89,8 +89,8 @@ def test_bad_rows_write_nothing(cuda, orc):
         pool.check("append")
 
 
-@pytest.mark.parametrize("dtype", ["f32", "bf16"])
-def test_tiny_lanes_next_to_huge_amax(cuda, orc, dtype):
+@pytest.mark.parametrize("dtype,inputs_ready", [("f32", False), ("bf16", False), ("bf16", True)])
+def test_tiny_lanes_next_to_huge_amax(cuda, orc, dtype, inputs_ready):
     """Lanes so small next to their block's amax that v / 2^e underflows: the
     reference's f32 division gives -0.0 or +0.0 and the code is 0x00 either
     way (sign = x < 0); subnormal and tiny negative quotients keep 0x80 where
@@ -114,7 +114,7 @@ def test_tiny_lanes_next_to_huge_amax(cuda, orc, dtype):
     slots = np.arange(n_tok, dtype=np.int32)
     pool = rk.PagedKvPool(2, 1, device=cuda)
     pool.storage.zero_()
-    pool.append_layer(0, rows_t.to(cuda), i32(slots, cuda))
+    pool.append_layer(0, rows_t.to(cuda), i32(slots, cuda), inputs_ready=inputs_ready)
     pool.check("append")
     ref = orc.new_pool(2, 1)
     assert orc.append_rows(ref, 2, 1, 0, ref_rows, slots) == 0
