@@ -24,13 +24,14 @@ namespace rkv {
 static inline rkv_pool_view pool_copy(const rkv_pool_view& p) { return p; }
 
 constexpr int kAppendWarps = 8;  // 256-thread CTAs
+constexpr unsigned long long kNegZero2 = 0x8000000080000000ull;  // -0.0 in both halves, a kernel argument
 
 // Quantise and store one row a warp holds: lane l has latent lanes
 // 16l..16l+15 in lat (inside 64-lane block l/4), lanes 0..7 hold 16 B each of
 // the RoPE part.  Every lane sees the same slot, so the branches are uniform.
 __device__ __forceinline__ void append_row(const rkv_pool_view& pool, int layer, int32_t slot,
                                            const uint32_t (&lat)[8], const uint4& rope, uint32_t* status,
-                                           int lane) {
+                                           int lane, unsigned long long nz2) {
   const unsigned FULL = 0xffffffffu;
   if (slot < 0) return;  // padding token
   const int64_t page = slot >> 6;
@@ -47,7 +48,7 @@ __device__ __forceinline__ void append_row(const rkv_pool_view& pool, int layer,
     return;
   }
   const int e = scale_exponent_bf16bits(m);
-  const uint4 codes = quant16(lat, __uint_as_float((uint32_t)(127 - e) << 23));
+  const uint4 codes = quant16(lat, __uint_as_float((uint32_t)(127 - e) << 23), nz2);
   uint8_t* pg = page_base(pool, layer, page);
   st_stream16(pg + codes_off(off) + lane * 16, codes);
   // lane j < 8 stores the scale of block j, held by lane 4j, and 16 B of RoPE
@@ -68,7 +69,7 @@ __device__ __forceinline__ void append_row(const rkv_pool_view& pool, int layer,
 __global__ void __launch_bounds__(kAppendWarps * 32)
 append_quant_kernel(rkv_pool_view pool, int layer0, uint32_t n_tokens, uint32_t n_rows,
                     const uint16_t* __restrict__ rows, const int32_t* __restrict__ slots,
-                    uint32_t* __restrict__ status) {
+                    uint32_t* __restrict__ status, unsigned long long nz2) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = threadIdx.x & 31;
@@ -89,7 +90,7 @@ append_quant_kernel(rkv_pool_view pool, int layer0, uint32_t n_tokens, uint32_t 
       if (lane < 8) nrope = ld_stream16(rows8 + (size_t)rn * (kRowDim * 2) + 1024 + lane * 16);
       nslot = __ldg(slots + rn % n_tokens);
     }
-    append_row(pool, layer0 + (int)(r / n_tokens), slot, lat, rope, status, lane);
+    append_row(pool, layer0 + (int)(r / n_tokens), slot, lat, rope, status, lane, nz2);
 #pragma unroll
     for (int j = 0; j < 8; ++j) lat[j] = nlat[j];
     rope = nrope;
@@ -105,7 +106,6 @@ append_quant_kernel(rkv_pool_view pool, int layer0, uint32_t n_tokens, uint32_t 
 // (r, r + W, then r + 2W, r + 3W, ...), each buffer refilled right after its
 // row is stored.  46 registers: five 256-thread CTAs per SM.
 constexpr int kEarlyRows = 2;
-constexpr unsigned long long kNegZero2 = 0x8000000080000000ull;  // -0.0 in both halves, a kernel argument
 
 __device__ __forceinline__ void append_row_rope4(const rkv_pool_view& pool, int layer, int32_t slot,
                                                  const uint32_t (&lat)[8], uint32_t rope, uint32_t* status,
@@ -126,7 +126,7 @@ __device__ __forceinline__ void append_row_rope4(const rkv_pool_view& pool, int 
     return;
   }
   const int e = scale_exponent_bf16bits(m);
-  const uint4 codes = quant16_nz(lat, __uint_as_float((uint32_t)(127 - e) << 23), nz2);
+  const uint4 codes = quant16(lat, __uint_as_float((uint32_t)(127 - e) << 23), nz2);
   uint8_t* pg = page_base(pool, layer, page);
   st_stream16(pg + codes_off(off) + lane * 16, codes);
   const float sc = __shfl_sync(FULL, __uint_as_float((uint32_t)(e + 127) << 23), (lane & 7) * 4);
@@ -175,14 +175,16 @@ append_quant_early_kernel(rkv_pool_view pool, int layer0, uint32_t n_tokens, uin
   }
 }
 
-// Exhaustive-check helper: the append kernel's lane conversion (packed
-// multiply by the inverse scale, here 1.0, -0.0 folded to +0.0, saturating RNE) applied to
-// raw f32 values that are already divided by their block scale.
-__global__ void e4m3_code_range_kernel(uint32_t first, int64_t n, uint8_t* __restrict__ out) {
+// Exhaustive-check helper: the append kernels' lane conversion (the product
+// with the inverse scale, here 1.0, as fma.rn.f32x2 with the run-time -0.0
+// pair, -0.0 folded to +0.0 by add.rn.f32x2 of +0.0, saturating RNE) applied
+// to raw f32 values that are already divided by their block scale.
+__global__ void e4m3_code_range_kernel(uint32_t first, int64_t n, uint8_t* __restrict__ out,
+                                       unsigned long long nz2) {
   const unsigned long long one2 = 0x3f8000003f800000ull;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const unsigned long long x = first + (uint32_t)i;  // lane 0 = x, lane 1 = +0.0
-    const unsigned long long t = clear_zero_sign2(mul_f32x2(x, one2));
+    const unsigned long long t = add_f32x2(fma_f32x2(x, one2, nz2), 0ull);
     out[i] = (uint8_t)(cvt_e4m3x2(__uint_as_float((uint32_t)t), 0.0f) & 0xffu);
   }
 }
@@ -249,7 +251,8 @@ static rkv_status append_bf16(const rkv_pool_view* pool, int32_t layer0, int32_t
                                              (uint32_t)n_tokens, (uint32_t)n_rows, rows, slot_mapping, d_status,
                                              kNegZero2)
                         : cudaLaunchKernelEx(&cfg, append_quant_kernel, pool_copy(*pool), (int)layer0,
-                                             (uint32_t)n_tokens, (uint32_t)n_rows, rows, slot_mapping, d_status);
+                                             (uint32_t)n_tokens, (uint32_t)n_rows, rows, slot_mapping, d_status,
+                                             kNegZero2);
   if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
   return check_launch(what);
 }
@@ -275,6 +278,6 @@ extern "C" rkv_status rkv_e4m3fn_code_range(uint32_t first_bits, int64_t n, uint
   if (n < 0 || (n > 0 && !out)) return fail(RKV_ERR_INVALID_ARGUMENT, "rkv_e4m3fn_code_range: bad output");
   if (n > 0x100000000LL - (int64_t)first_bits) return fail(RKV_ERR_SHAPE_MISMATCH, "rkv_e4m3fn_code_range: range wraps");
   if (n == 0) return RKV_OK;
-  e4m3_code_range_kernel<<<148 * 8, 256, 0, (cudaStream_t)stream>>>(first_bits, n, out);
+  e4m3_code_range_kernel<<<148 * 8, 256, 0, (cudaStream_t)stream>>>(first_bits, n, out, kNegZero2);
   return check_launch("rkv_e4m3fn_code_range");
 }

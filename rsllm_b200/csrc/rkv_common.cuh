@@ -91,15 +91,9 @@ __device__ __forceinline__ unsigned long long clear_zero_sign2(unsigned long lon
 // One bf16 pair -> two E4M3 codes (bits 0..15): t = v * 2^-e exactly as the
 // reference's v / 2^e (both correctly rounded), -0.0 folded into +0.0 (the
 // reference's sign is `x < 0`), then RNE with saturation.  For bf16 inputs
-// |t| <= 448 always holds, so the reference's clamp is the identity.
-__device__ __forceinline__ uint32_t quant_pair(uint32_t w, unsigned long long inv2) {
-  const unsigned long long v = ((unsigned long long)(w & 0xffff0000u) << 32) | (unsigned long long)(w << 16);
-  const unsigned long long t = clear_zero_sign2(mul_f32x2(v, inv2));
-  return cvt_e4m3x2(__uint_as_float((uint32_t)t), __uint_as_float((uint32_t)(t >> 32)));
-}
-
-// The same pair -> codes in two packed instructions instead of the bit-wise
-// clear: the product as fma.rn.f32x2(v, inv, nz) with nz = -0.0 in both
+// |t| <= 448 always holds, so the reference's clamp is the identity.  Two
+// packed instructions for the arithmetic: the product as
+// fma.rn.f32x2(v, inv, nz) with nz = -0.0 in both
 // halves, passed in at run time -- exactly the rounded product, sign included
 // -- then add.rn.f32x2 of +0.0, which turns a zero of either sign into +0.0
 // and leaves every other value as it is.  An add cannot be fused into an fma,
@@ -113,7 +107,7 @@ __device__ __forceinline__ unsigned long long fma_f32x2(unsigned long long a, un
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
   return r;
 }
-__device__ __forceinline__ uint32_t quant_pair_nz(uint32_t w, unsigned long long inv2, unsigned long long nz2) {
+__device__ __forceinline__ uint32_t quant_pair(uint32_t w, unsigned long long inv2, unsigned long long nz2) {
   const unsigned long long v = ((unsigned long long)(w & 0xffff0000u) << 32) | (unsigned long long)(w << 16);
   const unsigned long long t = add_f32x2(fma_f32x2(v, inv2, nz2), 0ull);
   return cvt_e4m3x2(__uint_as_float((uint32_t)t), __uint_as_float((uint32_t)(t >> 32)));
@@ -180,21 +174,13 @@ __device__ __forceinline__ void dequant16(const uint4& c, const DecodeScale& d, 
   o1.w = dequant2(c.w >> 16, d);
 }
 
-// 16 bf16 lanes (8 words) -> 16 codes (uint4).
-__device__ __forceinline__ uint4 quant16(const uint32_t (&w)[8], float inv) {
+// 16 bf16 lanes (8 words) -> 16 codes (uint4); nz2: -0.0 in both halves, a
+// run-time value (see quant_pair).
+__device__ __forceinline__ uint4 quant16(const uint32_t (&w)[8], float inv, unsigned long long nz2) {
   const unsigned long long inv2 = ((unsigned long long)__float_as_uint(inv) << 32) | __float_as_uint(inv);
   uint32_t c[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) c[i] = quant_pair(w[i], inv2);
-  return make_uint4(c[0] | (c[1] << 16), c[2] | (c[3] << 16), c[4] | (c[5] << 16), c[6] | (c[7] << 16));
-}
-
-// quant16 through quant_pair_nz (nz2: -0.0 in both halves, a run-time value).
-__device__ __forceinline__ uint4 quant16_nz(const uint32_t (&w)[8], float inv, unsigned long long nz2) {
-  const unsigned long long inv2 = ((unsigned long long)__float_as_uint(inv) << 32) | __float_as_uint(inv);
-  uint32_t c[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) c[i] = quant_pair_nz(w[i], inv2, nz2);
+  for (int i = 0; i < 8; ++i) c[i] = quant_pair(w[i], inv2, nz2);
   return make_uint4(c[0] | (c[1] << 16), c[2] | (c[3] << 16), c[4] | (c[5] << 16), c[6] | (c[7] << 16));
 }
 
