@@ -54,9 +54,9 @@ GB = 1e9
 # (profiles/append_quant_c2.md, gather_dequant_c3_small.md,
 # sparse_gather_c4_small.md).  The append's figure is the mean over four
 # consecutive launches captured without cache control, so each launch carries
-# the previous launch's page writes draining from L2: 17,992,640 B read +
-# 8,241,600 B written per 15,616-row launch.
-NCU_TRAFFIC_PER_ROW = {"append": (17992640 + 8241600) / 15616, "gather": (176206080 + 248001536) / 262144,
+# the previous launch's page writes draining from L2: 17,992,896 B read +
+# 8,830,016 B written per 15,616-row launch.
+NCU_TRAFFIC_PER_ROW = {"append": (17992896 + 8830016) / 15616, "gather": (176206080 + 248001536) / 262144,
                        "sparse_gather": (335133696 + 548617728) / 524288}
 
 
