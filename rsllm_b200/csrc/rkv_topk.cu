@@ -10,9 +10,9 @@
 // (0 = cannot win; -0.0 folded into +0.0 because `>` ties them), so "key >= t"
 // is "score >= float(t)".
 //  * n <= 8192: every key goes to the shared-memory candidate buffer.
-//  * Otherwise a 4096-key sample (32 contiguous chunks of 128) gives a
+//  * Otherwise a 2048-key sample (16 contiguous chunks of 128) gives a
 //    threshold t, the sample's r-th largest key, with r set from the sampling
-//    error so that effective_k to ~1.5 effective_k scores are expected at or
+//    error so that effective_k to ~1.7 effective_k scores are expected at or
 //    above it; a separate light kernel (128-thread CTAs, the sample in
 //    registers) picks every query's t before the selection kernel runs, so
 //    the selection streams its row from the start.  One pass over the
@@ -42,8 +42,8 @@ constexpr int kBucketBins = 2048;
 constexpr uint32_t kBucketMax = 32;     // bucket sort: largest bucket sorted by one thread
 constexpr int kSortedCap = kTopkMaxK + kBucketMax;
 constexpr int kSampleChunk = 128;                         // keys per chunk: one float4 per lane
-constexpr int kSampleChunks = 32;
-constexpr int kSample = kSampleChunks * kSampleChunk;     // 4096
+constexpr int kSampleChunks = 16;
+constexpr int kSample = kSampleChunks * kSampleChunk;     // 2048
 #ifndef RKV_TOPK_PREFETCH_ROUNDS
 #define RKV_TOPK_PREFETCH_ROUNDS 2
 #endif
@@ -248,11 +248,11 @@ __device__ uint32_t sample_kth_largest(const uint32_t (&keys)[PER], uint32_t ran
 // (the sample's rank-th largest key, 0 when the sample cannot supply one)
 // written to out[q * k] -- the first entry of the query's own output row,
 // which topk_select_kernel reads before it writes any output.  One 128-thread
-// CTA per query, 32 sample keys per thread in registers; many CTAs per SM, so
+// CTA per query, 16 sample keys per thread in registers; many CTAs per SM, so
 // a layer's queries take their latency-bound sample phases in about one wave
 // instead of inside the streaming kernel.
 constexpr int kThrThreads = 128;
-constexpr int kThrPerThread = kSample / kThrThreads;  // 32
+constexpr int kThrPerThread = kSample / kThrThreads;  // 16
 
 __global__ void __launch_bounds__(kThrThreads)
 topk_threshold_kernel(const float* __restrict__ scores, int64_t ld, const int32_t* __restrict__ n_visible, int k,
@@ -266,7 +266,7 @@ topk_threshold_kernel(const float* __restrict__ scores, int64_t ld, const int32_
   const float* row = scores + (int64_t)q * ld;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint32_t skeys[kThrPerThread];
-  constexpr int kChunksPerWarp = kSampleChunks / (kThrThreads / 32);  // 8
+  constexpr int kChunksPerWarp = kSampleChunks / (kThrThreads / 32);  // 4
 #pragma unroll
   for (int c = 0; c < kChunksPerWarp; ++c) {
     const int64_t c0 = sample_chunk_start(w * kChunksPerWarp + c, n, vec);
