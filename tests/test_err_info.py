@@ -79,3 +79,19 @@ def test_static_moves_outside_the_pool_name_the_page(lib):
                                          0, NULL, NULL)
     info = _abi.last_error_info()
     assert rc == _abi.RKV_ERR_INDEX_OUT_OF_RANGE and (info["what"], info["idx"], info["len"]) == ("dst", 9, 8)
+
+
+def test_copy_floor_validates_like_the_append(lib):
+    """rkv_copy_floor_bf16 (the append's traffic for measurement) rejects the
+    same bad arguments as the append, with the same error data, before any
+    device work."""
+    v = fake_view(n_layers=2)
+    rc = lib.rkv_copy_floor_bf16(byref(v), 1, 2, c_void_p(256), 8, c_void_p(256), NULL)
+    info = _abi.last_error_info()
+    assert rc == _abi.RKV_ERR_INVALID_LAYER and info["idx"] == 2 and info["max"] == 2
+    rc = lib.rkv_copy_floor_bf16(byref(v), 0, 1, c_void_p(256), -3, c_void_p(256), NULL)
+    info = _abi.last_error_info()
+    assert rc == _abi.RKV_ERR_SHAPE_MISMATCH and (info["what"], info["expected"], info["actual"]) == ("n_tokens", 0, -3)
+    rc = lib.rkv_copy_floor_bf16(byref(v), 0, 1, c_void_p(8), 4, c_void_p(256), NULL)  # rows not 32-byte aligned
+    assert rc == _abi.RKV_ERR_INVALID_ARGUMENT
+    assert lib.rkv_copy_floor_bf16(byref(v), 0, 1, c_void_p(256), 0, c_void_p(256), NULL) == _abi.RKV_OK
