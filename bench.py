@@ -367,6 +367,64 @@ def bench_append(args, dist: Dist, dev, peak, n_seq: int = N_SEQ_APPEND, e2e: bo
     return res
 
 
+def bench_append_f32(args, dist: Dist, dev, peak, n_seq: int = N_SEQ_APPEND) -> dict:
+    """Config 2's decode step with f32 rows, rsLLM's own row type
+    (rkv_append_quant_f32: the host log2f exponent through its threshold
+    table, RoPE rounded to bf16): the headline's slots and values with f32-only
+    low bits added, W eager steps then K steps in one CUDA graph after an L2
+    flush, max over ranks; parity of the whole pool against the oracle's f32
+    append."""
+    import oracle
+    import rsllm_b200 as rk
+
+    W, K = args.warmup, args.steps
+    wl = AppendWorkload(W + K, seed=5 + 7919 * dist.rank, dev=dev, n_seq=n_seq)
+    g = torch.Generator(device=dev)
+    g.manual_seed(17 + 7919 * dist.rank)
+    rows = torch.empty(wl.rows.shape, dtype=torch.float32, device=dev)
+    for j in range(W + K):
+        r = wl.rows[j].float()
+        rows[j] = r * (1.0 + torch.randn(r.shape, generator=g, device=dev) * 2.0 ** -10)
+    wl.rows = None
+    pool = rk.PagedKvPool(wl.n_pages, N_LAYERS, device=dev)
+    pool.storage.zero_()
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for j in range(W):
+            pool.append_layer(0, rows[j], wl.slots[j])
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for j in range(W, W + K):
+                pool.append_layer(0, rows[j], wl.slots[j])
+
+    def replay():
+        with torch.cuda.stream(stream):
+            graph.replay()
+
+    replay()
+    stream.synchronize()
+    flush_l2(dev)
+    dist.barrier()
+    ms = dist.max(events_time(replay, stream))
+    pool.check("append f32", stream)
+    del graph
+    ref = oracle.new_pool(wl.n_pages, N_LAYERS)
+    ok = True
+    for j in range(W + K):
+        ok = ok and oracle.append_rows(ref, wl.n_pages, N_LAYERS, 0, rows[j].cpu().numpy(), wl.slots_np[j],
+                                       n_threads=oracle.threads()) == 0
+    ok = ok and same_bytes(pool.storage, ref)
+    step_bytes = N_LAYERS * n_seq * (576 * 4 + 672) + n_seq * 4
+    del pool, rows
+    torch.cuda.empty_cache()
+    return {"config": f"c2 shape with f32 rows: {n_seq} sequences x {N_LAYERS} layers per step, K = {K} steps in "
+                      "one CUDA graph, L2 flushed",
+            "ms_per_step": ms / K, "gbs_per_gpu": step_bytes * K / (ms * 1e-3) / GB,
+            "frac_of_hbm_peak": step_bytes * K / (ms * 1e-3) / GB / peak, "step_bytes": step_bytes,
+            "parity": dist.all_true(ok),
+            "parity_sample": "the whole pool after all W + K steps vs the oracle's f32 append"}
+
+
 def append_parity(pool, wl: AppendWorkload) -> bool:
     """The pool after every step of the run equals the oracle's pool after
     the same appends (fp8_kv_quantize_row_inplace + slot-mapped append)."""
@@ -1373,6 +1431,10 @@ def summary(app: dict, phases: dict, split: dict | None) -> dict:
         if "parity" in p:
             d["parity"] = p["parity"]
         out[short] = d
+    p = phases.get("append_f32")
+    if isinstance(p, dict):
+        out["append_f32_c2"] = {"gbs": _r(p.get("gbs_per_gpu")), "frac": _r(p.get("frac_of_hbm_peak")),
+                                "us_step": _r(p["ms_per_step"] * 1e3), "parity": p.get("parity")}
     for name, short in (("prefix_cow_evict_compact", "prefix_c5"), ("prefix_cow_evict_compact_aligned", "prefix_c5a")):
         p = phases.get(name)
         if isinstance(p, dict):
@@ -1432,14 +1494,14 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--phases", default="gather,sparse,prefix,kvc,compress,indexer",
-                    help="extra configs to measure (comma list of gather,sparse,prefix,kvc,compress,indexer or "
-                         "'none')")
+    ap.add_argument("--phases", default="gather,sparse,prefix,kvc,compress,indexer,f32",
+                    help="extra configs to measure (comma list of gather,sparse,prefix,kvc,compress,indexer,f32 "
+                         "or 'none')")
     ap.add_argument("--phase-steps", type=int, default=3)
     ap.add_argument("--phase-warmup", type=int, default=1)
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--only", choices=["all", "append", "gather", "sparse", "prefix", "kvc", "compress", "indexer",
-                                       "split", "topk"],
+                                       "split", "topk", "f32"],
                     default="all",
                     help="run one workload alone (profiling)")
     ap.add_argument("--mla-splits", type=int, default=16,
@@ -1485,6 +1547,8 @@ def main():
             res = bench_split(args, dist, dev, peak)
         elif args.only == "topk":
             res = bench_topk_only(args, dist, dev, peak)
+        elif args.only == "f32":
+            res = bench_append_f32(args, dist, dev, peak)
         else:
             res = bench_sparse(args, dist, dev, peak)
         clocks.stop()
@@ -1511,6 +1575,8 @@ def main():
         phases.update(bench_compress(args, dist, dev, peak))
     if "indexer" in wanted:
         phases["indexer_score_topk"] = bench_indexer(args, dist, dev, peak)
+    if "f32" in wanted:
+        phases["append_f32"] = bench_append_f32(args, dist, dev, peak)
     split = bench_split(args, dist, dev, peak) if dist.world > 1 and not args.no_split else None
     clk = clocks.stop()
 

@@ -114,7 +114,11 @@ def test_summary_fits_the_kept_tail():
         phases[k] = {"compact_gbs": 6600.1, "compact_frac_of_hbm_peak": 1.01, "append_gbs": 4400.2, "parity": True}
     split = {k: {"aggregate_gbs": 12345.678, "parity": True} for k in ("append_c2", "gather_c3", "topk_c4",
                                                                         "sparse_c4", "prefix_c5")}
-    app = {"gbs_per_gpu": 3500.123, "frac": 0.5432, "ms_per_step": 0.0081408, "parity": True}
+    phases["append_f32"] = {"gbs_per_gpu": 5123.456, "frac_of_hbm_peak": 0.7834, "ms_per_step": 0.0090812,
+                            "parity": True}
+    app = {"gbs_per_gpu": 3500.123, "frac": 0.5432, "ms_per_step": 0.0081408, "parity": True,
+           "copy_floor_ms_per_step": 0.0055497, "append_speed_of_copy_floor": 0.8971}
     s = json.dumps(bench.summary(app, phases, split))
-    assert len(s) < 1300, len(s)
+    assert len(s) < 1400, len(s)
     assert json.loads(s)["mla_c3"]["frac"] == 0.321
+    assert json.loads(s)["append_f32_c2"]["parity"] is True
