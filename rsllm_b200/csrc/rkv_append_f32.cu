@@ -61,7 +61,7 @@ const ThresholdTable& f32_threshold_table() {
 __global__ void __launch_bounds__(kF32Warps * 32)
 append_quant_f32_kernel(rkv_pool_view pool, int layer0, uint32_t n_tokens, uint32_t n_rows,
                         const float* __restrict__ rows, const int32_t* __restrict__ slots,
-                        uint32_t* __restrict__ status, const ThresholdTable tab) {
+                        uint32_t* __restrict__ status, const ThresholdTable tab, unsigned long long nz2) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = threadIdx.x & 31;
@@ -74,7 +74,7 @@ append_quant_f32_kernel(rkv_pool_view pool, int layer0, uint32_t n_tokens, uint3
   for (; r < n_rows; r += stride) {
     const uint32_t rn = r + stride;
     if (rn < n_rows) load_row_f32(rows8, slots, rn, n_tokens, lane, nxt);
-    append_row_f32(pool, layer0 + (int)(r / n_tokens), cur, tab, status, lane);
+    append_row_f32(pool, layer0 + (int)(r / n_tokens), cur, tab, status, lane, nz2);
     cur = nxt;
   }
 }
@@ -130,7 +130,8 @@ extern "C" rkv_status rkv_append_quant_f32(const rkv_pool_view* pool, int32_t la
   cfg.numAttrs = 1;
   const rkv_pool_view v = *pool;
   cudaError_t e = cudaLaunchKernelEx(&cfg, append_quant_f32_kernel, v, (int)layer0, (uint32_t)n_tokens,
-                                     (uint32_t)n_rows, rows, slot_mapping, d_status, tab);
+                                     (uint32_t)n_rows, rows, slot_mapping, d_status, tab,
+                                     0x8000000080000000ull);  // -0.0 in both halves, for quant_pair_f32
   if (e != cudaSuccess) return fail(RKV_ERR_CUDA, "rkv_append_quant_f32: launch failed: %s", cudaGetErrorString(e));
   return check_launch("rkv_append_quant_f32");
 }

@@ -66,26 +66,10 @@ __device__ __forceinline__ int scale_exponent_bf16bits(uint32_t amax_bits) {
 }
 
 // Packed f32x2 arithmetic (sm_100): lo lane in bits 0..31.
-__device__ __forceinline__ unsigned long long mul_f32x2(unsigned long long a, unsigned long long b) {
-  unsigned long long r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
 __device__ __forceinline__ unsigned long long add_f32x2(unsigned long long a, unsigned long long b) {
   unsigned long long r;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
-}
-
-// -0.0 -> +0.0 in both halves of a packed pair (the reference's code sign is
-// `x < 0`, so a zero, negative or not, gets code 0x00).  Done on the bits: an
-// `add.rn.f32x2` of +0.0 after the multiply can be contracted by ptxas into a
-// fused multiply-add, which keeps the sign of a product that underflows to 0.
-__device__ __forceinline__ unsigned long long clear_zero_sign2(unsigned long long t) {
-  uint32_t lo = (uint32_t)t, hi = (uint32_t)(t >> 32);
-  lo = (lo & 0x7fffffffu) ? lo : 0u;
-  hi = (hi & 0x7fffffffu) ? hi : 0u;
-  return ((unsigned long long)hi << 32) | lo;
 }
 
 // One bf16 pair -> two E4M3 codes (bits 0..15): t = v * 2^-e exactly as the

@@ -44,9 +44,13 @@ __device__ __forceinline__ void load_row_f32(const uint8_t* rows, const int32_t*
   x.slot = __ldg(slots + r % n_tokens);
 }
 
-__device__ __forceinline__ uint32_t quant_pair_f32(uint32_t lo, uint32_t hi, unsigned long long inv2) {
+// Two f32 lanes -> two codes with quant_pair's arithmetic: the product as
+// fma.rn.f32x2 with the run-time -0.0 pair nz2 (exactly the rounded product),
+// then add.rn.f32x2 of +0.0 (a zero of either sign becomes +0.0).
+__device__ __forceinline__ uint32_t quant_pair_f32(uint32_t lo, uint32_t hi, unsigned long long inv2,
+                                                   unsigned long long nz2) {
   const unsigned long long v = ((unsigned long long)hi << 32) | lo;
-  const unsigned long long t = clear_zero_sign2(mul_f32x2(v, inv2));
+  const unsigned long long t = add_f32x2(fma_f32x2(v, inv2, nz2), 0ull);
   return cvt_e4m3x2(__uint_as_float((uint32_t)t), __uint_as_float((uint32_t)(t >> 32)));
 }
 
@@ -62,7 +66,8 @@ __device__ __forceinline__ uint32_t bf16x2_rn(uint32_t lo, uint32_t hi) {
 }
 
 __device__ __forceinline__ void append_row_f32(const rkv_pool_view& pool, int layer, const RowF32& x,
-                                               const ThresholdTable& tab, uint32_t* status, int lane) {
+                                               const ThresholdTable& tab, uint32_t* status, int lane,
+                                               unsigned long long nz2) {
   const unsigned FULL = 0xffffffffu;
   if (x.slot < 0) return;
   const int64_t page = x.slot >> 6;
@@ -85,9 +90,9 @@ __device__ __forceinline__ void append_row_f32(const rkv_pool_view& pool, int la
   const unsigned long long inv2 = ((unsigned long long)invb << 32) | invb;
   uint32_t c[8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) c[i] = quant_pair_f32(x.a[2 * i], x.a[2 * i + 1], inv2);
+  for (int i = 0; i < 4; ++i) c[i] = quant_pair_f32(x.a[2 * i], x.a[2 * i + 1], inv2, nz2);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) c[4 + i] = quant_pair_f32(x.b[2 * i], x.b[2 * i + 1], inv2);
+  for (int i = 0; i < 4; ++i) c[4 + i] = quant_pair_f32(x.b[2 * i], x.b[2 * i + 1], inv2, nz2);
   uint8_t* pg = page_base(pool, layer, page);
   st_stream16(pg + codes_off(off) + lane * 16,
               make_uint4(c[0] | (c[1] << 16), c[2] | (c[3] << 16), c[4] | (c[5] << 16), c[6] | (c[7] << 16)));
