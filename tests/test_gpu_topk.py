@@ -94,3 +94,24 @@ def test_large_bin_refinement(cuda, orc):
     s[1] = (1.0 + rng.integers(0, 16, n) * 2.0 ** -23).astype(np.float32)  # only 16 distinct values
     n_visible = np.full(n_q, n, np.int32)
     check(orc, s, n_visible, k, run(s, n_visible, k, cuda))
+
+
+@pytest.mark.parametrize("k", [4096, 2048, 512, 1])
+def test_sampled_threshold_near_the_buffer_size(cuda, orc, k):
+    """Rows just above the 8192-key buffer take the sampled-threshold path
+    (a 2048-key sample); with k up to the maximum the sample rank and the
+    expected candidate count are at their largest.  Also rows sorted
+    ascending and rows whose large scores all sit in one region, which the
+    evenly spread sample chunks must still bound."""
+    rng = np.random.default_rng(100 + k)
+    lens = np.array([8193, 8200, 8320, 9000, 12000, 16384, 20000, 24576], np.int32)
+    n = int(lens.max())
+    s = rng.standard_normal((3 * lens.size, n)).astype(np.float32)
+    for i in range(lens.size):
+        s[lens.size + i, :lens[i]] = np.sort(s[lens.size + i, :lens[i]])
+        r = s[2 * lens.size + i]
+        r[:lens[i]] = -np.abs(r[:lens[i]])
+        lo = int(lens[i]) // 3
+        r[lo:lo + 3000] = np.abs(r[lo:lo + 3000]) + 1.0
+    n_visible = np.tile(lens, 3)
+    check(orc, s, n_visible, k, run(s, n_visible, k, cuda))
