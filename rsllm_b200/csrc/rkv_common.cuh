@@ -106,6 +106,14 @@ __device__ __forceinline__ uint32_t cvt_f16x2_from_e4m3x2(uint32_t two_codes) {
   return r;
 }
 
+// Four E4M3 bytes -> two f16x2 words (codes 0-1 in lo, 2-3 in hi): the word
+// is split into its two 16-bit halves instead of shifting the upper pair down.
+__device__ __forceinline__ void cvt_f16x2x2_from_e4m3x4(uint32_t four_codes, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\tcvt.rn.f16x2.e4m3x2 %0, a;\n\tcvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(four_codes));
+}
+
 __device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
   uint32_t r;
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
@@ -146,16 +154,24 @@ __device__ __forceinline__ uint32_t dequant2(uint32_t two_codes, const DecodeSca
   return y;
 }
 
+// Two f16x2 words of E4M3 values -> bf16x2 times the block scale (dequant2's
+// second half).
+__device__ __forceinline__ uint32_t rebias_scale2(uint32_t h, const DecodeScale& d) {
+  uint32_t y = (h & 0x80008000u) | ((h >> 3) & 0x0fff0fffu);
+  y = mul_bf16x2(y, d.m1);
+  if (d.two) y = mul_bf16x2(y, d.m2);
+  return y;
+}
+
 // 16 codes (uint4) -> 16 bf16 lanes (two uint4).
 __device__ __forceinline__ void dequant16(const uint4& c, const DecodeScale& d, uint4& o0, uint4& o1) {
-  o0.x = dequant2(c.x & 0xffffu, d);
-  o0.y = dequant2(c.x >> 16, d);
-  o0.z = dequant2(c.y & 0xffffu, d);
-  o0.w = dequant2(c.y >> 16, d);
-  o1.x = dequant2(c.z & 0xffffu, d);
-  o1.y = dequant2(c.z >> 16, d);
-  o1.z = dequant2(c.w & 0xffffu, d);
-  o1.w = dequant2(c.w >> 16, d);
+  uint32_t h[8];
+  cvt_f16x2x2_from_e4m3x4(c.x, h[0], h[1]);
+  cvt_f16x2x2_from_e4m3x4(c.y, h[2], h[3]);
+  cvt_f16x2x2_from_e4m3x4(c.z, h[4], h[5]);
+  cvt_f16x2x2_from_e4m3x4(c.w, h[6], h[7]);
+  o0 = make_uint4(rebias_scale2(h[0], d), rebias_scale2(h[1], d), rebias_scale2(h[2], d), rebias_scale2(h[3], d));
+  o1 = make_uint4(rebias_scale2(h[4], d), rebias_scale2(h[5], d), rebias_scale2(h[6], d), rebias_scale2(h[7], d));
 }
 
 // 16 bf16 lanes (8 words) -> 16 codes (uint4); nz2: -0.0 in both halves, a
