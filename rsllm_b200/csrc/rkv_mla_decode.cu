@@ -231,6 +231,7 @@ struct Params {
   float* ws_ml;        // [n_q][n_splits][64][2]
   float* out;          // [n_q][64][512]
   uint32_t* status;
+  uint32_t m29;        // 2^29, for dequant16_mh
 };
 
 __device__ __forceinline__ void set_abort(volatile int* abort_flag, uint32_t* status) {
@@ -518,8 +519,8 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
         const DecodeScale ds = decode_scale(__uint_as_float((lane & 2) ? t.scl[2 * sg + 1] : t.scl[2 * sg]));
         const int c0 = 8 * (2 * sg + ((lane & 3) >> 1)) + 4 * (lane & 1);
         uint4 o0, o1, o2, o3;
-        dequant16(make_uint4(t.codes[sg][0], t.codes[sg][1], t.codes[sg][2], t.codes[sg][3]), ds, o0, o1);
-        dequant16(make_uint4(t.codes[sg][4], t.codes[sg][5], t.codes[sg][6], t.codes[sg][7]), ds, o2, o3);
+        dequant16_mh(make_uint4(t.codes[sg][0], t.codes[sg][1], t.codes[sg][2], t.codes[sg][3]), ds, o0, o1, p.m29);
+        dequant16_mh(make_uint4(t.codes[sg][4], t.codes[sg][5], t.codes[sg][6], t.codes[sg][7]), ds, o2, o3, p.m29);
         *reinterpret_cast<uint4*>(stage + sw_off(r, c0)) = o0;
         *reinterpret_cast<uint4*>(stage + sw_off(r, c0 + 1)) = o1;
         *reinterpret_cast<uint4*>(stage + sw_off(r, c0 + 2)) = o2;
@@ -796,6 +797,7 @@ extern "C" rkv_status rkv_mla_decode_fp8(const rkv_pool_view* pool, int32_t laye
   prm.ws_ml = ws ? ws + (int64_t)n_q * n_splits * kHeads * kV : nullptr;
   prm.out = out;
   prm.status = d_status;
+  prm.m29 = 1u << 29;
   cudaStream_t s = (cudaStream_t)stream;
   mla_decode_kernel<<<dim3(n_splits, n_q), kThreads, kSmemAlloc, s>>>(prm);
   if (n_splits > 1) mla_combine_kernel<<<dim3(kHeads, n_q), 128, 0, s>>>(prm.ws_o, prm.ws_ml, n_splits, sinks, out);
