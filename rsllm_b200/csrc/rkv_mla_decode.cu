@@ -463,6 +463,12 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
       }
       slots[tb * 64 + lane] = s0;
       slots[tb * 64 + lane + 32] = s1;
+      // dense: the tile is one page, 43 KB contiguous -- pull it into L2 now,
+      // up to four tiles before the loaders read it
+      if (!p.idx && lane == 0 && s0 >= 0)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(page_base(p.pool, p.layer, s0 >> 6)),
+                     "r"((uint32_t)kPageBytes)
+                     : "memory");
       const unsigned b0 = __ballot_sync(0xffffffffu, s0 >= 0), b1 = __ballot_sync(0xffffffffu, s1 >= 0);
       if (lane == 0) masks[j & 15] = ((uint64_t)b1 << 32) | b0;
       mbar_arrive(bar + kBarTabFull + 8 * tb);
