@@ -421,29 +421,31 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
     // table j & 3 and the key mask j & 15.  Index loads for tile j + 1 are
     // issued before tile j's page-table loads are consumed.
     const int32_t* pt_row = p.page_table + (int64_t)seq * p.pt_stride;
-    int first_zero = 0x7fffffff;  // later zeros repeat the top-k fill value
-    if (p.idx) {
-      const int32_t* il = p.idx + (int64_t)qi * p.k;
-      for (int i = lane; i < p.k; i += 32)
-        if (__ldg(il + i) == 0) {
-          first_zero = i;
-          break;
-        }
-      first_zero = __reduce_min_sync(0xffffffffu, first_zero);
-    }
     // The key position of row (j, l) or -1; for an index list, the entry.
     auto position = [&](int j, int row) -> int {
       const int pos = j * kTile + row;
       if (p.idx) {
         if (pos >= p.k) return -1;
         const int tok = __ldg(p.idx + (int64_t)qi * p.k + pos);
-        return (tok >= 0 && tok < len && (tok != 0 || pos == first_zero)) ? tok : -1;
+        return (tok >= 0 && tok < len) ? tok : -1;
       }
       return page0 * kTile + pos < len ? page0 * kTile + pos : -1;
     };
+    // Later zeros of an index list repeat the top-k fill value: only the
+    // list's first 0 is a key.  Tiles are resolved in list order (rows 0-31,
+    // then 32-63), so the first 0 met here is the list's first.
+    bool zero_seen = false;
     int tok0 = n_tiles > 0 ? position(0, lane) : -1, tok1 = n_tiles > 0 ? position(0, lane + 32) : -1;
     for (int j = 0; j < n_tiles; ++j) {
       const int tb = j & 3;
+      if (p.idx) {
+        const unsigned z0 = __ballot_sync(0xffffffffu, tok0 == 0), z1 = __ballot_sync(0xffffffffu, tok1 == 0);
+        const unsigned keep0 = zero_seen ? 0u : (z0 & (0u - z0));
+        const unsigned keep1 = (zero_seen || z0) ? 0u : (z1 & (0u - z1));
+        zero_seen = zero_seen || (z0 | z1) != 0u;
+        if (tok0 == 0 && !((keep0 >> lane) & 1u)) tok0 = -1;
+        if (tok1 == 0 && !((keep1 >> lane) & 1u)) tok1 = -1;
+      }
       const int pg0 = tok0 >= 0 ? __ldg(pt_row + tok0 / 64) : -1;
       const int pg1 = tok1 >= 0 ? __ldg(pt_row + tok1 / 64) : -1;
       const int ntok0 = j + 1 < n_tiles ? position(j + 1, lane) : -1;

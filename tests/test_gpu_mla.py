@@ -93,3 +93,28 @@ def test_sparse_from_topk(cuda, orc):
     assert (idx[0] == 0).sum() > 1
     got = run_gpu(case, q, sq, idx, None, 1 / 24.0, 1, cuda)
     check(orc, case, q, sq, idx, None, 1 / 24.0, got, "sparse top-k")
+
+
+@pytest.mark.parametrize("where", ["first_entry", "mid_tile_upper_half", "later_tile", "none"])
+def test_sparse_first_zero_only(cuda, orc, where):
+    """Only an index list's first 0 is a key; later 0s repeat the top-k fill
+    value and are dropped.  The first 0 sits at different rows and tiles
+    (including rows 32-63 of a tile and the list's first entry) with more 0s
+    before and after tile boundaries; the oracle applies the same rule."""
+    lens = [3000, 900]
+    case = mc.build(orc, lens, seed=30)
+    q, sq = mc.queries(4, len(lens), seed=31)
+    k = 320  # five 64-key tiles
+    rng = np.random.default_rng(32)
+    idx = np.empty((4, k), np.int32)
+    for i, s in enumerate(sq):
+        row = rng.permutation(np.arange(1, lens[s]))[:k].astype(np.int32)
+        first = {"first_entry": 0, "mid_tile_upper_half": 64 + 40, "later_tile": 3 * 64 + 5, "none": None}[where]
+        if first is not None:
+            row[first] = 0
+            for extra in (first + 1, first + 33, first + 70, k - 1):
+                if extra < k:
+                    row[extra] = 0
+        idx[i] = row
+    got = run_gpu(case, q, sq, idx, None, 1 / 24.0, 1, cuda)
+    check(orc, case, q, sq, idx, None, 1 / 24.0, got, f"sparse first zero {where}")
