@@ -300,47 +300,44 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // Q of this query, staged through stage 2 (free until the third tile is
-  // loaded): every thread copies a share (chunk c of head h at 16-byte
-  // position (c & ~7) | ((c ^ h) & 7) of row h, so that 16 heads read in
-  // parallel below fall on different banks).
-  {
-    const uint4* qg = reinterpret_cast<const uint4*>(p.q + (int64_t)qi * kHeads * kQk);
-    uint8_t* qs = smem + kSmemK0 + 2 * kOperandBytes;
-    for (int c = tid; c < kHeads * kQk / 8; c += kThreads) {
-      const int h = c / (kQk / 8), cc = c % (kQk / 8);
-      *reinterpret_cast<uint4*>(qs + h * (kQk * 2) + (((cc & ~7) | ((cc ^ h) & 7)) << 4)) = __ldg(qg + c);
-    }
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (warp < 4) {
-    // Q into TMEM as the A operand of S = Q K^T: head h in lane
-    // (h % 16) + 32 (h / 16), bf16 pairs along columns 0-287.  Lanes 16-31
-    // receive the same values; they hold O, which the first O update
-    // overwrites.
+    // Q into TMEM as the A operand of S = Q K^T, straight from global memory
+    // (the other roles start at once): head h in lane (h % 16) + 32 (h / 16),
+    // bf16 pairs along columns 0-287, one 64-lane column per store with the
+    // next column's loads already in flight.  Lanes 16-31 load the same
+    // addresses in the same instructions (merged) and write the same values
+    // into lanes 16-31, which hold O: the first O update overwrites them.
     const int h = warp * 16 + (lane & 15);
-    const uint8_t* qrow = smem + kSmemK0 + 2 * kOperandBytes + h * (kQk * 2);
+    const uint4* qrow = reinterpret_cast<const uint4*>(p.q + ((int64_t)qi * kHeads + h) * kQk);
     const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+    uint4 cur[8], nxt[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) cur[i] = __ldg(qrow + i);
 #pragma unroll 1
     for (int c = 0; c < kQk / 64; ++c) {
+      if (c + 1 < kQk / 64) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) nxt[i] = __ldg(qrow + 8 * (c + 1) + i);
+      }
       uint32_t v[32];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int cc = 8 * c + i;
-        const uint4 w = *reinterpret_cast<const uint4*>(qrow + (((cc & ~7) | ((cc ^ h) & 7)) << 4));
-        v[4 * i] = w.x;
-        v[4 * i + 1] = w.y;
-        v[4 * i + 2] = w.z;
-        v[4 * i + 3] = w.w;
+        v[4 * i] = cur[i].x;
+        v[4 * i + 1] = cur[i].y;
+        v[4 * i + 2] = cur[i].z;
+        v[4 * i + 3] = cur[i].w;
       }
       tmem_st32(tl + 32 * c, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
     }
     tmem_wait_st();
     tc_fence_before();
-    mbar_arrive(bar + kBarQReady);  // also hands stage 2 back to the loaders
+    mbar_arrive(bar + kBarQReady);
   }
 
   if (warp == kQkWarp || warp == kQkWarp + 1) {
@@ -512,15 +509,12 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
       }
       return true;
     };
-    // Waits for the stage (the O update three tiles back; stage 2 also for
-    // Q to leave it), then dequantises.  Per store instruction the warp writes
+    // Waits for the stage (the O update three tiles back), then dequantises.  Per store instruction the warp writes
     // 8 rows x 4 lanes of 16 B whose swizzled positions cover the 8 bank
     // groups evenly (4 wavefronts for 512 B, the minimum).
     auto store = [&](int j, const TileRegs& t) -> bool {
       const int b = j % kStages;
-      if (j < kStages ? (j == 2 && !mbar_wait(bar + kBarQReady, 0, abort_flag))
-                      : !mbar_wait(bar + kBarKEmpty + 8 * b, (j / kStages - 1) & 1, abort_flag))
-        return false;
+      if (j >= kStages && !mbar_wait(bar + kBarKEmpty + 8 * b, (j / kStages - 1) & 1, abort_flag)) return false;
       uint8_t* stage = smem + kSmemK0 + b * kOperandBytes;
 #pragma unroll
       for (int sg = 0; sg < 4; ++sg) {
