@@ -1504,7 +1504,7 @@ def main():
                                        "split", "topk", "f32"],
                     default="all",
                     help="run one workload alone (profiling)")
-    ap.add_argument("--mla-splits", type=int, default=16,
+    ap.add_argument("--mla-splits", type=int, default=9,
                     help="page-range splits per query for the dense MLA decode phase")
     ap.add_argument("--small", action="store_true",
                     help="profiling sizes for the phases: 8 seqs / 1 layer (gather), 4 seqs / 1 layer (sparse)")
