@@ -34,7 +34,8 @@
 // 0-287 (bf16 pairs) and S double-buffered at 288 and 352 -- an MMA with A in
 // TMEM keeps its accumulator in those same lanes.  Lanes 16-31: O, latent
 // 0-255 at columns 0-255 and 256-511 at 256-511.  Keeping Q out of shared
-// memory leaves room for three K/V stages (72 KB each) and P (8 KB).
+// memory leaves room for three K/V stages (72 KB each) and P (8 KB); Q passes
+// through stage 2 and P on its way into TMEM, before either is needed.
 //
 // Three stages keep the loads and the dequantisation ahead of the tensor
 // cores.  The online softmax keeps a per-head reference maximum m and
@@ -70,6 +71,15 @@ constexpr int kSmemBar = kSmemP + kColBytes;
 constexpr int kSmemRows = kSmemBar + 336;     // slot tables: 4 x 64 x int32 (page * 64 + row, -1 = none)
 constexpr int kSmemTotal = kSmemRows + 4 * 64 * 4;
 constexpr int kSmemAlloc = kSmemTotal + 1024; // slack for the 1024-byte alignment
+// Q arrives by bulk copies into stage 2 and P, which nothing else uses before
+// tile 2 is stored: row h at q_row_off(h), 16 B further round the banks per
+// row so that 16 rows read together take the minimum two wavefronts.
+constexpr int kSmemQ = kSmemK0 + (kStages - 1) * kOperandBytes;
+constexpr int kQRowBytes = kQk * 2;
+__host__ __device__ constexpr int q_row_off(int h) {
+  return (h >> 3) * (8 * kQRowBytes + 128) + (h & 7) * (kQRowBytes + 16);
+}
+static_assert(kSmemQ + q_row_off(kHeads - 1) + kQRowBytes <= kSmemP + kColBytes, "Q staging overruns P");
 constexpr int kThreads = 480;  // warps 0-3 softmax, 4-11 loaders, 12 S issuer, 13 O issuer, 14 resolver
 constexpr int kLoaders = 256;
 constexpr int kQkWarp = 12, kResolverWarp = 14;
@@ -84,7 +94,7 @@ constexpr uint64_t kTimeoutNs = 1000000000ull;
 // masks by j & 15.
 constexpr int kBarKFull = 0, kBarKEmpty = 24, kBarSFull = 48, kBarSFree = 64, kBarPFull = 80, kBarPvDone = 88,
               kBarDrain = 96, kBarQReady = 112, kBarTabFull = 120, kBarTabFree = 152;  // drain: S and O issuers
-constexpr int kTmemSlot = 184, kAbort = 188, kMask = 200;
+constexpr int kTmemSlot = 184, kAbort = 188, kBarQLoad = 192, kMask = 200;
 
 constexpr uint32_t kIdescQK = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((64u >> 4) << 24);
 constexpr uint32_t kIdescPV = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((256u >> 3) << 17) | ((64u >> 4) << 24);
@@ -110,6 +120,23 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
       : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
+}
+// Bounded wait for a bulk copy's barrier; it ignores the abort flag, so that a
+// CTA never leaves with a copy into its shared memory still in flight.
+__device__ bool mbar_wait_copy(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = now_ns();
+  while (!mbar_test(bar, parity))
+    if (now_ns() - t0 > kTimeoutNs) return false;
+  return true;
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// Global -> shared bulk copy (no multicast), completing on an mbarrier.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
 }
 // Bounded wait for the phase of the given parity; false on timeout or abort.
 __device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
@@ -291,6 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
     mbar_init(bar + kBarPFull, 128);
     mbar_init(bar + kBarPvDone, 1);
     mbar_init(bar + kBarQReady, 128);
+    mbar_init(bar + kBarQLoad, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -305,37 +333,39 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (warp < 4) {
-    // Q into TMEM as the A operand of S = Q K^T, straight from global memory
-    // (the other roles start at once): head h in lane (h % 16) + 32 (h / 16),
-    // bf16 pairs along columns 0-287, one 64-lane column per store with the
-    // next column's loads already in flight.  Lanes 16-31 load the same
-    // addresses in the same instructions (merged) and write the same values
-    // into lanes 16-31, which hold O: the first O update overwrites them.
-    const int h = warp * 16 + (lane & 15);
-    const uint4* qrow = reinterpret_cast<const uint4*>(p.q + ((int64_t)qi * kHeads + h) * kQk);
-    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-    uint4 cur[8], nxt[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) cur[i] = __ldg(qrow + i);
-#pragma unroll 1
-    for (int c = 0; c < kQk / 64; ++c) {
-      if (c + 1 < kQk / 64) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) nxt[i] = __ldg(qrow + 8 * (c + 1) + i);
-      }
-      uint32_t v[32];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        v[4 * i] = cur[i].x;
-        v[4 * i + 1] = cur[i].y;
-        v[4 * i + 2] = cur[i].z;
-        v[4 * i + 3] = cur[i].w;
-      }
-      tmem_st32(tl + 32 * c, v);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
+    // Q into TMEM as the A operand of S = Q K^T: one bulk copy per head row
+    // into shared memory (all 73 KB in flight at once), then head h into lane
+    // (h % 16) + 32 (h / 16), bf16 pairs along columns 0-287.  Lanes 16-31
+    // read the same addresses (broadcast) and write the same values into
+    // lanes 16-31, which hold O: the first O update overwrites them.
+    if (warp == 0) {
+      if (lane == 0) mbar_expect_tx(bar + kBarQLoad, kHeads * kQRowBytes);
+      __syncwarp();
+      const uint8_t* qsrc = reinterpret_cast<const uint8_t*>(p.q + (int64_t)qi * kHeads * kQk);
+      for (int h = lane; h < kHeads; h += 32)
+        bulk_g2s(sbase + kSmemQ + q_row_off(h), qsrc + h * kQRowBytes, kQRowBytes, bar + kBarQLoad);
     }
-    tmem_wait_st();
+    const int h = warp * 16 + (lane & 15);
+    const uint8_t* qs = smem + kSmemQ + q_row_off(h);
+    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+    if (mbar_wait_copy(bar + kBarQLoad, 0)) {
+#pragma unroll 1
+      for (int c = 0; c < kQk / 64; ++c) {
+        uint32_t v[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint4 u = *reinterpret_cast<const uint4*>(qs + 16 * (8 * c + i));
+          v[4 * i] = u.x;
+          v[4 * i + 1] = u.y;
+          v[4 * i + 2] = u.z;
+          v[4 * i + 3] = u.w;
+        }
+        tmem_st32(tl + 32 * c, v);
+      }
+      tmem_wait_st();
+    } else {
+      set_abort(abort_flag, p.status);
+    }
     tc_fence_before();
     mbar_arrive(bar + kBarQReady);
   }
@@ -509,12 +539,14 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
       }
       return true;
     };
-    // Waits for the stage (the O update three tiles back), then dequantises.  Per store instruction the warp writes
+    // Waits for the stage (the O update three tiles back; for tile 2, Q's
+    // move out of the staging area), then dequantises.  Per store instruction the warp writes
     // 8 rows x 4 lanes of 16 B whose swizzled positions cover the 8 bank
     // groups evenly (4 wavefronts for 512 B, the minimum).
     auto store = [&](int j, const TileRegs& t) -> bool {
       const int b = j % kStages;
       if (j >= kStages && !mbar_wait(bar + kBarKEmpty + 8 * b, (j / kStages - 1) & 1, abort_flag)) return false;
+      if (j == kStages - 1 && !mbar_wait(bar + kBarQReady, 0, abort_flag)) return false;  // Q staging read
       uint8_t* stage = smem + kSmemK0 + b * kOperandBytes;
 #pragma unroll
       for (int sg = 0; sg < 4; ++sg) {
