@@ -229,6 +229,20 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+__device__ __forceinline__ unsigned long long pk2(uint32_t lo, uint32_t hi) {
+  return ((unsigned long long)hi << 32) | lo;
+}
+__device__ __forceinline__ unsigned long long mul_f32x2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// max(a, b, c) in one instruction (sm_100); NaN handling as fmaxf.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -590,6 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
     const int hA = warp * 16 + g4, hB = hA + 8;
     const uint32_t tS = tmem + ((uint32_t)(warp * 32) << 16), tO = tS + kLaneO;
     float mA = -INFINITY, mB = -INFINITY, lA = 0.0f, lB = 0.0f;  // m: per head; l: this thread's keys
+    const unsigned long long sc2 = pk2(__float_as_uint(p.scale_log2), __float_as_uint(p.scale_log2));
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int b = j & 1;
@@ -606,14 +621,34 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
       tc_fence_before();
       mbar_arrive(bar + kBarSFree + 8 * b);  // S buffer b may be overwritten
       const uint64_t mask = masks[j & 15];
+      // Every key of the tile present (the same for all threads; all but the
+      // last tile of a dense range): packed scaling, three-input maxima and
+      // packed exponent arguments, with no masking.
+      const bool full = mask == ~0ull;
       float mxA = -INFINITY, mxB = -INFINITY;
+      if (full) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int key = 8 * (i >> 2) + 2 * t4 + (i & 1);
-        const float x = ((mask >> key) & 1) ? __uint_as_float(sv[i]) * p.scale_log2 : -INFINITY;
-        sv[i] = __float_as_uint(x);
-        if (i & 2) mxB = fmaxf(mxB, x);
-        else mxA = fmaxf(mxA, x);
+        for (int i = 0; i < 32; i += 2) {
+          const unsigned long long x2 = mul_f32x2(pk2(sv[i], sv[i + 1]), sc2);
+          sv[i] = (uint32_t)x2;
+          sv[i + 1] = (uint32_t)(x2 >> 32);
+        }
+        mxA = fmaxf(__uint_as_float(sv[0]), __uint_as_float(sv[1]));
+        mxB = fmaxf(__uint_as_float(sv[2]), __uint_as_float(sv[3]));
+#pragma unroll
+        for (int r = 1; r < 8; ++r) {
+          mxA = fmax3(mxA, __uint_as_float(sv[4 * r]), __uint_as_float(sv[4 * r + 1]));
+          mxB = fmax3(mxB, __uint_as_float(sv[4 * r + 2]), __uint_as_float(sv[4 * r + 3]));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int key = 8 * (i >> 2) + 2 * t4 + (i & 1);
+          const float x = ((mask >> key) & 1) ? __uint_as_float(sv[i]) * p.scale_log2 : -INFINITY;
+          sv[i] = __float_as_uint(x);
+          if (i & 2) mxB = fmaxf(mxB, x);
+          else mxA = fmaxf(mxA, x);
+        }
       }
       mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 1));
       mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 2));
@@ -634,14 +669,31 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
         lB *= alB;
       }
       uint32_t pa[8], pb[8];  // bf16 pairs: keys 8 r + 2 t4, +1 of hA / hB
+      if (full) {  // mA and mB are finite here: the tile's maxima are
+        const unsigned long long nA = pk2(__float_as_uint(-mA), __float_as_uint(-mA));
+        const unsigned long long nB = pk2(__float_as_uint(-mB), __float_as_uint(-mB));
+        unsigned long long sumA = 0ull, sumB = 0ull;  // the bf16-rounded weights, even and odd keys
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const float x0 = __uint_as_float(sv[4 * r]), x1 = __uint_as_float(sv[4 * r + 1]);
-        const float y0 = __uint_as_float(sv[4 * r + 2]), y1 = __uint_as_float(sv[4 * r + 3]);
-        pa[r] = pack_bf16x2(x0 > -INFINITY ? ex2(x0 - mA) : 0.0f, x1 > -INFINITY ? ex2(x1 - mA) : 0.0f);
-        pb[r] = pack_bf16x2(y0 > -INFINITY ? ex2(y0 - mB) : 0.0f, y1 > -INFINITY ? ex2(y1 - mB) : 0.0f);
-        lA += __uint_as_float(pa[r] << 16) + __uint_as_float(pa[r] & 0xffff0000u);
-        lB += __uint_as_float(pb[r] << 16) + __uint_as_float(pb[r] & 0xffff0000u);
+        for (int r = 0; r < 8; ++r) {
+          const unsigned long long a2 = add_f32x2(pk2(sv[4 * r], sv[4 * r + 1]), nA);
+          const unsigned long long b2 = add_f32x2(pk2(sv[4 * r + 2], sv[4 * r + 3]), nB);
+          pa[r] = pack_bf16x2(ex2(__uint_as_float((uint32_t)a2)), ex2(__uint_as_float((uint32_t)(a2 >> 32))));
+          pb[r] = pack_bf16x2(ex2(__uint_as_float((uint32_t)b2)), ex2(__uint_as_float((uint32_t)(b2 >> 32))));
+          sumA = add_f32x2(sumA, pk2(pa[r] << 16, pa[r] & 0xffff0000u));
+          sumB = add_f32x2(sumB, pk2(pb[r] << 16, pb[r] & 0xffff0000u));
+        }
+        lA += __uint_as_float((uint32_t)sumA) + __uint_as_float((uint32_t)(sumA >> 32));
+        lB += __uint_as_float((uint32_t)sumB) + __uint_as_float((uint32_t)(sumB >> 32));
+      } else {
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const float x0 = __uint_as_float(sv[4 * r]), x1 = __uint_as_float(sv[4 * r + 1]);
+          const float y0 = __uint_as_float(sv[4 * r + 2]), y1 = __uint_as_float(sv[4 * r + 3]);
+          pa[r] = pack_bf16x2(x0 > -INFINITY ? ex2(x0 - mA) : 0.0f, x1 > -INFINITY ? ex2(x1 - mA) : 0.0f);
+          pb[r] = pack_bf16x2(y0 > -INFINITY ? ex2(y0 - mB) : 0.0f, y1 > -INFINITY ? ex2(y1 - mB) : 0.0f);
+          lA += __uint_as_float(pa[r] << 16) + __uint_as_float(pa[r] & 0xffff0000u);
+          lB += __uint_as_float(pb[r] << 16) + __uint_as_float(pb[r] & 0xffff0000u);
+        }
       }
       // P and O are free once the O update of tile j - 1 is done.
       if (!bar_all(1, 128, j == 0 || mbar_wait(bar + kBarPvDone, (j - 1) & 1, abort_flag))) {
