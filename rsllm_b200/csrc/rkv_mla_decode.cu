@@ -10,7 +10,7 @@
 //
 // The FP8 rows are never written back as bf16: loader warps read a page's
 // codes, scales and RoPE lanes with 256-bit loads, dequantise them (exactly,
-// see rkv_common.cuh) straight into a 128-byte-swizzled shared-memory tile,
+// see BitScale below) straight into a 128-byte-swizzled shared-memory tile,
 // and the 5th-generation tensor cores consume that tile twice -- as K
 // (K-major) for S and as V (MN-major) for O:
 //
@@ -272,8 +272,51 @@ struct Params {
   float* ws_ml;        // [n_q][n_splits][64][2]
   float* out;          // [n_q][64][512]
   uint32_t* status;
-  uint32_t m29;        // 2^29, for dequant16_mh
 };
+
+// Latent lane order in shared memory and in Q's TMEM copy: within every group
+// of four lanes, stored order (0, 2, 1, 3).  The loaders then build each bf16
+// pair straight from two code bytes: an E4M3 byte's sign and 7 magnitude
+// bits placed as a bf16's sign, exponent and top mantissa bits read as
+// value * 2^-120 (normal or subnormal alike), so one bf16 multiply by
+// 2^(120+e) gives value * 2^e -- exact, or +-inf on overflow, the same bits
+// as the f32 product rounded to bf16.  S sums over lanes in any order the MMA
+// likes, so Q in the same lane order leaves it unchanged; O comes out with its
+// columns in that order and the epilogue writes them back in place.
+struct BitScale {
+  uint32_t m1, m2;  // bf16x2 multipliers: 2^(120+e), or 2^127 then 2^(e-7)
+  bool two;
+};
+__device__ __forceinline__ BitScale bit_scale(float scale) {
+  const uint32_t eb = (__float_as_uint(scale) >> 23) & 0xffu;  // e + 127
+  BitScale d;
+  if (eb <= 134u) {
+    const uint32_t h = (eb + 120u) << 7;
+    d.m1 = h | (h << 16);
+    d.m2 = 0u;
+    d.two = false;
+  } else {
+    const uint32_t h1 = 254u << 7, h2 = (eb - 7u) << 7;
+    d.m1 = h1 | (h1 << 16);
+    d.m2 = h2 | (h2 << 16);
+    d.two = true;
+  }
+  return d;
+}
+// Four codes (lanes 0-3, byte i = lane i) -> bf16 pairs (lane 0, lane 2) and
+// (lane 1, lane 3), times the block scale.
+__device__ __forceinline__ void dequant4_bits(uint32_t w, const BitScale& d, uint32_t& even, uint32_t& odd) {
+  uint32_t e = ((w << 8) & 0x80008000u) | ((w << 4) & 0x07f007f0u);
+  uint32_t o = (w & 0x80008000u) | ((w >> 4) & 0x07f007f0u);
+  e = mul_bf16x2(e, d.m1);
+  o = mul_bf16x2(o, d.m1);
+  if (d.two) {
+    e = mul_bf16x2(e, d.m2);
+    o = mul_bf16x2(o, d.m2);
+  }
+  even = e;
+  odd = o;
+}
 
 __device__ __forceinline__ void set_abort(volatile int* abort_flag, uint32_t* status) {
   *abort_flag = 1;
@@ -369,10 +412,17 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const uint4 u = *reinterpret_cast<const uint4*>(qs + 16 * (8 * c + i));
-          v[4 * i] = u.x;
-          v[4 * i + 1] = u.y;
-          v[4 * i + 2] = u.z;
-          v[4 * i + 3] = u.w;
+          if (c < kV / 64) {  // latent lanes in stored order (0, 2, 1, 3) per group of four
+            v[4 * i] = __byte_perm(u.x, u.y, 0x5410);
+            v[4 * i + 1] = __byte_perm(u.x, u.y, 0x7632);
+            v[4 * i + 2] = __byte_perm(u.z, u.w, 0x5410);
+            v[4 * i + 3] = __byte_perm(u.z, u.w, 0x7632);
+          } else {
+            v[4 * i] = u.x;
+            v[4 * i + 1] = u.y;
+            v[4 * i + 2] = u.z;
+            v[4 * i + 3] = u.w;
+          }
         }
         tmem_st32(tl + 32 * c, v);
       }
@@ -564,15 +614,15 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
       uint8_t* stage = smem + kSmemK0 + b * kOperandBytes;
 #pragma unroll
       for (int sg = 0; sg < 4; ++sg) {
-        const DecodeScale ds = decode_scale(__uint_as_float((lane & 2) ? t.scl[2 * sg + 1] : t.scl[2 * sg]));
+        const BitScale ds = bit_scale(__uint_as_float((lane & 2) ? t.scl[2 * sg + 1] : t.scl[2 * sg]));
         const int c0 = 8 * (2 * sg + ((lane & 3) >> 1)) + 4 * (lane & 1);
-        uint4 o0, o1, o2, o3;
-        dequant16_mh(make_uint4(t.codes[sg][0], t.codes[sg][1], t.codes[sg][2], t.codes[sg][3]), ds, o0, o1, p.m29);
-        dequant16_mh(make_uint4(t.codes[sg][4], t.codes[sg][5], t.codes[sg][6], t.codes[sg][7]), ds, o2, o3, p.m29);
-        *reinterpret_cast<uint4*>(stage + sw_off(r, c0)) = o0;
-        *reinterpret_cast<uint4*>(stage + sw_off(r, c0 + 1)) = o1;
-        *reinterpret_cast<uint4*>(stage + sw_off(r, c0 + 2)) = o2;
-        *reinterpret_cast<uint4*>(stage + sw_off(r, c0 + 3)) = o3;
+        uint32_t v[16];  // lanes in stored order, two per word
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dequant4_bits(t.codes[sg][i], ds, v[2 * i], v[2 * i + 1]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          *reinterpret_cast<uint4*>(stage + sw_off(r, c0 + k)) =
+              make_uint4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
       }
       *reinterpret_cast<uint4*>(stage + sw_off(r, 64 + 2 * (lane & 3))) =
           make_uint4(t.rope[0], t.rope[1], t.rope[2], t.rope[3]);
@@ -772,14 +822,17 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const Params p)
       }
 #pragma unroll
       for (int r = 0; r < 8; ++r) {
-        const int col = c + 8 * r + 2 * t4;
+        // stored columns 8 r + 2 t4 + {0, 1} are latent lanes l and l + 2
+        const int col = c + 8 * r + 4 * (t4 >> 1) + (t4 & 1);
         float2 va = make_float2(0.f, 0.f), vb = make_float2(0.f, 0.f);
         if (have_o) {
           va = make_float2(__uint_as_float(o[4 * r]) * scA, __uint_as_float(o[4 * r + 1]) * scA);
           vb = make_float2(__uint_as_float(o[4 * r + 2]) * scB, __uint_as_float(o[4 * r + 3]) * scB);
         }
-        *reinterpret_cast<float2*>(dA + col) = va;
-        *reinterpret_cast<float2*>(dB + col) = vb;
+        dA[col] = va.x;
+        dA[col + 2] = va.y;
+        dB[col] = vb.x;
+        dB[col + 2] = vb.y;
       }
     }
   }
@@ -883,7 +936,6 @@ extern "C" rkv_status rkv_mla_decode_fp8(const rkv_pool_view* pool, int32_t laye
   prm.ws_ml = ws ? ws + (int64_t)n_q * n_splits * kHeads * kV : nullptr;
   prm.out = out;
   prm.status = d_status;
-  prm.m29 = 1u << 29;
   cudaStream_t s = (cudaStream_t)stream;
   mla_decode_kernel<<<dim3(n_splits, n_q), kThreads, kSmemAlloc, s>>>(prm);
   if (n_splits > 1) mla_combine_kernel<<<dim3(kHeads, n_q), 128, 0, s>>>(prm.ws_o, prm.ws_ml, n_splits, sinks, out);
