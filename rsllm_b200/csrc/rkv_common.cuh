@@ -163,35 +163,6 @@ __device__ __forceinline__ uint32_t rebias_scale2(uint32_t h, const DecodeScale&
   return y;
 }
 
-// rebias_scale2 with the 3-bit right shift done as a multiply-high by
-// m29 = 2^29 passed in at run time (a constant would be turned back into a
-// shift): it runs on the FMA pipe instead of the integer ALU, which bounds
-// the MLA loaders.  With both sign bits cleared first, (a * 2^29) >> 32 is
-// a >> 3 and nothing crosses between the halves (the low 7 mantissa bits of an
-// f16 E4M3 value are zero), so this equals rebias_scale2.
-__device__ __forceinline__ uint32_t rebias_scale2_mh(uint32_t h, const DecodeScale& d, uint32_t m29) {
-  uint32_t y;
-  asm("mul.hi.u32 %0, %1, %2;" : "=r"(y) : "r"(h & 0x7fff7fffu), "r"(m29));
-  y |= h & 0x80008000u;
-  y = mul_bf16x2(y, d.m1);
-  if (d.two) y = mul_bf16x2(y, d.m2);
-  return y;
-}
-
-// dequant16 through rebias_scale2_mh (m29 = 2^29, a run-time value).
-__device__ __forceinline__ void dequant16_mh(const uint4& c, const DecodeScale& d, uint4& o0, uint4& o1,
-                                             uint32_t m29) {
-  uint32_t h[8];
-  cvt_f16x2x2_from_e4m3x4(c.x, h[0], h[1]);
-  cvt_f16x2x2_from_e4m3x4(c.y, h[2], h[3]);
-  cvt_f16x2x2_from_e4m3x4(c.z, h[4], h[5]);
-  cvt_f16x2x2_from_e4m3x4(c.w, h[6], h[7]);
-  o0 = make_uint4(rebias_scale2_mh(h[0], d, m29), rebias_scale2_mh(h[1], d, m29), rebias_scale2_mh(h[2], d, m29),
-                  rebias_scale2_mh(h[3], d, m29));
-  o1 = make_uint4(rebias_scale2_mh(h[4], d, m29), rebias_scale2_mh(h[5], d, m29), rebias_scale2_mh(h[6], d, m29),
-                  rebias_scale2_mh(h[7], d, m29));
-}
-
 // 16 codes (uint4) -> 16 bf16 lanes (two uint4).
 __device__ __forceinline__ void dequant16(const uint4& c, const DecodeScale& d, uint4& o0, uint4& o1) {
   uint32_t h[8];
