@@ -118,3 +118,31 @@ def test_sparse_first_zero_only(cuda, orc, where):
         idx[i] = row
     got = run_gpu(case, q, sq, idx, None, 1 / 24.0, 1, cuda)
     check(orc, case, q, sq, idx, None, 1 / 24.0, got, f"sparse first zero {where}")
+
+
+def test_single_key_returns_its_row_exactly(cuda, orc):
+    """With one key the softmax weight is exactly 1, so each head's output is
+    that key's latent dequantised to bf16: checked bit for bit against the
+    oracle's dequantisation, over every finite E4M3 code and block scales from
+    2^-21 (the quantiser's floor) to 2^15 (the two-multiply range), which
+    covers the loaders' conversion and the epilogue's column order."""
+    n = 64
+    page = 43008
+    pool = orc.new_pool(n, 1).reshape(n, page)
+    codes = (np.arange(n * 512) % 256).astype(np.uint8)
+    codes[(codes & 0x7F) == 0x7F] -= 1  # no NaN codes: the quantiser never writes them
+    pool[:, :512] = codes.reshape(n, 512)
+    exps = (np.arange(n * 8) % 37 - 21).astype(np.int32)  # e = -21 .. 15
+    scales = np.ldexp(np.ones(n * 8, np.float32), exps).astype(np.float32)
+    pool[:, 64 * 512:64 * 512 + 32] = scales.view(np.uint8).reshape(n, 32)
+    rope = np.random.default_rng(30).standard_normal((n, 64))
+    pool[:, 64 * 544:64 * 544 + 128] = mc.bf16_bits(rope).view(np.uint8).reshape(n, 128)
+    case = dict(pool=pool.reshape(-1), n_pages=n, n_layers=1, layer=0,
+                pt=np.arange(n, dtype=np.int32)[:, None], lens=np.ones(n, np.int32))
+    q, sq = mc.queries(n, n, seed=31)
+    got = run_gpu(case, q, sq, None, None, 1 / 24.0, 1, cuda)
+    rows, st = orc.gather_rows(case["pool"], n, 1, 0, case["pt"], np.arange(n + 1, dtype=np.int32))
+    assert st == 0
+    want = (rows[:, :512].astype(np.uint32) << 16).view(np.float32)  # bf16 -> f32
+    # equal as values: the tensor core's f32 sum turns the -0.0 of code 0x80 into +0.0
+    assert np.array_equal(got, np.broadcast_to(want[:, None, :], got.shape))
