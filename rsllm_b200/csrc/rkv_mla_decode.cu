@@ -20,9 +20,10 @@
 //   warps 4-11 loaders, software-pipelined over two register buffers: the
 //              loads of tile j + 1 are in flight while tile j is
 //              dequantised into its stage
-//   warp 12    TMEM allocation and the MMA-issuing thread: issues S = Q K^T
-//              for every loaded tile and O += P V for every softmaxed tile
-//              as each becomes ready
+//   warp 12    TMEM allocation and S = Q K^T of every loaded tile
+//   warp 13    O += P V of every softmaxed tile
+//   warp 14    resolver: key rows to pool slots and key masks up to four
+//              tiles ahead; in dense mode an L2 prefetch of each tile's page
 //
 // Shapes per tile (64 key rows, one page in dense mode), M = 64 heads:
 //   S[64 x 64]   = Q[64 x 576] . K^T    36 MMAs of K = 16, N = 64; Q from
